@@ -1,0 +1,364 @@
+"""Benchmark: 8B-shape Q4_0 batch-1 decode on the B200 backend.
+
+A Llama-3-8B-shaped model (32 layers, d_model 4096, 32/8 heads, head 128, FFN 14336, vocab 128256,
+RoPE theta 500000) with N(0, 0.02) weights from seed 0, projections and output head in Q4_0, is
+written as a ggml-compiler GGUF (the program the reference compiler emits for that shape at -O3)
+and loaded through the C ABI. A 512-token prompt (seed 1) is prefilled, then greedy decode steps
+are timed (one step = one token through all 32 layers; n_kv = 768).
+
+- value: decode tok/s with every input resident on the device: the program's `generate` entry
+  runs K steps back to back (device loop); time from CUDA events on the model's stream.
+- e2e: the same decode through the public C API from host buffers, one `decode` entry per token
+  (host -> device copies of token/position/mask from pinned memory, device -> host logits, host
+  argmax), timed with CUDA events on the same stream.
+- roofline: the quantized GEMV kernels (the dominant kernel family), algorithmic bytes per launch
+  (Q4_0 weight bytes + activation bytes) / mean launch time from a profiled pass of the same steps.
+- cpu_baseline / --impl reference: the reference's CPU arithmetic (this repository's C
+  restatement of ggml's CPU path, oracle/) timed on the host's cores on a few decode tokens.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 8b|tiny]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "ggml-compiler_b200"))
+sys.path.insert(0, str(REPO))
+
+METRIC = "8B-shape Q4_0 decode tok/s; quant-GEMV HBM GB/s as % of B200 peak"
+CACHE = Path(os.environ.get("GCB_BENCH_CACHE", "/tmp/gcb_bench"))
+
+
+def shape_for(config: str):
+    from ggml_compiler_b200.llm import LLAMA3_8B, TINY, LlamaShape
+
+    if config == "8b":
+        return LLAMA3_8B, "llama3-8b-shape Q4_0, batch 1, 512-token prompt, greedy decode (BASELINE config 3)"
+    if config == "tiny":
+        sh = LlamaShape(**{**TINY.__dict__, "max_prompt": 512})
+        return sh, "tiny Llama Q8_0 (BASELINE config 1 shape), batch 1"
+    raise ValueError(config)
+
+
+def model_path(sh, config: str, rank: int, world: int) -> Path:
+    from ggml_compiler_b200.llm import build_llama_gguf
+
+    CACHE.mkdir(parents=True, exist_ok=True)
+    p = CACHE / f"{config}_{sh.weight_type}_seed0.gguf"
+    if rank == 0 and not p.exists():
+        tmp = p.with_suffix(".part")
+        t = time.time()
+        build_llama_gguf(tmp, sh, seed=0)
+        tmp.rename(p)
+        print(f"[bench] wrote {p} ({p.stat().st_size / 1e9:.2f} GB) in {time.time() - t:.1f}s", file=sys.stderr)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    return p
+
+
+def weight_bytes(sh) -> float:
+    """Quantized weight bytes streamed per decode token (every projection + the output head)."""
+    from ggml_compiler_b200.llm import llama_weights
+
+    per = {"q4_0": 18 / 32, "q8_0": 34 / 32, "f16": 2, "f32": 4}
+    tot = 0.0
+    for _, hf, shape, typ in llama_weights(sh):
+        if "embed_tokens" in hf:
+            continue  # one row gathered per token
+        tot += float(np.prod(shape)) * per[typ]
+    return tot
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device, self.proc, self.out = device, None, None
+
+    def __enter__(self):
+        try:
+            self.out = open(CACHE / f"clocks_{self.device}.csv", "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.out:
+            self.out.close()
+
+    def summary(self) -> dict:
+        try:
+            rows = [r.split(", ") for r in (CACHE / f"clocks_{self.device}.csv").read_text().strip().splitlines()]
+        except OSError:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        rows = [r for r in rows if len(r) >= 9 and r[1].strip().isdigit()]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [int(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].strip() == "Active"})
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def ext(lib):
+    import ctypes
+
+    lib.ggml_compiler_b200_stream.argtypes = [ctypes.c_void_p]
+    lib.ggml_compiler_b200_stream.restype = ctypes.c_void_p
+    lib.ggml_compiler_b200_last_device_ms.argtypes = [ctypes.c_void_p]
+    lib.ggml_compiler_b200_last_device_ms.restype = ctypes.c_double
+    lib.ggml_compiler_b200_set_profiling.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    lib.ggml_compiler_b200_n_kernel_stats.argtypes = [ctypes.c_void_p]
+    lib.ggml_compiler_b200_kernel_stats.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
+                                                    ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int),
+                                                    ctypes.POINTER(ctypes.c_double)]
+    return lib
+
+
+def kernel_stats(lib, m) -> dict[str, dict]:
+    import ctypes
+
+    out = {}
+    for i in range(lib.ggml_compiler_b200_n_kernel_stats(m)):
+        k, ms, n, b = ctypes.c_char_p(), ctypes.c_double(), ctypes.c_int(), ctypes.c_double()
+        lib.ggml_compiler_b200_kernel_stats(m, i, ctypes.byref(k), ctypes.byref(ms), ctypes.byref(n), ctypes.byref(b))
+        out[k.value.decode()] = {"ms": ms.value, "launches": n.value, "bytes": b.value}
+    return out
+
+
+def peaks() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def cpu_baseline(gguf: Path, sh, n_tokens: int) -> dict:
+    """The reference's CPU arithmetic (oracle/, the C restatement of ggml's CPU path) on the host's
+    cores: a 4-token prompt, then `n_tokens` greedy decode tokens timed."""
+    import oracle
+    from oracle.interp import OracleGenerator, Program
+
+    p = Program(gguf)
+    g = OracleGenerator(p)
+    g.reset()
+    rng = np.random.default_rng(1)
+    logits = g.feed(rng.integers(0, sh.vocab, 4).tolist())
+    t = time.perf_counter()
+    for _ in range(n_tokens):
+        logits = g.feed([int(np.argmax(logits))])
+    dt = time.perf_counter() - t
+    return {"value": n_tokens / dt, "unit": "tok/s", "cores": oracle.lib().orc_get_threads(), "kind": "port",
+            "sample": f"{n_tokens} greedy decode tokens after a 4-token prompt (n_kv 512) of the same model, "
+                      f"oracle/ C restatement of ggml's CPU arithmetic, {dt:.1f}s"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="8b", choices=["8b", "tiny"])
+    ap.add_argument("--cpu-tokens", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    sh, workload = shape_for(args.config)
+    K, W = args.steps, max(3, args.warmup)
+    config = {"workload": workload, "layers": sh.layers, "d_model": sh.d_model, "heads": sh.heads,
+              "kv_heads": sh.kv_heads, "ffn": sh.ffn, "vocab": sh.vocab, "weights": sh.weight_type, "batch": 1,
+              "prompt": 512, "decode_tokens": K, "n_kv": 768,
+              "l2": "no flush: the decode step streams all weights (4.2 GB) through a 126 MB L2"}
+
+    if args.impl == "reference":
+        if world > 1 and rank != 0:
+            return
+        gguf = model_path(sh, args.config, 0, 1)
+        cb = cpu_baseline(gguf, sh, max(1, args.cpu_tokens))
+        print(json.dumps({"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tok/s",
+                          "n_gpus": args.gpus, "steps": args.cpu_tokens, "warmup": 0,
+                          "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "q4_0 weights, int8 x int4 block dots, f32 sums",
+                          "data": "synthetic", "config": config, "cpu_baseline": cb,
+                          "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return
+
+    import torch
+
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    from ggml_compiler_b200.llm import Generator
+    from ggml_compiler_b200.runtime import Session, load_library
+
+    lib = ext(load_library())
+    gguf = model_path(sh, args.config, rank, world)
+    s = Session(gguf, backend="cuda", device=local)
+    stream = torch.cuda.ExternalStream(lib.ggml_compiler_b200_stream(s._m), device=torch.device("cuda", local))
+    g = Generator(s)
+    prompt = np.random.default_rng(1).integers(0, sh.vocab, 512).tolist()
+
+    def prefill() -> int:
+        g.reset()
+        return int(np.argmax(g.feed(prompt)))
+
+    def generate(first: int, n: int) -> float:
+        s.set_symbol("max_new", n)
+        s.run(first=np.array([[first]], np.int32), start=np.array([512], np.int32), entry="generate")
+        return lib.ggml_compiler_b200_last_device_ms(s._m)
+
+    # warm-up: prefill + W device-loop steps (graphs captured for n_kv 768)
+    first = prefill()
+    generate(first, W)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    # timed: K decode steps in the device loop
+    barrier()
+    with Clocks(local) as clk:
+        dev_ms = generate(first, K)
+    barrier()
+    t = torch.tensor([dev_ms], device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    dev_ms = float(t.item())
+    value = world * K / (dev_ms / 1000.0)
+
+    # e2e: host loop through the public API, pinned host buffers, K decode steps
+    first = prefill()
+    n_kv = 768
+    tok_h = torch.empty((1, 1), dtype=torch.int32, pin_memory=True).numpy()
+    pos_h = torch.empty(1, dtype=torch.int32, pin_memory=True).numpy()
+    mask_h = torch.empty((1, 1, 1, n_kv), dtype=torch.float32, pin_memory=True).numpy()
+    out_h = torch.empty((1, 1, sh.vocab), dtype=torch.float32, pin_memory=True).numpy()
+    from ggml_compiler_b200.runtime import _error
+
+    def e2e_step(tok: int, p: int) -> int:
+        tok_h[0, 0] = tok
+        pos_h[0] = p
+        mask_h[...] = np.where(np.arange(n_kv) <= p, 0.0, -np.inf).astype(np.float32)
+        for name, arr in (("token", tok_h), ("position", pos_h), ("mask1", mask_h)):
+            if name == "mask1":
+                shp = (ctypes_i64 * 4)(*arr.shape)
+                if lib.ggml_compiler_set_input_shape(s._m, b"mask1", 4, shp) != 0:
+                    raise _error()
+            if lib.ggml_compiler_set_input(s._m, name.encode(), arr.ctypes.data, arr.nbytes) != 0:
+                raise _error()
+        if lib.ggml_compiler_run_entry(s._m, b"decode") != 0:
+            raise _error()
+        if lib.ggml_compiler_get_output(s._m, b"logits1", out_h.ctypes.data, out_h.nbytes) != 0:
+            raise _error()
+        return int(np.argmax(out_h))
+
+    import ctypes
+
+    ctypes_i64 = ctypes.c_int64
+    tok = first
+    for i in range(W):
+        tok = e2e_step(tok, 512 + i)
+    first = prefill()
+    tok = first
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    w0 = time.perf_counter()
+    for i in range(K):
+        tok = e2e_step(tok, 512 + i)
+    ev1.record(stream)
+    ev1.synchronize()
+    wall = time.perf_counter() - w0
+    e2e_ms = max(ev0.elapsed_time(ev1), wall * 1000.0)
+    t = torch.tensor([e2e_ms], device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    e2e_value = world * K / (float(t.item()) / 1000.0)
+
+    # roofline: profiled pass over the same decode steps, per kernel family
+    first = prefill()
+    lib.ggml_compiler_b200_set_profiling(s._m, 1)
+    n_prof = min(K, 16)
+    generate(first, n_prof)
+    ks = kernel_stats(lib, s._m)
+    lib.ggml_compiler_b200_set_profiling(s._m, 0)
+    gemv_kinds = [k for k in ks if k.startswith("gemv") or k == "mul_mat"]
+    gemv_ms = sum(ks[k]["ms"] for k in gemv_kinds)
+    gemv_bytes = sum(ks[k]["bytes"] for k in gemv_kinds)
+    gemv_launches = sum(ks[k]["launches"] for k in gemv_kinds)
+    total_ms = sum(v["ms"] for v in ks.values())
+    launches_per_step = sum(v["launches"] for v in ks.values()) / n_prof
+    peak, peak_kind = peaks()
+    achieved = gemv_bytes / (gemv_ms / 1000.0) / 1e9 if gemv_ms else 0.0
+
+    out = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": dev_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q4_0 weights, int8 x int4 block dots, f32 sums", "data": "synthetic",
+        "config": {**config, "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak if peak else None, "traffic": None,
+                     "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                     "kernel": "+".join(gemv_kinds),
+                     "bytes_per_launch": gemv_bytes / max(1, gemv_launches),
+                     "mean_launch_us": 1000.0 * gemv_ms / max(1, gemv_launches),
+                     "share_of_step": gemv_ms / total_ms if total_ms else None,
+                     "step_weight_bytes": weight_bytes(sh),
+                     "step_hbm_frac": weight_bytes(sh) / (dev_ms / K / 1000.0) / 1e9 / peak},
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4 + 4 + 4 * n_kv,
+                "d2h_bytes_per_step": 4 * sh.vocab, "wall_ms": wall * 1000.0},
+        "gpu_launches": int(round(launches_per_step * K + 2 * K)),
+        "clocks": clk.summary(),
+        "kernel_breakdown_ms_per_step": {k: v["ms"] / n_prof for k, v in sorted(ks.items(), key=lambda kv: -kv[1]["ms"])},
+    }
+    s.close()
+    if rank == 0 and not args.no_cpu_baseline:
+        try:
+            out["cpu_baseline"] = cpu_baseline(gguf, sh, max(1, args.cpu_tokens))
+        except Exception as e:  # the baseline is reported, not required for the GPU number
+            out["cpu_baseline"] = {"value": None, "unit": "tok/s", "error": str(e)[:200]}
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,67 @@
+// Call-site planner state and the fusion pass that replaces node groups with fused kernels.
+#pragma once
+
+#include <functional>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "gc_model.h"
+
+namespace gcb {
+
+struct Storage {
+    size_t bytes = 0;
+    int first = 0, last = 0;  // node indices of the first write and the last read
+    size_t offset = 0;
+};
+
+struct PlanStep {
+    const char *kind;
+    std::string node;
+    std::vector<TD> tds;  // arena TDs are resolved to pointers before the launch closure is made
+    std::function<void(cudaStream_t, const std::vector<TD> &)> fn;
+    double bytes;
+};
+
+struct Planner {
+    Planner(Model &m, CallSite &cs, const DriverOp &d);
+    Model &m;
+    CallSite &cs;
+    const DriverOp &d;
+    const StageSpec &s;
+    std::unordered_map<std::string, TD> env;  // node ids and stage params -> views
+    std::vector<Storage> storages;
+    std::vector<PlanStep> psteps;
+    int cur = 0;
+
+    TD alloc(Type t, const int64_t *ne);          // a fresh arena tensor written at `cur`
+    void *scratch_marker(size_t bytes, TD *out);  // scratch arena space for the launch at `cur`
+    void use(const TD &t);                        // `t` is read at `cur`
+    void add(const char *kind, const std::string &node, std::vector<TD> tds,
+             std::function<void(cudaStream_t, const std::vector<TD> &)> fn, double bytes);
+    TD src_of(const std::string &name);  // a node id, stage param or weight
+    TD plan_node(const NodeSpec &n, const std::vector<TD> &src);
+    void finish();
+};
+
+// A set of node groups, each emitted as fused launches at its anchor (its last node).
+struct FusionGroup {
+    std::vector<size_t> nodes;
+    size_t anchor = 0;
+    std::function<void(Planner &)> emit;  // plans the launches and defines the group's visible outputs
+};
+
+struct FusionPlan {
+    std::vector<int> group_of;  // node index -> group, or -1
+    std::vector<FusionGroup> groups;
+    bool covered(size_t i) const { return i < group_of.size() && group_of[i] >= 0; }
+    void emit_if_anchor(size_t i, Planner &p) {
+        const FusionGroup &g = groups[(size_t)group_of[i]];
+        if (g.anchor == i) g.emit(p);
+    }
+};
+
+FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p);
+
+}  // namespace gcb

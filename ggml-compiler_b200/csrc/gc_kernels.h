@@ -1,0 +1,84 @@
+// Device tensor descriptors and the host launchers of every CUDA kernel of the backend.
+//
+// A TD is a strided view in ggml's layout: ne innermost first, nb byte strides. A quantized weight
+// (Q4_0 / Q8_0) is stored on the device split in two arrays, repacked from the GGUF blocks at load:
+// `data` holds each row's codes block after block (Q4_0: 16 bytes per block, the GGUF nibble order;
+// Q8_0: 32 int8 per block) so every block starts on a 16-byte boundary, and `scales` holds the fp16
+// block scales [rows][K/32]. nb[1] is then the code bytes of one row.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "gc_types.h"
+
+namespace gcb {
+
+struct TD {
+    char *data = nullptr;
+    uint16_t *scales = nullptr;  // quantized types only
+    Type type = T_F32;
+    int64_t ne[4] = {1, 1, 1, 1};
+    int64_t nb[4] = {0, 0, 0, 0};
+    // Planning only: storage id in the call site's arena (-1: data is an absolute pointer) and
+    // byte offset into that storage.
+    int sid = -1;
+    size_t off = 0;
+
+    int64_t nelements() const { return ne[0] * ne[1] * ne[2] * ne[3]; }
+    int64_t nrows() const { return ne[1] * ne[2] * ne[3]; }
+    size_t elsize() const;  // bytes per element (non-quantized types)
+    bool contiguous() const;
+    size_t nbytes() const;  // bytes spanned by a contiguous tensor of this shape
+};
+
+// Contiguous strides for a shape (quantized: code bytes of a row in nb[1]).
+void set_contiguous(TD &t);
+size_t quant_code_bytes(Type t);  // code bytes per 32-block: Q4_0 16, Q8_0 32
+
+namespace k {
+
+// Repack raw GGUF Q4_0/Q8_0 rows into codes + scales.
+void repack_quant(Type t, const uint8_t *raw, int64_t nrows, int64_t K, char *codes, uint16_t *scales,
+                  cudaStream_t s);
+
+// Elementwise and row ops (generic strides).
+void copy(const TD &src, const TD &dst, cudaStream_t s);  // cont / cpy / cast (f32, f16, bf16, i32)
+enum BinOp { ADD = 0, SUB = 1, MUL = 2, DIV = 3 };
+void binary(int op, const TD &a, const TD &b, const TD &out, cudaStream_t s);
+enum UnOp {
+    SCALE = 0, CLAMP, SILU, NEG, ABS, SQR, SQRT, EXP, LOG, RELU, TANH, SIGMOID, STEP, SIN, COS, SOFTPLUS,
+    GELU_TANH, GELU_ERF,
+};
+void unary(int op, const TD &x, const TD &out, float p0, float p1, cudaStream_t s);
+void rms_norm(const TD &x, const TD &out, float eps, cudaStream_t s);
+void norm(const TD &x, const TD &out, float eps, cudaStream_t s);
+void soft_max(const TD &x, const TD *mask, const TD &out, float scale, cudaStream_t s);
+void rope_neox(const TD &x, const TD &pos, const TD &out, int n_dims, const float *table, int64_t table_npos,
+               float theta_scale, float freq_scale, float attn_factor, const float *freq_factors, cudaStream_t s);
+void rope_norm(const TD &x, const TD &pos, const TD &out, int n_dims, const float *table, int64_t table_npos,
+               float theta_scale, float freq_scale, float attn_factor, const float *freq_factors, cudaStream_t s);
+void get_rows(const TD &table, const TD &idx, const TD &out, cudaStream_t s);
+void set_rows(const TD &dst, const TD &src, const TD &idx, int *err, cudaStream_t s);
+void argmax(const TD &x, const TD &out, cudaStream_t s);
+void swiglu(const TD &g, const TD &u, const TD &out, cudaStream_t s);
+void sum_rows(const TD &x, const TD &out, float scale, cudaStream_t s);  // scale = 1/n for mean
+void repeat(const TD &x, const TD &out, cudaStream_t s);
+void concat(const TD &a, const TD &b, const TD &out, int dim, cudaStream_t s);
+void arange(const TD &out, float start, float step, cudaStream_t s);
+void fill_f32(float *dst, int64_t n, float v, cudaStream_t s);
+void causal_mask_row(float *dst, int64_t n_total, int64_t row_len, const int32_t *pos, cudaStream_t s);
+
+// mul_mat(a, b): out[n, m, i2, i3] = sum_k a[k, n, i2/r2, i3/r3] * b[k, m, i2, i3].
+// `scratch` must hold mul_mat_scratch_bytes(a, b) bytes.
+size_t mul_mat_scratch_bytes(const TD &a, const TD &b);
+void mul_mat(const TD &a, const TD &b, const TD &out, void *scratch, cudaStream_t s);
+
+// flash_attn_ext: q [D, Sq, H, B] f32, k/v [D, n_kv, Hkv, B] f16, mask [n_kv, >=Sq, ...] f16 (nullable)
+// -> out [D, H, Sq, B] f32.
+void flash_attn(const TD &q, const TD &k, const TD &v, const TD *mask, const TD &out, float scale, cudaStream_t s);
+
+}  // namespace k
+}  // namespace gcb

@@ -1,0 +1,142 @@
+// The executor behind the C ABI: one loaded program on one B200.
+//
+// Counterpart of the reference's runtime core (runtime/src/ggml_compiler_rt.cpp:138-732): load
+// (:250-281), weights (:445-479), driver values (:488-546), per-binding views (:548-568), call
+// sites (:570-732) and the driver loop (:356-443). Instead of ggml graphs, each call site is
+// planned into a list of kernel launches with every pointer resolved for the current binding, its
+// intermediates packed into one arena by liveness, and replayed as a CUDA graph.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <map>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "gc_gguf.h"
+#include "gc_kernels.h"
+#include "gc_program.h"
+
+namespace gcb {
+
+class DevBuf {
+  public:
+    DevBuf() = default;
+    DevBuf(const DevBuf &) = delete;
+    DevBuf &operator=(const DevBuf &) = delete;
+    DevBuf(DevBuf &&o) noexcept : p_(o.p_), n_(o.n_) { o.p_ = nullptr, o.n_ = 0; }
+    DevBuf &operator=(DevBuf &&o) noexcept;
+    ~DevBuf() { release(); }
+    void alloc(size_t n);  // frees any previous allocation; zero-filled
+    void release();
+    char *get() const { return (char *)p_; }
+    size_t size() const { return n_; }
+
+  private:
+    void *p_ = nullptr;
+    size_t n_ = 0;
+};
+
+struct Step {
+    const char *kind = "";  // kernel family, for profiles
+    std::string node;       // the node(s) it runs
+    std::function<void(cudaStream_t)> run;
+    double bytes = 0;       // algorithmic bytes moved (weights, activations, KV)
+};
+
+struct CallSite {
+    const StageSpec *stage = nullptr;
+    int stage_index = 0;
+    std::vector<Step> steps;
+    DevBuf arena;
+    bool stale = true;
+    cudaGraphExec_t graph = nullptr;
+    bool graph_ok = false;
+};
+
+struct Weight {
+    TD td;
+    DevBuf data, scales;
+};
+
+struct Value {
+    const TensorSpec *spec = nullptr;
+    DevBuf buf;  // room for the largest binding
+    TD td;       // bound view (contiguous)
+};
+
+struct KernelStat {
+    double ms = 0, bytes = 0;
+    int launches = 0;
+};
+
+struct Model {
+    ProgramSpec prog;
+    GgufFile gguf;
+    int device = -1;
+    std::string backend_name;
+    cudaStream_t stream = nullptr;
+    std::unordered_map<std::string, Weight> weights;
+    std::unordered_map<std::string, Value> values;
+    struct Entry {
+        const EntrySpec *spec = nullptr;
+        std::vector<const TensorSpec *> inputs, outputs;
+    };
+    std::vector<Entry> entries;
+    std::map<std::string, bool> input_set;
+    std::vector<CallSite> calls;
+    std::vector<int64_t> binding, built;
+    struct StageStat {
+        double ms = 0;
+        int calls = 0;
+    };
+    std::vector<StageStat> stage_stats;
+    double last_ms = 0, last_device_ms = 0;
+    int last_calls = 0;
+    cudaEvent_t run_ev[2] = {nullptr, nullptr};
+    int *d_err = nullptr;  // device error word (set_rows index out of range, ...)
+    int64_t rope_positions = 4096;
+    std::map<std::string, DevBuf> rope_tables;
+    bool use_graphs = true;
+    bool profiling = false;
+    std::map<std::string, KernelStat> kstats;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> event_pool;
+    size_t events_used = 0;
+    struct PendingTime {
+        int stage;
+        cudaEvent_t a, b;
+    };
+    std::vector<PendingTime> pending;
+    std::string profile_path;  // GGML_COMPILER_PROFILE
+    std::vector<std::string> profile_lines;
+
+    ~Model();
+    void load(const char *path, int backend, int device, bool allow_cpu_fallback);
+    void rebind();
+    void run_entry(const std::string &name);
+    void reset_state();
+    size_t nbytes_of(const TensorSpec &v, const std::vector<int64_t> &b) const;
+    const float *rope_table(int n_dims, float base, float scale, float attn, const std::string &ff_key,
+                            const float *ff_host, int64_t *npos);
+
+  private:
+    void load_weights();
+    void alloc_values();
+    void bind_values();
+    void build_ops(std::vector<DriverOp> &ops);
+    void build_site(const DriverOp &d);
+    void run_ops(const std::vector<DriverOp> &ops);
+    void run_call(const DriverOp &d);
+    std::pair<cudaEvent_t, cudaEvent_t> events();
+    void collect_times();
+};
+
+// Plans one stage call into kernel launches (gc_plan.cpp).
+void plan_call_site(Model &m, CallSite &cs, const DriverOp &d);
+
+void cuda_check(cudaError_t e, const char *what);
+
+}  // namespace gcb

@@ -1,0 +1,554 @@
+// Call-site planning: a stage's node list -> kernel launches for the current binding.
+//
+// The op table mirrors the reference's dispatcher (runtime/src/ops.cpp:74-351) for the ops that
+// language-model programs use, with the same preconditions and the same "produced shape / type"
+// check per node (ops.cpp:355-378). Views (view, reshape, permute) are pure stride arithmetic, as
+// the reference's ggml views are (runtime/include/ggml_compiler_ops.h:69-107). Every other node gets
+// a kernel; its output lives in the call site's arena, packed by liveness. Stage results are
+// copied into their driver values after every other launch, except a result that already is that
+// value's memory (set_rows into a state value: the reference skips that copy too,
+// ggml_compiler_rt.cpp:703-708).
+//
+// Fused decode/prefill kernels replace node groups here as well (gc_fuse.cpp).
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <set>
+#include <sstream>
+#include <stdexcept>
+
+#include "gc_fuse.h"
+#include "gc_model.h"
+
+namespace gcb {
+
+namespace {
+
+std::string shape_str(const int64_t *ne) {
+    std::ostringstream os;
+    os << "[" << ne[0] << ", " << ne[1] << ", " << ne[2] << ", " << ne[3] << "]";
+    return os.str();
+}
+
+[[noreturn]] void fail(const NodeSpec &n, const std::string &msg) { throw std::runtime_error(n.where() + ": " + msg); }
+
+void need_src(const NodeSpec &n, const std::vector<TD> &s, size_t lo, size_t hi) {
+    if (s.size() < lo || s.size() > hi)
+        fail(n, "expected " + std::to_string(lo) + (lo == hi ? "" : "-" + std::to_string(hi)) + " inputs, got " +
+                    std::to_string(s.size()));
+}
+
+bool can_repeat(const TD &b, const TD &a) {
+    for (int i = 0; i < 4; i++)
+        if (b.ne[i] == 0 || a.ne[i] % b.ne[i] != 0) return false;
+    return true;
+}
+
+bool same_shape(const TD &a, const TD &b) {
+    for (int i = 0; i < 4; i++)
+        if (a.ne[i] != b.ne[i]) return false;
+    return true;
+}
+
+bool is_quant(Type t) { return t == T_Q4_0 || t == T_Q8_0; }
+
+const std::map<std::string, int> &unary_ops() {
+    static const std::map<std::string, int> m = {
+        {"silu", k::SILU}, {"neg", k::NEG},   {"abs", k::ABS},         {"sqr", k::SQR},           {"sqrt", k::SQRT},
+        {"exp", k::EXP},   {"log", k::LOG},   {"relu", k::RELU},       {"tanh", k::TANH},         {"sigmoid", k::SIGMOID},
+        {"step", k::STEP}, {"sin", k::SIN},   {"cos", k::COS},         {"softplus", k::SOFTPLUS}, {"gelu", k::GELU_TANH},
+        {"gelu_tanh", k::GELU_TANH},          {"gelu_erf", k::GELU_ERF},
+    };
+    return m;
+}
+
+}  // namespace
+
+Planner::Planner(Model &m, CallSite &cs, const DriverOp &d) : m(m), cs(cs), d(d), s(*cs.stage) {}
+
+TD Planner::alloc(Type t, const int64_t *ne) {
+    TD o;
+    o.type = t;
+    for (int i = 0; i < 4; i++) o.ne[i] = ne[i];
+    set_contiguous(o);
+    Storage st;
+    st.bytes = std::max<size_t>(o.nbytes(), 4);
+    st.first = st.last = cur;
+    storages.push_back(st);
+    o.sid = (int)storages.size() - 1;
+    return o;
+}
+
+void *Planner::scratch_marker(size_t bytes, TD *out) {
+    int64_t ne[4] = {(int64_t)((bytes + 3) / 4), 1, 1, 1};
+    *out = alloc(T_F32, ne);
+    return nullptr;
+}
+
+void Planner::use(const TD &t) {
+    if (t.sid >= 0) storages[(size_t)t.sid].last = std::max(storages[(size_t)t.sid].last, cur);
+}
+
+void Planner::add(const char *kind, const std::string &node, std::vector<TD> tds,
+                  std::function<void(cudaStream_t, const std::vector<TD> &)> fn, double bytes) {
+    for (const auto &t : tds) use(t);
+    psteps.push_back(PlanStep{kind, node, std::move(tds), std::move(fn), bytes});
+}
+
+TD Planner::src_of(const std::string &name) {
+    auto it = env.find(name);
+    if (it != env.end()) return it->second;
+    auto w = m.weights.find(name);
+    if (w == m.weights.end()) throw std::runtime_error("stage '" + s.name + "' reads unknown tensor '" + name + "'");
+    return w->second.td;
+}
+
+// ------------------------------------------------------------------------------------------------
+
+TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
+    const std::string &op = n.op;
+    auto out_like = [&](Type t, const int64_t *ne) { return alloc(t, ne); };
+
+    if (op == "reshape") {
+        need_src(n, sv, 1, 1);
+        const TD &x = sv[0];
+        if (x.nelements() != n.ne[0] * n.ne[1] * n.ne[2] * n.ne[3])
+            fail(n, "cannot reshape " + shape_str(x.ne) + " to " + shape_str(n.ne.data()));
+        TD y = x;
+        for (int i = 0; i < 4; i++) y.ne[i] = n.ne[i];
+        if (is_quant(x.type)) {
+            if (n.ne[0] != x.ne[0] || !x.contiguous()) fail(n, "a quantized tensor can only be reshaped row for row");
+            set_contiguous(y);
+            return y;
+        }
+        if (x.contiguous()) {
+            set_contiguous(y);
+            return y;
+        }
+        // a strided view may only gain or lose size-1 dims (ggml_compiler_ops.h:85-107)
+        int64_t nb[4] = {x.nb[0], 0, 0, 0};
+        int k = 0;
+        for (int i = 0; i < 4; i++) {
+            if (n.ne[i] == 1) {
+                if (i > 0) nb[i] = nb[i - 1] * n.ne[i - 1];
+                continue;
+            }
+            while (k < 4 && x.ne[k] == 1) k++;
+            if (k == 4 || x.ne[k] != n.ne[i])
+                fail(n, "input is a strided view and the reshape does more than add or drop size-1 dims; it needs a cont first");
+            nb[i] = x.nb[k++];
+        }
+        while (k < 4 && x.ne[k] == 1) k++;
+        if (k != 4 || nb[0] != x.nb[0])
+            fail(n, "input is a strided view and the reshape does more than add or drop size-1 dims; it needs a cont first");
+        for (int i = 0; i < 4; i++) y.nb[i] = nb[i];
+        return y;
+    }
+    if (op == "view") {
+        need_src(n, sv, 1, 1);
+        const TD &x = sv[0];
+        const int dim = (int)n.pint("dim");
+        const int64_t start = n.pint("start");
+        if (dim < 0 || dim > 3 || start < 0 || start + n.ne[(size_t)dim] > x.ne[dim]) fail(n, "slice out of range of " + shape_str(x.ne));
+        if (is_quant(x.type)) fail(n, "views of quantized tensors are not supported");
+        TD y = x;
+        for (int i = 0; i < 4; i++) y.ne[i] = n.ne[i];
+        for (int i = 1; i < 4; i++)
+            if (y.ne[i] == 1) y.nb[i] = y.nb[i - 1] * y.ne[i - 1];
+        const size_t delta = (size_t)(start * x.nb[dim]);
+        if (y.sid >= 0) y.off += delta;
+        else y.data += delta;
+        return y;
+    }
+    if (op == "permute") {
+        need_src(n, sv, 1, 1);
+        const Json &ax = n.p.at("axes");
+        if (!ax.is_array() || ax.size() != 4) fail(n, "'axes' must have 4 entries");
+        const TD &x = sv[0];
+        TD y = x;
+        for (int i = 0; i < 4; i++) {
+            const int a = (int)ax[(size_t)i].as_int();
+            if (a < 0 || a > 3) fail(n, "bad permute axes");
+            y.ne[a] = x.ne[i];
+            y.nb[a] = x.nb[i];
+        }
+        return y;
+    }
+    if (op == "cont" || op == "cast") {
+        need_src(n, sv, 1, 1);
+        const TD &x = sv[0];
+        if (is_quant(x.type)) fail(n, "cannot copy a quantized tensor");
+        const Type t = op == "cast" ? n.type : x.type;
+        TD y = out_like(t, op == "cast" ? x.ne : n.ne.data());
+        if (op == "cont" && x.nelements() != y.nelements()) fail(n, "cont changes the element count");
+        add("copy", n.id, {x, y}, [](cudaStream_t st, const std::vector<TD> &t) { k::copy(t[0], t[1], st); },
+            (double)(x.nelements() * (x.elsize() + y.elsize())));
+        return y;
+    }
+    if (op == "add" || op == "sub" || op == "mul" || op == "div") {
+        need_src(n, sv, 2, 2);
+        const TD &a = sv[0], &b = sv[1];
+        if (!can_repeat(b, a)) fail(n, "cannot broadcast " + shape_str(b.ne) + " into " + shape_str(a.ne));
+        if (is_quant(a.type) || is_quant(b.type)) fail(n, "quantized operand");
+        const int bop = op == "add" ? k::ADD : op == "sub" ? k::SUB : op == "mul" ? k::MUL : k::DIV;
+        TD y = out_like(a.type, a.ne);
+        add("binary", n.id, {a, b, y}, [bop](cudaStream_t st, const std::vector<TD> &t) { k::binary(bop, t[0], t[1], t[2], st); },
+            (double)(a.nelements() * 12));
+        return y;
+    }
+    auto un = unary_ops().find(op);
+    if (un != unary_ops().end() || op == "scale" || op == "clamp") {
+        need_src(n, sv, 1, 1);
+        const TD &x = sv[0];
+        if (is_quant(x.type)) fail(n, "quantized operand");
+        int uop;
+        float p0 = 0, p1 = 0;
+        if (op == "scale") {
+            uop = k::SCALE;
+            p0 = n.pfloat("s");
+            p1 = n.has("b") ? n.pfloat("b") : 0.0f;
+        } else if (op == "clamp") {
+            uop = k::CLAMP;
+            p0 = n.pfloat("min");
+            p1 = n.pfloat("max");
+        } else {
+            uop = un->second;
+        }
+        TD y = out_like(x.type, x.ne);
+        add("unary", n.id, {x, y}, [uop, p0, p1](cudaStream_t st, const std::vector<TD> &t) { k::unary(uop, t[0], t[1], p0, p1, st); },
+            (double)(x.nelements() * 8));
+        return y;
+    }
+    if (op == "rms_norm" || op == "norm") {
+        need_src(n, sv, 1, 1);
+        const TD &x = sv[0];
+        if (x.type != T_F32 || x.nb[0] != 4) fail(n, "needs an f32 input with contiguous rows");
+        const float eps = n.pfloat("eps");
+        TD y = out_like(T_F32, x.ne);
+        if (op == "rms_norm")
+            add("rms_norm", n.id, {x, y}, [eps](cudaStream_t st, const std::vector<TD> &t) { k::rms_norm(t[0], t[1], eps, st); },
+                (double)(x.nelements() * 8));
+        else
+            add("norm", n.id, {x, y}, [eps](cudaStream_t st, const std::vector<TD> &t) { k::norm(t[0], t[1], eps, st); },
+                (double)(x.nelements() * 8));
+        return y;
+    }
+    if (op == "soft_max") {
+        need_src(n, sv, 1, 2);
+        const TD &x = sv[0];
+        const float scale = n.has("scale") ? n.pfloat("scale") : 1.0f;
+        if (n.has("max_bias") && n.pfloat("max_bias") != 0.0f) fail(n, "ALiBi (max_bias != 0) is not supported");
+        if (x.type != T_F32 || x.nb[0] != 4) fail(n, "needs an f32 input with contiguous rows");
+        TD y = out_like(T_F32, x.ne);
+        if (sv.size() > 1) {
+            const TD &mk = sv[1];
+            if (mk.ne[0] != x.ne[0] || mk.ne[1] < x.ne[1] || x.ne[2] % mk.ne[2] || x.ne[3] % mk.ne[3])
+                fail(n, "mask " + shape_str(mk.ne) + " does not fit " + shape_str(x.ne));
+            add("soft_max", n.id, {x, mk, y},
+                [scale](cudaStream_t st, const std::vector<TD> &t) { k::soft_max(t[0], &t[1], t[2], scale, st); },
+                (double)(x.nelements() * 12));
+        } else {
+            add("soft_max", n.id, {x, y}, [scale](cudaStream_t st, const std::vector<TD> &t) { k::soft_max(t[0], nullptr, t[1], scale, st); },
+                (double)(x.nelements() * 8));
+        }
+        return y;
+    }
+    if (op == "mul_mat") {
+        need_src(n, sv, 2, 2);
+        const TD &a = sv[0], &b = sv[1];
+        if (a.ne[0] != b.ne[0] || b.ne[2] % a.ne[2] != 0 || b.ne[3] % a.ne[3] != 0)
+            fail(n, "cannot multiply " + shape_str(a.ne) + " by " + shape_str(b.ne));
+        if (a.ne[0] > 1 && a.nb[0] > a.nb[1] && !is_quant(a.type)) fail(n, "weight operand is transposed; it needs a cont first");
+        if (is_quant(a.type) && !a.contiguous()) fail(n, "quantized weight must be contiguous");
+        if (!is_quant(a.type) && a.type != T_F32 && a.type != T_F16 && a.type != T_BF16)
+            fail(n, std::string("weight type ") + type_name(a.type) + " is not supported by this backend (Q4_0, Q8_0, f16, bf16, f32 are)");
+        if (b.type != T_F32) fail(n, "activation operand must be f32");
+        int64_t ne[4] = {a.ne[1], b.ne[1], b.ne[2], b.ne[3]};
+        TD y = out_like(T_F32, ne);
+        const size_t sb = k::mul_mat_scratch_bytes(a, b);
+        TD scratch;
+        if (sb) scratch_marker(sb, &scratch);
+        const double bytes = (double)(is_quant(a.type) ? (double)a.nrows() * (a.ne[0] / 32) * (quant_code_bytes(a.type) + 2)
+                                                        : (double)a.nelements() * a.elsize()) +
+                             (double)b.nelements() * 4 + (double)y.nelements() * 4;
+        if (sb)
+            add("mul_mat", n.id, {a, b, y, scratch},
+                [](cudaStream_t st, const std::vector<TD> &t) { k::mul_mat(t[0], t[1], t[2], t[3].data, st); }, bytes);
+        else
+            add("mul_mat", n.id, {a, b, y}, [](cudaStream_t st, const std::vector<TD> &t) { k::mul_mat(t[0], t[1], t[2], nullptr, st); },
+                bytes);
+        return y;
+    }
+    if (op == "flash_attn") {
+        need_src(n, sv, 3, 4);
+        const TD &q = sv[0], &kk = sv[1], &v = sv[2];
+        if (kk.ne[0] != q.ne[0] || kk.ne[1] != v.ne[1] || q.ne[3] != kk.ne[3] || q.ne[3] != v.ne[3] || q.ne[2] % kk.ne[2] != 0 ||
+            v.ne[0] != q.ne[0])
+            fail(n, "q " + shape_str(q.ne) + ", k " + shape_str(kk.ne) + ", v " + shape_str(v.ne) + " do not line up");
+        if (q.type != T_F32 || kk.type != T_F16 || v.type != T_F16) fail(n, "needs an f32 query and f16 K/V");
+        if (kk.nb[0] != 2 || v.nb[0] != 2) fail(n, "K/V rows must be contiguous");
+        if (q.ne[0] > 512) fail(n, "head size above 512");
+        const float scale = n.pfloat("scale");
+        int64_t ne[4] = {q.ne[0], q.ne[2], q.ne[1], q.ne[3]};
+        TD y = out_like(T_F32, ne);
+        const double bytes = (double)(kk.ne[1] * kk.ne[2] * kk.ne[3]) * kk.ne[0] * 4 + (double)q.nelements() * 8;
+        if (sv.size() > 3) {
+            const TD &mk = sv[3];
+            if (mk.type != T_F16 || !mk.contiguous() || q.ne[2] % mk.ne[2] != 0 || mk.ne[0] != kk.ne[1] || mk.ne[1] < q.ne[1])
+                fail(n, "mask must be a contiguous f16 tensor broadcastable over heads");
+            add("flash_attn", n.id, {q, kk, v, mk, y},
+                [scale](cudaStream_t st, const std::vector<TD> &t) { k::flash_attn(t[0], t[1], t[2], &t[3], t[4], scale, st); },
+                bytes);
+        } else {
+            add("flash_attn", n.id, {q, kk, v, y},
+                [scale](cudaStream_t st, const std::vector<TD> &t) { k::flash_attn(t[0], t[1], t[2], nullptr, t[3], scale, st); },
+                bytes);
+        }
+        return y;
+    }
+    if (op == "swiglu") {
+        need_src(n, sv, 2, 2);
+        const TD &g = sv[0], &u = sv[1];
+        if (!same_shape(g, u) || !g.contiguous() || !u.contiguous()) fail(n, "swiglu needs a gate and an up of one shape, both contiguous");
+        TD y = out_like(T_F32, g.ne);
+        add("swiglu", n.id, {g, u, y}, [](cudaStream_t st, const std::vector<TD> &t) { k::swiglu(t[0], t[1], t[2], st); },
+            (double)(g.nelements() * 12));
+        return y;
+    }
+    if (op == "set_rows") {
+        need_src(n, sv, 3, 3);
+        const TD &dst = sv[0], &src = sv[1], &idx = sv[2];
+        if (dst.ne[0] != src.ne[0] || dst.ne[2] != src.ne[2] || dst.ne[3] != src.ne[3] || src.ne[1] != idx.ne[0] ||
+            idx.ne[1] != 1 || idx.type != T_I32 || (src.type != T_F32 && src.type != T_F16))
+            fail(n, "cannot write rows " + shape_str(src.ne) + " at indices " + shape_str(idx.ne) + " into " + shape_str(dst.ne));
+        if (dst.nb[0] != (int64_t)dst.elsize() || src.nb[0] != (int64_t)src.elsize()) fail(n, "set_rows needs rows that are contiguous");
+        int *err = m.d_err;
+        add("set_rows", n.id, {dst, src, idx},
+            [err](cudaStream_t st, const std::vector<TD> &t) { k::set_rows(t[0], t[1], t[2], err, st); },
+            (double)(src.nelements() * (src.elsize() + dst.elsize())));
+        return dst;  // written in place
+    }
+    if (op == "rope") {
+        need_src(n, sv, 2, 3);
+        const TD &x = sv[0], &pos = sv[1];
+        const int n_dims = (int)n.pint("n_dims");
+        const int mode = (int)n.pint("mode");
+        if (x.type != T_F32 || x.nb[0] != 4 || pos.type != T_I32 || pos.ne[0] != x.ne[2] || pos.nrows() != 1 || n_dims % 2 ||
+            n_dims > x.ne[0] || (sv.size() > 2 && (sv[2].type != T_F32 || sv[2].ne[0] < n_dims / 2)))
+            fail(n, "cannot rotate " + shape_str(x.ne) + " at positions " + shape_str(pos.ne));
+        if (mode != 0 && mode != 2) fail(n, "rope mode " + std::to_string(mode) + " is not supported (0 and 2 (NEOX) are)");
+        const float base = n.pfloat("freq_base"), fs = n.pfloat("freq_scale"), af = n.pfloat("attn_factor");
+        std::vector<float> ff;
+        std::string ff_key = "-";
+        if (sv.size() > 2) {
+            if (sv[2].sid >= 0) fail(n, "rope frequency factors must be a weight");
+            ff.resize((size_t)(n_dims / 2));
+            cuda_check(cudaMemcpy(ff.data(), sv[2].data, ff.size() * 4, cudaMemcpyDeviceToHost), "rope factors");
+            ff_key = n.src[2];
+        }
+        int64_t npos = 0;
+        const float *table = m.rope_table(n_dims, base, fs, af, ff_key, ff.empty() ? nullptr : ff.data(), &npos);
+        const float theta_scale = ::powf(base, -2.0f / (float)n_dims);
+        const float *ffd = sv.size() > 2 ? (const float *)sv[2].data : nullptr;
+        TD y = out_like(T_F32, x.ne);
+        add("rope", n.id, {x, pos, y},
+            [=](cudaStream_t st, const std::vector<TD> &t) {
+                if (mode == 2)
+                    k::rope_neox(t[0], t[1], t[2], n_dims, table, npos, theta_scale, fs, af, ffd, st);
+                else
+                    k::rope_norm(t[0], t[1], t[2], n_dims, table, npos, theta_scale, fs, af, ffd, st);
+            },
+            (double)(x.nelements() * 8));
+        return y;
+    }
+    if (op == "argmax") {
+        need_src(n, sv, 1, 1);
+        const TD &x = sv[0];
+        if (x.ne[2] != 1 || x.ne[3] != 1) fail(n, "argmax needs a matrix, got " + shape_str(x.ne));
+        int64_t ne[4] = {x.ne[1], 1, 1, 1};
+        TD y = out_like(T_I32, ne);
+        add("argmax", n.id, {x, y}, [](cudaStream_t st, const std::vector<TD> &t) { k::argmax(t[0], t[1], st); },
+            (double)(x.nelements() * 4));
+        return y;
+    }
+    if (op == "get_rows") {
+        need_src(n, sv, 2, 2);
+        const TD &tab = sv[0], &idx = sv[1];
+        if (idx.type != T_I32) fail(n, "row indices must be i32");
+        if (is_quant(tab.type) && !tab.contiguous()) fail(n, "quantized table must be contiguous");
+        int64_t ne[4] = {tab.ne[0], idx.ne[0], idx.ne[1], idx.ne[2]};
+        TD y = out_like(T_F32, ne);
+        add("get_rows", n.id, {tab, idx, y}, [](cudaStream_t st, const std::vector<TD> &t) { k::get_rows(t[0], t[1], t[2], st); },
+            (double)(y.nelements() * 8));
+        return y;
+    }
+    if (op == "sum_rows" || op == "mean") {
+        need_src(n, sv, 1, 1);
+        const TD &x = sv[0];
+        int64_t ne[4] = {1, x.ne[1], x.ne[2], x.ne[3]};
+        TD y = out_like(T_F32, ne);
+        const float scale = op == "mean" ? 1.0f / (float)x.ne[0] : 1.0f;
+        add("sum_rows", n.id, {x, y}, [scale](cudaStream_t st, const std::vector<TD> &t) { k::sum_rows(t[0], t[1], scale, st); },
+            (double)(x.nelements() * 4));
+        return y;
+    }
+    if (op == "repeat") {
+        need_src(n, sv, 1, 1);
+        for (int i = 0; i < 4; i++)
+            if (n.ne[(size_t)i] % sv[0].ne[i] != 0) fail(n, "cannot repeat " + shape_str(sv[0].ne) + " to " + shape_str(n.ne.data()));
+        TD y = out_like(sv[0].type, n.ne.data());
+        add("repeat", n.id, {sv[0], y}, [](cudaStream_t st, const std::vector<TD> &t) { k::repeat(t[0], t[1], st); },
+            (double)(y.nelements() * 8));
+        return y;
+    }
+    if (op == "concat") {
+        need_src(n, sv, 2, 2);
+        const int dim = (int)n.pint("dim");
+        if (dim < 0 || dim > 3) fail(n, "bad concat dim");
+        for (int i = 0; i < 4; i++)
+            if (i != dim && sv[0].ne[i] != sv[1].ne[i])
+                fail(n, "cannot concat " + shape_str(sv[0].ne) + " and " + shape_str(sv[1].ne) + " along ggml dim " + std::to_string(dim));
+        int64_t ne[4] = {sv[0].ne[0], sv[0].ne[1], sv[0].ne[2], sv[0].ne[3]};
+        ne[dim] += sv[1].ne[dim];
+        TD y = out_like(sv[0].type, ne);
+        add("concat", n.id, {sv[0], sv[1], y}, [dim](cudaStream_t st, const std::vector<TD> &t) { k::concat(t[0], t[1], t[2], dim, st); },
+            (double)(y.nelements() * 8));
+        return y;
+    }
+    if (op == "arange") {
+        need_src(n, sv, 0, 0);
+        const float start = n.pfloat("start"), step = n.pfloat("step");
+        TD y = out_like(T_F32, n.ne.data());
+        add("arange", n.id, {y}, [start, step](cudaStream_t st, const std::vector<TD> &t) { k::arange(t[0], start, step, st); },
+            (double)(y.nelements() * 4));
+        return y;
+    }
+    fail(n, "op is not supported by this backend");
+}
+
+void Planner::finish() {
+    // stage results into their driver values, after every other launch
+    cur = (int)s.nodes.size();
+    for (size_t i = 0; i < s.outputs.size(); i++) {
+        auto it = env.find(s.outputs[i]);
+        if (it == env.end()) throw std::runtime_error("stage '" + s.name + "' returns unknown value '" + s.outputs[i] + "'");
+        const TD r = it->second;
+        auto vit = m.values.find(d.out[i]);
+        if (vit == m.values.end()) throw std::runtime_error("driver value '" + d.out[i] + "' is not declared");
+        const TD dst = vit->second.td;
+        use(r);
+        if (r.sid < 0 && r.data == dst.data && r.type == dst.type && same_shape(r, dst) && r.contiguous()) continue;
+        if (r.nelements() != dst.nelements() || r.type != dst.type)
+            throw std::runtime_error("stage '" + s.name + "' result " + std::to_string(i) + " does not match value '" + d.out[i] + "'");
+        add("copy", "out." + std::to_string(i), {r, dst}, [](cudaStream_t st, const std::vector<TD> &t) { k::copy(t[0], t[1], st); },
+            (double)(r.nelements() * r.elsize() * 2));
+    }
+
+    // pack storages: best fit over a free list, freed after their last use
+    std::vector<std::vector<int>> starts(s.nodes.size() + 2), ends(s.nodes.size() + 2);
+    for (size_t i = 0; i < storages.size(); i++) {
+        starts[(size_t)storages[i].first].push_back((int)i);
+        ends[(size_t)storages[i].last].push_back((int)i);
+    }
+    std::map<size_t, size_t> free_blocks;  // offset -> size
+    size_t top = 0;
+    auto take = [&](size_t bytes) {
+        bytes = (bytes + 255) / 256 * 256;
+        auto best = free_blocks.end();
+        for (auto it = free_blocks.begin(); it != free_blocks.end(); ++it)
+            if (it->second >= bytes && (best == free_blocks.end() || it->second < best->second)) best = it;
+        if (best == free_blocks.end()) {
+            const size_t o = top;
+            top += bytes;
+            return o;
+        }
+        const size_t o = best->first, sz = best->second;
+        free_blocks.erase(best);
+        if (sz > bytes) free_blocks[o + bytes] = sz - bytes;
+        return o;
+    };
+    auto give = [&](size_t off, size_t bytes) {
+        bytes = (bytes + 255) / 256 * 256;
+        auto it = free_blocks.emplace(off, bytes).first;
+        auto nx = std::next(it);
+        if (nx != free_blocks.end() && it->first + it->second == nx->first) {
+            it->second += nx->second;
+            free_blocks.erase(nx);
+        }
+        if (it != free_blocks.begin()) {
+            auto pv = std::prev(it);
+            if (pv->first + pv->second == it->first) {
+                pv->second += it->second;
+                free_blocks.erase(it);
+            }
+        }
+    };
+    for (size_t i = 0; i < starts.size(); i++) {
+        for (int sid : starts[i]) storages[(size_t)sid].offset = take(storages[(size_t)sid].bytes);
+        for (int sid : ends[i]) give(storages[(size_t)sid].offset, storages[(size_t)sid].bytes);
+    }
+    if (cs.arena.size() < top) {
+        cuda_check(cudaStreamSynchronize(m.stream), "arena");
+        cs.arena.alloc(top);
+    }
+    char *base = cs.arena.get();
+    cs.steps.clear();
+    for (auto &ps : psteps) {
+        for (auto &t : ps.tds)
+            if (t.sid >= 0) {
+                t.data = base + storages[(size_t)t.sid].offset + t.off;
+                t.sid = -1;
+                t.off = 0;
+            }
+        Step st;
+        st.kind = ps.kind;
+        st.node = ps.node;
+        st.bytes = ps.bytes;
+        auto fn = std::move(ps.fn);
+        auto tds = std::move(ps.tds);
+        st.run = [fn, tds](cudaStream_t stream) { fn(stream, tds); };
+        cs.steps.push_back(std::move(st));
+    }
+}
+
+void plan_call_site(Model &m, CallSite &cs, const DriverOp &d) {
+    const StageSpec &s = *cs.stage;
+    if (d.args.size() != s.params.size() || d.out.size() != s.outputs.size())
+        throw std::runtime_error("call to stage '" + s.name + "' has the wrong number of arguments or results");
+    Planner p(m, cs, d);
+    for (size_t i = 0; i < s.params.size(); i++) {
+        auto it = m.values.find(d.args[i]);
+        if (it == m.values.end()) throw std::runtime_error("driver value '" + d.args[i] + "' is not declared");
+        const TD &arg = it->second.td;
+        const TensorSpec &ps = s.params[i];
+        for (int k = 0; k < 4; k++)
+            if (arg.ne[k] != ps.ne[(size_t)k] || arg.type != ps.type)
+                throw std::runtime_error("stage '" + s.name + "' parameter " + ps.name + " does not match value '" + d.args[i] + "'");
+        p.env[ps.name] = arg;
+    }
+    std::vector<TD> sv;
+    FusionPlan fp = find_fusions(m, s, p);
+    for (size_t i = 0; i < s.nodes.size(); i++) {
+        const NodeSpec &n = s.nodes[i];
+        p.cur = (int)i;
+        if (fp.covered(i)) {
+            fp.emit_if_anchor(i, p);
+            continue;
+        }
+        sv.clear();
+        for (const auto &name : n.src) {
+            sv.push_back(p.src_of(name));
+            p.use(sv.back());
+        }
+        TD t = p.plan_node(n, sv);
+        if (t.type != n.type) fail(n, std::string("produced type ") + type_name(t.type) + ", program expects " + type_name(n.type));
+        for (int k = 0; k < 4; k++)
+            if (t.ne[k] != n.ne[(size_t)k]) fail(n, "produced shape " + shape_str(t.ne) + ", program expects " + shape_str(n.ne.data()));
+        p.env[n.id] = t;
+    }
+    p.finish();
+    cs.stale = false;
+    cs.graph_ok = false;
+}
+
+}  // namespace gcb

@@ -1,0 +1,104 @@
+"""The reference-compiled tiny Llama (tests/golden/ref_llama_q8_0.gguf: the reference compiler's O3
+program with Q8_0 weights) on the B200, through the C ABI and the reference's host driver
+(Generator), against the CPU oracle and against transformers.
+
+- prefill and decode logits equal the oracle's bit for bit (same arithmetic, same orders);
+- greedy tokens equal the oracle's, through the host loop and through the `generate` entry's
+  device loop, across a KV-block boundary (n_kv 512 -> 768);
+- logits stay within the ggml-semantics bound of transformers' fp32 logits (tolerance 2e-2 of
+  max(1, max|ref|), the Q8_0-activation bound the CPU tests establish for the oracle);
+- state persists across runs until reset (reference tests/unit/test_llm.py:109-116)."""
+
+import numpy as np
+import pytest
+from conftest import GOLDEN
+
+from oracle.interp import OracleGenerator, Program
+from ggml_compiler_b200.llm import Generator
+from ggml_compiler_b200.runtime import Session
+
+pytestmark = pytest.mark.gpu
+GGUF = GOLDEN / "ref_llama_q8_0.gguf"
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return np.load(GOLDEN / "ref_llama_q8_0.npz")
+
+
+@pytest.fixture(scope="module")
+def sess(gpu):
+    s = Session(GGUF, backend="cuda")
+    yield s
+    s.close()
+
+
+def scaled_err(out, ref):
+    return float(np.max(np.abs(np.asarray(out, np.float64) - ref))) / max(1.0, float(np.max(np.abs(ref))))
+
+
+def test_program_shape(sess):
+    assert set(sess.entries) == {"prefill", "decode", "generate"}
+    assert sess.symbols == {"max_new": (1, 768), "s": (2, 64), "kv_blocks": (2, 3)}
+    assert sess.metadata["eos"] == [7] and sess.metadata["max_context"] == 768
+    assert sess.backend_name.startswith("CUDA")
+
+
+def test_logits_bit_exact_vs_oracle(sess, golden):
+    ids = golden["ids"].tolist()
+    g, o = Generator(sess), OracleGenerator(Program(GGUF))
+    g.reset()
+    o.reset()
+    chunks = [ids[:16], ids[16:30]] + [[t] for t in ids[30:40]]
+    for c in chunks:
+        a, b = g.feed(c), o.feed(c)
+        np.testing.assert_array_equal(a, b)
+
+
+def test_logits_vs_transformers(sess, golden):
+    ids = golden["ids"].tolist()
+    g = Generator(sess)
+    g.reset()
+    got = {39: g.feed(ids)}
+    for i, row in got.items():
+        assert scaled_err(row, golden["logits"][i]) < 2e-2
+
+
+def test_greedy_host_and_device_loops_match_oracle(sess, golden):
+    """300 tokens from a 30-token prompt: the loop crosses from n_kv 512 into 768."""
+    prompt = golden["ids"][:30].tolist()
+    g = Generator(sess)
+    host = g.generate(prompt, max_new=300, stop=[])
+    dev_full = Generator(sess)
+    o = OracleGenerator(Program(GGUF))
+    ref, _ = o.generate(prompt, max_new=300)
+    assert host == ref
+    dev = dev_full.generate(prompt, max_new=300, device=True)
+    # the device loop stops at the model's EOS id (7); the host loop was told not to
+    n = len(dev)
+    assert dev == host[:n] and (n == 300 or dev[-1] == 7)
+    assert dev_full.n_past == len(prompt) + n - 1
+
+
+def test_state_persists_until_reset(sess):
+    g = Generator(sess)
+    a = g.generate([1, 2, 3, 4], max_new=5, stop=[])
+    g.feed([9, 9, 9])
+    b = g.generate([1, 2, 3, 4], max_new=5, stop=[])  # generate resets first
+    assert a == b
+    sess.reset()
+
+
+def test_input_errors(sess):
+    from ggml_compiler_b200.runtime import GgmlCompilerRuntimeError
+
+    with pytest.raises(GgmlCompilerRuntimeError, match="needs"):
+        import ctypes
+
+        lib = __import__("ggml_compiler_b200.runtime", fromlist=["x"]).load_library()
+        x = np.zeros(3, np.int32)
+        if lib.ggml_compiler_set_input(sess._m, b"token", x.ctypes.data, 12) != 0:
+            raise GgmlCompilerRuntimeError(lib.ggml_compiler_last_error().decode())
+    with pytest.raises(GgmlCompilerRuntimeError, match="no kv_blocks|cannot have shape"):
+        sess.run(token=np.zeros((1, 1), np.int32), position=np.zeros(1, np.int32),
+                 mask1=np.zeros((1, 1, 1, 300), np.float32), entry="decode")

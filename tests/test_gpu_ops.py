@@ -1,0 +1,57 @@
+"""Isolated quantized mul_mat on the B200 against the CPU oracle (BASELINE config 2's op sweep at
+sizes the oracle finishes in seconds): single-stage programs through the C ABI, as the reference's
+op tests run them (tests/unit/test_runtime_ops.py:86-102). The backend follows the oracle's reduction
+order, so results are compared bit for bit."""
+
+import numpy as np
+import pytest
+
+import oracle
+from ggml_compiler_b200.programs import write_mul_mat
+from ggml_compiler_b200.runtime import Session
+
+pytestmark = pytest.mark.gpu
+
+
+def weights(shape, seed=0):
+    return np.random.default_rng(seed).standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+
+
+def run_mm(tmp_path, w, wtype, x):
+    p = tmp_path / f"mm_{wtype}_{w.shape[0]}x{w.shape[1]}_{x.shape[0]}.gguf"
+    write_mul_mat(p, w, wtype, x.shape[0])
+    with Session(p, backend="cuda") as s:
+        return s.run(x=x[None])["out.0"].reshape(x.shape[0], w.shape[0])
+
+
+@pytest.mark.parametrize("wtype", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("N,K", [(256, 512), (4096, 4096), (1000, 14336)])
+@pytest.mark.parametrize("M", [1, 8, 64])
+def test_quant_mul_mat_bit_exact(gpu, tmp_path, wtype, N, K, M):
+    if N * K * M > 4096 * 4096 * 8:
+        pytest.skip("oracle time")
+    w = weights((N, K))
+    x = np.random.default_rng(1).standard_normal((M, K), dtype=np.float32)
+    got = run_mm(tmp_path, w, wtype, x)
+    ref = oracle.mul_mat(oracle.quantize(w, wtype), wtype, K, x)
+    np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("wtype", ["f32", "f16"])
+def test_float_mul_mat_bit_exact(gpu, tmp_path, wtype):
+    w = weights((96, 160))
+    x = np.random.default_rng(2).standard_normal((5, 160), dtype=np.float32)
+    got = run_mm(tmp_path, w, wtype, x)
+    wr = w.astype(np.float16) if wtype == "f16" else w
+    np.testing.assert_array_equal(got, oracle.mul_mat(wr, wtype, 160, x))
+
+
+def test_quant_mul_mat_edges(gpu, tmp_path):
+    """Zero activation blocks (d = 0), huge and tiny values, a single block per row."""
+    w = weights((64, 32))
+    x = np.zeros((3, 32), np.float32)
+    x[1, :5] = [1e4, -1e-30, 3.0, -3.0, 0.5]
+    x[2] = np.linspace(-1, 1, 32, dtype=np.float32)
+    for wtype in ("q4_0", "q8_0"):
+        got = run_mm(tmp_path, w, wtype, x)
+        np.testing.assert_array_equal(got, oracle.mul_mat(oracle.quantize(w, wtype), wtype, 32, x))
