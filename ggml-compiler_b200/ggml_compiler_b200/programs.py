@@ -13,16 +13,17 @@ from . import runtime
 from .gguf_write import TensorEntry, write_gguf
 
 
-def single_node_program(op: str, inputs: Sequence[tuple[str, str, list[int]]], src: Sequence[str], out_type: str,
-                        out_ne: list[int], params: dict[str, Any] | None = None) -> dict[str, Any]:
-    """One stage `main` computing node %0 = op(src...) from program inputs (name, type, ggml ne) and
-    GGUF weights (names in `src` that are not inputs). The output value is `out.0`."""
-    names = [n for n, _, _ in inputs]
+def single_node_program(op: str, inputs: Sequence[tuple[str, str, list[int], list[int]]], src: Sequence[str],
+                        out_type: str, out_ne: list[int], out_shape: list[int],
+                        params: dict[str, Any] | None = None) -> dict[str, Any]:
+    """One stage `main` computing node %0 = op(src...) from program inputs (name, type, ggml ne,
+    PyTorch shape) and GGUF weights (names in `src` that are not inputs). The output is `out.0`."""
+    names = [n for n, _, _, _ in inputs]
     pmap = {n: f"a.{i}" for i, n in enumerate(names)}
-    values = [{"name": n, "type": t, "ne": list(ne), "shape": list(reversed(_trim(ne)))} for n, t, ne in inputs]
-    values.append({"name": "out.0", "type": out_type, "ne": list(out_ne), "shape": list(reversed(_trim(out_ne)))})
+    values = [{"name": n, "type": t, "ne": list(ne), "shape": list(sh)} for n, t, ne, sh in inputs]
+    values.append({"name": "out.0", "type": out_type, "ne": list(out_ne), "shape": list(out_shape)})
     stage = {"name": "main",
-             "params": [{"name": pmap[n], "type": t, "ne": list(ne), "shape": list(reversed(_trim(ne)))} for n, t, ne in inputs],
+             "params": [{"name": pmap[n], "type": t, "ne": list(ne), "shape": list(sh)} for n, t, ne, sh in inputs],
              "outputs": ["%0"],
              "nodes": [{"id": "%0", "op": op, "src": [pmap.get(s, s) for s in src], "type": out_type, "ne": list(out_ne),
                         "p": params or {}}]}
@@ -30,13 +31,6 @@ def single_node_program(op: str, inputs: Sequence[tuple[str, str, list[int]]], s
     return {"format_version": 3, "symbols": [], "values": values, "inputs": names, "outputs": ["out.0"],
             "stages": [stage], "driver": driver,
             "entries": [{"name": "main", "inputs": names, "outputs": ["out.0"], "driver": driver}], "state": []}
-
-
-def _trim(ne: Sequence[int]) -> list[int]:
-    ne = list(ne)
-    while len(ne) > 1 and ne[-1] == 1:
-        ne.pop()
-    return ne
 
 
 def write_mul_mat(path: str | Path, w: np.ndarray, wtype: str, M: int, batch: int = 1) -> None:
@@ -48,5 +42,6 @@ def write_mul_mat(path: str | Path, w: np.ndarray, wtype: str, M: int, batch: in
         data = w.astype(np.float16)
     else:
         data = np.ascontiguousarray(w, np.float32)
-    prog = single_node_program("mul_mat", [("x", "f32", [K, M, batch, 1])], ["w.0", "x"], "f32", [N, M, batch, 1])
+    prog = single_node_program("mul_mat", [("x", "f32", [K, M, batch, 1], [batch, M, K])], ["w.0", "x"], "f32",
+                               [N, M, batch, 1], [batch, M, N])
     write_gguf(path, prog, [TensorEntry("w.0", wtype, (K, N), data)])
