@@ -1,0 +1,53 @@
+// Arguments of the fused decode GEMV kernel (kernels/gc_fused.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "gc_types.h"
+
+namespace gcb {
+
+enum { PRO_ACT = 0, PRO_NORM = 1 };
+enum { MAP_SINGLE = 0, MAP_ROPE_QKV = 1, MAP_SWIGLU = 2 };
+
+struct FusedArgs {
+    int qtype = T_Q4_0;  // of every weight
+    int pro = PRO_ACT;
+    int map = MAP_SINGLE;
+    // activation rows: x[m * ldx + k], m < M, k < K
+    const float *x = nullptr;
+    int64_t ldx = 0;
+    int M = 1;
+    int64_t K = 0;
+    const float *norm_w = nullptr;  // PRO_NORM
+    float eps = 0.0f;
+    // weights: repacked codes + fp16 scales, rows of K
+    const char *wc[3] = {nullptr, nullptr, nullptr};
+    const uint16_t *ws[3] = {nullptr, nullptr, nullptr};
+    int64_t wrows[3] = {0, 0, 0};
+    // MAP_SINGLE / MAP_SWIGLU output, optional residual (MAP_SINGLE)
+    float *out = nullptr;
+    int64_t ldo = 0;
+    const float *res = nullptr;
+    int64_t ldr = 0;
+    // MAP_ROPE_QKV
+    int64_t D = 0, H = 0, Hkv = 0;
+    float *q_out = nullptr;
+    int64_t ldq = 0;
+    char *kcache = nullptr, *vcache = nullptr;
+    int64_t cache_nb1 = 0, cache_nb2 = 0, cache_rows = 0;
+    const int32_t *pos = nullptr;
+    const float *table = nullptr;
+    int64_t npos = 0;
+    float theta_scale = 1.0f;
+    int *err = nullptr;
+};
+
+namespace k {
+bool fused_gemv_supported(int64_t K, int64_t M, int map);
+void fused_gemv(const FusedArgs &a, cudaStream_t s, bool pdl);
+}  // namespace k
+
+}  // namespace gcb

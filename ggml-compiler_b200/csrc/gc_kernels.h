@@ -1,10 +1,10 @@
 // Device tensor descriptors and the host launchers of every CUDA kernel of the backend.
 //
 // A TD is a strided view in ggml's layout: ne innermost first, nb byte strides. A quantized weight
-// (Q4_0 / Q8_0) is stored on the device split in two arrays, repacked from the GGUF blocks at load:
-// `data` holds each row's codes block after block (Q4_0: 16 bytes per block, the GGUF nibble order;
-// Q8_0: 32 int8 per block) so every block starts on a 16-byte boundary, and `scales` holds the fp16
-// block scales [rows][K/32]. nb[1] is then the code bytes of one row.
+// (Q4_0 / Q8_0) is stored on the device in the tiled layout of kernels/gc_qweight.cuh (8-row tiles
+// cut into 128-block segments, codes then scales per piece), repacked from the GGUF blocks at load;
+// `data` points at it and nb[1] is the code bytes of one row (a nominal stride: quantized tensors
+// are only viewed row for row).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -40,9 +40,9 @@ size_t quant_code_bytes(Type t);  // code bytes per 32-block: Q4_0 16, Q8_0 32
 
 namespace k {
 
-// Repack raw GGUF Q4_0/Q8_0 rows into codes + scales.
-void repack_quant(Type t, const uint8_t *raw, int64_t nrows, int64_t K, char *codes, uint16_t *scales,
-                  cudaStream_t s);
+// Repack raw GGUF Q4_0/Q8_0 rows into the tiled device layout of quant_device_bytes bytes.
+size_t quant_device_bytes(Type t, int64_t rows, int64_t K);
+void repack_quant(Type t, const uint8_t *raw, int64_t nrows, int64_t K, char *dst, cudaStream_t s);
 
 // Elementwise and row ops (generic strides).
 void copy(const TD &src, const TD &dst, cudaStream_t s);  // cont / cpy / cast (f32, f16, bf16, i32)
@@ -79,6 +79,15 @@ void mul_mat(const TD &a, const TD &b, const TD &out, void *scratch, cudaStream_
 // flash_attn_ext: q [D, Sq, H, B] f32, k/v [D, n_kv, Hkv, B] f16, mask [n_kv, >=Sq, ...] f16 (nullable)
 // -> out [D, H, Sq, B] f32.
 void flash_attn(const TD &q, const TD &k, const TD &v, const TD *mask, const TD &out, float scale, cudaStream_t s);
+
+// Split-KV flash attention (gc_flash.cu): head size <= 256 and a multiple of 32; same result as
+// flash_attn. `counters` (flash_split_counters ints) must be zero before the first launch and are
+// left zero by every launch; `scratch` holds flash_split_scratch_bytes.
+bool flash_split_ok(const TD &q);
+size_t flash_split_scratch_bytes(const TD &q, const TD &k);
+size_t flash_split_counters(const TD &q, const TD &k);
+void flash_attn_split(const TD &q, const TD &k, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
+                      int *counters, int *err, cudaStream_t s);
 
 }  // namespace k
 }  // namespace gcb

@@ -71,6 +71,7 @@ Model::~Model() {
     weights.clear();
     values.clear();
     rope_tables.clear();
+    counter_bufs.clear();
     if (stream) cudaStreamDestroy(stream);
 }
 
@@ -171,11 +172,9 @@ void Model::load_weights() {
             }
             if (q) {
                 const int64_t K = t.ne[0], rows = t.ne[1] * t.ne[2] * t.ne[3];
-                w.data.alloc((size_t)(rows * (K / 32)) * quant_code_bytes(t.type));
-                w.scales.alloc((size_t)(rows * (K / 32)) * 2);
-                k::repack_quant(t.type, (const uint8_t *)raw.get(), rows, K, w.data.get(), (uint16_t *)w.scales.get(), stream);
+                w.data.alloc(k::quant_device_bytes(t.type, rows, K));
+                k::repack_quant(t.type, (const uint8_t *)raw.get(), rows, K, w.data.get(), stream);
                 cuda_check(cudaStreamSynchronize(stream), "repack");
-                w.td.scales = (uint16_t *)w.scales.get();
             }
             w.td.data = w.data.get();
             set_contiguous(w.td);
@@ -507,6 +506,8 @@ void Model::run_entry(const std::string &name) {
     cuda_check(cudaMemcpy(&err, d_err, sizeof err, cudaMemcpyDeviceToHost), "error word");
     if (err) {
         cudaMemset(d_err, 0, sizeof(int));
+        if (err == 2)
+            throw std::runtime_error("entry '" + name + "': a kernel's pipeline wait timed out (results are invalid)");
         throw std::runtime_error("entry '" + name + "': a set_rows index was outside its destination (row skipped)");
     }
     if (!profile_path.empty() && !profile_lines.empty()) {
@@ -525,6 +526,17 @@ void Model::reset_state() {
         cuda_check(cudaMemsetAsync(v.buf.get(), 0, v.buf.size(), stream), "reset");
     }
     cuda_check(cudaStreamSynchronize(stream), "reset");
+}
+
+int *Model::counters(const std::string &key, size_t n) {
+    auto it = counter_bufs.find(key);
+    if (it != counter_bufs.end() && it->second.size() >= n * sizeof(int)) return (int *)it->second.get();
+    cuda_check(cudaStreamSynchronize(stream), "counters");
+    DevBuf b;
+    b.alloc(std::max<size_t>(n, 1) * sizeof(int));  // zero-filled
+    int *p = (int *)b.get();
+    counter_bufs[key] = std::move(b);
+    return p;
 }
 
 const float *Model::rope_table(int n_dims, float base, float scale, float attn, const std::string &ff_key,

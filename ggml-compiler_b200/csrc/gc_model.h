@@ -121,6 +121,9 @@ struct Model {
     size_t nbytes_of(const TensorSpec &v, const std::vector<int64_t> &b) const;
     const float *rope_table(int n_dims, float base, float scale, float attn, const std::string &ff_key,
                             const float *ff_host, int64_t *npos);
+    // Zeroed device ints that persist across launches (arrival counters), one buffer per key.
+    int *counters(const std::string &key, size_t n);
+    std::map<std::string, DevBuf> counter_bufs;
 
   private:
     void load_weights();

@@ -18,6 +18,7 @@
 #include <stdexcept>
 
 #include "gc_fuse.h"
+#include "gc_fused.h"
 #include "gc_model.h"
 
 namespace gcb {
@@ -265,12 +266,34 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
         if (b.type != T_F32) fail(n, "activation operand must be f32");
         int64_t ne[4] = {a.ne[1], b.ne[1], b.ne[2], b.ne[3]};
         TD y = out_like(T_F32, ne);
-        const size_t sb = k::mul_mat_scratch_bytes(a, b);
-        TD scratch;
-        if (sb) scratch_marker(sb, &scratch);
         const double bytes = (double)(is_quant(a.type) ? (double)a.nrows() * (a.ne[0] / 32) * (quant_code_bytes(a.type) + 2)
                                                         : (double)a.nelements() * a.elsize()) +
                              (double)b.nelements() * 4 + (double)y.nelements() * 4;
+        if (is_quant(a.type) && a.ne[2] == 1 && a.ne[3] == 1 && b.ne[2] == 1 && b.ne[3] == 1 && b.nb[0] == 4 &&
+            (b.ne[1] == 1 || b.nb[1] == 4 * b.ne[0]) && k::fused_gemv_supported(a.ne[0], b.ne[1], MAP_SINGLE)) {
+            const int64_t K = a.ne[0], N = a.ne[1], M = b.ne[1];
+            add(a.type == T_Q4_0 ? "gemv_q4_0" : "gemv_q8_0", n.id, {a, b, y},
+                [K, N, M](cudaStream_t st, const std::vector<TD> &t) {
+                    FusedArgs fa;
+                    fa.qtype = t[0].type;
+                    fa.pro = PRO_ACT;
+                    fa.map = MAP_SINGLE;
+                    fa.x = (const float *)t[1].data;
+                    fa.ldx = K;
+                    fa.M = (int)M;
+                    fa.K = K;
+                    fa.wc[0] = t[0].data;
+                    fa.wrows[0] = N;
+                    fa.out = (float *)t[2].data;
+                    fa.ldo = N;
+                    k::fused_gemv(fa, st, true);
+                },
+                bytes);
+            return y;
+        }
+        const size_t sb = k::mul_mat_scratch_bytes(a, b);
+        TD scratch;
+        if (sb) scratch_marker(sb, &scratch);
         if (sb)
             add("mul_mat", n.id, {a, b, y, scratch},
                 [](cudaStream_t st, const std::vector<TD> &t) { k::mul_mat(t[0], t[1], t[2], t[3].data, st); }, bytes);
@@ -296,8 +319,30 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
             const TD &mk = sv[3];
             if (mk.type != T_F16 || !mk.contiguous() || q.ne[2] % mk.ne[2] != 0 || mk.ne[0] != kk.ne[1] || mk.ne[1] < q.ne[1])
                 fail(n, "mask must be a contiguous f16 tensor broadcastable over heads");
+            if (k::flash_split_ok(q)) {
+                TD scratch;
+                scratch_marker(k::flash_split_scratch_bytes(q, kk), &scratch);
+                int *cnt = m.counters(s.name + "/" + n.id, k::flash_split_counters(q, kk));
+                int *err = m.d_err;
+                add("flash_attn", n.id, {q, kk, v, mk, y, scratch},
+                    [scale, cnt, err](cudaStream_t st, const std::vector<TD> &t) {
+                        k::flash_attn_split(t[0], t[1], t[2], &t[3], t[4], scale, t[5].data, cnt, err, st);
+                    },
+                    bytes);
+                return y;
+            }
             add("flash_attn", n.id, {q, kk, v, mk, y},
                 [scale](cudaStream_t st, const std::vector<TD> &t) { k::flash_attn(t[0], t[1], t[2], &t[3], t[4], scale, st); },
+                bytes);
+        } else if (k::flash_split_ok(q)) {
+            TD scratch;
+            scratch_marker(k::flash_split_scratch_bytes(q, kk), &scratch);
+            int *cnt = m.counters(s.name + "/" + n.id, k::flash_split_counters(q, kk));
+            int *err = m.d_err;
+            add("flash_attn", n.id, {q, kk, v, y, scratch},
+                [scale, cnt, err](cudaStream_t st, const std::vector<TD> &t) {
+                    k::flash_attn_split(t[0], t[1], t[2], nullptr, t[3], scale, t[4].data, cnt, err, st);
+                },
                 bytes);
         } else {
             add("flash_attn", n.id, {q, kk, v, y},

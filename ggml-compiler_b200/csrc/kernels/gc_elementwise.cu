@@ -8,6 +8,7 @@
 
 #include "../gc_kernels.h"
 #include "gc_math.cuh"
+#include "gc_qweight.cuh"
 
 namespace gcb {
 
@@ -111,26 +112,24 @@ __device__ __forceinline__ void stf(char *p, int type, float v) {
 
 // ------------------------------------------------------------------------------------------------
 
-__global__ void repack_kernel(int type, const uint8_t *raw, int64_t nblocks, char *codes, uint16_t *scales) {
-    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nblocks; b += (int64_t)gridDim.x * blockDim.x) {
-        if (type == T_Q4_0) {
-            const uint8_t *src = raw + b * 18;
-            scales[b] = (uint16_t)(src[0] | (src[1] << 8));
-            uint32_t w[4];
-            for (int i = 0; i < 4; i++)
-                w[i] = (uint32_t)src[2 + 4 * i] | ((uint32_t)src[3 + 4 * i] << 8) | ((uint32_t)src[4 + 4 * i] << 16) |
+// GGUF blocks (row-major, 18 or 34 bytes) -> the tiled device layout (gc_qweight.cuh).
+__global__ void repack_kernel(int type, const uint8_t *raw, int64_t rows, int64_t nb, char *dst) {
+    const int bs = type == T_Q4_0 ? 18 : 34;
+    const int cb = type == T_Q4_0 ? 16 : 32;
+    const QW w{dst, nb, cb};
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < rows * nb; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = t / nb, blk = t % nb;
+        const uint8_t *src = raw + t * bs;
+        char *code = (char *)qw_code(w, row, blk);
+        uint32_t words[8];
+        for (int i = 0; i < cb / 4; i++)
+            words[i] = (uint32_t)src[2 + 4 * i] | ((uint32_t)src[3 + 4 * i] << 8) | ((uint32_t)src[4 + 4 * i] << 16) |
                        ((uint32_t)src[5 + 4 * i] << 24);
-            *(uint4 *)(codes + b * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-        } else {
-            const uint8_t *src = raw + b * 34;
-            scales[b] = (uint16_t)(src[0] | (src[1] << 8));
-            uint32_t w[8];
-            for (int i = 0; i < 8; i++)
-                w[i] = (uint32_t)src[2 + 4 * i] | ((uint32_t)src[3 + 4 * i] << 8) | ((uint32_t)src[4 + 4 * i] << 16) |
-                       ((uint32_t)src[5 + 4 * i] << 24);
-            *(uint4 *)(codes + b * 32) = make_uint4(w[0], w[1], w[2], w[3]);
-            *(uint4 *)(codes + b * 32 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
-        }
+        *(uint4 *)code = make_uint4(words[0], words[1], words[2], words[3]);
+        if (cb == 32) *(uint4 *)(code + 16) = make_uint4(words[4], words[5], words[6], words[7]);
+        const int64_t g = blk / QSEG, sb = qw_seg_blocks(nb, g);
+        uint16_t *sc = (uint16_t *)(dst + qw_piece_off(nb, cb, row / QTR, g) + QTR * sb * cb);
+        sc[(row % QTR) * sb + blk % QSEG] = (uint16_t)(src[0] | (src[1] << 8));
     }
 }
 
@@ -322,7 +321,7 @@ __global__ void rope_kernel(int neox, Dk x, const int32_t *pos, Dk out, int n_di
 }
 
 // get_rows: out[:, i10, i11, i12] = table[:, idx[i10, i11, i12], i11, i12] as f32.
-__global__ void get_rows_kernel(Dk tab, const uint16_t *scales, int64_t scale_row, Dk idx, Dk out) {
+__global__ void get_rows_kernel(Dk tab, Dk idx, Dk out) {
     const int64_t n = out.ne0 * out.ne1 * out.ne2 * out.ne3;
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
         const int64_t i0 = t % out.ne0;
@@ -335,15 +334,16 @@ __global__ void get_rows_kernel(Dk tab, const uint16_t *scales, int64_t scale_ro
         float v = 0.0f;
         if (row >= 0 && row < tab.ne1) {
             if (tab.type == T_Q4_0 || tab.type == T_Q8_0) {
+                const QW w{tab.data, tab.ne0 / 32, tab.type == T_Q4_0 ? 16 : 32};
                 const int64_t rr = row + tab.ne1 * (i11 + tab.ne2 * i12);
-                const char *codes = tab.data + rr * tab.nb1;
-                const float d = h2f(scales[rr * scale_row + i0 / 32]);
+                const char *codes = qw_code(w, rr, i0 / 32);
+                const float d = h2f(qw_scale(w, rr, i0 / 32));
                 const int j = (int)(i0 % 32);
                 int q;
                 if (tab.type == T_Q8_0) {
-                    q = (int8_t)codes[(i0 / 32) * 32 + j];
+                    q = (int8_t)codes[j];
                 } else {
-                    const uint8_t byte = (uint8_t)codes[(i0 / 32) * 16 + (j & 15)];
+                    const uint8_t byte = (uint8_t)codes[j & 15];
                     q = (j < 16 ? (byte & 15) : (byte >> 4)) - 8;
                 }
                 v = __fmul_rn(d, (float)q);
@@ -486,11 +486,13 @@ __global__ void causal_mask_kernel(float *out, int64_t n, int64_t row_len, const
 
 }  // namespace
 
-void repack_quant(Type t, const uint8_t *raw, int64_t nrows, int64_t K, char *codes, uint16_t *scales, cudaStream_t s) {
+void repack_quant(Type t, const uint8_t *raw, int64_t nrows, int64_t K, char *dst, cudaStream_t s) {
     const int64_t nblocks = nrows * (K / 32);
-    repack_kernel<<<blocks_for(nblocks, 256), 256, 0, s>>>((int)t, raw, nblocks, codes, scales);
+    repack_kernel<<<blocks_for(nblocks, 256), 256, 0, s>>>((int)t, raw, nrows, K / 32, dst);
     check_launch("repack_quant");
 }
+
+size_t quant_device_bytes(Type t, int64_t rows, int64_t K) { return (size_t)qw_total_bytes(rows, K / 32, (int)quant_code_bytes(t)); }
 
 void copy(const TD &src, const TD &dst, cudaStream_t s) {
     const int64_t n = dst.nelements();
@@ -546,7 +548,7 @@ void rope_norm(const TD &x, const TD &pos, const TD &out, int n_dims, const floa
 
 void get_rows(const TD &table, const TD &idx, const TD &out, cudaStream_t s) {
     const int64_t n = out.nelements();
-    get_rows_kernel<<<blocks_for(n, 256), 256, 0, s>>>(dk(table), table.scales, table.ne[0] / 32, dk(idx), dk(out));
+    get_rows_kernel<<<blocks_for(n, 256), 256, 0, s>>>(dk(table), dk(idx), dk(out));
     check_launch("get_rows");
 }
 

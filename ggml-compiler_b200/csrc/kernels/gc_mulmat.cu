@@ -16,6 +16,7 @@
 
 #include "../gc_kernels.h"
 #include "gc_math.cuh"
+#include "gc_qweight.cuh"
 
 namespace gcb {
 namespace k {
@@ -85,27 +86,25 @@ __device__ __forceinline__ int block_isum(int atype, const char *codes, const in
     return s;
 }
 
-// One warp per output element (n, m, i2, i3), quantized weight.
+// One warp per output element (n, m, i2, i3), quantized weight (tiled layout, rows flattened).
 __global__ void mm_quant_kernel(MMk p, const int8_t *qx, const uint16_t *dx) {
     const int lane = threadIdx.x & 31;
     const int64_t nb = p.K / 32;
     const int64_t nout = p.N * p.M * p.B2 * p.B3;
-    const size_t cb = p.atype == T_Q4_0 ? 16 : 32;
+    const QW wq{p.a, nb, p.atype == T_Q4_0 ? 16 : 32};
     for (int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; w < nout;
          w += ((int64_t)gridDim.x * blockDim.x) >> 5) {
         const int64_t n = w % p.N;
         const int64_t r = w / p.N;  // (m, i2, i3)
         const int64_t i2 = (r / p.M) % p.B2, i3 = r / (p.M * p.B2);
         const int64_t a2 = i2 / (p.B2 / p.A2), a3 = i3 / (p.B3 / p.A3);
-        const char *arow = p.a + n * p.anb1 + a2 * p.anb2 + a3 * p.anb3;
-        const int64_t srow = n + p.N * (a2 + p.A2 * a3);
-        const uint16_t *asc = p.as + srow * nb;
+        const int64_t arow = n + p.N * (a2 + p.A2 * a3);
         const int8_t *xrow = qx + r * p.K;
         const uint16_t *xd = dx + r * nb;
         float acc = 0.0f;
         for (int64_t blk = lane; blk < nb; blk += 32) {
-            const int isum = block_isum(p.atype, arow + blk * cb, xrow + blk * 32);
-            const float dd = __fmul_rn(h2f(asc[blk]), h2f(xd[blk]));
+            const int isum = block_isum(p.atype, qw_code(wq, arow, blk), xrow + blk * 32);
+            const float dd = __fmul_rn(h2f(qw_scale(wq, arow, blk)), h2f(xd[blk]));
             acc = __fmaf_rn(dd, (float)isum, acc);
         }
         acc = warp_butterfly(acc);
