@@ -11,8 +11,10 @@ are timed (one step = one token through all 32 layers; n_kv = 768).
 - e2e: the same decode through the public C API from host buffers, one `decode` entry per token
   (host -> device copies of token/position/mask from pinned memory, device -> host logits, host
   argmax), timed with CUDA events on the same stream.
-- roofline: the quantized GEMV kernels (the dominant kernel family), algorithmic bytes per launch
-  (Q4_0 weight bytes + activation bytes) / mean launch time from a profiled pass of the same steps.
+- roofline: the weight-streaming kernel (the decode kernel, one launch per token running every
+  layer's fused GEMVs and attention; or, with GGML_COMPILER_B200_DECODE_KERNEL=0, the per-group
+  GEMV launches), algorithmic bytes per launch (Q4_0 weight bytes + activation bytes + the K/V rows
+  attention reads) / mean launch time from a profiled pass of the same steps.
 - cpu_baseline / --impl reference: the reference's CPU arithmetic (this repository's C
   restatement of ggml's CPU path, oracle/) timed on the host's cores on a few decode tokens.
 
@@ -127,32 +129,6 @@ class Clocks:
                 "samples": len(rows)}
 
 
-def ext(lib):
-    import ctypes
-
-    lib.ggml_compiler_b200_stream.argtypes = [ctypes.c_void_p]
-    lib.ggml_compiler_b200_stream.restype = ctypes.c_void_p
-    lib.ggml_compiler_b200_last_device_ms.argtypes = [ctypes.c_void_p]
-    lib.ggml_compiler_b200_last_device_ms.restype = ctypes.c_double
-    lib.ggml_compiler_b200_set_profiling.argtypes = [ctypes.c_void_p, ctypes.c_int]
-    lib.ggml_compiler_b200_n_kernel_stats.argtypes = [ctypes.c_void_p]
-    lib.ggml_compiler_b200_kernel_stats.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
-                                                    ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int),
-                                                    ctypes.POINTER(ctypes.c_double)]
-    return lib
-
-
-def kernel_stats(lib, m) -> dict[str, dict]:
-    import ctypes
-
-    out = {}
-    for i in range(lib.ggml_compiler_b200_n_kernel_stats(m)):
-        k, ms, n, b = ctypes.c_char_p(), ctypes.c_double(), ctypes.c_int(), ctypes.c_double()
-        lib.ggml_compiler_b200_kernel_stats(m, i, ctypes.byref(k), ctypes.byref(ms), ctypes.byref(n), ctypes.byref(b))
-        out[k.value.decode()] = {"ms": ms.value, "launches": n.value, "bytes": b.value}
-    return out
-
-
 def peaks() -> tuple[float, str]:
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -226,10 +202,10 @@ def main() -> None:
     from ggml_compiler_b200.llm import Generator
     from ggml_compiler_b200.runtime import Session, load_library
 
-    lib = ext(load_library())
+    lib = load_library()
     gguf = model_path(sh, args.config, rank, world)
     s = Session(gguf, backend="cuda", device=local)
-    stream = torch.cuda.ExternalStream(lib.ggml_compiler_b200_stream(s._m), device=torch.device("cuda", local))
+    stream = torch.cuda.ExternalStream(s.stream, device=torch.device("cuda", local))
     g = Generator(s)
     prompt = np.random.default_rng(1).integers(0, sh.vocab, 512).tolist()
 
@@ -240,7 +216,7 @@ def main() -> None:
     def generate(first: int, n: int) -> float:
         s.set_symbol("max_new", n)
         s.run(first=np.array([[first]], np.int32), start=np.array([512], np.int32), entry="generate")
-        return lib.ggml_compiler_b200_last_device_ms(s._m)
+        return s.last_device_ms
 
     # warm-up: prefill + W device-loop steps (graphs captured for n_kv 768)
     first = prefill()
@@ -313,12 +289,13 @@ def main() -> None:
 
     # roofline: profiled pass over the same decode steps, per kernel family
     first = prefill()
-    lib.ggml_compiler_b200_set_profiling(s._m, 1)
+    s.set_profiling(True)
     n_prof = min(K, 16)
     generate(first, n_prof)
-    ks = kernel_stats(lib, s._m)
-    lib.ggml_compiler_b200_set_profiling(s._m, 0)
-    gemv_kinds = [k for k in ks if k.startswith("gemv") or k == "mul_mat"]
+    ks = s.kernel_stats()
+    s.set_profiling(False)
+    # the weight-streaming kernels: the decode kernel (every layer in one launch) or the per-group GEMVs
+    gemv_kinds = [k for k in ks if k.startswith(("gemv", "decode_")) or k == "mul_mat"]
     gemv_ms = sum(ks[k]["ms"] for k in gemv_kinds)
     gemv_bytes = sum(ks[k]["bytes"] for k in gemv_kinds)
     gemv_launches = sum(ks[k]["launches"] for k in gemv_kinds)

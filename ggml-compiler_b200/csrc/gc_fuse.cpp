@@ -316,8 +316,8 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
                 const float theta_scale = ::powf(base, -2.0f / (float)D);
                 int *err = m.d_err;
                 const double bytes = weight_bytes(tq) + weight_bytes(tk) + weight_bytes(tv) + 4.0 * d * M;
-                pl.add(tq.type == T_Q4_0 ? "gemv_q4_0_qkv" : "gemv_q8_0_qkv", qid, {x, nw, tq, tk, tv, tp, tkc, tvc, qb},
-                       [=](cudaStream_t st, const std::vector<TD> &td) {
+                pl.add_gemv(tq.type == T_Q4_0 ? "gemv_q4_0_qkv" : "gemv_q8_0_qkv", qid, {x, nw, tq, tk, tv, tp, tkc, tvc, qb},
+                       [=](const std::vector<TD> &td) {
                            FusedArgs a;
                            a.pro = PRO_NORM;
                            a.map = MAP_ROPE_QKV;
@@ -345,7 +345,7 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
                            a.npos = npos;
                            a.theta_scale = theta_scale;
                            a.err = err;
-                           k::fused_gemv(a, st, true);
+                           return a;
                        },
                        bytes);
                 pl.env[qid] = qb;
@@ -398,8 +398,8 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
                 const int64_t ne[4] = {F, M, 1, 1};
                 TD hb = pl.alloc(T_F32, ne);
                 const double bytes = weight_bytes(tg) + weight_bytes(tu) + 4.0 * d * M + 4.0 * F * M;
-                pl.add(tg.type == T_Q4_0 ? "gemv_q4_0_glu" : "gemv_q8_0_glu", swid, {x, nw, tg, tu, hb},
-                       [=](cudaStream_t st, const std::vector<TD> &td) {
+                pl.add_gemv(tg.type == T_Q4_0 ? "gemv_q4_0_glu" : "gemv_q8_0_glu", swid, {x, nw, tg, tu, hb},
+                       [=](const std::vector<TD> &td) {
                            FusedArgs a;
                            a.pro = PRO_NORM;
                            a.map = MAP_SWIGLU;
@@ -413,7 +413,7 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
                            fill_weight(a, 1, td[3]);
                            a.out = (float *)td[4].data;
                            a.ldo = F;
-                           k::fused_gemv(a, st, true);
+                           return a;
                        },
                        bytes);
                 pl.env[swid] = hb;
@@ -434,8 +434,8 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
                 const int64_t ne[4] = {N, M, 1, 1};
                 TD yb = pl.alloc(T_F32, ne);
                 const double bytes = weight_bytes(tw) + 4.0 * d * M + 4.0 * N * M;
-                pl.add(tw.type == T_Q4_0 ? "gemv_q4_0_head" : "gemv_q8_0_head", mid, {x, nw, tw, yb},
-                       [=](cudaStream_t st, const std::vector<TD> &td) {
+                pl.add_gemv(tw.type == T_Q4_0 ? "gemv_q4_0_head" : "gemv_q8_0_head", mid, {x, nw, tw, yb},
+                       [=](const std::vector<TD> &td) {
                            FusedArgs a;
                            a.pro = PRO_NORM;
                            a.map = MAP_SINGLE;
@@ -448,7 +448,7 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
                            fill_weight(a, 0, td[2]);
                            a.out = (float *)td[3].data;
                            a.ldo = N;
-                           k::fused_gemv(a, st, true);
+                           return a;
                        },
                        bytes);
                 pl.env[mid] = yb;
@@ -487,8 +487,8 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
             const int64_t ne[4] = {N, M, 1, 1};
             TD yb = pl.alloc(T_F32, ne);
             const double bytes = weight_bytes(tw) + 4.0 * K * M + 8.0 * N * M;
-            pl.add(tw.type == T_Q4_0 ? "gemv_q4_0_res" : "gemv_q8_0_res", aid, {x, res, tw, yb},
-                   [=](cudaStream_t st, const std::vector<TD> &td) {
+            pl.add_gemv(tw.type == T_Q4_0 ? "gemv_q4_0_res" : "gemv_q8_0_res", aid, {x, res, tw, yb},
+                   [=](const std::vector<TD> &td) {
                        FusedArgs a;
                        a.pro = PRO_ACT;
                        a.map = MAP_SINGLE;
@@ -501,7 +501,7 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
                        a.ldr = N;
                        a.out = (float *)td[3].data;
                        a.ldo = N;
-                       k::fused_gemv(a, st, true);
+                       return a;
                    },
                    bytes);
             pl.env[aid] = yb;

@@ -6,6 +6,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "gc_fused.h"
 #include "gc_model.h"
 
 namespace gcb {
@@ -22,6 +23,9 @@ struct PlanStep {
     std::vector<TD> tds;  // arena TDs are resolved to pointers before the launch closure is made
     std::function<void(cudaStream_t, const std::vector<TD> &)> fn;
     double bytes;
+    // The same work as a phase of the decode kernel (gc_mega.cu), from the resolved TDs; false when
+    // this binding's layout does not fit it. Empty for steps that only run as their own launch.
+    std::function<bool(const std::vector<TD> &, MegaPhase &)> mega;
 };
 
 struct Planner {
@@ -40,6 +44,9 @@ struct Planner {
     void use(const TD &t);                        // `t` is read at `cur`
     void add(const char *kind, const std::string &node, std::vector<TD> tds,
              std::function<void(cudaStream_t, const std::vector<TD> &)> fn, double bytes);
+    // A fused GEMV step (gc_fused.h) that can also run as a decode-kernel phase.
+    void add_gemv(const char *kind, const std::string &node, std::vector<TD> tds,
+                  std::function<FusedArgs(const std::vector<TD> &)> build, double bytes);
     TD src_of(const std::string &name);  // a node id, stage param or weight
     TD plan_node(const NodeSpec &n, const std::vector<TD> &src);
     void finish();

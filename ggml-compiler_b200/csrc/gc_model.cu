@@ -1,4 +1,5 @@
 #include "gc_model.h"
+#include "gc_fused.h"
 
 #include <algorithm>
 #include <chrono>
@@ -115,7 +116,9 @@ void Model::load(const char *path, int backend, int dev, bool allow_cpu_fallback
     cuda_check(cudaMalloc(&d_err, sizeof(int)), "cudaMalloc");
     cuda_check(cudaMemset(d_err, 0, sizeof(int)), "cudaMemset");
     if (const char *p = std::getenv("GGML_COMPILER_PROFILE")) profile_path = p;
+    if (const char *p = std::getenv("GGML_COMPILER_B200_TRACE")) trace_path = p;
     if (const char *g = std::getenv("GGML_COMPILER_B200_GRAPHS")) use_graphs = std::atoi(g) != 0;
+    if (const char *g = std::getenv("GGML_COMPILER_B200_DECODE_KERNEL")) use_decode_kernel = std::atoi(g) != 0;
 
     load_weights();
     for (const auto &sy : prog.symbols) binding.push_back(sy.max);
@@ -508,8 +511,11 @@ void Model::run_entry(const std::string &name) {
         cudaMemset(d_err, 0, sizeof(int));
         if (err == 2)
             throw std::runtime_error("entry '" + name + "': a kernel's pipeline wait timed out (results are invalid)");
+        if (err == 3)
+            throw std::runtime_error("entry '" + name + "': a wait in the decode kernel timed out (results are invalid)");
         throw std::runtime_error("entry '" + name + "': a set_rows index was outside its destination (row skipped)");
     }
+    if (!trace_path.empty()) write_trace();
     if (!profile_path.empty() && !profile_lines.empty()) {
         if (FILE *f = std::fopen(profile_path.c_str(), "a")) {
             for (const auto &l : profile_lines) std::fprintf(f, "%s\n", l.c_str());
@@ -566,6 +572,35 @@ const float *Model::rope_table(int n_dims, float base, float scale, float attn, 
     const float *p = (const float *)buf.get();
     rope_tables.emplace(key, std::move(buf));
     return p;
+}
+
+// One text line per traced phase and CTA: label, CTA, then the four stamps in ns relative to the
+// earliest phase start of the call site.
+void Model::write_trace() {
+    FILE *f = std::fopen(trace_path.c_str(), "w");
+    if (!f) return;
+    const int nctas = k::mega_ctas();
+    for (auto &c : calls) {
+        if (!c.trace.size() || c.trace_labels.empty()) continue;
+        std::vector<uint64_t> h(c.trace.size() / 8);
+        cuda_check(cudaMemcpy(h.data(), c.trace.get(), c.trace.size(), cudaMemcpyDeviceToHost), "trace");
+        uint64_t t0 = ~0ull;
+        for (size_t i = 0; i < h.size(); i += 4)
+            if (h[i]) t0 = std::min(t0, h[i]);
+        std::fprintf(f, "# stage %s ctas %d phases %zu\n", c.stage->name.c_str(), nctas, c.trace_labels.size());
+        for (const auto &r : c.trace_runs) {
+            const uint64_t *run = &h[(size_t)nctas * r.first * 4];  // [CTA][phase of the run][4]
+            for (size_t p = 0; p < r.second; p++)
+                for (int cta = 0; cta < nctas; cta++) {
+                    const uint64_t *st = run + ((size_t)cta * r.second + p) * 4;
+                    std::fprintf(f, "%s\t%d", c.trace_labels[r.first + p].c_str(), cta);
+                    for (int k = 0; k < 4; k++) std::fprintf(f, "\t%lld", st[k] ? (long long)(st[k] - t0) : -1ll);
+                    std::fprintf(f, "\n");
+                }
+        }
+        cuda_check(cudaMemset(c.trace.get(), 0, c.trace.size()), "trace");
+    }
+    std::fclose(f);
 }
 
 }  // namespace gcb

@@ -52,6 +52,10 @@ struct CallSite {
     int stage_index = 0;
     std::vector<Step> steps;
     DevBuf arena;
+    DevBuf phases;  // decode-kernel phase lists (MegaPhase arrays) of the planned steps
+    DevBuf trace;   // decode-kernel phase stamps [run][CTA][phase][4] (GGML_COMPILER_B200_TRACE)
+    std::vector<std::string> trace_labels;  // "<kind> <node>" per traced phase, all runs in order
+    std::vector<std::pair<size_t, size_t>> trace_runs;  // (first phase, phases) per run
     bool stale = true;
     cudaGraphExec_t graph = nullptr;
     bool graph_ok = false;
@@ -101,6 +105,7 @@ struct Model {
     int64_t rope_positions = 4096;
     std::map<std::string, DevBuf> rope_tables;
     bool use_graphs = true;
+    bool use_decode_kernel = false;  // GGML_COMPILER_B200_DECODE_KERNEL=1: one persistent launch per decode step
     bool profiling = false;
     std::map<std::string, KernelStat> kstats;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> event_pool;
@@ -111,6 +116,7 @@ struct Model {
     };
     std::vector<PendingTime> pending;
     std::string profile_path;  // GGML_COMPILER_PROFILE
+    std::string trace_path;    // GGML_COMPILER_B200_TRACE: decode-kernel phase stamps, rewritten per entry run
     std::vector<std::string> profile_lines;
 
     ~Model();
@@ -135,6 +141,7 @@ struct Model {
     void run_call(const DriverOp &d);
     std::pair<cudaEvent_t, cudaEvent_t> events();
     void collect_times();
+    void write_trace();
 };
 
 // Plans one stage call into kernel launches (gc_plan.cpp).

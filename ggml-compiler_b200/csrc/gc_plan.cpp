@@ -16,6 +16,7 @@
 #include <set>
 #include <sstream>
 #include <stdexcept>
+#include <unordered_map>
 
 #include "gc_fuse.h"
 #include "gc_fused.h"
@@ -63,6 +64,38 @@ const std::map<std::string, int> &unary_ops() {
     return m;
 }
 
+// One query row of split-KV attention as a decode-kernel phase (MegaAttn): the query's heads
+// contiguous, K/V rows contiguous with 16-byte aligned heads, one mask row broadcast over heads.
+bool attn_phase(const std::vector<TD> &t, float scale, int *counters, MegaPhase &ph) {
+    const TD &q = t[0], &kk = t[1], &v = t[2], &mk = t[3], &y = t[4];
+    const int64_t D = q.ne[0];
+    if (q.ne[1] != 1 || q.ne[3] != 1 || q.nb[0] != 4 || q.nb[2] != 4 * D || !y.contiguous()) return false;
+    if (kk.nb[1] != 2 * D || v.nb[1] != 2 * D || kk.ne[3] != 1 || mk.ne[2] != 1 || mk.ne[3] != 1) return false;
+    if (((uintptr_t)kk.data | (uintptr_t)v.data | (uintptr_t)kk.nb[2] | (uintptr_t)v.nb[2]) % 16) return false;
+    ph.type = 1;
+    MegaAttn &a = ph.at;
+    a.q = (const float *)q.data;
+    a.D = D;
+    a.H = q.ne[2];
+    a.Hkv = kk.ne[2];
+    a.M = 1;
+    a.ldq = D * q.ne[2];
+    a.k = kk.data;
+    a.v = v.data;
+    a.knb1 = kk.nb[1];
+    a.knb2 = kk.nb[2];
+    a.vnb1 = v.nb[1];
+    a.vnb2 = v.nb[2];
+    a.nkv = kk.ne[1];
+    a.mask = (const __half *)mk.data;
+    a.mask_ld = mk.nb[1] / 2;
+    a.scale = scale;
+    a.part = (float *)t[5].data;
+    a.out = (float *)y.data;
+    a.counters = counters;
+    return true;
+}
+
 }  // namespace
 
 Planner::Planner(Model &m, CallSite &cs, const DriverOp &d) : m(m), cs(cs), d(d), s(*cs.stage) {}
@@ -94,6 +127,16 @@ void Planner::add(const char *kind, const std::string &node, std::vector<TD> tds
                   std::function<void(cudaStream_t, const std::vector<TD> &)> fn, double bytes) {
     for (const auto &t : tds) use(t);
     psteps.push_back(PlanStep{kind, node, std::move(tds), std::move(fn), bytes});
+}
+
+void Planner::add_gemv(const char *kind, const std::string &node, std::vector<TD> tds,
+                       std::function<FusedArgs(const std::vector<TD> &)> build, double bytes) {
+    add(kind, node, std::move(tds), [build](cudaStream_t st, const std::vector<TD> &t) { k::fused_gemv(build(t), st, true); }, bytes);
+    psteps.back().mega = [build](const std::vector<TD> &t, MegaPhase &ph) {
+        ph.type = 0;
+        ph.g = build(t);
+        return ph.g.M == 1 && k::fused_gemv_args_ok(ph.g);
+    };
 }
 
 TD Planner::src_of(const std::string &name) {
@@ -272,23 +315,23 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
         if (is_quant(a.type) && a.ne[2] == 1 && a.ne[3] == 1 && b.ne[2] == 1 && b.ne[3] == 1 && b.nb[0] == 4 &&
             (b.ne[1] == 1 || b.nb[1] == 4 * b.ne[0]) && k::fused_gemv_supported(a.ne[0], b.ne[1], MAP_SINGLE)) {
             const int64_t K = a.ne[0], N = a.ne[1], M = b.ne[1];
-            add(a.type == T_Q4_0 ? "gemv_q4_0" : "gemv_q8_0", n.id, {a, b, y},
-                [K, N, M](cudaStream_t st, const std::vector<TD> &t) {
-                    FusedArgs fa;
-                    fa.qtype = t[0].type;
-                    fa.pro = PRO_ACT;
-                    fa.map = MAP_SINGLE;
-                    fa.x = (const float *)t[1].data;
-                    fa.ldx = K;
-                    fa.M = (int)M;
-                    fa.K = K;
-                    fa.wc[0] = t[0].data;
-                    fa.wrows[0] = N;
-                    fa.out = (float *)t[2].data;
-                    fa.ldo = N;
-                    k::fused_gemv(fa, st, true);
-                },
-                bytes);
+            add_gemv(a.type == T_Q4_0 ? "gemv_q4_0" : "gemv_q8_0", n.id, {a, b, y},
+                     [K, N, M](const std::vector<TD> &t) {
+                         FusedArgs fa;
+                         fa.qtype = t[0].type;
+                         fa.pro = PRO_ACT;
+                         fa.map = MAP_SINGLE;
+                         fa.x = (const float *)t[1].data;
+                         fa.ldx = K;
+                         fa.M = (int)M;
+                         fa.K = K;
+                         fa.wc[0] = t[0].data;
+                         fa.wrows[0] = N;
+                         fa.out = (float *)t[2].data;
+                         fa.ldo = N;
+                         return fa;
+                     },
+                     bytes);
             return y;
         }
         const size_t sb = k::mul_mat_scratch_bytes(a, b);
@@ -329,6 +372,7 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
                         k::flash_attn_split(t[0], t[1], t[2], &t[3], t[4], scale, t[5].data, cnt, err, st);
                     },
                     bytes);
+                psteps.back().mega = [scale, cnt](const std::vector<TD> &t, MegaPhase &ph) { return attn_phase(t, scale, cnt, ph); };
                 return y;
             }
             add("flash_attn", n.id, {q, kk, v, mk, y},
@@ -537,14 +581,98 @@ void Planner::finish() {
         cs.arena.alloc(top);
     }
     char *base = cs.arena.get();
-    cs.steps.clear();
-    for (auto &ps : psteps) {
+    for (auto &ps : psteps)
         for (auto &t : ps.tds)
             if (t.sid >= 0) {
                 t.data = base + storages[(size_t)t.sid].offset + t.off;
                 t.sid = -1;
                 t.off = 0;
             }
+
+    // Runs of two or more consecutive steps that the decode kernel can take (one token row, one
+    // weight type, one head size) become one launch of it; the other steps keep their own launch.
+    struct Run {
+        size_t begin = 0, end = 0, phase0 = 0;
+        int qtype = -1;
+        int64_t kmax = 0;
+        int attn_d = 0;
+        double bytes = 0;
+    };
+    std::vector<MegaPhase> phases;
+    std::vector<Run> runs;
+    for (size_t i = 0; m.use_decode_kernel && i < psteps.size();) {
+        Run r;
+        r.begin = i;
+        r.phase0 = phases.size();
+        bool gemv = false;
+        size_t j = i;
+        for (; j < psteps.size() && psteps[j].mega; j++) {
+            MegaPhase ph;
+            if (!psteps[j].mega(psteps[j].tds, ph)) break;
+            int qt = r.qtype, d = r.attn_d;
+            int64_t km = r.kmax;
+            if (ph.type == 0) {
+                if (qt >= 0 && ph.g.qtype != qt) break;
+                qt = ph.g.qtype;
+                km = std::max<int64_t>(km, ph.g.K);
+            } else {
+                if (d && ph.at.D != d) break;
+                d = (int)ph.at.D;
+            }
+            if (!k::mega_supported(qt < 0 ? T_Q4_0 : qt, 1, km, d)) break;
+            r.qtype = qt, r.attn_d = d, r.kmax = km;
+            r.bytes += psteps[j].bytes;
+            gemv = gemv || ph.type == 0;
+            phases.push_back(ph);
+        }
+        if (j - i >= 2 && gemv) {
+            r.end = j;
+            runs.push_back(r);
+            i = j;
+        } else {
+            phases.resize(r.phase0);
+            i = std::max(j, i + 1);
+        }
+    }
+    const size_t pbytes = phases.size() * sizeof(MegaPhase);
+    if (pbytes) {
+        cuda_check(cudaStreamSynchronize(m.stream), "decode kernel phases");  // an earlier plan's launches may read them
+        if (cs.phases.size() < pbytes) cs.phases.alloc(pbytes);
+        cuda_check(cudaMemcpy(cs.phases.get(), phases.data(), pbytes, cudaMemcpyHostToDevice), "decode kernel phases");
+    }
+    int *gbar = runs.empty() ? nullptr : m.counters(s.name + "/decode_kernel", 1);
+    int *err = m.d_err;
+    cs.trace_labels.clear();
+    cs.trace_runs.clear();
+    if (!m.trace_path.empty() && !phases.empty()) {
+        const size_t tb = (size_t)k::mega_ctas() * phases.size() * 4 * sizeof(uint64_t);
+        if (cs.trace.size() < tb) cs.trace.alloc(tb);
+        for (const Run &r : runs) {
+            cs.trace_runs.emplace_back(r.phase0, r.end - r.begin);
+            for (size_t j = r.begin; j < r.end; j++) cs.trace_labels.push_back(std::string(psteps[j].kind) + " " + psteps[j].node);
+        }
+    }
+    uint64_t *trace = cs.trace_labels.empty() ? nullptr : (uint64_t *)cs.trace.get();
+    cs.steps.clear();
+    size_t ri = 0;
+    for (size_t i = 0; i < psteps.size();) {
+        if (ri < runs.size() && runs[ri].begin == i) {
+            const Run r = runs[ri++];
+            const MegaPhase *dev = (const MegaPhase *)cs.phases.get() + r.phase0;
+            const int nph = (int)(r.end - r.begin);
+            Step st;
+            st.kind = r.qtype == T_Q4_0 ? "decode_q4_0" : "decode_q8_0";
+            st.node = psteps[r.begin].node + ".." + psteps[r.end - 1].node;
+            st.bytes = r.bytes;
+            uint64_t *tr = trace ? trace + (size_t)k::mega_ctas() * r.phase0 * 4 : nullptr;
+            st.run = [dev, nph, r, gbar, err, tr](cudaStream_t stream) {
+                k::mega_step(dev, nph, r.qtype, 1, r.kmax, r.attn_d, gbar, err, tr, stream);
+            };
+            cs.steps.push_back(std::move(st));
+            i = r.end;
+            continue;
+        }
+        PlanStep &ps = psteps[i++];
         Step st;
         st.kind = ps.kind;
         st.node = ps.node;
@@ -573,9 +701,55 @@ void plan_call_site(Model &m, CallSite &cs, const DriverOp &d) {
     }
     std::vector<TD> sv;
     FusionPlan fp = find_fusions(m, s, p);
+
+    // Nodes that read only weights and stage parameters that no node writes (the mask conversion
+    // that every layer of a decode stage repeats) are planned first, and identical ones once, so
+    // the launches that remain, the fused groups, are adjacent. `cur` counts plan positions.
+    std::set<std::string> params, written;
+    for (const auto &ps : s.params) params.insert(ps.name);
+    for (const auto &n : s.nodes)
+        if (n.op == "set_rows" && !n.src.empty()) written.insert(n.src[0]);
+    std::unordered_map<std::string, size_t> index_of;
+    std::unordered_map<std::string, std::string> same_as;  // node id -> an earlier identical node
+    std::map<std::string, std::string> seen;
+    std::vector<char> hoisted(s.nodes.size(), 0);
     for (size_t i = 0; i < s.nodes.size(); i++) {
         const NodeSpec &n = s.nodes[i];
-        p.cur = (int)i;
+        index_of[n.id] = i;
+        if (fp.covered(i) || n.op == "set_rows") continue;
+        bool ok = true;
+        std::string key = n.op + "|" + std::to_string((int)n.type);
+        for (int k = 0; k < 4; k++) key += "," + std::to_string(n.ne[(size_t)k]);
+        for (const auto &name : n.src) {
+            auto it = index_of.find(name);
+            if (params.count(name)) ok = ok && !written.count(name);
+            else if (it != index_of.end()) ok = ok && hoisted[it->second];
+            auto al = same_as.find(name);
+            key += "|" + (al == same_as.end() ? name : al->second);
+        }
+        if (!ok) continue;
+        hoisted[i] = 1;
+        key += "|" + n.p.dump();
+        for (const auto &pb : n.p_bound) key += "|" + pb.first + "=" + std::to_string(pb.second);
+        auto it = seen.find(key);
+        if (it != seen.end()) same_as[n.id] = it->second;
+        else seen.emplace(key, n.id);
+    }
+    std::vector<size_t> order;
+    for (size_t i = 0; i < s.nodes.size(); i++)
+        if (hoisted[i]) order.push_back(i);
+    for (size_t i = 0; i < s.nodes.size(); i++)
+        if (!hoisted[i]) order.push_back(i);
+
+    for (size_t pos = 0; pos < order.size(); pos++) {
+        const size_t i = order[pos];
+        const NodeSpec &n = s.nodes[i];
+        p.cur = (int)pos;
+        auto al = same_as.find(n.id);
+        if (al != same_as.end()) {
+            p.env[n.id] = p.env.at(al->second);
+            continue;
+        }
         if (fp.covered(i)) {
             fp.emit_if_anchor(i, p);
             continue;

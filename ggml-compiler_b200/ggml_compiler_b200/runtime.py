@@ -94,6 +94,13 @@ def _sigs() -> dict[str, tuple[list[Any], Any]]:
         "ggml_compiler_n_stages": ([p], i),
         "ggml_compiler_stage_stats": ([p, i, ctypes.POINTER(c_str), ctypes.POINTER(ctypes.c_double),
                                        ctypes.POINTER(ctypes.c_int)], i),
+        # extensions of this backend (include/ggml_compiler_b200.h)
+        "ggml_compiler_b200_stream": ([p], p),
+        "ggml_compiler_b200_last_device_ms": ([p], ctypes.c_double),
+        "ggml_compiler_b200_set_profiling": ([p, i], i),
+        "ggml_compiler_b200_n_kernel_stats": ([p], i),
+        "ggml_compiler_b200_kernel_stats": ([p, i, ctypes.POINTER(c_str), ctypes.POINTER(ctypes.c_double),
+                                             ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_double)], i),
     }
 
 
@@ -291,6 +298,34 @@ class Session:
             lib.ggml_compiler_stage_stats(self._m, k, ctypes.byref(name), ctypes.byref(ms), ctypes.byref(calls))
             stages[name.value.decode()] = {"ms": ms.value, "calls": calls.value}
         return {"ms_total": st.ms_total, "n_calls": st.n_calls, "stages": stages}
+
+    # ---- extensions of this backend (no counterpart in the reference's Session)
+
+    @property
+    def stream(self) -> int:
+        """The CUDA stream (cudaStream_t as an int) every launch of this session goes to."""
+        return int(_load().ggml_compiler_b200_stream(self._m) or 0)
+
+    @property
+    def last_device_ms(self) -> float:
+        """Device time of the last run or run_entry, CUDA events around all its launches."""
+        return float(_load().ggml_compiler_b200_last_device_ms(self._m))
+
+    def set_profiling(self, on: bool) -> None:
+        """Per-launch timing (each launch synchronised, no CUDA graphs) while on; clears the stats."""
+        if _load().ggml_compiler_b200_set_profiling(self._m, int(bool(on))) != 0:
+            raise _error()
+
+    def kernel_stats(self) -> dict[str, dict[str, float]]:
+        """Per kernel family, since profiling was switched on: total ms, launches and algorithmic bytes."""
+        lib = _load()
+        out = {}
+        for k in range(lib.ggml_compiler_b200_n_kernel_stats(self._m)):
+            name, ms, n, b = ctypes.c_char_p(), ctypes.c_double(), ctypes.c_int(), ctypes.c_double()
+            lib.ggml_compiler_b200_kernel_stats(self._m, k, ctypes.byref(name), ctypes.byref(ms), ctypes.byref(n),
+                                                ctypes.byref(b))
+            out[name.value.decode()] = {"ms": ms.value, "launches": n.value, "bytes": b.value}
+        return out
 
     def close(self) -> None:
         if getattr(self, "_m", None):

@@ -26,9 +26,22 @@ def golden():
     return np.load(GOLDEN / "ref_llama_q8_0.npz")
 
 
-@pytest.fixture(scope="module")
-def sess(gpu):
-    s = Session(GGUF, backend="cuda")
+@pytest.fixture(scope="module", params=["decode_kernel", "per_group"])
+def sess(gpu, request):
+    """Every test runs twice: decode steps as one persistent kernel (GGML_COMPILER_B200_DECODE_KERNEL=1,
+    read when a session loads), and with one launch per fused group (=0)."""
+    import os
+
+    old = os.environ.get("GGML_COMPILER_B200_DECODE_KERNEL")
+    os.environ["GGML_COMPILER_B200_DECODE_KERNEL"] = "1" if request.param == "decode_kernel" else "0"
+    try:
+        s = Session(GGUF, backend="cuda")
+    finally:
+        if old is None:
+            del os.environ["GGML_COMPILER_B200_DECODE_KERNEL"]
+        else:
+            os.environ["GGML_COMPILER_B200_DECODE_KERNEL"] = old
+    s.mode = request.param
     yield s
     s.close()
 
@@ -53,6 +66,28 @@ def test_logits_bit_exact_vs_oracle(sess, golden):
     for c in chunks:
         a, b = g.feed(c), o.feed(c)
         np.testing.assert_array_equal(a, b)
+
+
+def test_decode_launches(sess):
+    """A decode step is the hoisted mask conversion, the embedding row, one decode-kernel launch
+    over every layer and the output head, then argmax: or one launch per fused group."""
+    g = Generator(sess)
+    g.reset()
+    g.feed([1, 2, 3])
+    sess.set_profiling(True)
+    try:
+        g.feed([4])
+        ks = sess.kernel_stats()
+    finally:
+        sess.set_profiling(False)
+    if sess.mode == "decode_kernel":
+        assert ks["decode_q8_0"]["launches"] == 1
+        assert not any(k.startswith("gemv") or k == "flash_attn" for k in ks), ks
+    else:
+        assert "decode_q8_0" not in ks
+        assert ks["gemv_q8_0_qkv"]["launches"] == ks["flash_attn"]["launches"] == ks["gemv_q8_0_glu"]["launches"]
+    # the per-layer mask conversion is planned once
+    assert ks.get("unary", {"launches": 0})["launches"] <= 1 and ks.get("copy", {"launches": 0})["launches"] <= 2
 
 
 def test_logits_vs_transformers(sess, golden):
