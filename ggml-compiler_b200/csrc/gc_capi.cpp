@@ -26,6 +26,8 @@ struct ggml_compiler_stage_build {
     int unused;
 };
 
+void gcb_set_last_error(const std::string &msg);
+
 namespace {
 
 thread_local std::string g_error;
@@ -129,6 +131,9 @@ bool has_b200() {
 }
 
 }  // namespace
+
+// The per-thread error message, for C entry points defined in other files (kernels/gc_flash_static.cu).
+void gcb_set_last_error(const std::string &msg) { set_error(msg); }
 
 extern "C" {
 

@@ -29,6 +29,32 @@ GGML_COMPILER_API int ggml_compiler_b200_n_kernel_stats(const ggml_compiler_mode
 GGML_COMPILER_API int ggml_compiler_b200_kernel_stats(const ggml_compiler_model * m, int i, const char ** kind,
                                                       double * ms, int * launches, double * bytes);
 
+/* Split-KV flash attention on caller-owned device buffers that allocates no device memory: the
+   kernel the flash_attn node runs (reference: runtime/src/ops.cpp:217-240 -> ggml_flash_attn_ext,
+   runtime/include/ggml_compiler_ops.h:133-135), with its scratch in a static device array of the
+   library. No counterpart in the reference, which has no entry point for a single op.
+   For callers without a loaded program that must not allocate: a custom op inside another engine's
+   decode loop, whose caching allocator owns the free device memory and which cudaMalloc / cudaFree
+   would stall by synchronising the device.
+     q     f32 [n_head][n_q][head_dim]                  (ggml ne {head_dim, n_q, n_head, 1})
+     k, v  f16, row j of K/V head h at element (h * kv_head_stride + j) * head_dim; 16-byte aligned
+     mask  f16 [n_q][n_kv], added to the scaled scores, the same for every head; NULL for none
+     out   f32 [n_q][n_head][head_dim]                  (ggml ne {head_dim, n_head, n_q, 1})
+   head_dim a multiple of 32 up to 256, n_head a multiple of n_head_kv, kv_head_stride >= n_kv.
+   Limit: the chunk partials of one launch (n_q x n_head x ceil(n_kv / 64) x (head_dim + 2) floats,
+   with n_q capped where 64 MiB would be exceeded) must fit 4 MiB, and n_q x n_head_kv must be at most
+   4096; larger calls are rejected (-1, ggml_compiler_last_error()).
+   Asynchronous on `stream` (a cudaStream_t; NULL: the legacy default stream) of the current device.
+   The arrival counters in the scratch must be zero when the kernel starts: each call zeroes them on
+   `stream` first. The first call on a device does the set-up (looks up the scratch's device address);
+   make it before any stream capture on that device. One scratch per device: calls whose executions
+   overlap race on it and return garbage; order them on one stream or with events. */
+GGML_COMPILER_API int ggml_compiler_b200_flash_attn_static(const float * q, const void * k, const void * v,
+                                                           const void * mask, float * out, int64_t head_dim,
+                                                           int64_t n_q, int64_t n_head, int64_t n_kv,
+                                                           int64_t n_head_kv, int64_t kv_head_stride, float scale,
+                                                           void * stream);
+
 #ifdef __cplusplus
 }
 #endif
