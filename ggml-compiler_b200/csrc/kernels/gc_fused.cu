@@ -21,9 +21,10 @@ namespace {
 constexpr int NCW = 8;  // consumer warps
 constexpr int NTHREADS = (NCW + 1) * 32;
 constexpr int MAXNS = 16;
+constexpr int CG = 2;  // row groups per chunk with one activation row (gc_gemv_dev.cuh)
 
 template <int QT, int NR, int M>
-__global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, GemvGeo G, int ns, int64_t slot_bytes) {
+__global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, GemvGeo G, int log2ns, int slot_bytes) {
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t *full = (uint64_t *)smem;
     uint64_t *empty = full + MAXNS;
@@ -32,11 +33,11 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
     float *sdf = (float *)(sq + (size_t)M * a.K);
     int *ss8 = (int *)(sdf + (size_t)M * G.nb);
     unsigned char *slots = (unsigned char *)(red + 256) + gemv_act_bytes(M, a.K);
-    const Ring R{full, empty, slots, ns, slot_bytes};
+    const Ring R{full, empty, slots, log2ns, slot_bytes};
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < ns; s++) {
+        for (int s = 0; s < (1 << log2ns); s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], NCW);
         }
@@ -47,17 +48,16 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
 
     if (warp == NCW) {  // producer
         if (lane != 0) return;
-        int64_t t = 0;
-        if (!produce_gemv(a, G, R, t, blockIdx.x, gridDim.x)) {
+        uint32_t t = 0;
+        if (!produce_gemv(a, G, R, t, blockIdx.x, gridDim.x, gemv_chunk(M, 1, CG))) {
             if (a.err) atomicExch(a.err, 2);
-            for (int64_t u = t - ns; u < t; u++)
-                if (u >= 0) mbar_wait(&full[u % ns], (uint32_t)((u / ns) & 1), 100000000ull);
+            drain_ring(R, t);
         }
         return;
     }
     pdl_wait();
     gemv_prologue<M, NCW * 32>(a, sq, sdf, ss8, red, 1);
-    if (!consume_gemv<QT, NR, M>(a, G, R, 0, blockIdx.x, gridDim.x, 0, 1, warp, sq, sdf, ss8))
+    if (!consume_gemv<QT, NR, M, CG>(a, G, R, 0, blockIdx.x, gridDim.x, 0, 1, warp, sq, sdf, ss8))
         if (a.err) atomicExch(a.err, 2);
 }
 
@@ -72,15 +72,15 @@ void launch_t(const FusedArgs &a, const GemvGeo &G, cudaStream_t s, bool pdl) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         attr = true;
     }
-    const int64_t slot_bytes = qw_piece_bytes(G.nb, G.cb, 0);
+    const int slot_bytes = (int)qw_piece_bytes(G.nb, G.cb, 0);
     const size_t head = (size_t)(2 * MAXNS) * 8 + 256 * 8 + gemv_act_bytes(M, a.K);
     const size_t budget = g_smem_budget ? g_smem_budget : 110 * 1024;
-    int ns = (int)((budget > head ? budget - head : 0) / (size_t)slot_bytes);
-    ns = ns < 2 * G.pieces ? 2 * G.pieces : (ns > MAXNS ? MAXNS : ns);
-    const size_t smem = head + (size_t)ns * (size_t)slot_bytes;
+    int log2ns = ring_log2(budget, head, (size_t)slot_bytes, MAXNS);
+    while ((1 << log2ns) < 2 * G.pieces) log2ns++;  // room for one group's pieces in flight and one consumed
+    const size_t smem = head + ((size_t)1 << log2ns) * (size_t)slot_bytes;
     const int per_sm = smem <= 113 * 1024 ? 2 : 1;
     const int64_t cap = (int64_t)g_num_sms * per_sm;
-    const int64_t ctas = G.groups < cap ? G.groups : cap;
+    const int64_t ctas = G.groups < cap ? (int64_t)G.groups : cap;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(ctas < 1 ? 1 : ctas));
     cfg.blockDim = dim3(NTHREADS);
@@ -91,7 +91,7 @@ void launch_t(const FusedArgs &a, const GemvGeo &G, cudaStream_t s, bool pdl) {
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, G, ns, slot_bytes);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, G, log2ns, slot_bytes);
     if (e != cudaSuccess) throw std::runtime_error(std::string("CUDA launch of gemv_tma failed: ") + cudaGetErrorString(e));
 }
 

@@ -2,16 +2,20 @@
 // and the per-token decode kernel (gc_mega.cu).
 //
 // Weights stream as pieces (one 8-row tile x one 128-block segment each, gc_qweight.cuh) through a
-// ring of NS shared-memory slots: the producer lane puts piece t in slot t % NS after the slot's
-// previous piece was released (empty barrier) and arms full[t % NS] with the byte count; the team of
-// 8 consumer warps owning that piece waits on full, computes and releases. A CTA's pieces are
-// numbered in the order (phase, local group, segment, piece of the group), which producer and
-// consumers both derive from the same geometry.
+// ring of NS (a power of two) shared-memory slots: the producer lane puts piece t in slot t % NS
+// after the slot's previous piece was released (empty barrier) and arms full[t % NS] with the byte
+// count; the team of 8 consumer warps owning that piece waits on full, computes and releases. A
+// CTA's local row groups are taken in chunks (gemv_chunk); its pieces are numbered in the order
+// (phase, chunk, segment, local group of the chunk, piece of the group), which producer and
+// consumers both derive from the same geometry. Counters and geometry are 32-bit: no 64-bit
+// division on the streaming path.
 //
 // Arithmetic is the CPU checker's: the activation row -> Q8_0 blocks (d = amax/127 in fp16,
 // codes = nearest-even(x * 127/amax)), lane l owns blocks l, l+32, ... of a row (segments are
 // multiples of 32 blocks, walked in order), acc = fma(d_w * d_x, isum, acc) with the exact integer
-// dot, then the 32-lane butterfly.
+// dot, then the 32-lane butterfly. Only the fma chain and the butterfly are ordered; the block
+// products they consume may be computed in any order, which is what lets a lane load a piece's
+// blocks ahead of the arithmetic.
 #pragma once
 
 #include "../gc_fused.h"
@@ -26,59 +30,63 @@ constexpr int GEMV_MAXM = 8;
 
 // Geometry of one GEMV over the tiled weights.
 struct GemvGeo {
-    int64_t nb, nseg, groups;  // blocks per row, segments per row, row groups (tiles / tile pairs)
-    int cb, pieces;            // code bytes per block, pieces per (group, segment)
-    int64_t half_tiles;        // ROPE_QKV: tiles per half head
+    int nb, nseg, groups;  // blocks per row, segments per row, row groups (tiles / tile pairs)
+    int cb, pieces;        // code bytes per block, pieces per (group, segment)
+    int half_tiles;        // ROPE_QKV: tiles per half head
 };
 
 __host__ __device__ inline GemvGeo gemv_geo(const FusedArgs &a) {
     GemvGeo G{};
-    G.nb = a.K / 32;
-    G.nseg = qw_nseg(G.nb);
+    G.nb = (int)(a.K / 32);
+    G.nseg = (int)qw_nseg(G.nb);
     G.cb = a.qtype == T_Q4_0 ? 16 : 32;
     if (a.map == MAP_SINGLE) {
-        G.groups = (a.wrows[0] + QTR - 1) / QTR;
+        G.groups = (int)((a.wrows[0] + QTR - 1) / QTR);
         G.pieces = 1;
     } else if (a.map == MAP_SWIGLU) {
-        G.groups = (a.wrows[0] + QTR - 1) / QTR;
+        G.groups = (int)((a.wrows[0] + QTR - 1) / QTR);
         G.pieces = 2;
     } else {
-        G.half_tiles = (a.D / 2) / QTR;
-        G.groups = (a.H + 2 * a.Hkv) * G.half_tiles;
+        G.half_tiles = (int)((a.D / 2) / QTR);
+        G.groups = (int)((a.H + 2 * a.Hkv) * G.half_tiles);
         G.pieces = 2;
     }
     return G;
 }
 
 // Groups of a GEMV handled by CTA `cta` of `nctas` (groups cta, cta + nctas, ...).
-__host__ __device__ inline int64_t local_groups(int64_t groups, int64_t cta, int64_t nctas) {
+__host__ __device__ inline int local_groups(int groups, int cta, int nctas) {
     return cta < groups ? (groups - cta + nctas - 1) / nctas : 0;
 }
 
+// Local row groups per chunk: segment-major walks (so a lane's activation registers serve the
+// chunk's `cg` groups per team) need one activation row; with more rows each group is its own chunk.
+__host__ __device__ inline int gemv_chunk(int M, int teams, int cg) { return M == 1 ? cg * teams : 1; }
+
 // Source of piece r (0/1) of group g, segment s; the matrix and the tile of piece r.
-__device__ __forceinline__ const char *gemv_piece(const FusedArgs &a, const GemvGeo &G, int64_t g, int r, int64_t s,
-                                                  int *mat, int64_t *tile) {
-    int m = 0;
-    int64_t t;
+__device__ __forceinline__ const char *gemv_piece(const FusedArgs &a, const GemvGeo &G, int g, int r, int s, int *mat,
+                                                  int *tile) {
+    int m = 0, t;
     if (a.map == MAP_SINGLE) {
         t = g;
     } else if (a.map == MAP_SWIGLU) {
         m = r;
         t = g;
     } else {
-        const int64_t head = g / G.half_tiles, p = g % G.half_tiles;
-        int64_t h;
-        if (head < a.H) {
+        const int H = (int)a.H, Hkv = (int)a.Hkv;
+        const int head = g / G.half_tiles, p = g - head * G.half_tiles;
+        int h;
+        if (head < H) {
             m = 0;
             h = head;
-        } else if (head < a.H + a.Hkv) {
+        } else if (head < H + Hkv) {
             m = 1;
-            h = head - a.H;
+            h = head - H;
         } else {
             m = 2;
-            h = head - a.H - a.Hkv;
+            h = head - H - Hkv;
         }
-        t = h * (a.D / QTR) + p + r * G.half_tiles;
+        t = h * (2 * G.half_tiles) + p + r * G.half_tiles;
     }
     *mat = m;
     *tile = t;
@@ -88,47 +96,73 @@ __device__ __forceinline__ const char *gemv_piece(const FusedArgs &a, const Gemv
 struct Ring {
     uint64_t *full, *empty;
     unsigned char *slots;
-    int ns;
-    int64_t slot_bytes;
+    int log2ns;  // slots = 1 << log2ns
+    int slot_bytes;
+    __device__ __forceinline__ int slot(uint32_t t) const { return (int)(t & ((1u << log2ns) - 1)); }
+    __device__ __forceinline__ uint32_t parity(uint32_t t) const { return (t >> log2ns) & 1u; }
+    __device__ __forceinline__ unsigned char *data(uint32_t t) const { return slots + (size_t)slot(t) * slot_bytes; }
 };
 
 // Producer: put this CTA's pieces of one GEMV into the ring, continuing the piece count `t`.
 // Returns false if a slot was never released (bounded wait).
-__device__ inline bool produce_gemv(const FusedArgs &a, const GemvGeo &G, const Ring &R, int64_t &t, int64_t cta,
-                                    int64_t nctas) {
-    for (int64_t g = cta; g < G.groups; g += nctas) {
-        for (int64_t s = 0; s < G.nseg; s++) {
+__device__ inline bool produce_gemv(const FusedArgs &a, const GemvGeo &G, const Ring &R, uint32_t &t, int cta, int nctas,
+                                    int chunk) {
+    const int L = local_groups(G.groups, cta, nctas);
+    for (int c0 = 0; c0 < L; c0 += chunk) {
+        const int c1 = c0 + chunk < L ? c0 + chunk : L;
+        for (int s = 0; s < G.nseg; s++) {
             const uint32_t pb = (uint32_t)qw_piece_bytes(G.nb, G.cb, s);
-            for (int r = 0; r < G.pieces; r++, t++) {
-                const int slot = (int)(t % R.ns);
-                if (t >= R.ns && !mbar_wait(&R.empty[slot], (uint32_t)(((t / R.ns) - 1) & 1))) return false;
-                mbar_expect_tx(&R.full[slot], pb);
-                int mat;
-                int64_t tile;
-                bulk_g2s(R.slots + slot * R.slot_bytes, gemv_piece(a, G, g, r, s, &mat, &tile), pb, &R.full[slot]);
-            }
+            for (int gl = c0; gl < c1; gl++)
+                for (int r = 0; r < G.pieces; r++, t++) {
+                    const int slot = R.slot(t);
+                    if ((t >> R.log2ns) && !mbar_wait(&R.empty[slot], R.parity(t) ^ 1u)) return false;
+                    mbar_expect_tx(&R.full[slot], pb);
+                    int mat, tile;
+                    bulk_g2s(R.data(t), gemv_piece(a, G, cta + gl * nctas, r, s, &mat, &tile), pb, &R.full[slot]);
+                }
         }
     }
     return true;
 }
 
+// Drain after a failed wait: the copies still in flight into the ring land before the CTA exits.
+__device__ inline void drain_ring(const Ring &R, uint32_t t) {
+    const uint32_t ns = 1u << R.log2ns;
+    for (uint32_t u = t > ns ? t - ns : 0; u < t; u++) mbar_wait(&R.full[R.slot(u)], R.parity(u), 100000000ull);
+}
+
 // Activation row(s) -> Q8_0 blocks in shared memory (sq codes, sdf scales as f32, ss8 8 x code sums),
 // with rms_norm * w first for PRO_NORM. Run by the NCT consumer threads (thread ids 0 .. NCT-1);
 // `bar` is their named barrier. The sum of squares uses the 256-partial double tree (threads 0..255).
+// Loads are issued in batches ahead of the arithmetic that consumes them.
 template <int M, int NCT>
 __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf, int *ss8, double *red, int bar) {
-    const int64_t K = a.K, nb = K / 32;
+    const int K = (int)a.K, nb = K / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     constexpr int NW = NCT / 32;
+    constexpr int U = 16;  // loads in flight per thread in the sum of squares
+    constexpr int UB = 4;  // 4-block groups in flight per warp in the quantization pass
 #pragma unroll
     for (int m = 0; m < M; m++) {
         const float *x = a.x + m * a.ldx;
         float scale = 1.0f;
         if (a.pro == PRO_NORM) {
-            double p = 0.0;
-            if (tid < 256)
-                for (int64_t i = tid; i < K; i += 256) p = __dadd_rn(p, (double)__fmul_rn(x[i], x[i]));
-            if (tid < 256) red[tid] = p;
+            if (tid < 256) {
+                double p = 0.0;
+                for (int i0 = tid; i0 < K; i0 += 256 * U) {
+                    float v[U];
+#pragma unroll
+                    for (int u = 0; u < U; u++) v[u] = i0 + 256 * u < K ? x[i0 + 256 * u] : 0.0f;
+#pragma unroll
+                    for (int u = 0; u < U; u++)
+                        if (i0 + 256 * u < K) p = __dadd_rn(p, (double)__fmul_rn(v[u], v[u]));
+                }
+                red[tid] = p;
+            } else if constexpr (NCT > 256) {
+                // threads the sum does not use pull the norm weights toward L1 for the pass below
+                for (int i = (tid - 256) * 32; i < K; i += (NCT - 256) * 32)
+                    asm volatile("prefetch.global.L1 [%0];" ::"l"(a.norm_w + i));
+            }
             named_bar(bar, NCT);
 #pragma unroll
             for (int off = 128; off >= 1; off >>= 1) {
@@ -141,32 +175,41 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
             scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
         }
         const int sub = lane >> 3, e = (lane & 7) * 4;
-        for (int64_t b0 = (int64_t)warp * 4; b0 < nb; b0 += NW * 4) {
-            const int64_t b = b0 + sub;
-            const bool ok = b < nb;
-            float4 v = ok ? *(const float4 *)(x + b * 32 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
-            if (a.pro == PRO_NORM && ok) {
-                const float4 w = *(const float4 *)(a.norm_w + b * 32 + e);
-                v.x = __fmul_rn(__fmul_rn(v.x, scale), w.x);
-                v.y = __fmul_rn(__fmul_rn(v.y, scale), w.y);
-                v.z = __fmul_rn(__fmul_rn(v.z, scale), w.z);
-                v.w = __fmul_rn(__fmul_rn(v.w, scale), w.w);
+        const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int b0 = warp * 4; b0 < nb; b0 += NW * 4 * UB) {
+            float4 v[UB], w[UB];
+#pragma unroll
+            for (int u = 0; u < UB; u++) {
+                const int b = b0 + u * NW * 4 + sub;
+                v[u] = b < nb ? *(const float4 *)(x + b * 32 + e) : zero;
+                w[u] = (a.pro == PRO_NORM && b < nb) ? *(const float4 *)(a.norm_w + b * 32 + e) : zero;
             }
-            float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
-            for (int off = 4; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-            const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-            const int q0 = __float2int_rn(__fmul_rn(v.x, id)), q1 = __float2int_rn(__fmul_rn(v.y, id));
-            const int q2 = __float2int_rn(__fmul_rn(v.z, id)), q3 = __float2int_rn(__fmul_rn(v.w, id));
-            int sum = q0 + q1 + q2 + q3;
+            for (int u = 0; u < UB; u++) {
+                const int b = b0 + u * NW * 4 + sub;
+                float4 t = v[u];
+                if (a.pro == PRO_NORM) {
+                    t.x = __fmul_rn(__fmul_rn(t.x, scale), w[u].x);
+                    t.y = __fmul_rn(__fmul_rn(t.y, scale), w[u].y);
+                    t.z = __fmul_rn(__fmul_rn(t.z, scale), w[u].z);
+                    t.w = __fmul_rn(__fmul_rn(t.w, scale), w[u].w);
+                }
+                float amax = fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w)));
 #pragma unroll
-            for (int off = 4; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-            if (ok) {
-                *(uint32_t *)(sq + (size_t)m * K + b * 32 + e) =
-                    (uint32_t)(q0 & 255) | ((uint32_t)(q1 & 255) << 8) | ((uint32_t)(q2 & 255) << 16) | ((uint32_t)(q3 & 255) << 24);
-                if ((lane & 7) == 0) {
-                    sdf[m * nb + b] = h2f(f2h(__fdiv_rn(amax, 127.0f)));
-                    ss8[m * nb + b] = 8 * sum;
+                for (int off = 4; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+                const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+                const int q0 = __float2int_rn(__fmul_rn(t.x, id)), q1 = __float2int_rn(__fmul_rn(t.y, id));
+                const int q2 = __float2int_rn(__fmul_rn(t.z, id)), q3 = __float2int_rn(__fmul_rn(t.w, id));
+                int sum = q0 + q1 + q2 + q3;
+#pragma unroll
+                for (int off = 4; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+                if (b < nb) {
+                    *(uint32_t *)(sq + m * K + b * 32 + e) = (uint32_t)(q0 & 255) | ((uint32_t)(q1 & 255) << 8) |
+                                                             ((uint32_t)(q2 & 255) << 16) | ((uint32_t)(q3 & 255) << 24);
+                    if ((lane & 7) == 0) {
+                        sdf[m * nb + b] = h2f(f2h(__fdiv_rn(amax, 127.0f)));
+                        ss8[m * nb + b] = 8 * sum;
+                    }
                 }
             }
         }
@@ -174,10 +217,235 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
     named_bar(bar, NCT);
 }
 
+// Epilogue operands of row `row0` (loaded by lane 0 before the row's pieces arrive): the residual
+// (SINGLE) or the rotation's cos / sin (ROPE_QKV, q and k rows).
+template <int M>
+__device__ __forceinline__ void gemv_epi_load(const FusedArgs &a, int mat, int row0, float (&e0)[M], float (&e1)[M]) {
+#pragma unroll
+    for (int m = 0; m < M; m++) e0[m] = e1[m] = 0.0f;
+    if (a.map == MAP_SINGLE) {
+        if (a.res && row0 < a.wrows[0])
+#pragma unroll
+            for (int m = 0; m < M; m++) e0[m] = a.res[m * a.ldr + row0];
+    } else if (a.map == MAP_ROPE_QKV && mat < 2) {
+        const int D = (int)a.D, half = D / 2, i = row0 % D;
+#pragma unroll
+        for (int m = 0; m < M; m++) {
+            const int32_t p = a.pos[m];
+            if (p >= 0 && p < a.npos) {
+                e0[m] = a.table[((int64_t)p * half + i) * 2];
+                e1[m] = a.table[((int64_t)p * half + i) * 2 + 1];
+            }
+        }
+    }
+}
+
+// Lane 0: row `row0`'s results y[piece][m] (already reduced over the warp) -> outputs.
+template <int NR, int M>
+__device__ __forceinline__ void gemv_epi_store(const FusedArgs &a, int mat, int row0, const float (&y)[NR][M],
+                                               const float (&e0)[M], const float (&e1)[M]) {
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+        if (a.map == MAP_SINGLE) {
+            if (row0 >= a.wrows[0]) continue;
+            float v = y[0][m];
+            if (a.res) v = __fadd_rn(e0[m], v);
+            a.out[m * a.ldo + row0] = v;
+        } else if (a.map == MAP_SWIGLU) {
+            if (row0 >= a.wrows[0]) continue;
+            a.out[m * a.ldo + row0] = __fmul_rn(gc_silu(y[0][m]), y[NR - 1][m]);
+        } else {
+            const int D = (int)a.D, half = D / 2, h = row0 / D, i = row0 - h * D;
+            const int32_t p = a.pos[m];
+            float y0 = y[0][m], y1 = y[NR - 1][m];
+            if (mat < 2) {
+                float c, sn;
+                if (p >= 0 && p < a.npos) {
+                    c = e0[m];
+                    sn = e1[m];
+                } else {
+                    float theta = (float)p;
+                    for (int kk = 0; kk < i; kk++) theta = __fmul_rn(theta, a.theta_scale);
+                    c = cosf(theta);
+                    sn = sinf(theta);
+                }
+                const float x0 = y0, x1 = y1;
+                y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+                y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+            }
+            if (mat == 0) {
+                float *qo = a.q_out + m * a.ldq + (int64_t)h * D;
+                qo[i] = y0;
+                qo[i + half] = y1;
+            } else if (p >= 0 && p < a.cache_rows) {
+                char *base = (mat == 1 ? a.kcache : a.vcache) + p * a.cache_nb1 + h * a.cache_nb2;
+                ((__half *)base)[i] = __float2half_rn(y0);
+                ((__half *)base)[i + half] = __float2half_rn(y1);
+            } else if (a.err) {
+                atomicExch(a.err, 1);
+            }
+        }
+    }
+}
+
+// Waits (lane 0, bounded) for piece t to land; the outcome is shared with the warp.
+__device__ __forceinline__ bool gemv_wait_piece(const Ring &R, uint32_t t) {
+    int ready = 1;
+    if ((threadIdx.x & 31) == 0) ready = mbar_wait(&R.full[R.slot(t)], R.parity(t)) ? 1 : 0;
+    return __shfl_sync(0xffffffffu, ready, 0) != 0;
+}
+
+// ---------------------------------------------------------------- one activation row
+
+constexpr int GEMV_NI = QSEG / 32;  // blocks of a lane in one segment
+
+// This lane's blocks (lane + 32 i) of one segment of the activation row, from shared memory.
+struct Act1 {
+    int4 lo[GEMV_NI], hi[GEMV_NI];
+    float d[GEMV_NI];
+    int s8[GEMV_NI];
+};
+
+__device__ __forceinline__ void act1_load(Act1 &x, const int8_t *sq, const float *sdf, const int *ss8, int bbase, int sb,
+                                          int lane) {
+#pragma unroll
+    for (int i = 0; i < GEMV_NI; i++) {
+        const int j = lane + 32 * i;
+        if (j < sb) {
+            const int4 *x4 = (const int4 *)(sq + (bbase + j) * 32);
+            x.lo[i] = x4[0];
+            x.hi[i] = x4[1];
+            x.d[i] = sdf[bbase + j];
+            x.s8[i] = ss8[bbase + j];
+        }
+    }
+}
+
+// acc += this lane's blocks of one row of a piece, against the activation registers: every load of
+// the row first, then the products in block order.
+template <int QT>
+__device__ __forceinline__ void piece_row1(float &acc, const unsigned char *codes, const uint16_t *scl, const Act1 &x,
+                                           int sb, int lane) {
+    constexpr int CB = QT == 0 ? 16 : 32;
+    int4 w0[GEMV_NI], w1[GEMV_NI];
+    uint16_t sw[GEMV_NI];
+#pragma unroll
+    for (int i = 0; i < GEMV_NI; i++) {
+        const int j = lane + 32 * i;
+        if (j < sb) {
+            w0[i] = *(const int4 *)(codes + j * CB);
+            if (QT == 1) w1[i] = *(const int4 *)(codes + j * CB + 16);
+            sw[i] = scl[j];
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < GEMV_NI; i++) {
+        if (lane + 32 * i >= sb) break;
+        int v = 0;
+        if (QT == 0) {
+            const uint32_t *w = (const uint32_t *)&w0[i];
+            v = __dp4a((int)(w[0] & 0x0f0f0f0fu), x.lo[i].x, v);
+            v = __dp4a((int)((w[0] >> 4) & 0x0f0f0f0fu), x.hi[i].x, v);
+            v = __dp4a((int)(w[1] & 0x0f0f0f0fu), x.lo[i].y, v);
+            v = __dp4a((int)((w[1] >> 4) & 0x0f0f0f0fu), x.hi[i].y, v);
+            v = __dp4a((int)(w[2] & 0x0f0f0f0fu), x.lo[i].z, v);
+            v = __dp4a((int)((w[2] >> 4) & 0x0f0f0f0fu), x.hi[i].z, v);
+            v = __dp4a((int)(w[3] & 0x0f0f0f0fu), x.lo[i].w, v);
+            v = __dp4a((int)((w[3] >> 4) & 0x0f0f0f0fu), x.hi[i].w, v);
+            v -= x.s8[i];
+        } else {
+            v = __dp4a(w0[i].x, x.lo[i].x, v);
+            v = __dp4a(w0[i].y, x.lo[i].y, v);
+            v = __dp4a(w0[i].z, x.lo[i].z, v);
+            v = __dp4a(w0[i].w, x.lo[i].w, v);
+            v = __dp4a(w1[i].x, x.hi[i].x, v);
+            v = __dp4a(w1[i].y, x.hi[i].y, v);
+            v = __dp4a(w1[i].z, x.hi[i].z, v);
+            v = __dp4a(w1[i].w, x.hi[i].w, v);
+        }
+        acc = __fmaf_rn(__fmul_rn(h2f(sw[i]), x.d[i]), (float)v, acc);
+    }
+}
+
+// Consumer side of one GEMV with one activation row: this team's groups (every `teams`-th local
+// group, starting at `team`), chunk by chunk and segment-major inside a chunk, pieces numbered from
+// t0; the butterflies and epilogues of a chunk's groups run together at its end. `wt` is the warp's
+// row within the tile. False on a timed-out wait.
+template <int QT, int NR, int CG>
+__device__ inline bool consume_gemv1(const FusedArgs &a, const GemvGeo &G, const Ring &R, uint32_t t0, int cta, int nctas,
+                                     int team, int teams, int wt, const int8_t *sq, const float *sdf, const int *ss8) {
+    constexpr int CB = QT == 0 ? 16 : 32;
+    const int lane = threadIdx.x & 31;
+    const int L = local_groups(G.groups, cta, nctas), chunk = gemv_chunk(1, teams, CG);
+    const int per_group = G.nseg * G.pieces;
+    Act1 x;
+    int loaded = -1;  // segment whose activation is in x
+    for (int c0 = 0; c0 < L; c0 += chunk) {
+        const int c1 = c0 + chunk < L ? c0 + chunk : L, n = c1 - c0;
+        int mat[CG], row0[CG];
+        float acc[CG][NR], e0[CG][1], e1[CG][1];
+#pragma unroll
+        for (int j = 0; j < CG; j++) {
+            const int q = team + j * teams;
+            mat[j] = row0[j] = 0;
+#pragma unroll
+            for (int r = 0; r < NR; r++) acc[j][r] = 0.0f;
+            e0[j][0] = e1[j][0] = 0.0f;
+            if (q < n) {
+                int tile;
+                gemv_piece(a, G, cta + (c0 + q) * nctas, 0, 0, &mat[j], &tile);
+                row0[j] = tile * QTR + wt;
+                if (lane == 0) gemv_epi_load<1>(a, mat[j], row0[j], e0[j], e1[j]);
+            }
+        }
+        const uint32_t tb = t0 + (uint32_t)(c0 * per_group);
+        for (int s = 0; s < G.nseg; s++) {
+            const int sb = (int)qw_seg_blocks(G.nb, s);
+            if (s != loaded) {
+                act1_load(x, sq, sdf, ss8, s * QSEG, sb, lane);
+                loaded = s;
+            }
+#pragma unroll
+            for (int j = 0; j < CG; j++) {
+                const int q = team + j * teams;
+                if (q >= n) break;
+#pragma unroll
+                for (int r = 0; r < NR; r++) {
+                    const uint32_t t = tb + (uint32_t)((s * n + q) * G.pieces + r);
+                    if (!gemv_wait_piece(R, t)) return false;
+                    const unsigned char *piece = R.data(t);
+                    piece_row1<QT>(acc[j][r], piece + wt * sb * CB, (const uint16_t *)(piece + QTR * sb * CB) + wt * sb,
+                                   x, sb, lane);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&R.empty[R.slot(t)]);
+                }
+            }
+        }
+        float y[CG][NR][1];
+#pragma unroll
+        for (int j = 0; j < CG; j++)
+#pragma unroll
+            for (int r = 0; r < NR; r++) y[j][r][0] = acc[j][r];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1)  // the butterflies of every group at once
+#pragma unroll
+            for (int j = 0; j < CG; j++)
+#pragma unroll
+                for (int r = 0; r < NR; r++) y[j][r][0] = __fadd_rn(y[j][r][0], __shfl_xor_sync(0xffffffffu, y[j][r][0], off));
+        if (lane == 0)
+#pragma unroll
+            for (int j = 0; j < CG; j++)
+                if (team + j * teams < n) gemv_epi_store<NR, 1>(a, mat[j], row0[j], y[j], e0[j], e1[j]);
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------- several activation rows
+
 // One quantized block of this lane's row against every activation row.
 template <int QT, int NR, int M>
 __device__ __forceinline__ void gemv_block(float (&acc)[NR][M], int r, const unsigned char *codes, const uint16_t *scl, int j,
-                                           int b, const int8_t *sq, const float *sdf, const int *ss8, int64_t K, int64_t nb) {
+                                           int b, const int8_t *sq, const float *sdf, const int *ss8, int K, int nb) {
     const float dw = h2f(scl[j]);
     if (QT == 0) {
         const uint4 w = *(const uint4 *)(codes + j * 16);
@@ -219,104 +487,72 @@ __device__ __forceinline__ void gemv_block(float (&acc)[NR][M], int r, const uns
 
 // Consumer side of one GEMV: this team's groups (every `teams`-th local group, starting at `team`),
 // pieces numbered from t0, then the epilogue. `wt` is the warp index within the team (the row of
-// the tile it owns). Returns false on a timed-out wait.
-template <int QT, int NR, int M>
-__device__ inline bool consume_gemv(const FusedArgs &a, const GemvGeo &G, const Ring &R, int64_t t0, int64_t cta,
-                                    int64_t nctas, int team, int teams, int wt, const int8_t *sq, const float *sdf,
-                                    const int *ss8) {
-    constexpr int CB = QT == 0 ? 16 : 32;
-    const int lane = threadIdx.x & 31;
-    const int64_t K = a.K, nb = G.nb;
-    const int64_t per_group = G.nseg * G.pieces;
-    int64_t gl = 0;
-    for (int64_t g = cta; g < G.groups; g += nctas, gl++) {
-        if (gl % teams != team) continue;
-        float acc[NR][M];
+// the tile it owns). CG: groups per team in one chunk with one activation row. False on a
+// timed-out wait.
+template <int QT, int NR, int M, int CG>
+__device__ inline bool consume_gemv(const FusedArgs &a, const GemvGeo &G, const Ring &R, uint32_t t0, int cta, int nctas,
+                                    int team, int teams, int wt, const int8_t *sq, const float *sdf, const int *ss8) {
+    if constexpr (M == 1) {
+        return consume_gemv1<QT, NR, CG>(a, G, R, t0, cta, nctas, team, teams, wt, sq, sdf, ss8);
+    } else {
+        constexpr int CB = QT == 0 ? 16 : 32;
+        const int lane = threadIdx.x & 31;
+        const int K = (int)a.K, nb = G.nb;
+        const int per_group = G.nseg * G.pieces;
+        const int L = local_groups(G.groups, cta, nctas);
+        for (int gl = team; gl < L; gl += teams) {
+            int mat, tile;
+            gemv_piece(a, G, cta + gl * nctas, 0, 0, &mat, &tile);
+            const int row0 = tile * QTR + wt;
+            float e0[M], e1[M];
+            if (lane == 0) gemv_epi_load<M>(a, mat, row0, e0, e1);
+            float acc[NR][M];
 #pragma unroll
-        for (int r = 0; r < NR; r++)
+            for (int r = 0; r < NR; r++)
 #pragma unroll
-            for (int m = 0; m < M; m++) acc[r][m] = 0.0f;
-        int64_t t = t0 + gl * per_group;
-        for (int64_t s = 0; s < G.nseg; s++) {
-            const int sb = (int)qw_seg_blocks(nb, s);
-            const int bbase = (int)(s * QSEG);
+                for (int m = 0; m < M; m++) acc[r][m] = 0.0f;
+            uint32_t t = t0 + (uint32_t)(gl * per_group);
+            for (int s = 0; s < G.nseg; s++) {
+                const int sb = (int)qw_seg_blocks(nb, s);
+                const int bbase = s * QSEG;
 #pragma unroll
-            for (int r = 0; r < NR; r++, t++) {
-                const int slot = (int)(t % R.ns);
-                int ready = 1;
-                if (lane == 0) ready = mbar_wait(&R.full[slot], (uint32_t)((t / R.ns) & 1)) ? 1 : 0;
-                if (!__shfl_sync(0xffffffffu, ready, 0)) return false;  // uniform within the warp
-                const unsigned char *piece = R.slots + slot * R.slot_bytes;
-                const unsigned char *codes = piece + wt * sb * CB;
-                const uint16_t *scl = (const uint16_t *)(piece + QTR * sb * CB) + wt * sb;
-                if (sb == QSEG) {
+                for (int r = 0; r < NR; r++, t++) {
+                    if (!gemv_wait_piece(R, t)) return false;
+                    const unsigned char *piece = R.data(t);
+                    const unsigned char *codes = piece + wt * sb * CB;
+                    const uint16_t *scl = (const uint16_t *)(piece + QTR * sb * CB) + wt * sb;
+                    if (sb == QSEG) {
 #pragma unroll
-                    for (int i = 0; i < QSEG / 32; i++)
-                        gemv_block<QT, NR, M>(acc, r, codes, scl, lane + 32 * i, bbase + lane + 32 * i, sq, sdf, ss8, K, nb);
-                } else {
-                    for (int j = lane; j < sb; j += 32) gemv_block<QT, NR, M>(acc, r, codes, scl, j, bbase + j, sq, sdf, ss8, K, nb);
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&R.empty[slot]);
-            }
-        }
-        // epilogue for this warp's row(s)
-        int mat;
-        int64_t tile;
-        gemv_piece(a, G, g, 0, 0, &mat, &tile);
-        const int64_t row0 = tile * QTR + wt;
-#pragma unroll
-        for (int m = 0; m < M; m++) {
-            float y[NR];
-#pragma unroll
-            for (int r = 0; r < NR; r++) y[r] = warp_butterfly(acc[r][m]);
-            if (lane != 0) continue;
-            if (a.map == MAP_SINGLE) {
-                if (row0 >= a.wrows[0]) continue;
-                float v = y[0];
-                if (a.res) v = __fadd_rn(a.res[m * a.ldr + row0], v);
-                a.out[m * a.ldo + row0] = v;
-            } else if (a.map == MAP_SWIGLU) {
-                if (row0 >= a.wrows[0]) continue;
-                a.out[m * a.ldo + row0] = __fmul_rn(gc_silu(y[0]), y[NR - 1]);
-            } else {
-                const int64_t half = a.D / 2, h = row0 / a.D, i = row0 % a.D;
-                const int32_t p = a.pos[m];
-                float y0 = y[0], y1 = y[NR - 1];
-                if (mat < 2) {
-                    float c, sn;
-                    if (p >= 0 && p < a.npos) {
-                        c = a.table[(p * half + i) * 2];
-                        sn = a.table[(p * half + i) * 2 + 1];
+                        for (int i = 0; i < QSEG / 32; i++)
+                            gemv_block<QT, NR, M>(acc, r, codes, scl, lane + 32 * i, bbase + lane + 32 * i, sq, sdf, ss8, K, nb);
                     } else {
-                        float theta = (float)p;
-                        for (int64_t kk = 0; kk < i; kk++) theta = __fmul_rn(theta, a.theta_scale);
-                        c = cosf(theta);
-                        sn = sinf(theta);
+                        for (int j = lane; j < sb; j += 32)
+                            gemv_block<QT, NR, M>(acc, r, codes, scl, j, bbase + j, sq, sdf, ss8, K, nb);
                     }
-                    const float x0 = y0, x1 = y1;
-                    y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-                    y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
-                }
-                if (mat == 0) {
-                    float *qo = a.q_out + m * a.ldq + h * a.D;
-                    qo[i] = y0;
-                    qo[i + half] = y1;
-                } else if (p >= 0 && p < a.cache_rows) {
-                    char *base = (mat == 1 ? a.kcache : a.vcache) + p * a.cache_nb1 + h * a.cache_nb2;
-                    ((__half *)base)[i] = __float2half_rn(y0);
-                    ((__half *)base)[i + half] = __float2half_rn(y1);
-                } else if (a.err) {
-                    atomicExch(a.err, 1);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&R.empty[R.slot(t)]);
                 }
             }
+            float y[NR][M];
+#pragma unroll
+            for (int m = 0; m < M; m++)
+#pragma unroll
+                for (int r = 0; r < NR; r++) y[r][m] = warp_butterfly(acc[r][m]);
+            if (lane == 0) gemv_epi_store<NR, M>(a, mat, row0, y, e0, e1);
         }
+        return true;
     }
-    return true;
 }
 
 __host__ __device__ inline size_t gemv_act_bytes(int M, int64_t K) {
     return ((size_t)M * (size_t)K + (size_t)M * (size_t)(K / 32) * 8 + 127) / 128 * 128;
+}
+
+// Ring slots for a shared-memory budget: the largest power of two that fits, at most `maxns`.
+__host__ inline int ring_log2(size_t budget, size_t head, size_t slot_bytes, int maxns) {
+    int l = 0;
+    while ((2 << l) <= maxns && head + ((size_t)2 << l) * slot_bytes <= budget) l++;
+    return l;
 }
 
 }  // namespace k

@@ -1,12 +1,12 @@
 // The decode step as one persistent kernel: a cooperative launch (one CTA per SM) runs a list of
 // phases, the fused GEMV groups and the attention of every layer, separated by grid barriers.
 //
-// Per CTA, warp 16 is the producer: one lane streams the weight pieces of every GEMV phase, in phase
+// Per CTA, warp 8 is the producer: one lane streams the weight pieces of every GEMV phase, in phase
 // order, into the shared-memory ring (gc_gemv_dev.cuh). Weights never depend on activations, so the
 // stream runs ahead through barriers and attention phases, limited only by free ring slots. Warps
-// 0-15 are two teams of 8 consumers: for a GEMV phase each team takes every other row group of the
-// CTA; for an attention phase the 16 warps work on (query row, K/V head, 64-key chunk) items as the
-// split-KV flash kernel does (gc_flash.cu), four warps per query head.
+// 0-7 are the consumers: for a GEMV phase one tile row each, with the activation row in registers;
+// for an attention phase they work on (query row, K/V head, 64-key chunk) items as the split-KV
+// flash kernel does (gc_flash.cu), two warps per query head.
 //
 // Every phase computes exactly what the per-op kernels compute (same prologue, same block order,
 // same epilogues, same attention chunking and merge), so results are bit-identical to them and to the
@@ -29,14 +29,15 @@ int num_sms();
 
 namespace {
 
-constexpr int TEAMS = 2;
+constexpr int TEAMS = 1;
+constexpr int CG = 2;                         // row groups per team in a GEMV chunk (gc_gemv_dev.cuh)
 constexpr int NCW = 8 * TEAMS;                // consumer warps
 constexpr int NCT = NCW * 32;                 // consumer threads
 constexpr int NTHREADS = NCT + 32;            // + producer warp
 constexpr int MAXNS = 32;
 constexpr int CH = 64;                        // attention chunk (keys)
 constexpr int MAXD = 128;  // decode kernel head sizes (larger heads use the per-op kernels)
-constexpr int WPH = 4;                        // warps per query head
+constexpr int WPH = 2;                        // warps per query head
 constexpr int MAXG = NCW / WPH;               // query heads per attention item pass
 constexpr size_t SMEM_LIMIT = 226 * 1024;     // dynamic shared memory (the opt-in 227 KB less the static part)
 
@@ -229,7 +230,8 @@ __device__ inline bool attn_item(const MegaAttn &at, int64_t iq, int64_t hk, int
 }
 
 template <int QT, int M>
-__global__ void __launch_bounds__(NTHREADS, 1) mega_kernel(const MegaPhase *phases, int nph, int ns, int64_t slot_bytes,
+// 9 warps: 3 share a scheduler partition, so at most 168 registers a thread keep one CTA per SM.
+__global__ void __maxnreg__(168) mega_kernel(const MegaPhase *phases, int nph, int log2ns, int slot_bytes,
                                                            size_t act_bytes, int attn_d, int *gbar, int *err,
                                                            uint64_t *trace) {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -243,14 +245,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) mega_kernel(const MegaPhase *phas
     float *sc = (float *)(Vs + CH * attn_d);
     unsigned char *slots = (unsigned char *)(sc + MAXG * CH);
     __shared__ int s_abort, s_last;
-    const Ring R{full, empty, slots, ns, slot_bytes};
+    const Ring R{full, empty, slots, log2ns, slot_bytes};
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t cta = blockIdx.x, nctas = gridDim.x;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < ns; s++) {
+        for (int s = 0; s < (1 << log2ns); s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 8);
+            mbar_init(&empty[s], 8);  // the 8 warps of the team that owns the piece
         }
         mbar_init(abar, 1);
         mbar_fence_init();
@@ -260,14 +262,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) mega_kernel(const MegaPhase *phas
 
     if (warp == NCW) {  // ---------------- producer: every GEMV phase's pieces, in order
         if (lane != 0) return;
-        int64_t t = 0;
+        uint32_t t = 0;
         for (int p = 0; p < nph; p++) {
             if (phases[p].type != 0) continue;
             const FusedArgs &a = phases[p].g;
-            if (!produce_gemv(a, gemv_geo(a), R, t, cta, nctas)) {
+            if (!produce_gemv(a, gemv_geo(a), R, t, (int)cta, (int)nctas, gemv_chunk(1, TEAMS, CG))) {
                 if (err) atomicExch(err, 3);
-                for (int64_t u = t - ns; u < t; u++)
-                    if (u >= 0) mbar_wait(&full[u % ns], (uint32_t)((u / ns) & 1), 100000000ull);
+                drain_ring(R, t);
                 return;
             }
             if (trace) trace[(cta * nph + p) * 4 + 3] = global_ns();
@@ -276,7 +277,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) mega_kernel(const MegaPhase *phas
     }
 
     // ---------------- consumers: every warp runs the same barrier sequence, even after an abort
-    int64_t t = 0;
+    uint32_t t = 0;
     uint32_t aphase = 0;
     const int team = warp / 8, wt = warp % 8;
     for (int p = 0; p < nph; p++) {
@@ -294,11 +295,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) mega_kernel(const MegaPhase *phas
                 gemv_prologue<M, NCT>(a, sq, sdf, ss8, red, 1);
                 if (stamp) stamp[1] = global_ns();
                 bool ok;
-                if (G.pieces == 2) ok = consume_gemv<QT, 2, M>(a, G, R, t, cta, nctas, team, TEAMS, wt, sq, sdf, ss8);
-                else ok = consume_gemv<QT, 1, M>(a, G, R, t, cta, nctas, team, TEAMS, wt, sq, sdf, ss8);
+                if (G.pieces == 2)
+                    ok = consume_gemv<QT, 2, M, CG>(a, G, R, t, (int)cta, (int)nctas, team, TEAMS, wt, sq, sdf, ss8);
+                else
+                    ok = consume_gemv<QT, 1, M, CG>(a, G, R, t, (int)cta, (int)nctas, team, TEAMS, wt, sq, sdf, ss8);
                 if (!ok) s_abort = 1;
             }
-            t += local_groups(G.groups, cta, nctas) * G.nseg * G.pieces;
+            t += (uint32_t)(local_groups(G.groups, (int)cta, (int)nctas) * G.nseg * G.pieces);
             named_bar(1, NCT);  // both teams done with the activation buffer
             if (stamp) stamp[2] = global_ns();
         } else {
@@ -333,10 +336,9 @@ void launch(const MegaPhase *phases, int nph, int64_t kmax, int attn_d, int64_t 
     }
     const size_t act = gemv_act_bytes(M, kmax);
     const size_t head = (size_t)(2 * MAXNS + 2) * 8 + 256 * 8 + act + (size_t)CH * attn_d * 4 + (size_t)MAXG * CH * 4;
-    int ns = (int)((SMEM_LIMIT - head) / (size_t)slot_bytes);
-    if (ns > MAXNS) ns = MAXNS;
-    if (ns < 4) throw std::runtime_error("decode kernel: shared memory too small for the weight ring");
-    const size_t smem = head + (size_t)ns * (size_t)slot_bytes;
+    const int log2ns = ring_log2(SMEM_LIMIT, head, (size_t)slot_bytes, MAXNS);
+    if ((1 << log2ns) < 4) throw std::runtime_error("decode kernel: shared memory too small for the weight ring");
+    const size_t smem = head + ((size_t)1 << log2ns) * (size_t)slot_bytes;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)num_sms());
     cfg.blockDim = dim3(NTHREADS);
@@ -347,18 +349,30 @@ void launch(const MegaPhase *phases, int nph, int64_t kmax, int attn_d, int64_t 
     at[0].val.cooperative = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, phases, nph, ns, slot_bytes, act, attn_d, gbar, err, trace);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, phases, nph, log2ns, (int)slot_bytes, act, attn_d, gbar, err, trace);
     if (e != cudaSuccess) throw std::runtime_error(std::string("CUDA launch of the decode kernel failed: ") + cudaGetErrorString(e));
 }
 
 }  // namespace
+
+// One CTA of the kernel fits an SM with `smem` bytes (a cooperative launch needs every CTA resident).
+template <int QT>
+bool resident(size_t smem) {
+    auto kern = mega_kernel<QT, 1>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_LIMIT) != cudaSuccess) return false;
+    int n = 0;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, NTHREADS, smem) == cudaSuccess && n >= 1;
+}
 
 bool mega_supported(int qtype, int M, int64_t kmax, int attn_d) {
     if (M != 1 || (qtype != T_Q4_0 && qtype != T_Q8_0) || attn_d > MAXD || attn_d % 32) return false;
     const int64_t slot = (int64_t)QTR * QSEG * ((qtype == T_Q4_0 ? 16 : 32) + 2);
     const size_t head = (size_t)(2 * MAXNS + 2) * 8 + 256 * 8 + gemv_act_bytes(M, kmax) + (size_t)CH * attn_d * 4 +
                         (size_t)MAXG * CH * 4;
-    return head + 4 * (size_t)slot <= SMEM_LIMIT;
+    const int log2ns = ring_log2(SMEM_LIMIT, head, (size_t)slot, MAXNS);
+    if ((1 << log2ns) < 4) return false;
+    const size_t smem = head + ((size_t)1 << log2ns) * (size_t)slot;
+    return qtype == T_Q4_0 ? resident<0>(smem) : resident<1>(smem);
 }
 
 int mega_ctas() { return num_sms(); }
