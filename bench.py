@@ -18,7 +18,8 @@ are timed (one step = one token through all 32 layers; n_kv = 768).
 - cpu_baseline / --impl reference: the reference's CPU arithmetic (this repository's C
   restatement of ggml's CPU path, oracle/) timed on the host's cores on a few decode tokens.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 8b|tiny]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 8b|tiny|sweep]
+    python bench.py --config sweep [--shape NxK] [--m M] [--wtype q4_0|q8_0]   # config 2, one line per case
 """
 
 from __future__ import annotations
@@ -156,17 +157,84 @@ def cpu_baseline(gguf: Path, sh, n_tokens: int) -> dict:
                       f"oracle/ C restatement of ggml's CPU arithmetic, {dt:.1f}s"}
 
 
+SWEEP_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]  # weight [N x K]
+SWEEP_M = [1, 8, 64, 512, 2048]
+
+
+def sweep(args) -> None:
+    """isolated quantized mul_mat (one-node programs through the C ABI), weights
+    from N(0, 0.02) seed 0 as Q4_0 / Q8_0, activations N(0, 1). Each case prints one JSON line with
+    the kernel's device time (profiled launch, L2 flushed by a 256 MB write before each rep) and its
+    bytes / FLOPs rates. `--shape NxK --m M --wtype T` runs one case (the ncu captures use that)."""
+    import torch
+
+    from ggml_compiler_b200.programs import write_mul_mat
+    from ggml_compiler_b200.runtime import Session
+
+    peak, peak_kind = peaks()
+    tflops = None
+    pk = REPO / "MEASURED_PEAKS.json"
+    if pk.exists():
+        tflops = float(json.loads(pk.read_text())["bf16_tflops"])
+    shapes = [tuple(int(v) for v in args.shape.lower().split("x"))] if args.shape else SWEEP_SHAPES
+    ms_ = [args.m] if args.m else SWEEP_M
+    wts = [args.wtype] if args.wtype else ["q4_0", "q8_0"]
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    CACHE.mkdir(parents=True, exist_ok=True)
+    for wt in wts:
+        for N, Kd in shapes:
+            rng = np.random.default_rng(0)
+            w = None
+            for M in ms_:
+                p = CACHE / f"mm_{wt}_{N}x{Kd}_m{M}.gguf"
+                if not p.exists():
+                    if w is None:
+                        w = rng.standard_normal((N, Kd), dtype=np.float32) * np.float32(0.02)
+                    write_mul_mat(p, w, wt, M)
+                x = np.random.default_rng(1).standard_normal((1, M, Kd), dtype=np.float32)
+                with Session(p, backend="cuda") as s:
+                    for _ in range(max(3, args.warmup)):
+                        s.run(x=x)
+                    s.set_profiling(True)
+                    for _ in range(args.steps):
+                        flush.fill_(1.0)
+                        torch.cuda.synchronize()
+                        s.run(x=x)
+                    ks = s.kernel_stats()
+                    s.set_profiling(False)
+                kinds = [k for k in ks if k.startswith(("gemv", "mul_mat"))]
+                ms = sum(ks[k]["ms"] for k in kinds) / max(1, sum(ks[k]["launches"] for k in kinds))
+                wbytes = N * Kd * (18 if wt == "q4_0" else 34) / 32
+                byts = wbytes + 4.0 * M * Kd + 4.0 * M * N
+                flops = 2.0 * M * N * Kd
+                print(json.dumps({"metric": "isolated quantized mul_mat (BASELINE config 2)", "kernel": "+".join(kinds),
+                                  "wtype": wt, "N": N, "K": Kd, "M": M, "us": ms * 1000.0,
+                                  "GB_s": byts / (ms / 1000.0) / 1e9, "hbm_frac": byts / (ms / 1000.0) / 1e9 / peak,
+                                  "TFLOP_s": flops / (ms / 1000.0) / 1e12,
+                                  "tensor_frac": (flops / (ms / 1000.0) / 1e12 / tflops) if tflops else None,
+                                  "peak_source": f"{peak_kind} MEASURED_PEAKS.json", "reps": args.steps,
+                                  "l2": "flushed before each rep (256 MB write)"}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="8b", choices=["8b", "tiny"])
+    ap.add_argument("--config", default="8b", choices=["8b", "tiny", "sweep"])
+    ap.add_argument("--shape", default=None, help="sweep: one weight shape NxK")
+    ap.add_argument("--m", type=int, default=None, help="sweep: one activation row count")
+    ap.add_argument("--wtype", default=None, choices=["q4_0", "q8_0"], help="sweep: one weight type")
     ap.add_argument("--cpu-tokens", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
 
+    if args.config == "sweep":
+        if args.steps == ap.get_default("steps"):
+            args.steps = 10
+        sweep(args)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
