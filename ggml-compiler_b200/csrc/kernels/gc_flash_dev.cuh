@@ -1,0 +1,206 @@
+// Device parts of split-KV flash attention shared by the split kernel (gc_flash.cu) and the decode
+// kernel's attention phases (gc_mega.cu): one 64-key chunk's partial for the query heads of one K/V
+// head, and the in-order merge of a head's chunk partials.
+//
+// The arithmetic is the CPU checker's, in its order: the query rounded to f16; a score is the head
+// dot in the lane-split order (lane l owns elements [l*D/32, (l+1)*D/32)), then the 32-lane
+// butterfly, times scale, plus the mask; per chunk the max m, p_j = exp(s_j - m), l = sum of p_j and
+// o = sum of p_j v_j in key order; chunks merged in order with weights exp(m_c - M). Only those
+// sums are ordered: the loads feeding them are issued ahead.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include <cstdint>
+
+#include "gc_math.cuh"
+
+namespace gcb {
+namespace k {
+
+constexpr int FL_CH = 64;  // keys per chunk (the order's chunk size)
+
+struct FlashChunk {
+    const char *q;        // query row of the group's first head
+    int64_t qnb0, qnbh;   // bytes between a head's elements, between heads
+    const char *mask;     // mask row of the group's first head at this chunk's first key, or null
+    int64_t mne2, mnbh;   // mask heads (broadcast when 1) and bytes between them
+    int hbase;            // global index of the group's first head (for the mask broadcast)
+    float scale;
+    int D, n, G;          // head size, keys in this chunk, heads in the group
+    float *part;          // partial (m, l, o[D]) of the group's first head
+    int64_t pstride;      // floats between the partials of consecutive heads
+};
+
+// Stages the group's query rows (rounded to f16) and this chunk's mask values into shared memory:
+// qs [G][D], ms [G][FL_CH] (0 where there is no mask). Threads tid = 0 .. nthreads-1; the caller
+// synchronises before flash_chunk reads them. Issued while the chunk's K/V copies are in flight.
+__device__ inline void flash_stage(const FlashChunk &c, float *qs, float *ms, int tid, int nthreads) {
+    for (int i = tid; i < c.G * c.D; i += nthreads) {
+        const int g = i / c.D, e = i - g * c.D;
+        qs[i] = __half2float(__float2half_rn(*(const float *)(c.q + g * c.qnbh + e * c.qnb0)));
+    }
+    for (int i = tid; i < c.G * FL_CH; i += nthreads) {
+        const int g = i / FL_CH, j = i - g * FL_CH;
+        float v = 0.0f;
+        if (c.mask && j < c.n)
+            v = __half2float(((const __half *)(c.mask + (int64_t)((c.hbase + g) % c.mne2 - c.hbase % c.mne2) * c.mnbh))[j]);
+        ms[i] = v;
+    }
+}
+
+// The chunk's K and V rows are in shared memory (Ks, Vs: [n][D] halves), the query rows and mask
+// values staged by flash_stage (qs, ms). `nslots` head slots of WPH warps each (warps 0 ..
+// nslots*WPH-1 call this); sc: [nslots][FL_CH] scores, ps: [warps][FL_CH] probabilities. `bar`
+// synchronises those warps.
+template <int WPH, int MAXD, class Bar>
+__device__ inline void flash_chunk(const FlashChunk &c, const __half *Ks, const __half *Vs, const float *qs,
+                                   const float *ms, float *sc, float *ps, int nslots, Bar bar) {
+    const int D = c.D, cpl = D / 32, n = c.n;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hw = warp / WPH, quarter = warp % WPH;
+    const float ninf = -__int_as_float(0x7f800000);
+    constexpr int OE = MAXD / 32 / WPH > 0 ? MAXD / 32 / WPH : 1;  // output elements per lane
+
+    for (int g0 = 0; g0 < c.G; g0 += nslots) {
+        const int g = g0 + hw;
+        const bool active = g < c.G;
+        const int gg = active ? g : 0;
+        float *sh = sc + hw * FL_CH;
+        float qv[MAXD / 32];
+#pragma unroll
+        for (int e = 0; e < MAXD / 32; e++) qv[e] = e < cpl ? qs[gg * D + lane * cpl + e] : 0.0f;
+        const float *mrow = ms + gg * FL_CH;
+        // scores: this warp's CH/WPH keys, 8 at a time
+        for (int k0 = quarter * (FL_CH / WPH); k0 < (quarter + 1) * (FL_CH / WPH); k0 += 8) {
+            float p[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int j = k0 + u;
+                float acc = 0.0f;
+                if (j < n) {
+                    const __half *kr = Ks + j * D + lane * cpl;
+#pragma unroll
+                    for (int e = 0; e < MAXD / 32; e++)
+                        if (e < cpl) acc = __fmaf_rn(qv[e], __half2float(kr[e]), acc);
+                }
+                p[u] = acc;
+            }
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+                for (int u = 0; u < 8; u++) p[u] = __fadd_rn(p[u], __shfl_xor_sync(0xffffffffu, p[u], off));
+            if (lane < 8 && active) {
+                const int j = k0 + lane;
+                float pu = p[0];
+#pragma unroll
+                for (int u = 1; u < 8; u++)
+                    if (lane == u) pu = p[u];
+                float s = ninf;
+                if (j < n) {
+                    s = __fmul_rn(pu, c.scale);
+                    s = __fadd_rn(s, mrow[j]);
+                }
+                sh[j] = s;
+            }
+        }
+        bar();
+        // chunk max and weights (every warp of the head computes the same values)
+        const float s0 = sh[lane], s1 = sh[lane + 32];
+        const float m = warp_max(fmaxf(s0, s1));
+        float *dst = c.part + gg * c.pstride;
+        if (active) {
+            if (m == ninf) {
+                if (quarter == 0 && lane == 0) {
+                    dst[0] = ninf;
+                    dst[1] = 0.0f;
+                }
+                for (int d = quarter * 32 + lane; d < D; d += WPH * 32) dst[2 + d] = 0.0f;
+            } else {
+                float *pw = ps + warp * FL_CH;  // this warp's copy of the chunk's probabilities
+                pw[lane] = lane < n ? gc_expf(__fsub_rn(s0, m)) : 0.0f;
+                pw[lane + 32] = lane + 32 < n ? gc_expf(__fsub_rn(s1, m)) : 0.0f;
+                __syncwarp();
+                float l = 0.0f, o[OE];
+#pragma unroll
+                for (int e = 0; e < OE; e++) o[e] = 0.0f;
+#pragma unroll 8
+                for (int j = 0; j < n; j++) {
+                    const float pj = pw[j];
+                    l = __fadd_rn(l, pj);
+                    const __half *vr = Vs + j * D;
+#pragma unroll
+                    for (int e = 0; e < OE; e++) {
+                        const int d = quarter * 32 + lane + e * WPH * 32;
+                        if (d < D) o[e] = __fmaf_rn(pj, __half2float(vr[d]), o[e]);
+                    }
+                }
+                if (quarter == 0 && lane == 0) {
+                    dst[0] = m;
+                    dst[1] = l;
+                }
+#pragma unroll
+                for (int e = 0; e < OE; e++) {
+                    const int d = quarter * 32 + lane + e * WPH * 32;
+                    if (d < D) dst[2 + d] = o[e];
+                }
+            }
+        }
+        bar();
+    }
+}
+
+// Synchronises every thread of the CTA (a flash_chunk barrier for kernels that run it with all warps).
+struct SyncCta {
+    __device__ void operator()() const { __syncthreads(); }
+};
+
+// One warp: merge head partials pp[c * (D + 2)], c < nch, in chunk order into orow[D]. The
+// partials were written by other CTAs: they are read from L2 (ld.global.cg), all of a batch of
+// chunks at once.
+template <int MAXD>
+__device__ inline void flash_merge(const float *pp, int nch, int D, float *orow) {
+    const int lane = threadIdx.x & 31, cpl = D / 32;
+    const float ninf = -__int_as_float(0x7f800000);
+    constexpr int BATCH = MAXD <= 128 ? 16 : 8;  // chunks fetched at once (registers: BATCH x MAXD/32)
+    float M = ninf, L = 0.0f, O[MAXD / 32];
+#pragma unroll
+    for (int e = 0; e < MAXD / 32; e++) O[e] = 0.0f;
+    // the overall max first (one load per lane per 32 chunks), unless one batch holds every chunk
+    if (nch > BATCH) {
+        for (int c0 = 0; c0 < nch; c0 += 32)
+            if (c0 + lane < nch) M = fmaxf(M, __ldcg(pp + (int64_t)(c0 + lane) * (D + 2)));
+        M = warp_max(M);
+    }
+    for (int c0 = 0; c0 < nch; c0 += BATCH) {
+        float bm[BATCH], bl[BATCH], bo[BATCH][MAXD / 32];
+#pragma unroll
+        for (int u = 0; u < BATCH; u++) {
+            const bool ok = c0 + u < nch;
+            const float *pc = pp + (int64_t)(c0 + u) * (D + 2);
+            bm[u] = ok ? __ldcg(pc) : ninf;
+            bl[u] = ok ? __ldcg(pc + 1) : 0.0f;
+#pragma unroll
+            for (int e = 0; e < MAXD / 32; e++) bo[u][e] = (ok && e < cpl) ? __ldcg(pc + 2 + lane * cpl + e) : 0.0f;
+        }
+        if (nch <= BATCH)
+#pragma unroll
+            for (int u = 0; u < BATCH; u++) M = fmaxf(M, bm[u]);
+#pragma unroll
+        for (int u = 0; u < BATCH; u++) {
+            if (bm[u] == ninf) continue;
+            const float wgt = gc_expf(__fsub_rn(bm[u], M));
+            L = __fmaf_rn(wgt, bl[u], L);
+#pragma unroll
+            for (int e = 0; e < MAXD / 32; e++)
+                if (e < cpl) O[e] = __fmaf_rn(wgt, bo[u][e], O[e]);
+        }
+    }
+    const float inv = L == 0.0f ? 0.0f : __fdiv_rn(1.0f, L);
+#pragma unroll
+    for (int e = 0; e < MAXD / 32; e++)
+        if (e < cpl) orow[lane * cpl + e] = __fmul_rn(O[e], inv);
+}
+
+}  // namespace k
+}  // namespace gcb

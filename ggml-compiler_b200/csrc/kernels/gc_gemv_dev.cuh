@@ -299,6 +299,13 @@ __device__ __forceinline__ bool gemv_wait_piece(const Ring &R, uint32_t t) {
 
 constexpr int GEMV_NI = QSEG / 32;  // blocks of a lane in one segment
 
+// a: four unsigned bytes, b: four signed bytes; c + their dot product.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 // This lane's blocks (lane + 32 i) of one segment of the activation row, from shared memory.
 struct Act1 {
     int4 lo[GEMV_NI], hi[GEMV_NI];
@@ -343,16 +350,19 @@ __device__ __forceinline__ void piece_row1(float &acc, const unsigned char *code
         if (lane + 32 * i >= sb) break;
         int v = 0;
         if (QT == 0) {
+            // low nibbles as they are; high nibbles masked in place (16 x their value), so that dot
+            // product is exactly 16 x the high-nibble dot and is shifted back once (exact: integer)
             const uint32_t *w = (const uint32_t *)&w0[i];
-            v = __dp4a((int)(w[0] & 0x0f0f0f0fu), x.lo[i].x, v);
-            v = __dp4a((int)((w[0] >> 4) & 0x0f0f0f0fu), x.hi[i].x, v);
-            v = __dp4a((int)(w[1] & 0x0f0f0f0fu), x.lo[i].y, v);
-            v = __dp4a((int)((w[1] >> 4) & 0x0f0f0f0fu), x.hi[i].y, v);
-            v = __dp4a((int)(w[2] & 0x0f0f0f0fu), x.lo[i].z, v);
-            v = __dp4a((int)((w[2] >> 4) & 0x0f0f0f0fu), x.hi[i].z, v);
-            v = __dp4a((int)(w[3] & 0x0f0f0f0fu), x.lo[i].w, v);
-            v = __dp4a((int)((w[3] >> 4) & 0x0f0f0f0fu), x.hi[i].w, v);
-            v -= x.s8[i];
+            int lo = -x.s8[i], hi = 0;  // the 8 x sum(x) offset of Q4_0's (q - 8) folded into the start
+            lo = __dp4a((int)(w[0] & 0x0f0f0f0fu), x.lo[i].x, lo);
+            hi = dp4a_us(w[0] & 0xf0f0f0f0u, x.hi[i].x, hi);
+            lo = __dp4a((int)(w[1] & 0x0f0f0f0fu), x.lo[i].y, lo);
+            hi = dp4a_us(w[1] & 0xf0f0f0f0u, x.hi[i].y, hi);
+            lo = __dp4a((int)(w[2] & 0x0f0f0f0fu), x.lo[i].z, lo);
+            hi = dp4a_us(w[2] & 0xf0f0f0f0u, x.hi[i].z, hi);
+            lo = __dp4a((int)(w[3] & 0x0f0f0f0fu), x.lo[i].w, lo);
+            hi = dp4a_us(w[3] & 0xf0f0f0f0u, x.hi[i].w, hi);
+            v = lo + (hi >> 4);
         } else {
             v = __dp4a(w0[i].x, x.lo[i].x, v);
             v = __dp4a(w0[i].y, x.lo[i].y, v);

@@ -20,6 +20,7 @@
 #include <string>
 
 #include "../gc_kernels.h"
+#include "gc_flash_dev.cuh"
 #include "gc_gemv_dev.cuh"
 
 namespace gcb {
@@ -35,10 +36,11 @@ constexpr int NCW = 8 * TEAMS;                // consumer warps
 constexpr int NCT = NCW * 32;                 // consumer threads
 constexpr int NTHREADS = NCT + 32;            // + producer warp
 constexpr int MAXNS = 32;
-constexpr int CH = 64;                        // attention chunk (keys)
+constexpr int CH = FL_CH;                     // attention chunk (keys)
 constexpr int MAXD = 128;  // decode kernel head sizes (larger heads use the per-op kernels)
 constexpr int WPH = 2;                        // warps per query head
 constexpr int MAXG = NCW / WPH;               // query heads per attention item pass
+constexpr int MAXGQ = 8;                      // query heads per K/V head (staging)
 constexpr size_t SMEM_LIMIT = 226 * 1024;     // dynamic shared memory (the opt-in 227 KB less the static part)
 
 __device__ __forceinline__ int ld_acquire(const int *p) {
@@ -70,161 +72,66 @@ __device__ inline bool grid_sync(int *ctr, int target, int *s_abort) {
     return *s_abort == 0;
 }
 
-// One attention item: chunk `ch` of K/V head `hk` for query row `iq` (split-KV flash attention).
-__device__ inline bool attn_item(const MegaAttn &at, int64_t iq, int64_t hk, int64_t ch, __half *Ks, __half *Vs,
-                                 float *sc, uint64_t *abar, uint32_t parity, int *s_last) {
-    const int D = (int)at.D, c = D / 32;
-    const int64_t j0 = ch * CH;
-    const int n = (int)min((int64_t)CH, at.nkv - j0);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t G = at.H / at.Hkv;
-    const int hw = warp / WPH, quarter = warp % WPH;
-    const float ninf = -__int_as_float(0x7f800000);
-    const int64_t nch = (at.nkv + CH - 1) / CH;
+// Named barrier of the consumer warps (the flash_chunk barrier of attention phases).
+struct SyncConsumers {
+    __device__ void operator()() const { named_bar(3, NCT); }
+};
 
+// One attention item: chunk `ch` of K/V head `hk` for query row `iq` (split-KV flash attention,
+// gc_flash_dev.cuh); the last item of a (query row, K/V head) merges its heads' chunks.
+__device__ inline bool attn_item(const MegaAttn &at, int iq, int hk, int ch, __half *Ks, __half *Vs, float *sc, float *ps,
+                                 float *qs, float *ms, uint64_t *abar, uint32_t parity, int *s_last) {
+    const int D = (int)at.D;
+    const int j0 = ch * CH;
+    const int n = (int)min((int64_t)CH, at.nkv - j0);
+    const int warp = threadIdx.x >> 5;
+    const int G = (int)(at.H / at.Hkv);
+    const int nch = (int)((at.nkv + CH - 1) / CH);
+
+    FlashChunk fc;
+    fc.q = (const char *)(at.q + iq * at.ldq + (int64_t)hk * G * D);
+    fc.qnb0 = 4;
+    fc.qnbh = 4 * (int64_t)D;
+    fc.mask = at.mask ? (const char *)(at.mask + iq * at.mask_ld + j0) : nullptr;
+    fc.mne2 = 1;
+    fc.mnbh = 0;
+    fc.hbase = hk * G;
+    fc.scale = at.scale;
+    fc.D = D;
+    fc.n = n;
+    fc.G = G;
+    fc.part = at.part + (((int64_t)iq * at.H + (int64_t)hk * G) * nch + ch) * (D + 2);
+    fc.pstride = (int64_t)nch * (D + 2);
     if (threadIdx.x == 0) {
         const uint32_t bytes = (uint32_t)(n * D * 2);
         mbar_expect_tx(abar, 2 * bytes);
-        bulk_g2s(Ks, at.k + hk * at.knb2 + j0 * at.knb1, bytes, abar);
-        bulk_g2s(Vs, at.v + hk * at.vnb2 + j0 * at.vnb1, bytes, abar);
-        *s_last = mbar_wait(abar, parity) ? 1 : 0;  // one bounded wait, its outcome shared
+        bulk_g2s(Ks, at.k + hk * at.knb2 + (int64_t)j0 * at.knb1, bytes, abar);
+        bulk_g2s(Vs, at.v + hk * at.vnb2 + (int64_t)j0 * at.vnb1, bytes, abar);
     }
+    flash_stage(fc, qs, ms, threadIdx.x, NCT);  // while the copies are in flight
+    named_bar(3, NCT);
+    if (threadIdx.x == 0) *s_last = mbar_wait(abar, parity) ? 1 : 0;  // one bounded wait, its outcome shared
     named_bar(3, NCT);
     if (!*s_last) return false;  // uniform: every consumer thread leaves here
 
-    for (int64_t g0 = 0; g0 < G; g0 += MAXG) {
-        const int64_t g = g0 + hw;
-        const bool active = g < G;
-        const int64_t h = hk * G + (active ? g : 0);
-        float *sh = sc + hw * CH;
-        float qv[MAXD / 32];
-        const float *qrow = at.q + iq * at.ldq + h * at.D;
-#pragma unroll
-        for (int e = 0; e < MAXD / 32; e++) qv[e] = e < c ? __half2float(__float2half_rn(qrow[lane * c + e])) : 0.0f;
-        const __half *mrow = at.mask ? at.mask + iq * at.mask_ld : nullptr;
-        for (int k0 = quarter * (CH / WPH); k0 < (quarter + 1) * (CH / WPH); k0 += 8) {
-            float p[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const int j = k0 + u;
-                float acc = 0.0f;
-                if (j < n) {
-                    const __half *kr = Ks + j * D + lane * c;
-#pragma unroll
-                    for (int e = 0; e < MAXD / 32; e++)
-                        if (e < c) acc = __fmaf_rn(qv[e], __half2float(kr[e]), acc);
-                }
-                p[u] = acc;
-            }
-#pragma unroll
-            for (int off = 16; off >= 1; off >>= 1)
-#pragma unroll
-                for (int u = 0; u < 8; u++) p[u] = __fadd_rn(p[u], __shfl_xor_sync(0xffffffffu, p[u], off));
-            if (lane < 8 && active) {
-                const int j = k0 + lane;
-                float pu = p[0];
-#pragma unroll
-                for (int u = 1; u < 8; u++)
-                    if (lane == u) pu = p[u];
-                float s = ninf;
-                if (j < n) {
-                    s = __fmul_rn(pu, at.scale);
-                    s = __fadd_rn(s, mrow ? __half2float(mrow[j0 + j]) : 0.0f);
-                }
-                sh[j] = s;
-            }
-        }
-        named_bar(3, NCT);
-        const float s0 = sh[lane], s1 = sh[lane + 32];
-        const float m = warp_max(fmaxf(s0, s1));
-        float *dst = at.part + (((iq * at.H + h) * nch + ch) * (at.D + 2));
-        if (active) {
-            if (m == ninf) {
-                if (quarter == 0 && lane == 0) {
-                    dst[0] = ninf;
-                    dst[1] = 0.0f;
-                }
-                for (int d = quarter * 32 + lane; d < D; d += WPH * 32) dst[2 + d] = 0.0f;
-            } else {
-                const float p0 = lane < n ? gc_expf(__fsub_rn(s0, m)) : 0.0f;
-                const float p1 = lane + 32 < n ? gc_expf(__fsub_rn(s1, m)) : 0.0f;
-                float l = 0.0f;
-                constexpr int OE = MAXD / 32 / WPH;
-                float o[OE];
-#pragma unroll
-                for (int e = 0; e < OE; e++) o[e] = 0.0f;
-                for (int j = 0; j < n; j++) {
-                    const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
-                    l = __fadd_rn(l, pj);
-                    const __half *vr = Vs + j * D;
-#pragma unroll
-                    for (int e = 0; e < OE; e++) {
-                        const int d = quarter * 32 + lane + e * WPH * 32;
-                        if (d < D) o[e] = __fmaf_rn(pj, __half2float(vr[d]), o[e]);
-                    }
-                }
-                if (quarter == 0 && lane == 0) {
-                    dst[0] = m;
-                    dst[1] = l;
-                }
-#pragma unroll
-                for (int e = 0; e < OE; e++) {
-                    const int d = quarter * 32 + lane + e * WPH * 32;
-                    if (d < D) dst[2 + d] = o[e];
-                }
-            }
-        }
-        named_bar(3, NCT);
-    }
+    flash_chunk<WPH, MAXD>(fc, Ks, Vs, qs, ms, sc, ps, NCW / WPH, SyncConsumers());
 
     // the last item of this (query row, K/V head) merges its heads' chunks in chunk order
-    __threadfence();
     named_bar(3, NCT);
     if (threadIdx.x == 0) {
+        __threadfence();
         int *cnt = at.counters + iq * at.Hkv + hk;
-        *s_last = atomicAdd(cnt, 1) == (int)nch - 1;
-        if (*s_last) *cnt = 0;
+        *s_last = atomicAdd(cnt, 1) == nch - 1;
+        if (*s_last) {
+            *cnt = 0;
+            __threadfence();
+        }
     }
     named_bar(3, NCT);
     if (!*s_last) return true;
-    __threadfence();
-    for (int64_t g = warp; g < G; g += NCW) {
-        const int64_t h = hk * G + g;
-        const float *pp = at.part + ((iq * at.H + h) * nch) * (at.D + 2);
-        float M = ninf;
-        for (int64_t c0 = 0; c0 < nch; c0 += 32)
-            if (c0 + lane < nch) M = fmaxf(M, __ldcg(pp + (c0 + lane) * (at.D + 2)));
-        M = warp_max(M);
-        constexpr int BATCH = 8;
-        float L = 0.0f, O[MAXD / 32];
-#pragma unroll
-        for (int e = 0; e < MAXD / 32; e++) O[e] = 0.0f;
-        for (int64_t c0 = 0; c0 < nch; c0 += BATCH) {
-            float bm[BATCH], bl[BATCH], bo[BATCH][MAXD / 32];
-#pragma unroll
-            for (int u = 0; u < BATCH; u++) {
-                const bool ok = c0 + u < nch;
-                const float *pc = pp + (c0 + u) * (at.D + 2);
-                bm[u] = ok ? __ldcg(pc) : ninf;
-                bl[u] = ok ? __ldcg(pc + 1) : 0.0f;
-#pragma unroll
-                for (int e = 0; e < MAXD / 32; e++) bo[u][e] = (ok && e < c) ? __ldcg(pc + 2 + lane * c + e) : 0.0f;
-            }
-#pragma unroll
-            for (int u = 0; u < BATCH; u++) {
-                if (bm[u] == ninf) continue;
-                const float wgt = gc_expf(__fsub_rn(bm[u], M));
-                L = __fmaf_rn(wgt, bl[u], L);
-#pragma unroll
-                for (int e = 0; e < MAXD / 32; e++)
-                    if (e < c) O[e] = __fmaf_rn(wgt, bo[u][e], O[e]);
-            }
-        }
-        const float inv = L == 0.0f ? 0.0f : __fdiv_rn(1.0f, L);
-        float *orow = at.out + at.D * (h + at.H * iq);
-#pragma unroll
-        for (int e = 0; e < MAXD / 32; e++)
-            if (e < c) orow[lane * c + e] = __fmul_rn(O[e], inv);
+    for (int g = warp; g < G; g += NCW) {
+        const int64_t h = (int64_t)hk * G + g;
+        flash_merge<MAXD>(at.part + ((iq * at.H + h) * nch) * (D + 2), nch, D, at.out + at.D * (h + at.H * iq));
     }
     return true;
 }
@@ -243,7 +150,10 @@ __global__ void __maxnreg__(168) mega_kernel(const MegaPhase *phases, int nph, i
     __half *Ks = (__half *)((unsigned char *)sq + act_bytes);
     __half *Vs = Ks + CH * attn_d;
     float *sc = (float *)(Vs + CH * attn_d);
-    unsigned char *slots = (unsigned char *)(sc + MAXG * CH);
+    float *ps = sc + MAXG * CH;  // [NCW][CH] attention probabilities
+    float *qs = ps + NCW * CH;   // [MAXGQ][MAXD] query rows
+    float *ms = qs + MAXGQ * MAXD;  // [MAXGQ][CH] mask values
+    unsigned char *slots = (unsigned char *)(ms + MAXGQ * CH);
     __shared__ int s_abort, s_last;
     const Ring R{full, empty, slots, log2ns, slot_bytes};
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -312,7 +222,7 @@ __global__ void __maxnreg__(168) mega_kernel(const MegaPhase *phases, int nph, i
             bool ok = !skip;
             for (int64_t i = cta; i < items && ok; i += nctas) {
                 const int64_t ch = i % nch, hk = (i / nch) % at.Hkv, iq = i / (nch * at.Hkv);
-                ok = attn_item(at, iq, hk, ch, Ks, Vs, sc, abar, aphase & 1, &s_last);
+                ok = attn_item(at, (int)iq, (int)hk, (int)ch, Ks, Vs, sc, ps, qs, ms, abar, aphase & 1, &s_last);
                 aphase++;
                 named_bar(3, NCT);  // the K/V staging area is free again
             }
@@ -335,7 +245,8 @@ void launch(const MegaPhase *phases, int nph, int64_t kmax, int attn_d, int64_t 
         attr = true;
     }
     const size_t act = gemv_act_bytes(M, kmax);
-    const size_t head = (size_t)(2 * MAXNS + 2) * 8 + 256 * 8 + act + (size_t)CH * attn_d * 4 + (size_t)MAXG * CH * 4;
+    const size_t head = (size_t)(2 * MAXNS + 2) * 8 + 256 * 8 + act + (size_t)CH * attn_d * 4 + (size_t)(MAXG + NCW) * CH * 4 +
+                        (size_t)MAXGQ * (MAXD + CH) * 4;
     const int log2ns = ring_log2(SMEM_LIMIT, head, (size_t)slot_bytes, MAXNS);
     if ((1 << log2ns) < 4) throw std::runtime_error("decode kernel: shared memory too small for the weight ring");
     const size_t smem = head + ((size_t)1 << log2ns) * (size_t)slot_bytes;
@@ -368,7 +279,8 @@ bool mega_supported(int qtype, int M, int64_t kmax, int attn_d) {
     if (M != 1 || (qtype != T_Q4_0 && qtype != T_Q8_0) || attn_d > MAXD || attn_d % 32) return false;
     const int64_t slot = (int64_t)QTR * QSEG * ((qtype == T_Q4_0 ? 16 : 32) + 2);
     const size_t head = (size_t)(2 * MAXNS + 2) * 8 + 256 * 8 + gemv_act_bytes(M, kmax) + (size_t)CH * attn_d * 4 +
-                        (size_t)MAXG * CH * 4;
+                        (size_t)(MAXG + NCW) * CH * 4 +
+                        (size_t)MAXGQ * (MAXD + CH) * 4;
     const int log2ns = ring_log2(SMEM_LIMIT, head, (size_t)slot, MAXNS);
     if ((1 << log2ns) < 4) return false;
     const size_t smem = head + ((size_t)1 << log2ns) * (size_t)slot;
