@@ -63,6 +63,10 @@ void rope_norm(const TD &x, const TD &pos, const TD &out, int n_dims, const floa
 void get_rows(const TD &table, const TD &idx, const TD &out, cudaStream_t s);
 void set_rows(const TD &dst, const TD &src, const TD &idx, int *err, cudaStream_t s);
 void argmax(const TD &x, const TD &out, cudaStream_t s);
+// Long f32 rows: slices per row (0: use argmax), then the split form with scratch of rows x parts
+// float2 pairs and rows zeroed counters (reset by the kernel).
+int argmax_split_parts(const TD &x);
+void argmax_split(const TD &x, const TD &out, void *scratch, int *counters, cudaStream_t s);
 void swiglu(const TD &g, const TD &u, const TD &out, cudaStream_t s);
 void sum_rows(const TD &x, const TD &out, float scale, cudaStream_t s);  // scale = 1/n for mean
 void repeat(const TD &x, const TD &out, cudaStream_t s);

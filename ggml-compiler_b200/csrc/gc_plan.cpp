@@ -457,6 +457,15 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
         if (x.ne[2] != 1 || x.ne[3] != 1) fail(n, "argmax needs a matrix, got " + shape_str(x.ne));
         int64_t ne[4] = {x.ne[1], 1, 1, 1};
         TD y = out_like(T_I32, ne);
+        if (const int parts = k::argmax_split_parts(x)) {
+            TD scratch;
+            scratch_marker((size_t)x.nrows() * parts * 8, &scratch);
+            int *cnt = m.counters(s.name + "/" + n.id, (size_t)x.nrows());
+            add("argmax", n.id, {x, y, scratch},
+                [cnt](cudaStream_t st, const std::vector<TD> &t) { k::argmax_split(t[0], t[1], t[2].data, cnt, st); },
+                (double)(x.nelements() * 4));
+            return y;
+        }
         add("argmax", n.id, {x, y}, [](cudaStream_t st, const std::vector<TD> &t) { k::argmax(t[0], t[1], st); },
             (double)(x.nelements() * 4));
         return y;

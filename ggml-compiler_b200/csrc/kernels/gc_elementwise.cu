@@ -2,6 +2,7 @@
 // binary ops, unary ops, row norms, softmax, rope, row gather/scatter, argmax, swiglu and a few
 // layout ops. Every kernel takes strided views (ggml's ne/nb). The reductions follow the fixed
 // orders the CPU checker restates (see gc_math.cuh), so results do not depend on the launch shape.
+#include <algorithm>
 #include <cstdio>
 #include <stdexcept>
 #include <string>
@@ -414,6 +415,67 @@ __global__ void argmax_kernel(Dk x, Dk out) {
     }
 }
 
+// argmax of long rows over `gridDim.x` CTAs per row: each CTA reduces one slice of f32 elements
+// (contiguous rows) to its (max, first index) pair, and the last CTA of the row to finish combines
+// the pairs in slice order with the same rule, so the result is the first index of the maximum.
+__global__ void argmax_split_kernel(const float *x, int64_t ne0, int64_t ld, int32_t *out, float2 *part, int *counters) {
+    __shared__ float sv[32];
+    __shared__ int32_t si[32];
+    __shared__ int last;
+    const int64_t row = blockIdx.y, P = gridDim.x, p = blockIdx.x;
+    const int64_t chunk = (ne0 + P - 1) / P, i0 = p * chunk, i1 = min(ne0, i0 + chunk);
+    const float *xr = x + row * ld;
+    float best = -__int_as_float(0x7f800000);
+    int32_t bi = 0x7fffffff;
+    for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        const float v = xr[i];
+        if (v > best || (v == best && (int32_t)i < bi)) {
+            best = v;
+            bi = (int32_t)i;
+        }
+    }
+    for (int off = 16; off >= 1; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+        const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+        }
+    }
+    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        sv[w] = best;
+        si[w] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < nw; k++)
+            if (sv[k] > best || (sv[k] == best && si[k] < bi)) {
+                best = sv[k];
+                bi = si[k];
+            }
+        part[row * P + p] = make_float2(best, __int_as_float(bi));
+        __threadfence();
+        last = atomicAdd(&counters[row], 1) == (int)P - 1;
+        if (last) {
+            counters[row] = 0;
+            __threadfence();
+            best = -__int_as_float(0x7f800000);
+            bi = 0x7fffffff;
+            for (int64_t k = 0; k < P; k++) {
+                const float2 q = __ldcg(&part[row * P + k]);
+                const int32_t qi = __float_as_int(q.y);
+                if (q.x > best || (q.x == best && qi < bi)) {
+                    best = q.x;
+                    bi = qi;
+                }
+            }
+            if (bi == 0x7fffffff) bi = 0;
+            out[row] = bi;
+        }
+    }
+}
+
 __global__ void swiglu_kernel(Dk g, Dk u, Dk out, int64_t n) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const float a = ldf(at_lin(g, i), g.type), b = ldf(at_lin(u, i), u.type);
@@ -561,6 +623,18 @@ void set_rows(const TD &dst, const TD &src, const TD &idx, int *err, cudaStream_
 void argmax(const TD &x, const TD &out, cudaStream_t s) {
     argmax_kernel<<<(unsigned)x.nrows(), 1024, 0, s>>>(dk(x), dk(out));
     check_launch("argmax");
+}
+
+int argmax_split_parts(const TD &x) {
+    if (x.type != T_F32 || x.nb[0] != 4 || !x.contiguous() || x.ne[0] < 16384) return 0;
+    return (int)std::min<int64_t>(128, (x.ne[0] + 4095) / 4096);
+}
+
+void argmax_split(const TD &x, const TD &out, void *scratch, int *counters, cudaStream_t s) {
+    const int P = argmax_split_parts(x);
+    argmax_split_kernel<<<dim3((unsigned)P, (unsigned)x.nrows()), 256, 0, s>>>((const float *)x.data, x.ne[0], x.nb[1] / 4,
+                                                                               (int32_t *)out.data, (float2 *)scratch, counters);
+    check_launch("argmax_split");
 }
 
 void swiglu(const TD &g, const TD &u, const TD &out, cudaStream_t s) {

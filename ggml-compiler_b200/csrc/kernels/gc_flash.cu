@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
         __syncthreads();
     }
     const int nslots = (int)(blockDim.x / 32) / WPH;
-    flash_chunk<WPH, MAXD>(fc, Ks, Vs, qs, ms, sc, ps, nslots, SyncCta());
+    flash_chunk<WPH, MAXD>(fc, Ks, Vs, qs, ms, sc, ps, nslots, SyncCta());  // MAXD is the head size
 
     // the last CTA of this (batch, query row, K/V head) merges every chunk of its heads
     __syncthreads();
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
     if (!last) return;
     for (int64_t g = warp; g < G; g += blockDim.x / 32) {
         const int64_t h = hk * G + g;
-        flash_merge<MAXD>(a.part + (((b * a.Sq + iq) * a.H + h) * a.nch) * (a.D + 2), (int)a.nch, D,
+        flash_merge<MAXD>(a.part + (((b * a.Sq + iq) * a.H + h) * a.nch) * (a.D + 2), (int)a.nch,
                           a.out + a.D * (h + a.H * (iq + a.Sq * b)));
     }
 }
@@ -194,13 +194,19 @@ void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, co
     const int threads = hslots * WPH * 32;
     const size_t smem = (size_t)CH * a.D * 2 * 2 + (size_t)MAXG * CH * 4 + (size_t)MAXG * WPH * CH * 4 +
                         (size_t)G * (a.D + CH) * 4;
-    auto kern = a.D <= 128 ? flash_split_kernel<128> : flash_split_kernel<MAXD_ALL>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(flash_split_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        cudaFuncSetAttribute(flash_split_kernel<MAXD_ALL>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr_set = true;
+    void (*kern)(SplitArgs) = nullptr;  // one instantiation per head size
+    switch (a.D) {
+        case 32: kern = flash_split_kernel<32>; break;
+        case 64: kern = flash_split_kernel<64>; break;
+        case 96: kern = flash_split_kernel<96>; break;
+        case 128: kern = flash_split_kernel<128>; break;
+        case 160: kern = flash_split_kernel<160>; break;
+        case 192: kern = flash_split_kernel<192>; break;
+        case 224: kern = flash_split_kernel<224>; break;
+        case 256: kern = flash_split_kernel<256>; break;
+        default: throw std::runtime_error("flash_split: head size must be a multiple of 32 up to 256");
     }
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     const int64_t Sq = q.ne[1];
     const size_t per_row = (size_t)(a.H * a.B * a.nch * (a.D + 2)) * 4;
     const int64_t rows_per = std::max<int64_t>(1, (int64_t)(kMaxPartBytes / per_row));

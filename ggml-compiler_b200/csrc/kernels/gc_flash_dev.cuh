@@ -49,27 +49,48 @@ __device__ inline void flash_stage(const FlashChunk &c, float *qs, float *ms, in
     }
 }
 
+// The lane's D/32 consecutive key elements (f16 in shared memory) as floats.
+template <int CPL>
+__device__ __forceinline__ void load_krow(const __half *kr, float (&kv)[CPL]) {
+    if constexpr (CPL == 2) {
+        const float2 f = __half22float2(*(const __half2 *)kr);
+        kv[0] = f.x;
+        kv[1] = f.y;
+    } else if constexpr (CPL == 4) {
+        const uint2 u = *(const uint2 *)kr;
+        const float2 a = __half22float2(*(const __half2 *)&u.x), b = __half22float2(*(const __half2 *)&u.y);
+        kv[0] = a.x;
+        kv[1] = a.y;
+        kv[2] = b.x;
+        kv[3] = b.y;
+    } else {
+#pragma unroll
+        for (int e = 0; e < CPL; e++) kv[e] = __half2float(kr[e]);
+    }
+}
+
 // The chunk's K and V rows are in shared memory (Ks, Vs: [n][D] halves), the query rows and mask
 // values staged by flash_stage (qs, ms). `nslots` head slots of WPH warps each (warps 0 ..
 // nslots*WPH-1 call this); sc: [nslots][FL_CH] scores, ps: [warps][FL_CH] probabilities. `bar`
-// synchronises those warps.
-template <int WPH, int MAXD, class Bar>
+// synchronises those warps. D (head size) is a multiple of 32.
+template <int WPH, int D, class Bar>
 __device__ inline void flash_chunk(const FlashChunk &c, const __half *Ks, const __half *Vs, const float *qs,
                                    const float *ms, float *sc, float *ps, int nslots, Bar bar) {
-    const int D = c.D, cpl = D / 32, n = c.n;
+    constexpr int CPL = D / 32;                                     // elements of a lane in a dot
+    constexpr int OE = D / 32 / WPH > 0 ? D / 32 / WPH : 1;         // output elements per lane
+    const int n = c.n;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int hw = warp / WPH, quarter = warp % WPH;
     const float ninf = -__int_as_float(0x7f800000);
-    constexpr int OE = MAXD / 32 / WPH > 0 ? MAXD / 32 / WPH : 1;  // output elements per lane
 
     for (int g0 = 0; g0 < c.G; g0 += nslots) {
         const int g = g0 + hw;
         const bool active = g < c.G;
         const int gg = active ? g : 0;
         float *sh = sc + hw * FL_CH;
-        float qv[MAXD / 32];
+        float qv[CPL];
 #pragma unroll
-        for (int e = 0; e < MAXD / 32; e++) qv[e] = e < cpl ? qs[gg * D + lane * cpl + e] : 0.0f;
+        for (int e = 0; e < CPL; e++) qv[e] = qs[gg * D + lane * CPL + e];
         const float *mrow = ms + gg * FL_CH;
         // scores: this warp's CH/WPH keys, 8 at a time
         for (int k0 = quarter * (FL_CH / WPH); k0 < (quarter + 1) * (FL_CH / WPH); k0 += 8) {
@@ -79,10 +100,10 @@ __device__ inline void flash_chunk(const FlashChunk &c, const __half *Ks, const 
                 const int j = k0 + u;
                 float acc = 0.0f;
                 if (j < n) {
-                    const __half *kr = Ks + j * D + lane * cpl;
+                    float kv[CPL];
+                    load_krow<CPL>(Ks + j * D + lane * CPL, kv);
 #pragma unroll
-                    for (int e = 0; e < MAXD / 32; e++)
-                        if (e < cpl) acc = __fmaf_rn(qv[e], __half2float(kr[e]), acc);
+                    for (int e = 0; e < CPL; e++) acc = __fmaf_rn(qv[e], kv[e], acc);
                 }
                 p[u] = acc;
             }
@@ -124,15 +145,19 @@ __device__ inline void flash_chunk(const FlashChunk &c, const __half *Ks, const 
                 float l = 0.0f, o[OE];
 #pragma unroll
                 for (int e = 0; e < OE; e++) o[e] = 0.0f;
-#pragma unroll 8
-                for (int j = 0; j < n; j++) {
-                    const float pj = pw[j];
-                    l = __fadd_rn(l, pj);
-                    const __half *vr = Vs + j * D;
+                const __half *vcol = Vs + quarter * 32 + lane;
+                // keys in order, four probabilities per (broadcast) load; p = 0 past the chunk's end
+                for (int j0 = 0; j0 < n; j0 += 4) {
+                    const float4 p4 = *(const float4 *)(pw + j0);
+                    const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
-                    for (int e = 0; e < OE; e++) {
-                        const int d = quarter * 32 + lane + e * WPH * 32;
-                        if (d < D) o[e] = __fmaf_rn(pj, __half2float(vr[d]), o[e]);
+                    for (int u = 0; u < 4; u++) {
+                        if (j0 + u >= n) break;
+                        l = __fadd_rn(l, pj[u]);
+                        const __half *vr = vcol + (j0 + u) * D;
+#pragma unroll
+                        for (int e = 0; e < OE; e++)
+                            if (D >= WPH * 32 || quarter * 32 < D) o[e] = __fmaf_rn(pj[u], __half2float(vr[e * WPH * 32]), o[e]);
                     }
                 }
                 if (quarter == 0 && lane == 0) {
@@ -140,10 +165,8 @@ __device__ inline void flash_chunk(const FlashChunk &c, const __half *Ks, const 
                     dst[1] = l;
                 }
 #pragma unroll
-                for (int e = 0; e < OE; e++) {
-                    const int d = quarter * 32 + lane + e * WPH * 32;
-                    if (d < D) dst[2 + d] = o[e];
-                }
+                for (int e = 0; e < OE; e++)
+                    if (D >= WPH * 32 || quarter * 32 < D) dst[2 + quarter * 32 + lane + e * WPH * 32] = o[e];
             }
         }
         bar();
@@ -158,8 +181,9 @@ struct SyncCta {
 // One warp: merge head partials pp[c * (D + 2)], c < nch, in chunk order into orow[D]. The
 // partials were written by other CTAs: they are read from L2 (ld.global.cg), all of a batch of
 // chunks at once.
-template <int MAXD>
-__device__ inline void flash_merge(const float *pp, int nch, int D, float *orow) {
+template <int D>
+__device__ inline void flash_merge(const float *pp, int nch, float *orow) {
+    constexpr int MAXD = D;
     const int lane = threadIdx.x & 31, cpl = D / 32;
     const float ninf = -__int_as_float(0x7f800000);
     constexpr int BATCH = MAXD <= 128 ? 16 : 8;  // chunks fetched at once (registers: BATCH x MAXD/32)

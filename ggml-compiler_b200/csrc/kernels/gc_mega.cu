@@ -114,7 +114,8 @@ __device__ inline bool attn_item(const MegaAttn &at, int iq, int hk, int ch, __h
     named_bar(3, NCT);
     if (!*s_last) return false;  // uniform: every consumer thread leaves here
 
-    flash_chunk<WPH, MAXD>(fc, Ks, Vs, qs, ms, sc, ps, NCW / WPH, SyncConsumers());
+    if (D == 128) flash_chunk<WPH, 128>(fc, Ks, Vs, qs, ms, sc, ps, NCW / WPH, SyncConsumers());
+    else flash_chunk<WPH, 64>(fc, Ks, Vs, qs, ms, sc, ps, NCW / WPH, SyncConsumers());
 
     // the last item of this (query row, K/V head) merges its heads' chunks in chunk order
     named_bar(3, NCT);
@@ -131,7 +132,8 @@ __device__ inline bool attn_item(const MegaAttn &at, int iq, int hk, int ch, __h
     if (!*s_last) return true;
     for (int g = warp; g < G; g += NCW) {
         const int64_t h = (int64_t)hk * G + g;
-        flash_merge<MAXD>(at.part + ((iq * at.H + h) * nch) * (D + 2), nch, D, at.out + at.D * (h + at.H * iq));
+        if (D == 128) flash_merge<128>(at.part + ((iq * at.H + h) * nch) * (D + 2), nch, at.out + at.D * (h + at.H * iq));
+        else flash_merge<64>(at.part + ((iq * at.H + h) * nch) * (D + 2), nch, at.out + at.D * (h + at.H * iq));
     }
     return true;
 }
@@ -276,7 +278,7 @@ bool resident(size_t smem) {
 }
 
 bool mega_supported(int qtype, int M, int64_t kmax, int attn_d) {
-    if (M != 1 || (qtype != T_Q4_0 && qtype != T_Q8_0) || attn_d > MAXD || attn_d % 32) return false;
+    if (M != 1 || (qtype != T_Q4_0 && qtype != T_Q8_0) || (attn_d != 0 && attn_d != 64 && attn_d != 128)) return false;
     const int64_t slot = (int64_t)QTR * QSEG * ((qtype == T_Q4_0 ? 16 : 32) + 2);
     const size_t head = (size_t)(2 * MAXNS + 2) * 8 + 256 * 8 + gemv_act_bytes(M, kmax) + (size_t)CH * attn_d * 4 +
                         (size_t)(MAXG + NCW) * CH * 4 +
