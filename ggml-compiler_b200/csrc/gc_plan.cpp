@@ -71,7 +71,7 @@ bool attn_phase(const std::vector<TD> &t, float scale, int *counters, MegaPhase 
     const int64_t D = q.ne[0];
     if (q.ne[1] != 1 || q.ne[3] != 1 || q.nb[0] != 4 || q.nb[2] != 4 * D || !y.contiguous()) return false;
     if (kk.nb[1] != 2 * D || v.nb[1] != 2 * D || kk.ne[3] != 1 || mk.ne[2] != 1 || mk.ne[3] != 1) return false;
-    if (q.ne[2] % kk.ne[2] || q.ne[2] / kk.ne[2] > 8) return false;  // up to 8 query heads per K/V head
+    if (q.ne[2] % kk.ne[2] || q.ne[2] / kk.ne[2] > 4) return false;  // up to 4 query heads per K/V head
     if (((uintptr_t)kk.data | (uintptr_t)v.data | (uintptr_t)kk.nb[2] | (uintptr_t)v.nb[2]) % 16) return false;
     ph.type = 1;
     MegaAttn &a = ph.at;

@@ -69,106 +69,130 @@ __device__ __forceinline__ void load_krow(const __half *kr, float (&kv)[CPL]) {
     }
 }
 
-// The chunk's K and V rows are in shared memory (Ks, Vs: [n][D] halves), the query rows and mask
-// values staged by flash_stage (qs, ms). `nslots` head slots of WPH warps each (warps 0 ..
-// nslots*WPH-1 call this); sc: [nslots][FL_CH] scores, ps: [warps][FL_CH] probabilities. `bar`
-// synchronises those warps. D (head size) is a multiple of 32.
+// Scores of head-slot pass g0 against the chunk's K rows (Ks: [n][D] halves in shared memory), then
+// each active warp's copy of the chunk's probabilities (ps). The query rows and mask values were
+// staged by flash_stage (qs, ms). `nslots` head slots of WPH warps each (warps 0 .. nslots*WPH-1
+// call this); sc: [nslots][FL_CH] scores, ps: [warps][FL_CH]. `bar` synchronises those warps; Ks is
+// no longer read once this returns. D (head size) is a multiple of 32.
 template <int WPH, int D, class Bar>
-__device__ inline void flash_chunk(const FlashChunk &c, const __half *Ks, const __half *Vs, const float *qs,
-                                   const float *ms, float *sc, float *ps, int nslots, Bar bar) {
-    constexpr int CPL = D / 32;                                     // elements of a lane in a dot
-    constexpr int OE = D / 32 / WPH > 0 ? D / 32 / WPH : 1;         // output elements per lane
+__device__ inline void flash_scores(const FlashChunk &c, const __half *Ks, const float *qs, const float *ms, float *sc,
+                                    float *ps, int g0, int nslots, Bar bar) {
+    constexpr int CPL = D / 32;  // elements of a lane in a dot
     const int n = c.n;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int hw = warp / WPH, quarter = warp % WPH;
     const float ninf = -__int_as_float(0x7f800000);
+    const int g = g0 + hw;
+    const bool active = g < c.G;
+    const int gg = active ? g : 0;
+    float *sh = sc + hw * FL_CH;
+    float qv[CPL];
+#pragma unroll
+    for (int e = 0; e < CPL; e++) qv[e] = qs[gg * D + lane * CPL + e];
+    const float *mrow = ms + gg * FL_CH;
+    // this warp's CH/WPH keys, 8 at a time
+    for (int k0 = quarter * (FL_CH / WPH); k0 < (quarter + 1) * (FL_CH / WPH); k0 += 8) {
+        float p[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int j = k0 + u;
+            float acc = 0.0f;
+            if (j < n) {
+                float kv[CPL];
+                load_krow<CPL>(Ks + j * D + lane * CPL, kv);
+#pragma unroll
+                for (int e = 0; e < CPL; e++) acc = __fmaf_rn(qv[e], kv[e], acc);
+            }
+            p[u] = acc;
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+            for (int u = 0; u < 8; u++) p[u] = __fadd_rn(p[u], __shfl_xor_sync(0xffffffffu, p[u], off));
+        if (lane < 8 && active) {
+            const int j = k0 + lane;
+            float pu = p[0];
+#pragma unroll
+            for (int u = 1; u < 8; u++)
+                if (lane == u) pu = p[u];
+            float s = ninf;
+            if (j < n) {
+                s = __fmul_rn(pu, c.scale);
+                s = __fadd_rn(s, mrow[j]);
+            }
+            sh[j] = s;
+        }
+    }
+    bar();
+    // chunk max and weights (every warp of the head computes the same values)
+    const float s0 = sh[lane], s1 = sh[lane + 32];
+    const float m = warp_max(fmaxf(s0, s1));
+    if (active && m != ninf) {
+        float *pw = ps + warp * FL_CH;
+        pw[lane] = lane < n ? gc_expf(__fsub_rn(s0, m)) : 0.0f;
+        pw[lane + 32] = lane + 32 < n ? gc_expf(__fsub_rn(s1, m)) : 0.0f;
+    }
+    __syncwarp();
+}
 
+// The chunk partial (m, l, o) of head-slot pass g0 from its scores (sc) and this warp's
+// probabilities (ps) against the chunk's V rows (Vs: [n][D] halves in shared memory). Per warp: no
+// barrier inside.
+template <int WPH, int D>
+__device__ inline void flash_values(const FlashChunk &c, const __half *Vs, const float *sc, const float *ps, int g0) {
+    constexpr int OE = D / 32 / WPH > 0 ? D / 32 / WPH : 1;  // output elements per lane
+    const int n = c.n;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hw = warp / WPH, quarter = warp % WPH;
+    const float ninf = -__int_as_float(0x7f800000);
+    const int g = g0 + hw;
+    if (g >= c.G) return;
+    const float *sh = sc + hw * FL_CH;
+    const float m = warp_max(fmaxf(sh[lane], sh[lane + 32]));
+    float *dst = c.part + g * c.pstride;
+    if (m == ninf) {
+        if (quarter == 0 && lane == 0) {
+            dst[0] = ninf;
+            dst[1] = 0.0f;
+        }
+        for (int d = quarter * 32 + lane; d < D; d += WPH * 32) dst[2 + d] = 0.0f;
+        return;
+    }
+    const float *pw = ps + warp * FL_CH;
+    float l = 0.0f, o[OE];
+#pragma unroll
+    for (int e = 0; e < OE; e++) o[e] = 0.0f;
+    const __half *vcol = Vs + quarter * 32 + lane;
+    // keys in order, four probabilities per (broadcast) load; p = 0 past the chunk's end
+    for (int j0 = 0; j0 < n; j0 += 4) {
+        const float4 p4 = *(const float4 *)(pw + j0);
+        const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            if (j0 + u >= n) break;
+            l = __fadd_rn(l, pj[u]);
+            const __half *vr = vcol + (j0 + u) * D;
+#pragma unroll
+            for (int e = 0; e < OE; e++)
+                if (D >= WPH * 32 || quarter * 32 < D) o[e] = __fmaf_rn(pj[u], __half2float(vr[e * WPH * 32]), o[e]);
+        }
+    }
+    if (quarter == 0 && lane == 0) {
+        dst[0] = m;
+        dst[1] = l;
+    }
+#pragma unroll
+    for (int e = 0; e < OE; e++)
+        if (D >= WPH * 32 || quarter * 32 < D) dst[2 + quarter * 32 + lane + e * WPH * 32] = o[e];
+}
+
+// Both halves with K and V resident together (Ks, Vs), every head of the group.
+template <int WPH, int D, class Bar>
+__device__ inline void flash_chunk(const FlashChunk &c, const __half *Ks, const __half *Vs, const float *qs,
+                                   const float *ms, float *sc, float *ps, int nslots, Bar bar) {
     for (int g0 = 0; g0 < c.G; g0 += nslots) {
-        const int g = g0 + hw;
-        const bool active = g < c.G;
-        const int gg = active ? g : 0;
-        float *sh = sc + hw * FL_CH;
-        float qv[CPL];
-#pragma unroll
-        for (int e = 0; e < CPL; e++) qv[e] = qs[gg * D + lane * CPL + e];
-        const float *mrow = ms + gg * FL_CH;
-        // scores: this warp's CH/WPH keys, 8 at a time
-        for (int k0 = quarter * (FL_CH / WPH); k0 < (quarter + 1) * (FL_CH / WPH); k0 += 8) {
-            float p[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const int j = k0 + u;
-                float acc = 0.0f;
-                if (j < n) {
-                    float kv[CPL];
-                    load_krow<CPL>(Ks + j * D + lane * CPL, kv);
-#pragma unroll
-                    for (int e = 0; e < CPL; e++) acc = __fmaf_rn(qv[e], kv[e], acc);
-                }
-                p[u] = acc;
-            }
-#pragma unroll
-            for (int off = 16; off >= 1; off >>= 1)
-#pragma unroll
-                for (int u = 0; u < 8; u++) p[u] = __fadd_rn(p[u], __shfl_xor_sync(0xffffffffu, p[u], off));
-            if (lane < 8 && active) {
-                const int j = k0 + lane;
-                float pu = p[0];
-#pragma unroll
-                for (int u = 1; u < 8; u++)
-                    if (lane == u) pu = p[u];
-                float s = ninf;
-                if (j < n) {
-                    s = __fmul_rn(pu, c.scale);
-                    s = __fadd_rn(s, mrow[j]);
-                }
-                sh[j] = s;
-            }
-        }
-        bar();
-        // chunk max and weights (every warp of the head computes the same values)
-        const float s0 = sh[lane], s1 = sh[lane + 32];
-        const float m = warp_max(fmaxf(s0, s1));
-        float *dst = c.part + gg * c.pstride;
-        if (active) {
-            if (m == ninf) {
-                if (quarter == 0 && lane == 0) {
-                    dst[0] = ninf;
-                    dst[1] = 0.0f;
-                }
-                for (int d = quarter * 32 + lane; d < D; d += WPH * 32) dst[2 + d] = 0.0f;
-            } else {
-                float *pw = ps + warp * FL_CH;  // this warp's copy of the chunk's probabilities
-                pw[lane] = lane < n ? gc_expf(__fsub_rn(s0, m)) : 0.0f;
-                pw[lane + 32] = lane + 32 < n ? gc_expf(__fsub_rn(s1, m)) : 0.0f;
-                __syncwarp();
-                float l = 0.0f, o[OE];
-#pragma unroll
-                for (int e = 0; e < OE; e++) o[e] = 0.0f;
-                const __half *vcol = Vs + quarter * 32 + lane;
-                // keys in order, four probabilities per (broadcast) load; p = 0 past the chunk's end
-                for (int j0 = 0; j0 < n; j0 += 4) {
-                    const float4 p4 = *(const float4 *)(pw + j0);
-                    const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        if (j0 + u >= n) break;
-                        l = __fadd_rn(l, pj[u]);
-                        const __half *vr = vcol + (j0 + u) * D;
-#pragma unroll
-                        for (int e = 0; e < OE; e++)
-                            if (D >= WPH * 32 || quarter * 32 < D) o[e] = __fmaf_rn(pj[u], __half2float(vr[e * WPH * 32]), o[e]);
-                    }
-                }
-                if (quarter == 0 && lane == 0) {
-                    dst[0] = m;
-                    dst[1] = l;
-                }
-#pragma unroll
-                for (int e = 0; e < OE; e++)
-                    if (D >= WPH * 32 || quarter * 32 < D) dst[2 + quarter * 32 + lane + e * WPH * 32] = o[e];
-            }
-        }
+        flash_scores<WPH, D>(c, Ks, qs, ms, sc, ps, g0, nslots, bar);
+        flash_values<WPH, D>(c, Vs, sc, ps, g0);
         bar();
     }
 }
@@ -181,12 +205,11 @@ struct SyncCta {
 // One warp: merge head partials pp[c * (D + 2)], c < nch, in chunk order into orow[D]. The
 // partials were written by other CTAs: they are read from L2 (ld.global.cg), all of a batch of
 // chunks at once.
-template <int D>
+template <int D, int BATCH = (D <= 128 ? 16 : 8)>  // BATCH: chunks fetched at once (registers: BATCH x D/32)
 __device__ inline void flash_merge(const float *pp, int nch, float *orow) {
     constexpr int MAXD = D;
     const int lane = threadIdx.x & 31, cpl = D / 32;
     const float ninf = -__int_as_float(0x7f800000);
-    constexpr int BATCH = MAXD <= 128 ? 16 : 8;  // chunks fetched at once (registers: BATCH x MAXD/32)
     float M = ninf, L = 0.0f, O[MAXD / 32];
 #pragma unroll
     for (int e = 0; e < MAXD / 32; e++) O[e] = 0.0f;

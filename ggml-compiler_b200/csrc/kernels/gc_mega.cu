@@ -1,12 +1,15 @@
-// The decode step as one persistent kernel: a cooperative launch (one CTA per SM) runs a list of
+// The decode step as one persistent kernel: a cooperative launch (two CTAs per SM) runs a list of
 // phases, the fused GEMV groups and the attention of every layer, separated by grid barriers.
 //
 // Per CTA, warp 8 is the producer: one lane streams the weight pieces of every GEMV phase, in phase
 // order, into the shared-memory ring (gc_gemv_dev.cuh). Weights never depend on activations, so the
 // stream runs ahead through barriers and attention phases, limited only by free ring slots. Warps
-// 0-7 are the consumers: for a GEMV phase one tile row each, with the activation row in registers;
-// for an attention phase they work on (query row, K/V head, 64-key chunk) items as the split-KV
-// flash kernel does (gc_flash.cu), two warps per query head.
+// 0-7 are the consumers: for a GEMV phase one tile row each, with the activation row in registers
+// (the same consumer as the per-op kernel, gc_fused.cu); for an attention phase they work on
+// (query row, K/V head, 64-key chunk) items as the split-KV flash kernel does (gc_flash_dev.cuh),
+// two warps per query head. An item stages the chunk's K rows, then its V rows, in the buffer that
+// holds the quantized activation during GEMV phases, so a CTA needs ~100 KB of shared memory and
+// two fit an SM.
 //
 // Every phase computes exactly what the per-op kernels compute (same prologue, same block order,
 // same epilogues, same attention chunking and merge), so results are bit-identical to them and to the
@@ -31,17 +34,17 @@ int num_sms();
 namespace {
 
 constexpr int TEAMS = 1;
-constexpr int CG = 2;                         // row groups per team in a GEMV chunk (gc_gemv_dev.cuh)
+constexpr int CG = 1;                         // row groups per team in a GEMV chunk (gc_gemv_dev.cuh)
 constexpr int NCW = 8 * TEAMS;                // consumer warps
 constexpr int NCT = NCW * 32;                 // consumer threads
 constexpr int NTHREADS = NCT + 32;            // + producer warp
-constexpr int MAXNS = 32;
+constexpr int MAXNS = 8;
 constexpr int CH = FL_CH;                     // attention chunk (keys)
 constexpr int MAXD = 128;  // decode kernel head sizes (larger heads use the per-op kernels)
 constexpr int WPH = 2;                        // warps per query head
 constexpr int MAXG = NCW / WPH;               // query heads per attention item pass
-constexpr int MAXGQ = 8;                      // query heads per K/V head (staging)
-constexpr size_t SMEM_LIMIT = 226 * 1024;     // dynamic shared memory (the opt-in 227 KB less the static part)
+constexpr int MAXGQ = MAXG;                   // query heads per K/V head (one pass)
+constexpr size_t SMEM_LIMIT = 112 * 1024;     // dynamic shared memory of a CTA: two per SM
 
 __device__ __forceinline__ int ld_acquire(const int *p) {
     int v;
@@ -78,15 +81,17 @@ struct SyncConsumers {
 };
 
 // One attention item: chunk `ch` of K/V head `hk` for query row `iq` (split-KV flash attention,
-// gc_flash_dev.cuh); the last item of a (query row, K/V head) merges its heads' chunks.
-__device__ inline bool attn_item(const MegaAttn &at, int iq, int hk, int ch, __half *Ks, __half *Vs, float *sc, float *ps,
-                                 float *qs, float *ms, uint64_t *abar, uint32_t parity, int *s_last) {
+// gc_flash_dev.cuh): the chunk's K rows, then its V rows, pass through the staging buffer KV; the
+// last item of a (query row, K/V head) merges its heads' chunks.
+__device__ inline bool attn_item(const MegaAttn &at, int iq, int hk, int ch, __half *KV, float *sc, float *ps, float *qs,
+                                 float *ms, uint64_t *abar, uint32_t &aphase, int *s_last) {
     const int D = (int)at.D;
     const int j0 = ch * CH;
     const int n = (int)min((int64_t)CH, at.nkv - j0);
     const int warp = threadIdx.x >> 5;
     const int G = (int)(at.H / at.Hkv);
     const int nch = (int)((at.nkv + CH - 1) / CH);
+    const uint32_t bytes = (uint32_t)(n * D * 2);
 
     FlashChunk fc;
     fc.q = (const char *)(at.q + iq * at.ldq + (int64_t)hk * G * D);
@@ -102,20 +107,31 @@ __device__ inline bool attn_item(const MegaAttn &at, int iq, int hk, int ch, __h
     fc.G = G;
     fc.part = at.part + (((int64_t)iq * at.H + (int64_t)hk * G) * nch + ch) * (D + 2);
     fc.pstride = (int64_t)nch * (D + 2);
-    if (threadIdx.x == 0) {
-        const uint32_t bytes = (uint32_t)(n * D * 2);
-        mbar_expect_tx(abar, 2 * bytes);
-        bulk_g2s(Ks, at.k + hk * at.knb2 + (int64_t)j0 * at.knb1, bytes, abar);
-        bulk_g2s(Vs, at.v + hk * at.vnb2 + (int64_t)j0 * at.vnb1, bytes, abar);
+    if (threadIdx.x == 0) {  // the buffer's earlier plain reads are ordered before the copy's writes
+        fence_proxy_async_shared();
+        mbar_expect_tx(abar, bytes);
+        bulk_g2s(KV, at.k + hk * at.knb2 + (int64_t)j0 * at.knb1, bytes, abar);
     }
-    flash_stage(fc, qs, ms, threadIdx.x, NCT);  // while the copies are in flight
+    flash_stage(fc, qs, ms, threadIdx.x, NCT);  // while the copy is in flight
     named_bar(3, NCT);
-    if (threadIdx.x == 0) *s_last = mbar_wait(abar, parity) ? 1 : 0;  // one bounded wait, its outcome shared
+    if (threadIdx.x == 0) *s_last = mbar_wait(abar, aphase & 1) ? 1 : 0;  // one bounded wait, its outcome shared
+    aphase++;
     named_bar(3, NCT);
     if (!*s_last) return false;  // uniform: every consumer thread leaves here
-
-    if (D == 128) flash_chunk<WPH, 128>(fc, Ks, Vs, qs, ms, sc, ps, NCW / WPH, SyncConsumers());
-    else flash_chunk<WPH, 64>(fc, Ks, Vs, qs, ms, sc, ps, NCW / WPH, SyncConsumers());
+    if (D == 128) flash_scores<WPH, 128>(fc, KV, qs, ms, sc, ps, 0, MAXG, SyncConsumers());
+    else flash_scores<WPH, 64>(fc, KV, qs, ms, sc, ps, 0, MAXG, SyncConsumers());
+    // every consumer passed the barrier inside flash_scores: K is no longer read
+    if (threadIdx.x == 0) {
+        fence_proxy_async_shared();
+        mbar_expect_tx(abar, bytes);
+        bulk_g2s(KV, at.v + hk * at.vnb2 + (int64_t)j0 * at.vnb1, bytes, abar);
+        *s_last = mbar_wait(abar, aphase & 1) ? 1 : 0;
+    }
+    aphase++;
+    named_bar(3, NCT);
+    if (!*s_last) return false;
+    if (D == 128) flash_values<WPH, 128>(fc, KV, sc, ps, 0);
+    else flash_values<WPH, 64>(fc, KV, sc, ps, 0);
 
     // the last item of this (query row, K/V head) merges its heads' chunks in chunk order
     named_bar(3, NCT);
@@ -132,15 +148,14 @@ __device__ inline bool attn_item(const MegaAttn &at, int iq, int hk, int ch, __h
     if (!*s_last) return true;
     for (int g = warp; g < G; g += NCW) {
         const int64_t h = (int64_t)hk * G + g;
-        if (D == 128) flash_merge<128>(at.part + ((iq * at.H + h) * nch) * (D + 2), nch, at.out + at.D * (h + at.H * iq));
-        else flash_merge<64>(at.part + ((iq * at.H + h) * nch) * (D + 2), nch, at.out + at.D * (h + at.H * iq));
+        if (D == 128) flash_merge<128, 4>(at.part + ((iq * at.H + h) * nch) * (D + 2), nch, at.out + at.D * (h + at.H * iq));
+        else flash_merge<64, 4>(at.part + ((iq * at.H + h) * nch) * (D + 2), nch, at.out + at.D * (h + at.H * iq));
     }
     return true;
 }
 
 template <int QT, int M>
-// 9 warps: 3 share a scheduler partition, so at most 168 registers a thread keep one CTA per SM.
-__global__ void __maxnreg__(168) mega_kernel(const MegaPhase *phases, int nph, int log2ns, int slot_bytes,
+__global__ void __launch_bounds__(NTHREADS, 2) mega_kernel(const MegaPhase *phases, int nph, int log2ns, int slot_bytes,
                                                            size_t act_bytes, int attn_d, int *gbar, int *err,
                                                            uint64_t *trace) {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -148,13 +163,11 @@ __global__ void __maxnreg__(168) mega_kernel(const MegaPhase *phases, int nph, i
     uint64_t *empty = full + MAXNS;
     uint64_t *abar = empty + MAXNS;
     double *red = (double *)(abar + 2);  // [256]
-    int8_t *sq = (int8_t *)(red + 256);
-    __half *Ks = (__half *)((unsigned char *)sq + act_bytes);
-    __half *Vs = Ks + CH * attn_d;
-    float *sc = (float *)(Vs + CH * attn_d);
-    float *ps = sc + MAXG * CH;  // [NCW][CH] attention probabilities
-    float *qs = ps + NCW * CH;   // [MAXGQ][MAXD] query rows
-    float *ms = qs + MAXGQ * MAXD;  // [MAXGQ][CH] mask values
+    int8_t *sq = (int8_t *)(red + 256);  // the activation (GEMV phases) or a K/V chunk (attention)
+    float *sc = (float *)((unsigned char *)sq + act_bytes);
+    float *ps = sc + MAXG * CH;       // [NCW][CH] attention probabilities
+    float *qs = ps + NCW * CH;        // [MAXGQ][MAXD] query rows
+    float *ms = qs + MAXGQ * MAXD;    // [MAXGQ][CH] mask values
     unsigned char *slots = (unsigned char *)(ms + MAXGQ * CH);
     __shared__ int s_abort, s_last;
     const Ring R{full, empty, slots, log2ns, slot_bytes};
@@ -192,10 +205,14 @@ __global__ void __maxnreg__(168) mega_kernel(const MegaPhase *phases, int nph, i
     uint32_t t = 0;
     uint32_t aphase = 0;
     const int team = warp / 8, wt = warp % 8;
+    __shared__ __align__(16) MegaPhase sph;  // the current phase's arguments (cheap to re-read)
     for (int p = 0; p < nph; p++) {
         if (p > 0) grid_sync(gbar, p * (int)nctas, &s_abort);
+        for (int i = threadIdx.x; i < (int)(sizeof(MegaPhase) / 4); i += NCT)
+            ((int *)&sph)[i] = __ldg((const int *)&phases[p] + i);
+        named_bar(1, NCT);
         const bool skip = s_abort != 0;  // read after a named barrier: the same in every warp
-        const MegaPhase &ph = phases[p];
+        const MegaPhase &ph = sph;
         uint64_t *stamp = trace && threadIdx.x == 0 ? trace + (cta * nph + p) * 4 : nullptr;
         if (stamp) stamp[0] = global_ns();
         if (ph.type == 0) {
@@ -224,8 +241,7 @@ __global__ void __maxnreg__(168) mega_kernel(const MegaPhase *phases, int nph, i
             bool ok = !skip;
             for (int64_t i = cta; i < items && ok; i += nctas) {
                 const int64_t ch = i % nch, hk = (i / nch) % at.Hkv, iq = i / (nch * at.Hkv);
-                ok = attn_item(at, (int)iq, (int)hk, (int)ch, Ks, Vs, sc, ps, qs, ms, abar, aphase & 1, &s_last);
-                aphase++;
+                ok = attn_item(at, (int)iq, (int)hk, (int)ch, (__half *)sq, sc, ps, qs, ms, abar, aphase, &s_last);
                 named_bar(3, NCT);  // the K/V staging area is free again
             }
             if (!ok && !skip && threadIdx.x == 0) s_abort = 1;
@@ -234,6 +250,26 @@ __global__ void __maxnreg__(168) mega_kernel(const MegaPhase *phases, int nph, i
         }
     }
     if (s_abort && err && threadIdx.x == 0) atomicExch(err, 3);
+}
+
+// The activation buffer, also the K/V staging buffer of attention items.
+size_t work_bytes(int64_t kmax, int attn_d) {
+    const size_t act = gemv_act_bytes(1, kmax), kv = (size_t)CH * attn_d * 2;
+    return ((act > kv ? act : kv) + 127) / 128 * 128;
+}
+
+size_t head_bytes(int64_t kmax, int attn_d) {
+    return (size_t)(2 * MAXNS + 2) * 8 + 256 * 8 + work_bytes(kmax, attn_d) + (size_t)(MAXG + NCW) * CH * 4 +
+           (size_t)MAXGQ * (MAXD + CH) * 4;
+}
+
+// Two CTAs of the kernel fit an SM with `smem` bytes each (a cooperative launch needs every CTA resident).
+template <int QT>
+bool resident(size_t smem) {
+    auto kern = mega_kernel<QT, 1>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_LIMIT) != cudaSuccess) return false;
+    int n = 0;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, NTHREADS, smem) == cudaSuccess && n >= 2;
 }
 
 template <int QT, int M>
@@ -246,14 +282,13 @@ void launch(const MegaPhase *phases, int nph, int64_t kmax, int attn_d, int64_t 
         if (e != cudaSuccess) throw std::runtime_error(std::string("decode kernel: ") + cudaGetErrorString(e));
         attr = true;
     }
-    const size_t act = gemv_act_bytes(M, kmax);
-    const size_t head = (size_t)(2 * MAXNS + 2) * 8 + 256 * 8 + act + (size_t)CH * attn_d * 4 + (size_t)(MAXG + NCW) * CH * 4 +
-                        (size_t)MAXGQ * (MAXD + CH) * 4;
+    const size_t act = work_bytes(kmax, attn_d);
+    const size_t head = head_bytes(kmax, attn_d);
     const int log2ns = ring_log2(SMEM_LIMIT, head, (size_t)slot_bytes, MAXNS);
-    if ((1 << log2ns) < 4) throw std::runtime_error("decode kernel: shared memory too small for the weight ring");
+    if ((1 << log2ns) < 2) throw std::runtime_error("decode kernel: shared memory too small for the weight ring");
     const size_t smem = head + ((size_t)1 << log2ns) * (size_t)slot_bytes;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)num_sms());
+    cfg.gridDim = dim3((unsigned)(2 * num_sms()));
     cfg.blockDim = dim3(NTHREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -268,28 +303,17 @@ void launch(const MegaPhase *phases, int nph, int64_t kmax, int attn_d, int64_t 
 
 }  // namespace
 
-// One CTA of the kernel fits an SM with `smem` bytes (a cooperative launch needs every CTA resident).
-template <int QT>
-bool resident(size_t smem) {
-    auto kern = mega_kernel<QT, 1>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_LIMIT) != cudaSuccess) return false;
-    int n = 0;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, NTHREADS, smem) == cudaSuccess && n >= 1;
-}
-
 bool mega_supported(int qtype, int M, int64_t kmax, int attn_d) {
     if (M != 1 || (qtype != T_Q4_0 && qtype != T_Q8_0) || (attn_d != 0 && attn_d != 64 && attn_d != 128)) return false;
     const int64_t slot = (int64_t)QTR * QSEG * ((qtype == T_Q4_0 ? 16 : 32) + 2);
-    const size_t head = (size_t)(2 * MAXNS + 2) * 8 + 256 * 8 + gemv_act_bytes(M, kmax) + (size_t)CH * attn_d * 4 +
-                        (size_t)(MAXG + NCW) * CH * 4 +
-                        (size_t)MAXGQ * (MAXD + CH) * 4;
+    const size_t head = head_bytes(kmax, attn_d);
     const int log2ns = ring_log2(SMEM_LIMIT, head, (size_t)slot, MAXNS);
-    if ((1 << log2ns) < 4) return false;
+    if (head + ((size_t)1 << log2ns) * (size_t)slot > SMEM_LIMIT || (1 << log2ns) < 2) return false;
     const size_t smem = head + ((size_t)1 << log2ns) * (size_t)slot;
     return qtype == T_Q4_0 ? resident<0>(smem) : resident<1>(smem);
 }
 
-int mega_ctas() { return num_sms(); }
+int mega_ctas() { return 2 * num_sms(); }
 
 void mega_step(const MegaPhase *phases_dev, int nph, int qtype, int M, int64_t kmax, int attn_d, int *gbar, int *err,
                uint64_t *trace, cudaStream_t s) {

@@ -59,6 +59,10 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  : "memory");
 }
 
+// Orders this thread's (and, after a barrier, its CTA's) shared-memory accesses through the generic
+// proxy with later bulk copies into shared memory.
+__device__ __forceinline__ void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // Orders this thread's generic-proxy global accesses with later bulk copies (the async proxy).
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
