@@ -62,6 +62,15 @@ void rope_norm(const TD &x, const TD &pos, const TD &out, int n_dims, const floa
                float theta_scale, float freq_scale, float attn_factor, const float *freq_factors, cudaStream_t s);
 void get_rows(const TD &table, const TD &idx, const TD &out, cudaStream_t s);
 void set_rows(const TD &dst, const TD &src, const TD &idx, int *err, cudaStream_t s);
+// Quantized mul_mat of 9+ activation rows on the tensor cores (gc_gemm_tc.cu): shapes it takes, and
+// the launch over activation codes / fp16 scales as act_quant writes them.
+bool gemm_tc_ok(const TD &a, const TD &b);
+void gemm_tc(const TD &a, int64_t M, const int8_t *qx, const uint16_t *dx, float *out, int *err, cudaStream_t s);
+
+// Activation rows from which a quantized mul_mat sums its blocks in order (GEMM) rather than into 32
+// lane partials and a butterfly (GEMV); the CPU checker uses the same rule.
+constexpr int64_t GEMM_MIN_ROWS = 9;
+
 void argmax(const TD &x, const TD &out, cudaStream_t s);
 // Long f32 rows: slices per row (0: use argmax), then the split form with scratch of rows x parts
 // float2 pairs and rows zeroed counters (reset by the kernel).
@@ -78,7 +87,7 @@ void causal_mask_row(float *dst, int64_t n_total, int64_t row_len, const int32_t
 // mul_mat(a, b): out[n, m, i2, i3] = sum_k a[k, n, i2/r2, i3/r3] * b[k, m, i2, i3].
 // `scratch` must hold mul_mat_scratch_bytes(a, b) bytes.
 size_t mul_mat_scratch_bytes(const TD &a, const TD &b);
-void mul_mat(const TD &a, const TD &b, const TD &out, void *scratch, cudaStream_t s);
+void mul_mat(const TD &a, const TD &b, const TD &out, void *scratch, cudaStream_t s, int *err = nullptr);
 
 // flash_attn_ext: q [D, Sq, H, B] f32, k/v [D, n_kv, Hkv, B] f16, mask [n_kv, >=Sq, ...] f16 (nullable)
 // -> out [D, H, Sq, B] f32.

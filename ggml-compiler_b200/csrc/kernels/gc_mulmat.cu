@@ -11,6 +11,8 @@
 //
 // This is the correctness path for every shape; the decode-time fused GEMVs (gc_gemv.cu) and the
 // tensor-core prefill GEMM replace it on the hot path.
+#include <algorithm>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -112,6 +114,31 @@ __global__ void mm_quant_kernel(MMk p, const int8_t *qx, const uint16_t *dx) {
     }
 }
 
+// Nine or more activation rows: one thread per output element (n, m, i2, i3), every block of the
+// row fma'd in order into one sum (the order the tensor-core GEMM and the CPU checker use).
+// Consecutive threads take consecutive weight rows of one activation row.
+__global__ void mm_quant_seq_kernel(MMk p, const int8_t *qx, const uint16_t *dx) {
+    const int64_t nb = p.K / 32;
+    const int64_t nout = p.N * p.M * p.B2 * p.B3;
+    const QW wq{p.a, nb, p.atype == T_Q4_0 ? 16 : 32};
+    for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < nout; w += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = w % p.N;
+        const int64_t r = w / p.N;  // (m, i2, i3)
+        const int64_t i2 = (r / p.M) % p.B2, i3 = r / (p.M * p.B2);
+        const int64_t a2 = i2 / (p.B2 / p.A2), a3 = i3 / (p.B3 / p.A3);
+        const int64_t arow = n + p.N * (a2 + p.A2 * a3);
+        const int8_t *xrow = qx + r * p.K;
+        const uint16_t *xd = dx + r * nb;
+        float acc = 0.0f;
+        for (int64_t blk = 0; blk < nb; blk++) {
+            const int isum = block_isum(p.atype, qw_code(wq, arow, blk), xrow + blk * 32);
+            const float dd = __fmul_rn(h2f(qw_scale(wq, arow, blk)), h2f(xd[blk]));
+            acc = __fmaf_rn(dd, (float)isum, acc);
+        }
+        p.out[w] = acc;
+    }
+}
+
 __device__ __forceinline__ float lda(int t, const char *p) {
     return t == T_F16 ? __half2float(*(const __half *)p) : (t == T_BF16 ? __bfloat162float(*(const __nv_bfloat16 *)p) : *(const float *)p);
 }
@@ -180,7 +207,7 @@ size_t mul_mat_scratch_bytes(const TD &a, const TD &b) {
     return (q + 255) / 256 * 256 + (size_t)(rows * (a.ne[0] / 32)) * 2 + 256;
 }
 
-void mul_mat(const TD &a, const TD &b, const TD &out, void *scratch, cudaStream_t s) {
+void mul_mat(const TD &a, const TD &b, const TD &out, void *scratch, cudaStream_t s, int *err) {
     MMk p = make(a, b, out);
     const int64_t nout = p.N * p.M * p.B2 * p.B3;
     if (a.type == T_Q4_0 || a.type == T_Q8_0) {
@@ -189,7 +216,13 @@ void mul_mat(const TD &a, const TD &b, const TD &out, void *scratch, cudaStream_
         uint16_t *dx = (uint16_t *)((char *)scratch + ((size_t)(rows * p.K) + 255) / 256 * 256);
         act_quant_kernel<<<warps_grid(rows * (p.K / 32)), 256, 0, s>>>(p, qx, dx);
         check_launch("act_quant");
-        mm_quant_kernel<<<warps_grid(nout), 256, 0, s>>>(p, qx, dx);
+        if (gemm_tc_ok(a, b) && !std::getenv("GCB_NO_TC_GEMM")) {
+            gemm_tc(a, p.M, qx, dx, (float *)out.data, err, s);
+        } else if (p.M >= GEMM_MIN_ROWS) {
+            mm_quant_seq_kernel<<<(unsigned)std::min<int64_t>((nout + 255) / 256, 1 << 20), 256, 0, s>>>(p, qx, dx);
+        } else {
+            mm_quant_kernel<<<warps_grid(nout), 256, 0, s>>>(p, qx, dx);
+        }
         check_launch("mul_mat_q");
     } else {
         mm_float_kernel<<<warps_grid(nout), 256, 0, s>>>(p, a.nb[0]);

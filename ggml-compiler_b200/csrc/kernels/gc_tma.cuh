@@ -35,6 +35,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that may suspend the thread until the phase completes, for up to `hint_ns` (the waiting
+// thread then takes no issue slots from the warps doing work).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -46,6 +58,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     while (!mbar_try_wait(bar, parity))
+        if (global_ns() - t0 > limit_ns) return false;
+    return true;
+}
+
+// mbar_wait with suspending polls (each poll may sleep up to 0.1 ms until the phase completes).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t limit_ns = 2000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait_sleep(bar, parity, 100000u))
         if (global_ns() - t0 > limit_ns) return false;
     return true;
 }

@@ -29,7 +29,9 @@
  * order for every reduction; the B200 kernels follow the same orders, so their decode results can
  * be compared bit for bit. The orders:
  * - 32-lane butterfly: 32 partial sums, then p[i] += p[i ^ off] for off = 16, 8, 4, 2, 1.
- * - quantized dot: block b goes to partial b % 32 (fmaf(d_w*d_x, isum, p)), then the butterfly.
+ * - quantized dot, up to 8 activation rows: block b goes to partial b % 32
+ *   (fmaf(d_w*d_x, isum, p)), then the butterfly; 9 or more rows: every block in order into one sum
+ *   (the integer block dots are exact, so only the order of the fmaf chain matters).
  * - float dot: element k goes to partial k % 32 (fmaf), then the butterfly.
  * - head dot (attention, D % 32 == 0): lane l owns elements [l*D/32, (l+1)*D/32), then butterfly.
  * - 256-way double tree (rms_norm, softmax sums): element i goes to partial i % 256, then
@@ -302,13 +304,20 @@ typedef struct {
     float *Y;
 } mm_ctx;
 
+/* Block products fma'd into the result in one of two orders (the GPU kernels follow the same):
+ * up to GEMM_MIN_ROWS - 1 = 8 activation rows (decode GEMVs), block b into partial b % 32 and the
+ * 32 partials reduced by the butterfly; more rows (prefill GEMMs, integer tensor-core MMA per block),
+ * every block in order into one sum. */
+#define GEMM_MIN_ROWS 9
+
 static void mm_quant_rows(void *cv, int64_t n0, int64_t n1) {
     const mm_ctx *c = (const mm_ctx *)cv;
     const int64_t K = c->K, nb = K / QK;
+    const int seq = c->M >= GEMM_MIN_ROWS;
     for (int64_t n = n0; n < n1; n++) {
         const uint8_t *w = c->W + (size_t)n * c->wrb;
         for (int64_t m = 0; m < c->M; m++) {
-            float p[32] = {0};
+            float p[32] = {0}, acc = 0.0f;
             const int8_t *xq = c->qx + m * K;
             for (int64_t b = 0; b < nb; b++) {
                 int32_t isum = 0;
@@ -326,9 +335,10 @@ static void mm_quant_rows(void *cv, int64_t n0, int64_t n1) {
                     for (int j = 0; j < 32; j++) isum += (int)(int8_t)blk[2 + j] * xq[b * QK + j];
                 }
                 const float dd = h2f(dwh) * h2f(c->dx[m * nb + b]);
-                p[b & 31] = fmaf(dd, (float)isum, p[b & 31]);
+                if (seq) acc = fmaf(dd, (float)isum, acc);
+                else p[b & 31] = fmaf(dd, (float)isum, p[b & 31]);
             }
-            c->Y[m * c->ldy + n] = butterfly32(p);
+            c->Y[m * c->ldy + n] = seq ? acc : butterfly32(p);
         }
     }
 }

@@ -55,3 +55,15 @@ def test_quant_mul_mat_edges(gpu, tmp_path):
     for wtype in ("q4_0", "q8_0"):
         got = run_mm(tmp_path, w, wtype, x)
         np.testing.assert_array_equal(got, oracle.mul_mat(oracle.quantize(w, wtype), wtype, 32, x))
+
+
+@pytest.mark.parametrize("wtype", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("N,K,M", [(384, 1024, 9), (384, 1024, 64), (300, 2048, 200), (128, 256, 70)])
+def test_quant_gemm_bit_exact(gpu, tmp_path, wtype, N, K, M):
+    """9+ activation rows: the tensor-core GEMM (integer MMA per block, blocks summed in order),
+    ragged in both the weight rows (N % 128) and the activation rows (M % 64)."""
+    w = weights((N, K), seed=3)
+    x = np.random.default_rng(4).standard_normal((M, K), dtype=np.float32)
+    got = run_mm(tmp_path, w, wtype, x)
+    ref = oracle.mul_mat(oracle.quantize(w, wtype), wtype, K, x)
+    np.testing.assert_array_equal(got, ref)
