@@ -226,6 +226,8 @@ def main() -> None:
     ap.add_argument("--shape", default=None, help="sweep: one weight shape NxK")
     ap.add_argument("--m", type=int, default=None, help="sweep: one activation row count")
     ap.add_argument("--wtype", default=None, choices=["q4_0", "q8_0"], help="sweep: one weight type")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
+                    help="N>1: one sequence tensor-parallel over the N GPUs (tp), or N independent sequences")
     ap.add_argument("--cpu-tokens", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -273,6 +275,12 @@ def main() -> None:
     lib = load_library()
     gguf = model_path(sh, args.config, rank, world)
     s = Session(gguf, backend="cuda", device=local)
+    tp = world > 1 and args.parallel == "tp"
+    if tp:
+        from ggml_compiler_b200.runtime import torch_all_gather
+
+        s.tensor_parallel(rank, world, torch_all_gather())
+    seqs = 1 if tp else world  # sequences decoded by the whole job
     stream = torch.cuda.ExternalStream(s.stream, device=torch.device("cuda", local))
     g = Generator(s)
     prompt = np.random.default_rng(1).integers(0, sh.vocab, 512).tolist()
@@ -304,7 +312,7 @@ def main() -> None:
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     dev_ms = float(t.item())
-    value = world * K / (dev_ms / 1000.0)
+    value = seqs * K / (dev_ms / 1000.0)
 
     # e2e: host loop through the public API, pinned host buffers, K decode steps
     first = prefill()
@@ -353,7 +361,7 @@ def main() -> None:
     t = torch.tensor([e2e_ms], device="cuda")
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    e2e_value = world * K / (float(t.item()) / 1000.0)
+    e2e_value = seqs * K / (float(t.item()) / 1000.0)
 
     # roofline: profiled pass over the same decode steps, per kernel family
     first = prefill()
@@ -374,9 +382,10 @@ def main() -> None:
 
     out = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": dev_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "q4_0 weights, int8 x int4 block dots, f32 sums", "data": "synthetic",
-        "config": {**config, "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "ms_per_step": dev_ms / K, "higher_is_better": True, "scaling": "strong" if tp else "weak",
+        "vs_baseline": None, "dtype": "q4_0 weights, int8 x int4 block dots, f32 sums", "data": "synthetic",
+        "config": {**config, "parallelism": (f"tp{world}: rows / heads split, exchanges over NVLink peer memory" if tp
+                                             else f"replicas x{world}" if world > 1 else "single GPU")},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak if peak else None, "traffic": None,
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
@@ -384,8 +393,8 @@ def main() -> None:
                      "bytes_per_launch": gemv_bytes / max(1, gemv_launches),
                      "mean_launch_us": 1000.0 * gemv_ms / max(1, gemv_launches),
                      "share_of_step": gemv_ms / total_ms if total_ms else None,
-                     "step_weight_bytes": weight_bytes(sh),
-                     "step_hbm_frac": weight_bytes(sh) / (dev_ms / K / 1000.0) / 1e9 / peak},
+                     "step_weight_bytes": weight_bytes(sh) / (world if tp else 1),
+                     "step_hbm_frac": weight_bytes(sh) / (world if tp else 1) / (dev_ms / K / 1000.0) / 1e9 / peak},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4 + 4 + 4 * n_kv,
                 "d2h_bytes_per_step": 4 * sh.vocab, "wall_ms": wall * 1000.0},
         "gpu_launches": int(round(launches_per_step * K + 2 * K)),
@@ -393,7 +402,7 @@ def main() -> None:
         "kernel_breakdown_ms_per_step": {k: v["ms"] / n_prof for k, v in sorted(ks.items(), key=lambda kv: -kv[1]["ms"])},
     }
     s.close()
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             out["cpu_baseline"] = cpu_baseline(gguf, sh, max(1, args.cpu_tokens))
         except Exception as e:  # the baseline is reported, not required for the GPU number

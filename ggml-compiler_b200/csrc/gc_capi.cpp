@@ -7,6 +7,7 @@
 #include <memory>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "ggml_compiler_rt.h"
 #include "ggml_compiler_b200.h"
@@ -426,6 +427,47 @@ int ggml_compiler_b200_set_profiling(ggml_compiler_model *mm, int on) {
     mm->m.profiling = on != 0;
     if (on) mm->m.kstats.clear();
     return 0;
+}
+
+int ggml_compiler_b200_tp_init(ggml_compiler_model *mm, int rank, int world, size_t window_bytes, void *handle, size_t cap) {
+    if (!mm || !handle) {
+        set_error("model and handle must not be NULL");
+        return -1;
+    }
+    if (cap < sizeof(cudaIpcMemHandle_t)) {
+        set_error("tp_init: the handle needs " + std::to_string(sizeof(cudaIpcMemHandle_t)) + " bytes");
+        return -1;
+    }
+    try {
+        cudaIpcMemHandle_t h;
+        mm->m.tp_init(rank, world, window_bytes, &h);
+        std::memcpy(handle, &h, sizeof h);
+        return (int)sizeof h;
+    } catch (const std::exception &e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int ggml_compiler_b200_tp_connect(ggml_compiler_model *mm, const void *handles, size_t nbytes) {
+    if (!mm || !handles) {
+        set_error("model and handles must not be NULL");
+        return -1;
+    }
+    if (nbytes != (size_t)mm->m.tp.world * sizeof(cudaIpcMemHandle_t)) {
+        set_error("tp_connect: expected " + std::to_string(mm->m.tp.world) + " handles of " +
+                  std::to_string(sizeof(cudaIpcMemHandle_t)) + " bytes");
+        return -1;
+    }
+    try {
+        std::vector<cudaIpcMemHandle_t> hs((size_t)mm->m.tp.world);
+        std::memcpy(hs.data(), handles, nbytes);
+        mm->m.tp_connect(hs.data());
+        return 0;
+    } catch (const std::exception &e) {
+        set_error(e.what());
+        return -1;
+    }
 }
 
 int ggml_compiler_b200_n_kernel_stats(const ggml_compiler_model *mm) { return mm ? (int)mm->m.kstats.size() : -1; }

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <functional>
+#include <set>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -38,15 +39,23 @@ struct Planner {
     std::vector<Storage> storages;
     std::vector<PlanStep> psteps;
     int cur = 0;
+    std::set<int> head_sharded;  // tensor parallel: storages holding only this rank's query heads
 
     TD alloc(Type t, const int64_t *ne);          // a fresh arena tensor written at `cur`
     void *scratch_marker(size_t bytes, TD *out);  // scratch arena space for the launch at `cur`
     void use(const TD &t);                        // `t` is read at `cur`
     void add(const char *kind, const std::string &node, std::vector<TD> tds,
              std::function<void(cudaStream_t, const std::vector<TD> &)> fn, double bytes);
-    // A fused GEMV step (gc_fused.h) that can also run as a decode-kernel phase.
+    // A fused GEMV step (gc_fused.h) that can also run as a decode-kernel phase. Under tensor
+    // parallelism it computes this rank's rows and is followed by an exchange of its output (the
+    // rope/QKV form: this rank's heads, no exchange; its query output is marked head_sharded).
     void add_gemv(const char *kind, const std::string &node, std::vector<TD> tds,
                   std::function<FusedArgs(const std::vector<TD> &)> build, double bytes);
+    // Tensor parallel: after a step that wrote bytes [col[r], col[r + 1]) of each of `rows` rows of
+    // `buf` on rank r, every rank gets the whole rows. False (nothing added) if the slices do not fit.
+    bool add_exchange(const std::string &node, const TD &buf, int64_t rows, int64_t ld, const std::vector<int64_t> &col);
+    bool exchange_fits(int64_t rows, int64_t ld, const std::vector<int64_t> &col) const;
+    k::TpExchange exchange_args(int64_t rows, int64_t ld, const std::vector<int64_t> &col) const;
     TD src_of(const std::string &name);  // a node id, stage param or weight
     TD plan_node(const NodeSpec &n, const std::vector<TD> &src);
     void finish();

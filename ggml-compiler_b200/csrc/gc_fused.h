@@ -44,6 +44,9 @@ struct FusedArgs {
     int64_t npos = 0;
     float theta_scale = 1.0f;
     int *err = nullptr;
+    // Tensor-parallel shard: this launch computes shard `shard` of `nshard` of the rows (a run of
+    // 8-row tiles; for MAP_ROPE_QKV the query and K/V heads H / nshard * shard.., Hkv / nshard * shard..).
+    int shard = 0, nshard = 1;
 };
 
 // An attention phase of the decode kernel: split-KV flash attention of M query rows

@@ -102,5 +102,23 @@ size_t flash_split_counters(const TD &q, const TD &k);
 void flash_attn_split(const TD &q, const TD &k, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
                       int *counters, int *err, cudaStream_t s);
 
+// Tensor-parallel exchange (gc_tp.cu). A window is TP_FLAG_BYTES of flag words (one per sender)
+// followed by two slots of slot_bytes; every rank maps every window.
+constexpr int TP_MAX = 8;
+constexpr int64_t TP_FLAG_BYTES = 256;
+struct TpExchange {
+    char *buf = nullptr;  // the local buffer: `rows` rows at a stride of `ld` bytes
+    int64_t rows = 0, ld = 0, row_bytes = 0;
+    int64_t col[TP_MAX + 1] = {};  // rank r computed bytes [col[r], col[r + 1]) of every row
+    int rank = 0, world = 1;
+    char *win[TP_MAX] = {};  // the window of every rank (this rank's included)
+    int64_t slot_bytes = 0;
+    unsigned *seq = nullptr;  // exchanges done by this rank (device word)
+    int *err = nullptr;
+    uint64_t timeout_ns = 0;
+};
+bool tp_exchange_ok(const TpExchange &x);  // geometry (the buffer's alignment is checked at launch)
+void tp_exchange(const TpExchange &x, cudaStream_t s);
+
 }  // namespace k
 }  // namespace gcb

@@ -59,8 +59,11 @@ __global__ void set_i32_kernel(int32_t *p, int32_t v) { *p = v; }
 
 Model::~Model() {
     if (device >= 0) cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
     for (auto &c : calls)
         if (c.graph) cudaGraphExecDestroy(c.graph);
+    for (size_t r = 0; r < tp.win.size(); r++)
+        if ((int)r != tp.rank && tp.win[r]) cudaIpcCloseMemHandle(tp.win[r]);
     for (auto &e : event_pool) {
         cudaEventDestroy(e.first);
         cudaEventDestroy(e.second);
@@ -513,6 +516,9 @@ void Model::run_entry(const std::string &name) {
             throw std::runtime_error("entry '" + name + "': a kernel's pipeline wait timed out (results are invalid)");
         if (err == 3)
             throw std::runtime_error("entry '" + name + "': a wait in the decode kernel timed out (results are invalid)");
+        if (err == 4)
+            throw std::runtime_error("entry '" + name + "': a tensor-parallel exchange timed out waiting for a peer rank "
+                                     "(results are invalid)");
         throw std::runtime_error("entry '" + name + "': a set_rows index was outside its destination (row skipped)");
     }
     if (!trace_path.empty()) write_trace();
@@ -532,6 +538,46 @@ void Model::reset_state() {
         cuda_check(cudaMemsetAsync(v.buf.get(), 0, v.buf.size(), stream), "reset");
     }
     cuda_check(cudaStreamSynchronize(stream), "reset");
+}
+
+void Model::tp_init(int rank, int world, size_t window_bytes, cudaIpcMemHandle_t *handle) {
+    if (world < 2 || world > k::TP_MAX || rank < 0 || rank >= world)
+        throw std::runtime_error("tensor parallel: world must be 2.." + std::to_string(k::TP_MAX) + " and 0 <= rank < world");
+    if (tp.connected || !tp.win.empty()) throw std::runtime_error("tensor parallel: this model already joined a group");
+    cuda_check(cudaSetDevice(device), "cudaSetDevice");
+    if (window_bytes == 0) window_bytes = (size_t)64 << 20;
+    tp.slot_bytes = (window_bytes / 2) / 256 * 256;
+    if (tp.slot_bytes < 256) throw std::runtime_error("tensor parallel: window too small");
+    tp.rank = rank;
+    tp.world = world;
+    tp.window.alloc((size_t)k::TP_FLAG_BYTES + 2 * tp.slot_bytes);
+    tp.seq.alloc(sizeof(unsigned));
+    cuda_check(cudaIpcGetMemHandle(handle, tp.window.get()), "cudaIpcGetMemHandle");
+    if (const char *e = std::getenv("GGML_COMPILER_B200_TP_TIMEOUT_MS")) tp.timeout_ns = (uint64_t)std::atoll(e) * 1000000ull;
+}
+
+void Model::tp_connect(const cudaIpcMemHandle_t *handles) {
+    if (tp.window.size() == 0) throw std::runtime_error("tensor parallel: tp_init first");
+    if (tp.connected) throw std::runtime_error("tensor parallel: already connected");
+    cuda_check(cudaSetDevice(device), "cudaSetDevice");
+    tp.win.assign((size_t)tp.world, nullptr);
+    for (int r = 0; r < tp.world; r++) {
+        if (r == tp.rank) {
+            tp.win[(size_t)r] = tp.window.get();
+            continue;
+        }
+        void *p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, handles[r], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            throw std::runtime_error("tensor parallel: mapping the window of rank " + std::to_string(r) + " failed: " +
+                                     cudaGetErrorString(e));
+        tp.win[(size_t)r] = (char *)p;
+    }
+    tp.connected = true;
+    for (auto &c : calls) {
+        c.stale = true;
+        c.graph_ok = false;
+    }
 }
 
 int *Model::counters(const std::string &key, size_t n) {

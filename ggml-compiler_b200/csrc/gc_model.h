@@ -77,6 +77,20 @@ struct KernelStat {
     int launches = 0;
 };
 
+// Tensor parallelism: this process is rank `rank` of `world`, one GPU each. Decode GEMVs split
+// their rows (attention its heads) over the ranks and exchange the slices through the ranks'
+// windows (kernels/gc_tp.cu); everything else runs whole on every rank.
+struct TpGroup {
+    int rank = 0, world = 1;
+    DevBuf window;  // flag words + two exchange slots, exported to the peers
+    size_t slot_bytes = 0;
+    DevBuf seq;                        // exchanges done (device word)
+    std::vector<char *> win;           // every rank's window as mapped here (own: window.get())
+    bool connected = false;
+    uint64_t timeout_ns = 60000000000ull;  // GGML_COMPILER_B200_TP_TIMEOUT_MS
+    bool active() const { return connected && world > 1; }
+};
+
 struct Model {
     ProgramSpec prog;
     GgufFile gguf;
@@ -118,8 +132,13 @@ struct Model {
     std::string profile_path;  // GGML_COMPILER_PROFILE
     std::string trace_path;    // GGML_COMPILER_B200_TRACE: decode-kernel phase stamps, rewritten per entry run
     std::vector<std::string> profile_lines;
+    TpGroup tp;
 
     ~Model();
+    // Tensor parallelism: allocate and export this rank's window (before any run), then map every
+    // rank's window from the handles of all ranks in rank order; plans made before are redone.
+    void tp_init(int rank, int world, size_t window_bytes, cudaIpcMemHandle_t *handle);
+    void tp_connect(const cudaIpcMemHandle_t *handles);
     void load(const char *path, int backend, int device, bool allow_cpu_fallback);
     void rebind();
     void run_entry(const std::string &name);

@@ -26,6 +26,8 @@ namespace gcb {
 
 namespace {
 
+constexpr int64_t QTR = 8;  // rows per tile of the quantized weight layout (kernels/gc_qweight.cuh)
+
 std::string shape_str(const int64_t *ne) {
     std::ostringstream os;
     os << "[" << ne[0] << ", " << ne[1] << ", " << ne[2] << ", " << ne[3] << "]";
@@ -132,12 +134,77 @@ void Planner::add(const char *kind, const std::string &node, std::vector<TD> tds
 
 void Planner::add_gemv(const char *kind, const std::string &node, std::vector<TD> tds,
                        std::function<FusedArgs(const std::vector<TD> &)> build, double bytes) {
-    add(kind, node, std::move(tds), [build](cudaStream_t st, const std::vector<TD> &t) { k::fused_gemv(build(t), st, true); }, bytes);
-    psteps.back().mega = [build](const std::vector<TD> &t, MegaPhase &ph) {
-        ph.type = 0;
-        ph.g = build(t);
-        return ph.g.M == 1 && k::fused_gemv_args_ok(ph.g);
+    int shard = 0, nshard = 1;
+    std::vector<int64_t> col;
+    TD out;
+    int64_t rows = 0, ld = 0;
+    if (m.tp.active()) {
+        // the geometry of the arguments does not depend on where the arena puts the tensors
+        const FusedArgs g = build(tds);
+        const int W = m.tp.world;
+        if (g.map == MAP_ROPE_QKV) {
+            if (g.H % W == 0 && g.Hkv % W == 0) {
+                shard = m.tp.rank, nshard = W;
+                head_sharded.insert(tds.back().sid);
+                bytes /= W;
+            }
+        } else {
+            const int64_t N = g.wrows[0], tiles = (N + QTR - 1) / QTR;
+            out = tds.back();
+            rows = g.M, ld = g.ldo * 4;
+            col.resize((size_t)W + 1);
+            for (int r = 0; r <= W; r++) col[(size_t)r] = std::min<int64_t>(N, tiles * r / W * QTR) * 4;
+            if (tiles >= W && exchange_fits(rows, ld, col) && out.off % 16 == 0) {
+                shard = m.tp.rank, nshard = W;
+                bytes *= (double)(col[(size_t)shard + 1] - col[(size_t)shard]) / (double)col.back();
+            }
+        }
+    }
+    auto b2 = [build, shard, nshard](const std::vector<TD> &t) {
+        FusedArgs a = build(t);
+        a.shard = shard;
+        a.nshard = nshard;
+        return a;
     };
+    add(kind, node, std::move(tds), [b2](cudaStream_t st, const std::vector<TD> &t) { k::fused_gemv(b2(t), st, true); }, bytes);
+    psteps.back().mega = [b2](const std::vector<TD> &t, MegaPhase &ph) {
+        ph.type = 0;
+        ph.g = b2(t);
+        return ph.g.M == 1 && ph.g.nshard == 1 && k::fused_gemv_args_ok(ph.g);
+    };
+    if (nshard > 1 && !col.empty()) add_exchange(node, out, rows, ld, col);
+}
+
+k::TpExchange Planner::exchange_args(int64_t rows, int64_t ld, const std::vector<int64_t> &col) const {
+    k::TpExchange x;
+    x.rank = m.tp.rank;
+    x.world = m.tp.world;
+    x.rows = rows;
+    x.ld = ld;
+    x.row_bytes = col.back();
+    for (size_t r = 0; r < col.size() && r <= (size_t)k::TP_MAX; r++) x.col[r] = col[r];
+    for (int r = 0; r < x.world; r++) x.win[r] = m.tp.win[(size_t)r];
+    x.slot_bytes = (int64_t)m.tp.slot_bytes;
+    x.seq = (unsigned *)m.tp.seq.get();
+    x.err = m.d_err;
+    x.timeout_ns = m.tp.timeout_ns;
+    return x;
+}
+
+bool Planner::exchange_fits(int64_t rows, int64_t ld, const std::vector<int64_t> &col) const {
+    return (int)col.size() == m.tp.world + 1 && k::tp_exchange_ok(exchange_args(rows, ld, col));
+}
+
+bool Planner::add_exchange(const std::string &node, const TD &buf, int64_t rows, int64_t ld, const std::vector<int64_t> &col) {
+    if (!exchange_fits(rows, ld, col) || (buf.sid >= 0 ? buf.off : (size_t)(uintptr_t)buf.data) % 16) return false;
+    const k::TpExchange x = exchange_args(rows, ld, col);
+    add("tp_exchange", node, {buf}, [x](cudaStream_t st, const std::vector<TD> &t) {
+            k::TpExchange y = x;
+            y.buf = t[0].data;
+            k::tp_exchange(y, st);
+        },
+        (double)(rows * x.row_bytes));
+    return true;
 }
 
 TD Planner::src_of(const std::string &name) {
@@ -359,6 +426,49 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
         int64_t ne[4] = {q.ne[0], q.ne[2], q.ne[1], q.ne[3]};
         TD y = out_like(T_F32, ne);
         const double bytes = (double)(kk.ne[1] * kk.ne[2] * kk.ne[3]) * kk.ne[0] * 4 + (double)q.nelements() * 8;
+        if (q.sid >= 0 && head_sharded.count(q.sid)) {
+            // tensor parallel: this rank's query heads (and their K/V heads, the only ones its
+            // cache holds), then an exchange of the output rows' head slices
+            const int W = m.tp.world, r = m.tp.rank;
+            const int64_t D = q.ne[0], H = q.ne[2], Hkv = kk.ne[2], hw = H / W, kw = Hkv / W;
+            const TD *mk = sv.size() > 3 ? &sv[3] : nullptr;
+            if (!k::flash_split_ok(q) || H % W || Hkv % W || (mk && (mk->type != T_F16 || !mk->contiguous() || mk->ne[2] != 1 ||
+                                                                     mk->ne[0] != kk.ne[1] || mk->ne[1] < q.ne[1])))
+                fail(n, "tensor parallel: attention over this rank's query heads needs the split-KV kernel, head counts "
+                        "divisible by the ranks and one mask for all heads");
+            auto shift = [](TD t, int64_t bytes) {
+                if (t.sid >= 0) t.off += (size_t)bytes;
+                else t.data += bytes;
+                return t;
+            };
+            TD qs = shift(q, hw * r * q.nb[2]), ks = shift(kk, kw * r * kk.nb[2]), vs = shift(v, kw * r * v.nb[2]);
+            TD ys = shift(y, hw * r * D * 4);
+            qs.ne[2] = hw;
+            ks.ne[2] = vs.ne[2] = kw;
+            ys.ne[1] = hw;
+            TD scratch;
+            scratch_marker(k::flash_split_scratch_bytes(qs, ks), &scratch);
+            int *cnt = m.counters(s.name + "/" + n.id, k::flash_split_counters(qs, ks));
+            int *err = m.d_err;
+            const double sbytes = bytes / W;
+            if (mk)
+                add("flash_attn", n.id, {qs, ks, vs, *mk, ys, scratch},
+                    [scale, cnt, err](cudaStream_t st, const std::vector<TD> &t) {
+                        k::flash_attn_split(t[0], t[1], t[2], &t[3], t[4], scale, t[5].data, cnt, err, st);
+                    },
+                    sbytes);
+            else
+                add("flash_attn", n.id, {qs, ks, vs, ys, scratch},
+                    [scale, cnt, err](cudaStream_t st, const std::vector<TD> &t) {
+                        k::flash_attn_split(t[0], t[1], t[2], nullptr, t[3], scale, t[4].data, cnt, err, st);
+                    },
+                    sbytes);
+            std::vector<int64_t> col((size_t)W + 1);
+            for (int i = 0; i <= W; i++) col[(size_t)i] = hw * i * D * 4;
+            if (!add_exchange(n.id, y, q.ne[1] * q.ne[3], H * D * 4, col))
+                fail(n, "tensor parallel: the attention output does not fit the exchange window");
+            return y;
+        }
         if (sv.size() > 3) {
             const TD &mk = sv[3];
             if (mk.type != T_F16 || !mk.contiguous() || q.ne[2] % mk.ne[2] != 0 || mk.ne[0] != kk.ne[1] || mk.ne[1] < q.ne[1])
@@ -610,7 +720,7 @@ void Planner::finish() {
     };
     std::vector<MegaPhase> phases;
     std::vector<Run> runs;
-    for (size_t i = 0; m.use_decode_kernel && i < psteps.size();) {
+    for (size_t i = 0; m.use_decode_kernel && !m.tp.active() && i < psteps.size();) {
         Run r;
         r.begin = i;
         r.phase0 = phases.size();

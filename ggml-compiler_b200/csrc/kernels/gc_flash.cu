@@ -42,7 +42,8 @@ struct SplitArgs {
     int64_t mne2, mne3, mnb1, mnb2, mnb3;
     float scale;
     float *part;     // [B][Sq][H][nch][D + 2]
-    float *out;      // [D, H, Sq, B] rows of this launch
+    float *out;      // [D, oH, Sq, B] rows of this launch (heads 0..H-1 of each row)
+    int64_t oH;      // heads per output row: H, or more when this launch writes a slice of the heads
     int *counters;   // [B][Sq][Hkv], zero between launches
     int *err;
     int64_t nch;
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
     for (int64_t g = warp; g < G; g += blockDim.x / 32) {
         const int64_t h = hk * G + g;
         flash_merge<MAXD>(a.part + (((b * a.Sq + iq) * a.H + h) * a.nch) * (a.D + 2), (int)a.nch,
-                          a.out + a.D * (h + a.H * (iq + a.Sq * b)));
+                          a.out + a.D * (h + a.oH * (iq + a.Sq * b)));
     }
 }
 
@@ -185,6 +186,9 @@ void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, co
         a.mnb3 = mask->nb[3];
     }
     a.scale = scale;
+    a.oH = out.nb[2] / (4 * a.D);
+    if (out.nb[0] != 4 || out.nb[1] != 4 * a.D || out.nb[2] % (4 * a.D) || a.oH < a.H || out.nb[3] != out.nb[2] * q.ne[1])
+        throw std::runtime_error("flash_split: output rows must be [D, heads] blocks of f32 with contiguous heads");
     a.nch = (a.nkv + CH - 1) / CH;
     a.part = (float *)scratch;
     a.counters = counters;
@@ -217,7 +221,7 @@ void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, co
         g.q = a.q + q0 * a.qnb1;
         g.mask = mask ? mask->data + q0 * a.mnb1 : nullptr;
         g.Sq = nq;
-        g.out = (float *)out.data + q0 * a.D * a.H;  // out [D, H, Sq, B]: rows q0.. (one batch)
+        g.out = (float *)out.data + q0 * a.D * a.oH;  // out [D, oH, Sq, B]: rows q0.. (one batch)
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)a.nch, (unsigned)(a.Hkv * a.B), (unsigned)nq);
         cfg.blockDim = dim3(threads);

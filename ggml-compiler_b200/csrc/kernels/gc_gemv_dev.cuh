@@ -28,27 +28,37 @@ namespace k {
 
 constexpr int GEMV_MAXM = 8;
 
-// Geometry of one GEMV over the tiled weights.
+// Geometry of one GEMV over the tiled weights. With a.nshard > 1 the groups are this shard's: a
+// contiguous run of tiles (MAP_SINGLE, MAP_SWIGLU) or this shard's query and K/V heads (MAP_ROPE_QKV);
+// gemv_piece maps them back to the global tiles, so every row keeps its single-shard arithmetic.
 struct GemvGeo {
     int nb, nseg, groups;  // blocks per row, segments per row, row groups (tiles / tile pairs)
     int cb, pieces;        // code bytes per block, pieces per (group, segment)
     int half_tiles;        // ROPE_QKV: tiles per half head
+    int gbase;             // SINGLE / SWIGLU: first tile of the shard
+    int hq, hkv, q0, kv0;  // ROPE_QKV: query / K/V heads of the shard, first of each
 };
+
+// First tile of shard `r` of `n` over `tiles` tiles (the host planner splits exchanges the same way).
+__host__ __device__ inline int shard_tile(int tiles, int r, int n) { return (int)((int64_t)tiles * r / n); }
 
 __host__ __device__ inline GemvGeo gemv_geo(const FusedArgs &a) {
     GemvGeo G{};
     G.nb = (int)(a.K / 32);
     G.nseg = (int)qw_nseg(G.nb);
     G.cb = a.qtype == T_Q4_0 ? 16 : 32;
-    if (a.map == MAP_SINGLE) {
-        G.groups = (int)((a.wrows[0] + QTR - 1) / QTR);
-        G.pieces = 1;
-    } else if (a.map == MAP_SWIGLU) {
-        G.groups = (int)((a.wrows[0] + QTR - 1) / QTR);
-        G.pieces = 2;
+    if (a.map == MAP_SINGLE || a.map == MAP_SWIGLU) {
+        const int tiles = (int)((a.wrows[0] + QTR - 1) / QTR);
+        G.gbase = shard_tile(tiles, a.shard, a.nshard);
+        G.groups = shard_tile(tiles, a.shard + 1, a.nshard) - G.gbase;
+        G.pieces = a.map == MAP_SINGLE ? 1 : 2;
     } else {
         G.half_tiles = (int)((a.D / 2) / QTR);
-        G.groups = (int)((a.H + 2 * a.Hkv) * G.half_tiles);
+        G.hq = (int)(a.H / a.nshard);
+        G.hkv = (int)(a.Hkv / a.nshard);
+        G.q0 = a.shard * G.hq;
+        G.kv0 = a.shard * G.hkv;
+        G.groups = (G.hq + 2 * G.hkv) * G.half_tiles;
         G.pieces = 2;
     }
     return G;
@@ -68,23 +78,22 @@ __device__ __forceinline__ const char *gemv_piece(const FusedArgs &a, const Gemv
                                                   int *tile) {
     int m = 0, t;
     if (a.map == MAP_SINGLE) {
-        t = g;
+        t = g + G.gbase;
     } else if (a.map == MAP_SWIGLU) {
         m = r;
-        t = g;
+        t = g + G.gbase;
     } else {
-        const int H = (int)a.H, Hkv = (int)a.Hkv;
         const int head = g / G.half_tiles, p = g - head * G.half_tiles;
         int h;
-        if (head < H) {
+        if (head < G.hq) {
             m = 0;
-            h = head;
-        } else if (head < H + Hkv) {
+            h = G.q0 + head;
+        } else if (head < G.hq + G.hkv) {
             m = 1;
-            h = head - H;
+            h = G.kv0 + head - G.hq;
         } else {
             m = 2;
-            h = head - H - Hkv;
+            h = G.kv0 + head - G.hq - G.hkv;
         }
         t = h * (2 * G.half_tiles) + p + r * G.half_tiles;
     }

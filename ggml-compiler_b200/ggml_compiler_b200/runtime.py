@@ -14,7 +14,7 @@ import json
 import os
 from dataclasses import dataclass
 from pathlib import Path
-from typing import Any
+from typing import Any, Callable
 
 import numpy as np
 
@@ -101,6 +101,8 @@ def _sigs() -> dict[str, tuple[list[Any], Any]]:
         "ggml_compiler_b200_n_kernel_stats": ([p], i),
         "ggml_compiler_b200_kernel_stats": ([p, i, ctypes.POINTER(c_str), ctypes.POINTER(ctypes.c_double),
                                              ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_double)], i),
+        "ggml_compiler_b200_tp_init": ([p, i, i, c_size, p, c_size], i),
+        "ggml_compiler_b200_tp_connect": ([p, p, c_size], i),
     }
 
 
@@ -327,6 +329,21 @@ class Session:
             out[name.value.decode()] = {"ms": ms.value, "launches": n.value, "bytes": b.value}
         return out
 
+    def tensor_parallel(self, rank: int, world: int, all_gather: Callable[[bytes], list[bytes]],
+                        window_bytes: int = 0) -> None:
+        """Join a tensor-parallel group of `world` processes, one GPU each, that loaded the same
+        program (ggml_compiler_b200_tp_init / _tp_connect). `all_gather(b)` returns every rank's
+        bytes in rank order (for example `torch_all_gather()`); call before the first run, on every
+        rank. Afterwards every rank must make the same runs; results equal one GPU's."""
+        lib = _load()
+        h = ctypes.create_string_buffer(256)
+        n = lib.ggml_compiler_b200_tp_init(self._m, rank, world, window_bytes, h, len(h))
+        if n < 0:
+            raise _error()
+        handles = exchange_handles(h.raw[:n], rank, world, all_gather)
+        if lib.ggml_compiler_b200_tp_connect(self._m, handles, len(handles)) != 0:
+            raise _error()
+
     def close(self) -> None:
         if getattr(self, "_m", None):
             _load().ggml_compiler_free(self._m)
@@ -340,6 +357,28 @@ class Session:
 
     def __del__(self) -> None:
         self.close()
+
+
+def exchange_handles(mine: bytes, rank: int, world: int, all_gather: Callable[[bytes], list[bytes]]) -> bytes:
+    """Every rank's window handle, concatenated in rank order, checked for shape."""
+    got = list(all_gather(bytes(mine)))
+    if len(got) != world:
+        raise ValueError(f"all_gather returned {len(got)} handles for a group of {world}")
+    if got[rank] != mine or any(len(g) != len(mine) for g in got):
+        raise ValueError("all_gather must return every rank's handle, in rank order, all of one size")
+    return b"".join(got)
+
+
+def torch_all_gather(group: Any = None) -> Callable[[bytes], list[bytes]]:
+    """An all_gather for Session.tensor_parallel over an initialised torch.distributed group."""
+    import torch.distributed as dist
+
+    def gather(b: bytes) -> list[bytes]:
+        out: list[Any] = [None] * dist.get_world_size(group)
+        dist.all_gather_object(out, b, group=group)
+        return out
+
+    return gather
 
 
 def _as_numpy(x: Any, dtype: np.dtype) -> np.ndarray:

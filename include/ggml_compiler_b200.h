@@ -29,6 +29,21 @@ GGML_COMPILER_API int ggml_compiler_b200_n_kernel_stats(const ggml_compiler_mode
 GGML_COMPILER_API int ggml_compiler_b200_kernel_stats(const ggml_compiler_model * m, int i, const char ** kind,
                                                       double * ms, int * launches, double * bytes);
 
+/* Tensor parallelism over NVLink peer memory. No counterpart in the reference, which runs on one
+   device (ggml_compiler_rt.h:57-62, options.device). Processes 0 .. world-1 (2..8), one GPU each,
+   load the same program. Each calls tp_init before its first run; it exports this rank's exchange
+   window and writes an opaque handle (the return value is its size, at most cap bytes). The caller
+   moves the handles between the processes with its own transport (torch.distributed, MPI, a file)
+   and every rank calls tp_connect with all ranks' handles concatenated in rank order. From then on
+   the decode GEMVs compute only this rank's rows (the QKV projection and attention its heads) and
+   the slices are exchanged through the peers' windows; every result stays identical to one GPU's.
+   All ranks must make the same sequence of runs; an exchange whose peer never arrives gives up
+   after 60 s (GGML_COMPILER_B200_TP_TIMEOUT_MS) and the run fails. window_bytes: 0 for 64 MiB (two
+   slots of half of it each bound the largest exchanged buffer). Returns -1 on failure. */
+GGML_COMPILER_API int ggml_compiler_b200_tp_init(ggml_compiler_model * m, int rank, int world, size_t window_bytes,
+                                                 void * handle, size_t cap);
+GGML_COMPILER_API int ggml_compiler_b200_tp_connect(ggml_compiler_model * m, const void * handles, size_t nbytes);
+
 /* Split-KV flash attention on caller-owned device buffers that allocates no device memory: the
    kernel the flash_attn node runs (reference: runtime/src/ops.cpp:217-240 -> ggml_flash_attn_ext,
    runtime/include/ggml_compiler_ops.h:133-135), with its scratch in a static device array of the

@@ -1,0 +1,55 @@
+"""One rank of the tensor-parallel GPU test (test_gpu_tp.py), run as its own process:
+
+    python tests/tp_worker.py MODEL.gguf OUT_DIR RANK WORLD PORT CASE.json
+
+Loads the model on GPU RANK, joins the group (handles moved by torch.distributed over gloo on
+127.0.0.1), feeds the case's chunks and greedy-decodes, and saves every step's logits and the tokens
+to OUT_DIR/rank{RANK}.npz."""
+
+import json
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parents[1]
+sys.path[:0] = [str(REPO), str(REPO / "ggml-compiler_b200")]
+
+
+def run_case(sess, case: dict) -> dict:
+    """Logits after each chunk (last row), greedy tokens through the host loop and the device loop."""
+    from ggml_compiler_b200.llm import Generator
+
+    g = Generator(sess)
+    g.reset()
+    logits = []
+    for c in case["chunks"]:
+        x = np.asarray(g.feed(c), np.float32)
+        logits.append(x if x.ndim == 1 else x[-1])
+    toks = g.generate(case["prompt"], case["max_new"])
+    dev = g.generate(case["prompt"], case["max_new"], device=True)
+    return {"logits": np.stack(logits), "tokens": np.array(toks), "device_tokens": np.array(dev)}
+
+
+def main() -> None:
+    import torch.distributed as dist
+
+    from ggml_compiler_b200.runtime import Session, torch_all_gather
+
+    path, out, rank, world, port, case = sys.argv[1], Path(sys.argv[2]), int(sys.argv[3]), int(sys.argv[4]), sys.argv[5], sys.argv[6]
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=120))
+    try:
+        sess = Session(path, backend="cuda", device=rank)
+        sess.tensor_parallel(rank, world, torch_all_gather())
+        res = run_case(sess, json.loads(Path(case).read_text()))
+        np.savez(out / f"rank{rank}.npz", **res)
+        dist.barrier()  # no rank frees its window while a peer may still push into it
+        sess.close()
+    finally:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
