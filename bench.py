@@ -20,6 +20,7 @@ are timed (one step = one token through all 32 layers; n_kv = 768).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 8b|tiny|sweep]
     python bench.py --config sweep [--shape NxK] [--m M] [--wtype q4_0|q8_0]   # config 2, one line per case
+    python bench.py --config prefill   # config 4: 8 x 2048-token Q8_0 prefill, tensor-core roofline
 """
 
 from __future__ import annotations
@@ -216,18 +217,101 @@ def sweep(args) -> None:
                                   "l2": "flushed before each rep (256 MB write)"}), flush=True)
 
 
+PREFILL_METRIC = "8B-shape Q8_0 prefill tok/s (8 sequences x 2048-token prompts); tensor-core TFLOP/s"
+
+
+def prefill_bench(args) -> None:
+    """BASELINE config 4's prefill: the 8B shape with Q8_0 projections, 8 random 2048-token prompts
+    (seed 2), each prefilled in one 2048-row call (tensor-core GEMMs, flash prefill), then 64 greedy
+    decode steps per sequence. The reference program is batch 1, so the 8 sequences run one after
+    another. One JSON line: prefill tok/s (device time), e2e (host arrays through Session.run:
+    tokens, positions and the f32 mask up, logits down), and the GEMMs' FLOP rate from a profiled
+    pass against the measured dense bf16 peak (the int8 MMAs' nominal peak is twice that)."""
+    import dataclasses
+
+    import torch
+
+    from ggml_compiler_b200.llm import LLAMA3_8B, Generator, build_llama_gguf
+    from ggml_compiler_b200.runtime import Session
+
+    sh = dataclasses.replace(LLAMA3_8B, weight_type="q8_0", max_context=2304, max_prompt=2048)
+    CACHE.mkdir(parents=True, exist_ok=True)
+    gguf = CACHE / "8b_q8_0_ctx2304_seed0.gguf"
+    if not gguf.exists():
+        tmp = gguf.with_suffix(".part")
+        build_llama_gguf(tmp, sh, seed=0)
+        tmp.rename(gguf)
+    n_seq, plen, n_dec = 8, 2048, 64
+    prompts = np.random.default_rng(2).integers(0, sh.vocab, (n_seq, plen))
+    s = Session(gguf, backend="cuda")
+    g = Generator(s)
+    # warm-up: one sequence (plans and graphs for the 2048-row call and decode at n_kv 2304)
+    g.reset()
+    tok = int(np.argmax(g.feed(prompts[0].tolist())))
+    for _ in range(max(3, args.warmup)):
+        tok = int(np.argmax(g.feed([tok])))
+    pre_dev = pre_wall = dec_dev = 0.0
+    with Clocks(0) as clk:
+        for i in range(n_seq):
+            g.reset()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            tok = int(np.argmax(g.feed(prompts[i].tolist())))
+            pre_wall += time.perf_counter() - t0
+            pre_dev += s.last_device_ms
+            for _ in range(n_dec):
+                tok = int(np.argmax(g.feed([tok])))
+                dec_dev += s.last_device_ms
+    # profiled pass over one prefill: the GEMM kernels' share and FLOP rate
+    g.reset()
+    s.set_profiling(True)
+    g.feed(prompts[0].tolist())
+    ks = s.kernel_stats()
+    s.set_profiling(False)
+    s.close()
+    d, H, Hkv, D, F = sh.d_model, sh.heads, sh.kv_heads, sh.hd, sh.ffn
+    gemm_flops = 2.0 * plen * d * (H * D + 2 * Hkv * D + d + 3 * F) * sh.layers + 2.0 * d * sh.vocab  # head: last row
+    attn_flops = 4.0 * H * D * (plen * (plen + 1) / 2) * sh.layers  # QK^T and PV over the causal half
+    mm = ks.get("mul_mat", {"ms": 0.0, "launches": 0})
+    total_ms = sum(v["ms"] for v in ks.values())
+    pk = REPO / "MEASURED_PEAKS.json"
+    tflops_peak = float(json.loads(pk.read_text())["bf16_tflops"]) if pk.exists() else 1590.0
+    achieved = gemm_flops / (mm["ms"] / 1000.0) / 1e12 if mm["ms"] else 0.0
+    value = n_seq * plen / (pre_dev / 1000.0)
+    print(json.dumps({
+        "metric": PREFILL_METRIC, "value": value, "unit": "tok/s", "n_gpus": 1, "steps": n_seq, "warmup": max(3, args.warmup),
+        "ms_per_step": pre_dev / n_seq, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q8_0 weights, int8 x int8 tcgen05.mma (kind::i8) block products, f32 scaling", "data": "synthetic",
+        "config": {"workload": "llama3-8b-shape Q8_0, 8 x 2048-token prefill (one call each) + 64 decode steps each "
+                               "(BASELINE config 4; batch 1 per call: the reference program has no batch dim)",
+                   "layers": sh.layers, "d_model": d, "heads": H, "kv_heads": Hkv, "ffn": F, "vocab": sh.vocab,
+                   "weights": "q8_0", "l2": "no flush: each call streams 7.5 GB of weights and GBs of activations"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s",
+                     "frac": achieved / tflops_peak, "traffic": None, "kernel": "mul_mat (gemm_tc)",
+                     "peak_source": "measured bf16_tflops (MEASURED_PEAKS.json); int8 nominal peak is 2x",
+                     "gemm_flops_per_call": gemm_flops, "attn_flops_per_call": attn_flops,
+                     "gemm_share_of_call": mm["ms"] / total_ms if total_ms else None},
+        "e2e": {"value": n_seq * plen / pre_wall, "unit": "tok/s", "h2d_bytes_per_step": plen * 8 + plen * plen * 4,
+                "d2h_bytes_per_step": 4 * sh.vocab},
+        "decode_tok_s": n_seq * n_dec / (dec_dev / 1000.0),
+        "gpu_launches": int(sum(v["launches"] for v in ks.values()) * n_seq),
+        "clocks": clk.summary(),
+        "kernel_breakdown_ms_per_call": {k: v["ms"] for k, v in sorted(ks.items(), key=lambda kv: -kv[1]["ms"])},
+    }), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="8b", choices=["8b", "tiny", "sweep"])
+    ap.add_argument("--config", default="8b", choices=["8b", "tiny", "sweep", "prefill"])
     ap.add_argument("--shape", default=None, help="sweep: one weight shape NxK")
     ap.add_argument("--m", type=int, default=None, help="sweep: one activation row count")
     ap.add_argument("--wtype", default=None, choices=["q4_0", "q8_0"], help="sweep: one weight type")
-    ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
-                    help="N>1: one sequence tensor-parallel over the N GPUs (tp), or N independent sequences")
+    ap.add_argument("--parallel", default="replicas", choices=["tp", "replicas"],
+                    help="N>1: N independent sequences (replicas), or one sequence tensor-parallel over the N GPUs (tp)")
     ap.add_argument("--cpu-tokens", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -236,6 +320,9 @@ def main() -> None:
         if args.steps == ap.get_default("steps"):
             args.steps = 10
         sweep(args)
+        return
+    if args.config == "prefill":
+        prefill_bench(args)
         return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -101,6 +101,11 @@ size_t flash_split_scratch_bytes(const TD &q, const TD &k);
 size_t flash_split_counters(const TD &q, const TD &k);
 void flash_attn_split(const TD &q, const TD &k, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
                       int *counters, int *err, cudaStream_t s);
+// The same result for prefill calls (16+ query rows, head size 64 or 128, K/V rows contiguous):
+// one CTA per 64 (row, head) pairs over every chunk, merge in the CTA (gc_flash_prefill.cu).
+bool flash_prefill_ok(const TD &q, const TD &k, const TD &v, const TD &out);
+void flash_prefill(const TD &q, const TD &k, const TD &v, const TD *mask, const TD &out, float scale, int *err,
+                   cudaStream_t s);
 
 // Tensor-parallel exchange (gc_tp.cu). A window is TP_FLAG_BYTES of flag words (one per sender)
 // followed by two slots of slot_bytes; every rank maps every window.

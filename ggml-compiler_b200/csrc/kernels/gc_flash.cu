@@ -30,6 +30,7 @@ constexpr int CH = FL_CH;  // keys per chunk (the order's chunk size)
 constexpr int MAXD_ALL = 256;  // head sizes up to 256 here (D % 32 == 0); others use the generic kernel
 constexpr int WPH = 4;     // warps per query head
 constexpr int MAXG = 4;    // query heads per CTA (larger GQA groups loop)
+constexpr int RQ = 16;     // query rows per CTA (prefill): the chunk's K/V rows are staged once for all
 
 struct SplitArgs {
     const char *q;
@@ -65,11 +66,12 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
 
     const int64_t ch = blockIdx.x;
     const int64_t hk = blockIdx.y % a.Hkv, b = blockIdx.y / a.Hkv;
-    const int64_t iq = blockIdx.z;
+    const int64_t iq0 = blockIdx.z * (int64_t)RQ, iq1 = min(iq0 + RQ, a.Sq);
     const int64_t j0 = ch * CH;
     const int n = (int)min((int64_t)CH, a.nkv - j0);
     const int warp = threadIdx.x >> 5;
     const int64_t G = a.H / a.Hkv;
+    const float ninf = -__int_as_float(0x7f800000);
 
     pdl_wait();  // the KV cache row of this step was written by the previous kernel
     if (threadIdx.x == 0) {
@@ -77,20 +79,6 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
         mbar_fence_init();
     }
     __syncthreads();
-    FlashChunk fc;
-    fc.q = a.q + iq * a.qnb1 + (hk * G) * a.qnb2 + b * a.qnb3;
-    fc.qnb0 = a.qnb0;
-    fc.qnbh = a.qnb2;
-    fc.mask = a.mask ? a.mask + iq * a.mnb1 + ((hk * G) % a.mne2) * a.mnb2 + (b % a.mne3) * a.mnb3 + j0 * 2 : nullptr;
-    fc.mne2 = a.mne2;
-    fc.mnbh = a.mnb2;
-    fc.hbase = (int)(hk * G);
-    fc.scale = a.scale;
-    fc.D = D;
-    fc.n = n;
-    fc.G = (int)G;
-    fc.part = a.part + ((((b * a.Sq + iq) * a.H + hk * G) * a.nch + ch) * (a.D + 2));
-    fc.pstride = a.nch * (a.D + 2);
     const bool rows_contig = a.knb1 == 2 * a.D && a.vnb1 == 2 * a.D;
     if (rows_contig) {
         if (threadIdx.x == 0) {
@@ -99,45 +87,71 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
             bulk_g2s(Ks, a.k + hk * a.knb2 + b * a.knb3 + j0 * a.knb1, bytes, &bar);
             bulk_g2s(Vs, a.v + hk * a.vnb2 + b * a.vnb3 + j0 * a.vnb1, bytes, &bar);
         }
-        flash_stage(fc, qs, ms, threadIdx.x, blockDim.x);  // while the copies are in flight
-        __syncthreads();
-        if (!mbar_wait(&bar, 0)) {
-            if (a.err) atomicExch(a.err, 2);
-            return;
-        }
     } else {
         for (int t = threadIdx.x; t < n * D / 2; t += blockDim.x) {
             const int r = t / (D / 2), w = t % (D / 2);
             ((uint32_t *)(Ks + r * D))[w] = ((const uint32_t *)(a.k + hk * a.knb2 + b * a.knb3 + (j0 + r) * a.knb1))[w];
             ((uint32_t *)(Vs + r * D))[w] = ((const uint32_t *)(a.v + hk * a.vnb2 + b * a.vnb3 + (j0 + r) * a.vnb1))[w];
         }
-        flash_stage(fc, qs, ms, threadIdx.x, blockDim.x);
-        __syncthreads();
     }
-    const int nslots = (int)(blockDim.x / 32) / WPH;
-    flash_chunk<WPH, MAXD>(fc, Ks, Vs, qs, ms, sc, ps, nslots, SyncCta());  // MAXD is the head size
-
-    // the last CTA of this (batch, query row, K/V head) merges every chunk of its heads
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();  // this CTA's partials (ordered before by the barrier) are visible first
-        int *cnt = a.counters + (b * a.Sq + iq) * a.Hkv + hk;
-        last = atomicAdd(cnt, 1) == (int)a.nch - 1;
-        if (last) {
-            *cnt = 0;
-            __threadfence();
+    // The chunk's K/V rows stay in shared memory for every query row of this CTA; each row's
+    // partials are exactly the one-row kernel's (same chunk, same order).
+    for (int64_t iq = iq0; iq < iq1; iq++) {
+        FlashChunk fc;
+        fc.q = a.q + iq * a.qnb1 + (hk * G) * a.qnb2 + b * a.qnb3;
+        fc.qnb0 = a.qnb0;
+        fc.qnbh = a.qnb2;
+        fc.mask = a.mask ? a.mask + iq * a.mnb1 + ((hk * G) % a.mne2) * a.mnb2 + (b % a.mne3) * a.mnb3 + j0 * 2 : nullptr;
+        fc.mne2 = a.mne2;
+        fc.mnbh = a.mnb2;
+        fc.hbase = (int)(hk * G);
+        fc.scale = a.scale;
+        fc.D = D;
+        fc.n = n;
+        fc.G = (int)G;
+        fc.part = a.part + ((((b * a.Sq + iq) * a.H + hk * G) * a.nch + ch) * (a.D + 2));
+        fc.pstride = a.nch * (a.D + 2);
+        flash_stage(fc, qs, ms, threadIdx.x, blockDim.x);  // the first row: while the copies are in flight
+        // a chunk whose keys the mask hides from every head of this row contributes nothing: its
+        // partial is (m = -inf, l = 0), which the merge skips, without the arithmetic
+        int live = !fc.mask;
+        for (int i = threadIdx.x; !live && i < (int)G * CH; i += blockDim.x) live = (i % CH) < n && ms[i] != ninf;
+        live = __syncthreads_or(live);
+        if (iq == iq0 && rows_contig && !__syncthreads_and(mbar_wait(&bar, 0))) {  // every thread leaves together
+            if (threadIdx.x == 0 && a.err) atomicExch(a.err, 2);
+            return;
         }
-    }
-    __syncthreads();
-    if (!last) return;
-    for (int64_t g = warp; g < G; g += blockDim.x / 32) {
-        const int64_t h = hk * G + g;
-        flash_merge<MAXD>(a.part + (((b * a.Sq + iq) * a.H + h) * a.nch) * (a.D + 2), (int)a.nch,
-                          a.out + a.D * (h + a.oH * (iq + a.Sq * b)));
+        if (live) {
+            const int nslots = (int)(blockDim.x / 32) / WPH;
+            flash_chunk<WPH, MAXD>(fc, Ks, Vs, qs, ms, sc, ps, nslots, SyncCta());  // MAXD is the head size
+        } else if (threadIdx.x < G) {
+            fc.part[threadIdx.x * fc.pstride] = ninf;
+            fc.part[threadIdx.x * fc.pstride + 1] = 0.0f;
+        }
+
+        // the last CTA of this (batch, query row, K/V head) merges every chunk of its heads
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();  // this CTA's partials (ordered before by the barrier) are visible first
+            int *cnt = a.counters + (b * a.Sq + iq) * a.Hkv + hk;
+            last = atomicAdd(cnt, 1) == (int)a.nch - 1;
+            if (last) {
+                *cnt = 0;
+                __threadfence();
+            }
+        }
+        __syncthreads();
+        if (last)
+            for (int64_t g = warp; g < G; g += blockDim.x / 32) {
+                const int64_t h = hk * G + g;
+                flash_merge<MAXD>(a.part + (((b * a.Sq + iq) * a.H + h) * a.nch) * (a.D + 2), (int)a.nch,
+                                  a.out + a.D * (h + a.oH * (iq + a.Sq * b)));
+            }
+        __syncthreads();  // qs / ms / sc / ps and `last` are reused by the next row
     }
 }
 
-constexpr size_t kMaxPartBytes = 64u << 20;  // scratch for chunk partials per row group
+constexpr size_t kMaxPartBytes = 256u << 20;  // scratch for chunk partials per row group
 
 }  // namespace
 
@@ -158,6 +172,10 @@ size_t flash_split_counters(const TD &q, const TD &kk) {
 
 void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
                       int *counters, int *err, cudaStream_t s) {
+    if (flash_prefill_ok(q, kk, v, out)) {
+        flash_prefill(q, kk, v, mask, out, scale, err, s);
+        return;
+    }
     SplitArgs a{};
     a.q = q.data;
     a.D = q.ne[0];
@@ -223,7 +241,7 @@ void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, co
         g.Sq = nq;
         g.out = (float *)out.data + q0 * a.D * a.oH;  // out [D, oH, Sq, B]: rows q0.. (one batch)
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)a.nch, (unsigned)(a.Hkv * a.B), (unsigned)nq);
+        cfg.gridDim = dim3((unsigned)a.nch, (unsigned)(a.Hkv * a.B), (unsigned)((nq + RQ - 1) / RQ));
         cfg.blockDim = dim3(threads);
         cfg.dynamicSmemBytes = smem;
         cfg.stream = s;

@@ -15,6 +15,10 @@
 // in between, whose flag the reader sets only after its own earlier exchange (the one reading the
 // slot) has finished: stream order on the reader, so no slot is overwritten while it is read.
 //
+// The kernel is launched with programmatic stream serialization and triggers its dependents at
+// once, so the next GEMV streams its weights while the exchange waits; every kernel reads its
+// inputs only after griddepcontrol.wait, which covers the exchange's writes.
+//
 // Waits give up after a time limit and set error word 4 (and skip the pull); a rank whose error
 // word is already set does not wait at all, so a dead peer costs one time-out, not one per
 // exchange.
@@ -22,6 +26,7 @@
 #include <string>
 
 #include "../gc_kernels.h"
+#include "gc_tma.cuh"
 
 namespace gcb {
 namespace k {
@@ -54,9 +59,13 @@ __device__ __forceinline__ void copy_rows(char *dst, int64_t ld, const char *src
     }
 }
 
-__global__ void __launch_bounds__(1024) tp_exchange_kernel(TpExchange x) {
+__global__ void __launch_bounds__(512) tp_exchange_kernel(TpExchange x) {
     __shared__ unsigned s_seq;
     __shared__ int s_fail;
+    // Launched early (PDL): let the next kernel start too (its weight stream reads nothing this
+    // kernel writes; its griddepcontrol.wait covers the rest), then wait for the slices' producer.
+    pdl_trigger();
+    pdl_wait();
     if (threadIdx.x == 0) {
         s_seq = *x.seq + 1;
         s_fail = *(volatile int *)x.err != 0;
@@ -110,8 +119,16 @@ bool tp_exchange_ok(const TpExchange &x) {
 void tp_exchange(const TpExchange &x, cudaStream_t s) {
     if (!tp_exchange_ok(x) || (uintptr_t)x.buf % 16)
         throw std::runtime_error("tp_exchange: slices are not 16-byte aligned or exceed the window slot");
-    tp_exchange_kernel<<<1, 1024, 0, s>>>(x);
-    const cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(512);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, tp_exchange_kernel, x);
     if (e != cudaSuccess) throw std::runtime_error(std::string("CUDA launch of tp_exchange failed: ") + cudaGetErrorString(e));
 }
 

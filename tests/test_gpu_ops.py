@@ -67,3 +67,47 @@ def test_quant_gemm_bit_exact(gpu, tmp_path, wtype, N, K, M):
     got = run_mm(tmp_path, w, wtype, x)
     ref = oracle.mul_mat(oracle.quantize(w, wtype), wtype, K, x)
     np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("D,H,HKV,NQ,NKV,mask", [
+    (128, 32, 8, 300, 700, "causal"),  # prefill kernel: GQA 4, 11 chunks, -65504 above the diagonal
+    (128, 8, 8, 16, 130, "none"),      # prefill kernel: no GQA, no mask, ragged last chunk
+    (64, 16, 2, 40, 260, "inf"),       # prefill kernel: GQA 8, -inf above the diagonal
+    (64, 4, 4, 70, 64, "random"),      # prefill kernel: one chunk, finite random mask
+    (128, 32, 8, 9, 700, "causal"),    # split-KV kernel (fewer than 16 rows)
+])
+def test_flash_attn_bit_exact(gpu, tmp_path, D, H, HKV, NQ, NKV, mask):
+    """flash_attn as a one-node program against the oracle, bit for bit, through the prefill kernel
+    (16+ query rows) and the split-KV kernel; the causal masks use the reference programs' -65504 (every
+    chunk computed) or -inf (hidden chunks skipped by the merge), with rows whose keys are all hidden
+    in the later chunks."""
+    from ggml_compiler_b200.gguf_write import write_gguf
+    from ggml_compiler_b200.programs import single_node_program
+    from oracle.interp import Program
+
+    rng = np.random.default_rng(D + H + NQ)
+    q = rng.standard_normal((1, H, NQ, D), dtype=np.float32)
+    k = (rng.standard_normal((1, HKV, NKV, D), dtype=np.float32) * 0.5).astype(np.float16)
+    v = rng.standard_normal((1, HKV, NKV, D), dtype=np.float32).astype(np.float16)
+    ins = [("q", "f32", [D, NQ, H, 1], [1, H, NQ, D]), ("k", "f16", [D, NKV, HKV, 1], [1, HKV, NKV, D]),
+           ("v", "f16", [D, NKV, HKV, 1], [1, HKV, NKV, D])]
+    feed = {"q": q, "k": k, "v": v}
+    if mask != "none":
+        m = np.zeros((NQ, NKV), np.float32)
+        if mask == "random":
+            m = rng.standard_normal((NQ, NKV), dtype=np.float32) * 2
+        else:
+            hide = np.float32(-65504.0) if mask == "causal" else np.float32(-np.inf)
+            for i in range(NQ):
+                m[i, NKV - NQ + i + 1:] = hide
+        ins.append(("mask", "f16", [NKV, NQ, 1, 1], [1, 1, NQ, NKV]))
+        feed["mask"] = m.astype(np.float16)[None, None]
+    prog = single_node_program("flash_attn", ins, [n for n, *_ in ins], "f32", [D, H, NQ, 1], [1, NQ, H, D],
+                               {"scale": float(1.0 / np.sqrt(D))})
+    path = tmp_path / "fa.gguf"
+    write_gguf(path, prog, [])
+    with Session(path, backend="cuda") as s:
+        got = s.run(**feed)["out.0"]
+    want = Program(path).run("main", **feed)["out.0"]
+    assert np.isfinite(got).all()
+    np.testing.assert_array_equal(got, want)
