@@ -73,7 +73,8 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
     const int64_t G = a.H / a.Hkv;
     const float ninf = -__int_as_float(0x7f800000);
 
-    pdl_wait();  // the KV cache row of this step was written by the previous kernel
+    pdl_trigger();  // the next GEMV may start streaming its weights now; it waits for this grid to finish before reading
+    pdl_wait();     // the KV cache row of this step was written by the previous kernel
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         mbar_fence_init();
