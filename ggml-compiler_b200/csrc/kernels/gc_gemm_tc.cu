@@ -74,6 +74,28 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// Packed f32x2 arithmetic (sm_100): two independent IEEE single-precision operations, low word
+// first; the results are those of the scalar operations.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+    return ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t f32x2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f32x2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+constexpr uint64_t kBias2 = 0xCB400000CB400000ull;  // (-12582912.0f, -12582912.0f)
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
@@ -158,9 +180,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(GemmArgs g) {
         // ------------------------------------------------------------ epilogue
         const int q = warp & 3, h = warp >> 2;
         const int row = q * 32 + lane;  // weight row within the tile = TMEM lane
-        float acc[EC];
+        uint64_t acc2[EC / 2];  // two f32 sums per register pair
 #pragma unroll
-        for (int i = 0; i < EC; i++) acc[i] = 0.0f;
+        for (int i = 0; i < EC / 2; i++) acc2[i] = 0ull;
         const int nst = nb / KB;
         for (int st = 0; st < nst; st++) {
             const int s = st % S;
@@ -177,13 +199,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(GemmArgs g) {
                 if (j + 1 < KB) tmem_ld16(t0 + (uint32_t)((j + 1) * BN), v[(j + 1) & 1]);
                 const float dw = dws[(s * KB + j) * BM + row];
                 const float *dxr = dxs + (s * KB + j) * BN + h * EC;
+                const uint64_t dw2 = f2pack(dw, dw);
 #pragma unroll
-                for (int c = 0; c < EC; c += 4) {
-                    const float4 d4 = *(const float4 *)(dxr + c);
-                    const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
-#pragma unroll
-                    for (int u = 0; u < 4; u++)
-                        acc[c + u] = __fmaf_rn(__fmul_rn(dw, dd[u]), (float)(int)v[j & 1][c + u], acc[c + u]);
+                for (int c = 0; c < EC; c += 2) {
+                    // acc = fma(dw * dx, (float)isum, acc) for two columns at once (packed f32x2,
+                    // each lane an ordinary IEEE op); isum -> float exactly through the 1.5 * 2^23
+                    // bias (|isum| <= 32 * 127 * 127 < 2^22)
+                    const uint64_t p2 = f32x2_mul(dw2, *(const uint64_t *)(dxr + c));
+                    const uint64_t i2 = f2pack(__uint_as_float(v[j & 1][c] + 0x4B400000u), __uint_as_float(v[j & 1][c + 1] + 0x4B400000u));
+                    acc2[c / 2] = f32x2_fma(p2, f32x2_add(i2, kBias2), acc2[c / 2]);
                 }
                 if (j + 1 < KB) tmem_wait(v[(j + 1) & 1]);
             }
@@ -196,7 +220,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc_kernel(GemmArgs g) {
 #pragma unroll
             for (int i = 0; i < EC; i++) {
                 const int m = m0 + h * EC + i;
-                if (m < g.M) g.out[(int64_t)m * g.N + n] = acc[i];
+                if (m < g.M) g.out[(int64_t)m * g.N + n] = __uint_as_float((unsigned)(acc2[i / 2] >> (32 * (i & 1))));
             }
     } else if (warp < NEPI + NLD) {
         // ------------------------------------------------------------ loaders
