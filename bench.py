@@ -44,13 +44,17 @@ CACHE = Path(os.environ.get("GCB_BENCH_CACHE", "/tmp/gcb_bench"))
 
 
 def shape_for(config: str):
-    from ggml_compiler_b200.llm import LLAMA3_8B, TINY, LlamaShape
+    """(shape, workload, prompt tokens, n_kv of the timed decode steps)."""
+    from ggml_compiler_b200.llm import LLAMA3_8B, LLAMA3_70B, TINY, LlamaShape
 
     if config == "8b":
-        return LLAMA3_8B, "llama3-8b-shape Q4_0, batch 1, 512-token prompt, greedy decode (BASELINE config 3)"
+        return LLAMA3_8B, "llama3-8b-shape Q4_0, batch 1, 512-token prompt, greedy decode (BASELINE config 3)", 512, 768
+    if config == "70b":
+        return (LLAMA3_70B, "llama3-70b-shape Q4_0, batch 1, 1024-token prompt, greedy decode (BASELINE config 5)",
+                1024, 1280)
     if config == "tiny":
         sh = LlamaShape(**{**TINY.__dict__, "max_prompt": 512})
-        return sh, "tiny Llama Q8_0 (BASELINE config 1 shape), batch 1"
+        return sh, "tiny Llama Q8_0 (BASELINE config 1 shape), batch 1", 512, 768
     raise ValueError(config)
 
 
@@ -306,7 +310,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="8b", choices=["8b", "tiny", "sweep", "prefill"])
+    ap.add_argument("--config", default="8b", choices=["8b", "70b", "tiny", "sweep", "prefill"])
     ap.add_argument("--shape", default=None, help="sweep: one weight shape NxK")
     ap.add_argument("--m", type=int, default=None, help="sweep: one activation row count")
     ap.add_argument("--wtype", default=None, choices=["q4_0", "q8_0"], help="sweep: one weight type")
@@ -327,19 +331,21 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    sh, workload = shape_for(args.config)
-    K, W = args.steps, max(3, args.warmup)
+    sh, workload, P, NKV = shape_for(args.config)
+    K, W = min(args.steps, NKV - P), max(3, args.warmup)
+    metric = METRIC if args.config != "70b" else "70B-shape Q4_0 decode tok/s; quant-GEMV HBM GB/s as % of B200 peak"
+    wgb = weight_bytes(sh) / 1e9
     config = {"workload": workload, "layers": sh.layers, "d_model": sh.d_model, "heads": sh.heads,
               "kv_heads": sh.kv_heads, "ffn": sh.ffn, "vocab": sh.vocab, "weights": sh.weight_type, "batch": 1,
-              "prompt": 512, "decode_tokens": K, "n_kv": 768,
-              "l2": "no flush: the decode step streams all weights (4.2 GB) through a 126 MB L2"}
+              "prompt": P, "decode_tokens": K, "n_kv": NKV,
+              "l2": f"no flush: the decode step streams all weights ({wgb:.1f} GB) through a 126 MB L2"}
 
     if args.impl == "reference":
         if world > 1 and rank != 0:
             return
         gguf = model_path(sh, args.config, 0, 1)
         cb = cpu_baseline(gguf, sh, max(1, args.cpu_tokens))
-        print(json.dumps({"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tok/s",
+        print(json.dumps({"impl": "reference", "metric": metric, "value": cb["value"], "unit": "tok/s",
                           "n_gpus": args.gpus, "steps": args.cpu_tokens, "warmup": 0,
                           "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
                           "vs_baseline": None, "dtype": "q4_0 weights, int8 x int4 block dots, f32 sums",
@@ -370,7 +376,7 @@ def main() -> None:
     seqs = 1 if tp else world  # sequences decoded by the whole job
     stream = torch.cuda.ExternalStream(s.stream, device=torch.device("cuda", local))
     g = Generator(s)
-    prompt = np.random.default_rng(1).integers(0, sh.vocab, 512).tolist()
+    prompt = np.random.default_rng(1).integers(0, sh.vocab, P).tolist()
 
     def prefill() -> int:
         g.reset()
@@ -378,10 +384,10 @@ def main() -> None:
 
     def generate(first: int, n: int) -> float:
         s.set_symbol("max_new", n)
-        s.run(first=np.array([[first]], np.int32), start=np.array([512], np.int32), entry="generate")
+        s.run(first=np.array([[first]], np.int32), start=np.array([P], np.int32), entry="generate")
         return s.last_device_ms
 
-    # warm-up: prefill + W device-loop steps (graphs captured for n_kv 768)
+    # warm-up: prefill + W device-loop steps (graphs captured for the decode n_kv)
     first = prefill()
     generate(first, W)
 
@@ -403,7 +409,7 @@ def main() -> None:
 
     # e2e: host loop through the public API, pinned host buffers, K decode steps
     first = prefill()
-    n_kv = 768
+    n_kv = NKV
     tok_h = torch.empty((1, 1), dtype=torch.int32, pin_memory=True).numpy()
     pos_h = torch.empty(1, dtype=torch.int32, pin_memory=True).numpy()
     mask_h = torch.empty((1, 1, 1, n_kv), dtype=torch.float32, pin_memory=True).numpy()
@@ -432,7 +438,7 @@ def main() -> None:
     ctypes_i64 = ctypes.c_int64
     tok = first
     for i in range(W):
-        tok = e2e_step(tok, 512 + i)
+        tok = e2e_step(tok, P + i)
     first = prefill()
     tok = first
     barrier()
@@ -440,7 +446,7 @@ def main() -> None:
     ev0.record(stream)
     w0 = time.perf_counter()
     for i in range(K):
-        tok = e2e_step(tok, 512 + i)
+        tok = e2e_step(tok, P + i)
     ev1.record(stream)
     ev1.synchronize()
     wall = time.perf_counter() - w0
@@ -468,7 +474,7 @@ def main() -> None:
     achieved = gemv_bytes / (gemv_ms / 1000.0) / 1e9 if gemv_ms else 0.0
 
     out = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "metric": metric, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": dev_ms / K, "higher_is_better": True, "scaling": "strong" if tp else "weak",
         "vs_baseline": None, "dtype": "q4_0 weights, int8 x int4 block dots, f32 sums", "data": "synthetic",
         "config": {**config, "parallelism": (f"tp{world}: rows / heads split, exchanges over NVLink peer memory" if tp

@@ -18,7 +18,9 @@
 //   weight is exactly 0 for every pair of the CTA (the causal mask's hidden keys, -65504 in the
 //   reference's programs) changes nothing, L + 0 = L and O + 0 * o_c = O, as long as O is
 //   nonzero; such chunks are skipped unless some O element is still zero (where the sign of the
-//   zero could depend on o_c), in which case the chunk is computed as usual.
+//   zero could depend on o_c), in which case the chunk is computed as usual. Pass 1 also skips the
+//   scores of a chunk when a bound (|q|_1 max|k| |scale| plus the chunk's largest mask value) puts
+//   every pair's chunk maximum 128 below one already computed: its weight is then exactly 0.
 #include <stdexcept>
 #include <string>
 
@@ -60,6 +62,10 @@ constexpr size_t prefill_smem() {
 
 __device__ __forceinline__ float f16_round(float x) { return __half2float(__float2half_rn(x)); }
 
+// Stand-in maximum of a chunk whose weight is provably 0: finite (so the merge folds it, as the
+// checker folds every finite chunk) and far below any real maximum it is compared with.
+constexpr float kNegligible = -3.0e38f;
+
 template <int D>
 __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) {
     constexpr int CPL = D / 32, KC = FL_CH, DG = D / 4, RPT = PF_RH * DG / PF_NT;
@@ -74,6 +80,10 @@ __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) 
     __half *Kraw = (__half *)(Mr + PF_RH);  // [KC][D] bulk-copy target for K
     __half *Vs = Kraw + KC * D;             // [KC][D]
     __shared__ uint64_t bar;
+    __shared__ float qL1[PF_RH];   // sum of |q| per pair (bounds the pair's scores)
+    __shared__ float Mk[PF_RH];    // pass 1: the largest chunk maximum computed so far
+    __shared__ float mmax[PF_RH];  // the chunk's largest mask value per pair
+    __shared__ unsigned kmax_bits; // the chunk's largest |k| (float bits, non-negative)
 
     const int tid = threadIdx.x;
     const int G = (int)(a.H / a.Hkv), R = PF_RH / G;
@@ -98,6 +108,12 @@ __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) 
         Qs[i] = x;
     }
     __syncthreads();
+    if (tid < PF_RH) {
+        float l1 = 0.0f;
+        for (int e = 0; e < D; e++) l1 = __fadd_rn(l1, fabsf(Qs[tid * D + e]));
+        qL1[tid] = l1;
+        Mk[tid] = -__int_as_float(0x7f800000);
+    }
     uint32_t phase = 0;
     bool ok = true;
 
@@ -106,6 +122,7 @@ __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) 
         const int64_t j0 = c * KC;
         const int n = (int)min((int64_t)KC, a.nkv - j0);
         if (tid == 0) {
+            kmax_bits = 0u;
             const uint32_t bytes = (uint32_t)(n * D * 2);
             mbar_expect_tx(&bar, with_v ? 2 * bytes : bytes);
             bulk_g2s(Kraw, kbase + j0 * 2 * D, bytes, &bar);
@@ -123,6 +140,7 @@ __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) 
         const bool got = __syncthreads_and(mbar_wait(&bar, phase));
         phase ^= 1u;
         if (!got) return false;
+        float kabs = 0.0f;
         for (int i = tid; i < KC * (D / 8); i += PF_NT) {
             const int j = i % KC, eg = i / KC;
             float f[8];
@@ -140,8 +158,24 @@ __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) 
                 for (int t = 0; t < 8; t++) f[t] = 0.0f;
             }
 #pragma unroll
-            for (int t = 0; t < 8; t++) Kt[(eg * 8 + t) * PF_KTS + j] = f[t];
+            for (int t = 0; t < 8; t++) {
+                Kt[(eg * 8 + t) * PF_KTS + j] = f[t];
+                kabs = fmaxf(kabs, fabsf(f[t]));
+            }
         }
+        // per pair: the largest mask value of the chunk's keys (8 threads per pair)
+        {
+            const int pr = tid >> 3, part = tid & 7;
+            float mx = -__int_as_float(0x7f800000);
+            for (int j = part * 8; j < part * 8 + 8; j++)
+                if (j < n) mx = fmaxf(mx, Ms[pr * KC + j]);
+#pragma unroll
+            for (int off = 4; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            if (part == 0) mmax[pr] = mx;
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) kabs = fmaxf(kabs, __shfl_xor_sync(0xffffffffu, kabs, off));
+        if ((tid & 31) == 0) atomicMax(&kmax_bits, __float_as_uint(kabs));  // NaN bits compare above every finite value
         __syncthreads();
         return true;
     };
@@ -209,11 +243,27 @@ __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) 
             ok = false;
             break;
         }
+        // A pair's scores in this chunk are at most |q|_1 max|k| |scale| + its largest mask value (the
+        // factor and the 1 cover rounding). When that is 128 below a chunk maximum already computed,
+        // the chunk's weight exp(m_c - M) is exactly 0 and m_c does not raise M: every pair of the
+        // CTA records a stand-in maximum (finite, weight 0) and the scores are not computed.
+        int hidden = 1;
+        if (tid < PF_RH && valid(tid)) {
+            const float bound = __fadd_rn(__fmul_rn(__fmul_rn(__fmul_rn(qL1[tid], __uint_as_float(kmax_bits)), fabsf(a.scale)), 1.01f), 1.0f);
+            hidden = __fadd_rn(bound, mmax[tid]) < __fsub_rn(Mk[tid], 128.0f);
+        }
+        if (__syncthreads_and(hidden)) {
+            if (tid < PF_RH) mc[tid * PF_MAXCH + c] = kNegligible;
+            __syncthreads();
+            continue;
+        }
         float m[2];
         scores(n, m);
         if (kg == 0) {
             mc[(2 * rp) * PF_MAXCH + c] = m[0];
             mc[(2 * rp + 1) * PF_MAXCH + c] = m[1];
+            Mk[2 * rp] = fmaxf(Mk[2 * rp], m[0]);
+            Mk[2 * rp + 1] = fmaxf(Mk[2 * rp + 1], m[1]);
         }
         __syncthreads();  // Kt and Ms are rewritten by the next chunk
     }
