@@ -21,6 +21,8 @@ are timed (one step = one token through all 32 layers; n_kv = 768).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 8b|tiny|sweep]
     python bench.py --config sweep [--shape NxK] [--m M] [--wtype q4_0|q8_0]   # config 2, one line per case
     python bench.py --config prefill   # config 4: 8 x 2048-token Q8_0 prefill, tensor-core roofline
+    python bench.py --config attn      # isolated flash_attn at the 8B shape (prefill and decode rows)
+    python bench.py --config 70b [--gpus N --parallel tp]   # config 5 shape, tensor parallel over N GPUs
 """
 
 from __future__ import annotations
@@ -221,6 +223,60 @@ def sweep(args) -> None:
                                   "l2": "flushed before each rep (256 MB write)"}), flush=True)
 
 
+ATTN_CASES = [(2048, 2048, "prefill"), (1, 768, "decode")]  # (query rows, n_kv): 8B shape, 32 / 8 heads, D 128
+
+
+def attn(args) -> None:
+    """Isolated flash_attn at the 8B shape (one-node programs through the C ABI): a 2048-row causal
+    prefill over 2048 keys and one decode row over 768 keys (the 8B decode bench's n_kv, keys past
+    position 520 hidden). The reference programs' mask value -65504 hides keys. One JSON line per
+    case: the kernel's device time (profiled launch, L2 flushed before each rep), the FLOPs of the
+    visible keys and the K/V bytes."""
+    import torch
+
+    from ggml_compiler_b200.gguf_write import write_gguf
+    from ggml_compiler_b200.programs import single_node_program
+    from ggml_compiler_b200.runtime import Session
+
+    D, H, HKV = 128, 32, 8
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    CACHE.mkdir(parents=True, exist_ok=True)
+    for nq, nkv, kind in ATTN_CASES:
+        rng = np.random.default_rng(3)
+        q = rng.standard_normal((1, H, nq, D), dtype=np.float32)
+        k = rng.standard_normal((1, HKV, nkv, D), dtype=np.float32).astype(np.float16)
+        v = rng.standard_normal((1, HKV, nkv, D), dtype=np.float32).astype(np.float16)
+        pos0 = nkv - nq if kind == "prefill" else 520
+        m = np.zeros((nq, nkv), np.float32)
+        for i in range(nq):
+            m[i, pos0 + i + 1:] = -65504.0
+        ins = [("q", "f32", [D, nq, H, 1], [1, H, nq, D]), ("k", "f16", [D, nkv, HKV, 1], [1, HKV, nkv, D]),
+               ("v", "f16", [D, nkv, HKV, 1], [1, HKV, nkv, D]), ("mask", "f16", [nkv, nq, 1, 1], [1, 1, nq, nkv])]
+        prog = single_node_program("flash_attn", ins, ["q", "k", "v", "mask"], "f32", [D, H, nq, 1], [1, nq, H, D],
+                                   {"scale": float(1.0 / np.sqrt(D))})
+        p = CACHE / f"attn_{kind}_{nq}x{nkv}.gguf"
+        write_gguf(p, prog, [])
+        feed = {"q": q, "k": k, "v": v, "mask": m.astype(np.float16)[None, None]}
+        with Session(p, backend="cuda") as s:
+            for _ in range(max(3, args.warmup)):
+                s.run(**feed)
+            s.set_profiling(True)
+            for _ in range(args.steps):
+                flush.fill_(1.0)
+                torch.cuda.synchronize()
+                s.run(**feed)
+            ks = s.kernel_stats()
+            s.set_profiling(False)
+        fa = ks.get("flash_attn", {"ms": 0.0, "launches": 1})
+        us = 1000.0 * fa["ms"] / max(1, fa["launches"])
+        visible = sum(min(nkv, pos0 + i + 1) for i in range(nq))
+        flops = 4.0 * H * D * visible
+        kv_bytes = 2.0 * HKV * nkv * D * 2
+        print(json.dumps({"metric": "isolated flash_attn (8B shape)", "case": kind, "rows": nq, "n_kv": nkv, "us": us,
+                          "TFLOP_s_visible": flops / (us * 1e-6) / 1e12, "kv_GB_s": kv_bytes / (us * 1e-6) / 1e9,
+                          "reps": args.steps, "l2": "flushed before each rep (256 MB write)"}), flush=True)
+
+
 PREFILL_METRIC = "8B-shape Q8_0 prefill tok/s (8 sequences x 2048-token prompts); tensor-core TFLOP/s"
 
 
@@ -310,7 +366,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="8b", choices=["8b", "70b", "tiny", "sweep", "prefill"])
+    ap.add_argument("--config", default="8b", choices=["8b", "70b", "tiny", "sweep", "prefill", "attn"])
     ap.add_argument("--shape", default=None, help="sweep: one weight shape NxK")
     ap.add_argument("--m", type=int, default=None, help="sweep: one activation row count")
     ap.add_argument("--wtype", default=None, choices=["q4_0", "q8_0"], help="sweep: one weight type")
@@ -327,6 +383,11 @@ def main() -> None:
         return
     if args.config == "prefill":
         prefill_bench(args)
+        return
+    if args.config == "attn":
+        if args.steps == ap.get_default("steps"):
+            args.steps = 10
+        attn(args)
         return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -56,7 +56,7 @@ struct PrefillArgs {
 
 template <int D>
 constexpr size_t prefill_smem() {
-    return (size_t)4 * (D * PF_KTS + PF_RH * D + PF_RH * FL_CH + PF_RH * PF_PS + PF_RH * PF_MAXCH + PF_RH) +
+    return (size_t)4 * (D * PF_KTS + PF_RH * (D + 4) + PF_RH * FL_CH + PF_RH * PF_PS + PF_RH * PF_MAXCH + PF_RH) +
            (size_t)2 * 2 * FL_CH * D;
 }
 
@@ -69,11 +69,12 @@ constexpr float kNegligible = -3.0e38f;
 template <int D>
 __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) {
     constexpr int CPL = D / 32, KC = FL_CH, DG = D / 4, RPT = PF_RH * DG / PF_NT;
+    constexpr int QS = D + 4;  // floats between two pairs' query rows (rows land on different banks)
     static_assert(RPT >= 1 && PF_NT % DG == 0, "head size");
     extern __shared__ __align__(128) unsigned char smem[];
     float *Kt = (float *)smem;              // [D][PF_KTS] chunk keys, element-major
-    float *Qs = Kt + D * PF_KTS;            // [RH][D] queries rounded to f16
-    float *Ms = Qs + PF_RH * D;             // [RH][KC] mask values of the chunk
+    float *Qs = Kt + D * PF_KTS;            // [RH][QS] queries rounded to f16
+    float *Ms = Qs + PF_RH * QS;            // [RH][KC] mask values of the chunk
     float *Ps = Ms + PF_RH * KC;            // [RH][PF_PS] scores, then probabilities
     float *mc = Ps + PF_RH * PF_PS;         // [RH][PF_MAXCH] chunk maxima (pass 1)
     float *Mr = mc + PF_RH * PF_MAXCH;      // [RH] overall maxima
@@ -105,12 +106,12 @@ __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) 
             const int64_t iq = row0 + rh / G, h = hk * G + rh % G;
             x = f16_round(*(const float *)(a.q + iq * a.qnb1 + h * a.qnb2 + b * a.qnb3 + e * a.qnb0));
         }
-        Qs[i] = x;
+        Qs[rh * QS + e] = x;
     }
     __syncthreads();
     if (tid < PF_RH) {
         float l1 = 0.0f;
-        for (int e = 0; e < D; e++) l1 = __fadd_rn(l1, fabsf(Qs[tid * D + e]));
+        for (int e = 0; e < D; e++) l1 = __fadd_rn(l1, fabsf(Qs[tid * QS + e]));
         qL1[tid] = l1;
         Mk[tid] = -__int_as_float(0x7f800000);
     }
@@ -194,17 +195,27 @@ __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) 
             for (int p = 0; p < 2; p++)
 #pragma unroll
                 for (int u = 0; u < 4; u++) acc[p][u] = 0.0f;
+            float qv[2][CPL];  // the leaf's CPL query elements of both pairs, one vector load each
+#pragma unroll
+            for (int p = 0; p < 2; p++) {
+                const float *qr = Qs + (2 * rp + p) * QS + l * CPL;
+                if constexpr (CPL == 4) {
+                    const float4 t = *(const float4 *)qr;
+                    qv[p][0] = t.x, qv[p][1] = t.y, qv[p][2] = t.z, qv[p][3] = t.w;
+                } else {
+                    const float2 t = *(const float2 *)qr;
+                    qv[p][0] = t.x, qv[p][1] = t.y;
+                }
+            }
 #pragma unroll
             for (int e = 0; e < CPL; e++) {
                 const int d = l * CPL + e;
                 const float4 kv = *(const float4 *)(Kt + d * PF_KTS + 4 * kg);
                 const float kk[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
-                for (int p = 0; p < 2; p++) {
-                    const float qv = Qs[(2 * rp + p) * D + d];
+                for (int p = 0; p < 2; p++)
 #pragma unroll
-                    for (int u = 0; u < 4; u++) acc[p][u] = __fmaf_rn(qv, kk[u], acc[p][u]);
-                }
+                    for (int u = 0; u < 4; u++) acc[p][u] = __fmaf_rn(qv[p][e], kk[u], acc[p][u]);
             }
             // push the lane chain into the pairwise tree (bit i of the count = level carry)
 #pragma unroll
