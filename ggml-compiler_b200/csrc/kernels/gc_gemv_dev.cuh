@@ -173,11 +173,20 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
                     asm volatile("prefetch.global.L1 [%0];" ::"l"(a.norm_w + i));
             }
             named_bar(bar, NCT);
+            // the tree red[t] += red[t + off], off = 128 .. 1: three levels through shared memory,
+            // the last five in warp 0 with shuffles (lane t adds lane t + off: the same pairs)
 #pragma unroll
-            for (int off = 128; off >= 1; off >>= 1) {
+            for (int off = 128; off >= 32; off >>= 1) {
                 if (tid < off) red[tid] = __dadd_rn(red[tid], red[tid + off]);
                 named_bar(bar, NCT);
             }
+            if (tid < 32) {
+                double v = red[tid];
+#pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) v = __dadd_rn(v, __shfl_down_sync(0xffffffffu, v, off));
+                if (tid == 0) red[0] = v;
+            }
+            named_bar(bar, NCT);
             const double tot = red[0];
             named_bar(bar, NCT);
             const float mean = __double2float_rn(__ddiv_rn(tot, (double)K));

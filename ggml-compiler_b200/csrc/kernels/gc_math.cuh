@@ -54,10 +54,17 @@ __device__ __forceinline__ double block_tree256(double p, double *sh) {
     sh[t] = p;
     __syncthreads();
 #pragma unroll
-    for (int off = 128; off >= 1; off >>= 1) {
+    for (int off = 128; off >= 32; off >>= 1) {
         if (t < off) sh[t] = __dadd_rn(sh[t], sh[t + off]);
         __syncthreads();
     }
+    if (t < 32) {  // the last five levels in warp 0: lane t adds lane t + off, the same pairs
+        double v = sh[t];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) v = __dadd_rn(v, __shfl_down_sync(0xffffffffu, v, off));
+        if (t == 0) sh[0] = v;
+    }
+    __syncthreads();
     const double r = sh[0];
     __syncthreads();
     return r;
