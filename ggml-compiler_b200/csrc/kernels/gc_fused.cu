@@ -55,8 +55,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
         }
         return;
     }
+    float4 wpre[GEMV_UB];
+    gemv_norm_prefetch<NCW * 32>(a, wpre);
     pdl_wait();
-    gemv_prologue<M, NCW * 32>(a, sq, sdf, ss8, red, 1);
+    gemv_prologue<M, NCW * 32>(a, sq, sdf, ss8, red, 1, wpre);
     if (!consume_gemv<QT, NR, M, CG>(a, G, R, 0, blockIdx.x, gridDim.x, 0, 1, warp, sq, sdf, ss8))
         if (a.err) atomicExch(a.err, 2);
 }

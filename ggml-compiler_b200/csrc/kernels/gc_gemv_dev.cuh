@@ -144,13 +144,31 @@ __device__ inline void drain_ring(const Ring &R, uint32_t t) {
 // with rms_norm * w first for PRO_NORM. Run by the NCT consumer threads (thread ids 0 .. NCT-1);
 // `bar` is their named barrier. The sum of squares uses the 256-partial double tree (threads 0..255).
 // Loads are issued in batches ahead of the arithmetic that consumes them.
+constexpr int GEMV_UB = 4;  // 4-block groups in flight per warp in the quantization pass
+
+// The norm weights of the quantization pass's first round (PRO_NORM): a weight, written by no
+// kernel of the step, so consumers may load it before griddepcontrol.wait and overlap the latency
+// with the previous kernel's tail. `w` then goes to gemv_prologue.
+template <int NCT>
+__device__ __forceinline__ void gemv_norm_prefetch(const FusedArgs &a, float4 (&w)[GEMV_UB]) {
+    const int nb = (int)(a.K / 32), warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int NW = NCT / 32;
+    const int sub = lane >> 3, e = (lane & 7) * 4;
+#pragma unroll
+    for (int u = 0; u < GEMV_UB; u++) {
+        const int b = warp * 4 + u * NW * 4 + sub;
+        w[u] = (a.pro == PRO_NORM && b < nb) ? *(const float4 *)(a.norm_w + b * 32 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
 template <int M, int NCT>
-__device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf, int *ss8, double *red, int bar) {
+__device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf, int *ss8, double *red, int bar,
+                                     const float4 *wpre = nullptr) {
     const int K = (int)a.K, nb = K / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     constexpr int NW = NCT / 32;
     constexpr int U = 16;  // loads in flight per thread in the sum of squares
-    constexpr int UB = 4;  // 4-block groups in flight per warp in the quantization pass
+    constexpr int UB = GEMV_UB;
 #pragma unroll
     for (int m = 0; m < M; m++) {
         const float *x = a.x + m * a.ldx;
@@ -200,7 +218,8 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
             for (int u = 0; u < UB; u++) {
                 const int b = b0 + u * NW * 4 + sub;
                 v[u] = b < nb ? *(const float4 *)(x + b * 32 + e) : zero;
-                w[u] = (a.pro == PRO_NORM && b < nb) ? *(const float4 *)(a.norm_w + b * 32 + e) : zero;
+                w[u] = (wpre && b0 == warp * 4) ? wpre[u]  // first round, loaded before the wait
+                                                : (a.pro == PRO_NORM && b < nb) ? *(const float4 *)(a.norm_w + b * 32 + e) : zero;
             }
 #pragma unroll
             for (int u = 0; u < UB; u++) {
