@@ -119,6 +119,7 @@ struct TpExchange {
     char *win[TP_MAX] = {};  // the window of every rank (this rank's included)
     int64_t slot_bytes = 0;
     unsigned *seq = nullptr;  // exchanges done by this rank (device word)
+    unsigned *done = nullptr; // CTAs of the running exchange that finished (device word, left at 0)
     int *err = nullptr;
     uint64_t timeout_ns = 0;
 };

@@ -552,6 +552,7 @@ void Model::tp_init(int rank, int world, size_t window_bytes, cudaIpcMemHandle_t
     tp.world = world;
     tp.window.alloc((size_t)k::TP_FLAG_BYTES + 2 * tp.slot_bytes);
     tp.seq.alloc(sizeof(unsigned));
+    tp.done.alloc(sizeof(unsigned));
     cuda_check(cudaIpcGetMemHandle(handle, tp.window.get()), "cudaIpcGetMemHandle");
     if (const char *e = std::getenv("GGML_COMPILER_B200_TP_TIMEOUT_MS")) tp.timeout_ns = (uint64_t)std::atoll(e) * 1000000ull;
 }

@@ -85,6 +85,7 @@ struct TpGroup {
     DevBuf window;  // flag words + two exchange slots, exported to the peers
     size_t slot_bytes = 0;
     DevBuf seq;                        // exchanges done (device word)
+    DevBuf done;                       // CTAs of the running exchange that finished (device word)
     std::vector<char *> win;           // every rank's window as mapped here (own: window.get())
     bool connected = false;
     uint64_t timeout_ns = 60000000000ull;  // GGML_COMPILER_B200_TP_TIMEOUT_MS

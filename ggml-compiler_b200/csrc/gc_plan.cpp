@@ -186,6 +186,7 @@ k::TpExchange Planner::exchange_args(int64_t rows, int64_t ld, const std::vector
     for (int r = 0; r < x.world; r++) x.win[r] = m.tp.win[(size_t)r];
     x.slot_bytes = (int64_t)m.tp.slot_bytes;
     x.seq = (unsigned *)m.tp.seq.get();
+    x.done = (unsigned *)m.tp.done.get();
     x.err = m.d_err;
     x.timeout_ns = m.tp.timeout_ns;
     return x;

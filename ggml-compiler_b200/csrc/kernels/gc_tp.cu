@@ -4,7 +4,7 @@
 //
 // Each rank owns a window (ipc-exported device memory, mapped by every peer): a flag word per
 // sender, then two slots that each hold an image of the exchanged buffer. One exchange, on every
-// rank, in the same order:
+// rank, in the same order, run by one CTA per peer (the pairs do not wait for one another):
 //   1. seq = this rank's exchange count + 1; slot = seq & 1.
 //   2. Push: the rank's own slice of every row -> the same bytes of the slot image in each peer's
 //      window (16-byte stores over NVLink).
@@ -59,13 +59,16 @@ __device__ __forceinline__ void copy_rows(char *dst, int64_t ld, const char *src
     }
 }
 
-__global__ void __launch_bounds__(512) tp_exchange_kernel(TpExchange x) {
+// One CTA per peer p: push this rank's slice into p's window, publish to p, wait for p's flag,
+// pull p's slice. The pairs run in parallel; the last CTA to finish advances the exchange count.
+__global__ void __launch_bounds__(256) tp_exchange_kernel(TpExchange x) {
     __shared__ unsigned s_seq;
     __shared__ int s_fail;
     // Launched early (PDL): let the next kernel start too (its weight stream reads nothing this
     // kernel writes; its griddepcontrol.wait covers the rest), then wait for the slices' producer.
     pdl_trigger();
     pdl_wait();
+    const int p = (int)blockIdx.x < x.rank ? (int)blockIdx.x : (int)blockIdx.x + 1;  // this CTA's peer
     if (threadIdx.x == 0) {
         s_seq = *x.seq + 1;
         s_fail = *(volatile int *)x.err != 0;
@@ -74,18 +77,12 @@ __global__ void __launch_bounds__(512) tp_exchange_kernel(TpExchange x) {
     const unsigned seq = s_seq;
     const int64_t slot_off = TP_FLAG_BYTES + (int64_t)(seq & 1u) * x.slot_bytes;
     const int64_t own0 = x.col[x.rank], own = x.col[x.rank + 1] - own0;
-    if (!s_fail)
-        for (int p = 0; p < x.world; p++)
-            if (p != x.rank)
-                copy_rows(x.win[p] + slot_off + own0, x.row_bytes, x.buf + own0, x.ld, x.rows, own, false);
+    if (!s_fail) copy_rows(x.win[p] + slot_off + own0, x.row_bytes, x.buf + own0, x.ld, x.rows, own, false);
     __syncthreads();
     if (threadIdx.x == 0 && !s_fail) {
         __threadfence_system();
-        for (int p = 0; p < x.world; p++)
-            if (p != x.rank) st_release_sys((unsigned *)x.win[p] + x.rank, seq);
-    }
-    if (threadIdx.x < (unsigned)x.world && (int)threadIdx.x != x.rank && !s_fail) {
-        const unsigned *flag = (const unsigned *)x.win[x.rank] + threadIdx.x;
+        st_release_sys((unsigned *)x.win[p] + x.rank, seq);
+        const unsigned *flag = (const unsigned *)x.win[x.rank] + p;
         const uint64_t t0 = globaltimer();
         while ((int)(ld_acquire_sys(flag) - seq) < 0) {
             if (globaltimer() - t0 > x.timeout_ns) {
@@ -98,11 +95,16 @@ __global__ void __launch_bounds__(512) tp_exchange_kernel(TpExchange x) {
     }
     __syncthreads();
     if (!s_fail)
-        for (int p = 0; p < x.world; p++)
-            if (p != x.rank)
-                copy_rows(x.buf + x.col[p], x.ld, x.win[x.rank] + slot_off + x.col[p], x.row_bytes, x.rows,
-                          x.col[p + 1] - x.col[p], true);
-    if (threadIdx.x == 0) *x.seq = seq;
+        copy_rows(x.buf + x.col[p], x.ld, x.win[x.rank] + slot_off + x.col[p], x.row_bytes, x.rows, x.col[p + 1] - x.col[p],
+                  true);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(x.done, 1u) == gridDim.x - 1) {  // every CTA has read the count: advance it
+            *x.done = 0;
+            *x.seq = seq;
+        }
+    }
 }
 
 }  // namespace
@@ -120,8 +122,8 @@ void tp_exchange(const TpExchange &x, cudaStream_t s) {
     if (!tp_exchange_ok(x) || (uintptr_t)x.buf % 16)
         throw std::runtime_error("tp_exchange: slices are not 16-byte aligned or exceed the window slot");
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(1);
-    cfg.blockDim = dim3(512);
+    cfg.gridDim = dim3((unsigned)(x.world - 1));
+    cfg.blockDim = dim3(256);
     cfg.stream = s;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
