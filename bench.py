@@ -42,6 +42,10 @@ sys.path.insert(0, str(REPO / "ggml-compiler_b200"))
 sys.path.insert(0, str(REPO))
 
 METRIC = "8B-shape Q4_0 decode tok/s; quant-GEMV HBM GB/s as % of B200 peak"
+# DRAM traffic / algorithmic bytes from ncu captures of the same kernels (profiles/): the GEMV moves
+# 9,515,264 B for 9,469,952 algorithmic; the GEMM 11,694,336 B for 11,665,408 (weights + codes + scales)
+GEMV_TRAFFIC_RATIO = 9515264 / 9469952
+GEMM_TRAFFIC_RATIO = 11694336 / 11665408
 CACHE = Path(os.environ.get("GCB_BENCH_CACHE", "/tmp/gcb_bench"))
 
 
@@ -333,6 +337,9 @@ def prefill_bench(args) -> None:
     gemm_flops = 2.0 * plen * d * (H * D + 2 * Hkv * D + d + 3 * F) * sh.layers + 2.0 * d * sh.vocab  # head: last row
     attn_flops = 4.0 * H * D * (plen * (plen + 1) / 2) * sh.layers  # QK^T and PV over the causal half
     mm = ks.get("mul_mat", {"ms": 0.0, "launches": 0})
+    # algorithmic bytes of the call's GEMMs: Q8_0 weights (34 B per 32) and Q8_0 activation codes
+    gemm_alg_bytes = (sh.layers * d * (H * D + 2 * Hkv * D + d + 3 * F) * (34 / 32)
+                      + sh.layers * plen * (5 * d + H * D + F) * (34 / 32))
     total_ms = sum(v["ms"] for v in ks.values())
     pk = REPO / "MEASURED_PEAKS.json"
     tflops_peak = float(json.loads(pk.read_text())["bf16_tflops"]) if pk.exists() else 1590.0
@@ -347,7 +354,11 @@ def prefill_bench(args) -> None:
                    "layers": sh.layers, "d_model": d, "heads": H, "kv_heads": Hkv, "ffn": F, "vocab": sh.vocab,
                    "weights": "q8_0", "l2": "no flush: each call streams 7.5 GB of weights and GBs of activations"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s",
-                     "frac": achieved / tflops_peak, "traffic": None, "kernel": "mul_mat (gemm_tc)",
+                     "frac": achieved / tflops_peak, "kernel": "mul_mat (gemm_tc)",
+                     "traffic": GEMM_TRAFFIC_RATIO * gemm_alg_bytes / max(1, mm["launches"]),
+                     "traffic_source": "DRAM bytes per launch = 1.0025 x algorithmic (weights + activation codes), the "
+                                       "ratio of the ncu capture of the 4096x4096 M=512 Q4_0 GEMM "
+                                       "(profiles/gemm_tc_q4_0_4096x4096_m512.md), scaled to this call's GEMMs",
                      "peak_source": "measured bf16_tflops (MEASURED_PEAKS.json); int8 nominal peak is 2x",
                      "gemm_flops_per_call": gemm_flops, "attn_flops_per_call": attn_flops,
                      "gemm_share_of_call": mm["ms"] / total_ms if total_ms else None},
@@ -541,7 +552,11 @@ def main() -> None:
         "config": {**config, "parallelism": (f"tp{world}: rows / heads split, exchanges over NVLink peer memory" if tp
                                              else f"replicas x{world}" if world > 1 else "single GPU")},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak if peak else None, "traffic": None,
+                     "frac": achieved / peak if peak else None,
+                     "traffic": GEMV_TRAFFIC_RATIO * gemv_bytes / max(1, gemv_launches),
+                     "traffic_source": "DRAM bytes per launch = 1.0048 x algorithmic, the ratio of the ncu capture of "
+                                       "the 4096x4096 Q4_0 GEMV (profiles/gemv_q4_0_4096x4096_m1.md), scaled to this "
+                                       "mix of launches",
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                      "kernel": "+".join(gemv_kinds),
                      "bytes_per_launch": gemv_bytes / max(1, gemv_launches),
