@@ -94,3 +94,22 @@ def test_tensor_parallel_matches_oracle(gpu, tmp_path, synthetic_q4, model, worl
         np.testing.assert_array_equal(got["logits"], want["logits"], err_msg=f"rank {r}")
         np.testing.assert_array_equal(got["tokens"], want["tokens"], err_msg=f"rank {r}")
         np.testing.assert_array_equal(got["device_tokens"], want["tokens"], err_msg=f"rank {r}")
+
+
+def test_absent_peer_times_out(gpu, tmp_path):
+    """Failure detection without a GPU fault: rank 1 stays alive with its window mapped but never
+    runs the decode step, so rank 0's first exchange waits for a flag that nothing sets. The wait
+    gives up after 2 s (GGML_COMPILER_B200_TP_TIMEOUT_MS), the kernel returns, and the run reports
+    the timeout through the C ABI's error string; no GPU is left waiting."""
+    if _gpus() < 2:
+        pytest.skip(f"needs 2 GPUs, {_gpus()} visible")
+    port = _free_port()
+    env = {**os.environ, "NCCL_NVLS_ENABLE": "0", "GGML_COMPILER_B200_TP_TIMEOUT_MS": "2000"}
+    procs = [subprocess.Popen([sys.executable, str(REPO / "tests" / "tp_worker.py"), str(GOLDEN / "ref_llama_q8_0.gguf"),
+                               str(tmp_path), str(r), "2", str(port), "absent-peer"], env=env, stdout=subprocess.PIPE,
+                              stderr=subprocess.STDOUT, text=True) for r in range(2)]
+    logs = [p.communicate(timeout=600)[0] for p in procs]
+    for r, p in enumerate(procs):
+        assert p.returncode == 0, f"rank {r} failed:\n{logs[r][-3000:]}"
+    msg = (tmp_path / "rank0.txt").read_text()
+    assert "tensor-parallel exchange timed out" in msg, msg

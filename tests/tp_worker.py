@@ -1,10 +1,16 @@
 """One rank of the tensor-parallel GPU test (test_gpu_tp.py), run as its own process:
 
     python tests/tp_worker.py MODEL.gguf OUT_DIR RANK WORLD PORT CASE.json
+    python tests/tp_worker.py MODEL.gguf OUT_DIR RANK WORLD PORT absent-peer
 
 Loads the model on GPU RANK, joins the group (handles moved by torch.distributed over gloo on
 127.0.0.1), feeds the case's chunks and greedy-decodes, and saves every step's logits and the tokens
-to OUT_DIR/rank{RANK}.npz."""
+to OUT_DIR/rank{RANK}.npz.
+
+absent-peer: every rank prefills (no exchange), then rank 0 alone runs a decode step while the
+other ranks wait on the host, alive, with their windows mapped; rank 0's first exchange waits for
+flags that nothing sets, gives up after GGML_COMPILER_B200_TP_TIMEOUT_MS and the run fails. Rank 0
+writes the error (or "no error") to OUT_DIR/rank0.txt; then all ranks meet and exit."""
 
 import json
 import sys
@@ -43,8 +49,23 @@ def main() -> None:
     try:
         sess = Session(path, backend="cuda", device=rank)
         sess.tensor_parallel(rank, world, torch_all_gather())
-        res = run_case(sess, json.loads(Path(case).read_text()))
-        np.savez(out / f"rank{rank}.npz", **res)
+        if case == "absent-peer":
+            from ggml_compiler_b200.llm import Generator
+            from ggml_compiler_b200.runtime import GgmlCompilerRuntimeError
+
+            g = Generator(sess)
+            g.reset()
+            g.feed(list(range(1, 17)))  # 16 rows: the prefill path, which exchanges nothing
+            if rank == 0:
+                try:
+                    g.feed([5])
+                    outcome = "no error"
+                except GgmlCompilerRuntimeError as e:
+                    outcome = str(e)
+                (out / "rank0.txt").write_text(outcome)
+        else:
+            res = run_case(sess, json.loads(Path(case).read_text()))
+            np.savez(out / f"rank{rank}.npz", **res)
         dist.barrier()  # no rank frees its window while a peer may still push into it
         sess.close()
     finally:
