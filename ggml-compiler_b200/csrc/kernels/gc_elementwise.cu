@@ -163,6 +163,15 @@ __device__ __forceinline__ float binop(int op, float a, float b) {
     }
 }
 
+// Contiguous f32 operands: four elements per step. b either has a's shape (bper4 = 0) or is one
+// contiguous row of bper4 * 4 elements repeated over a's rows.
+__global__ void binary_f32x4_kernel(int op, const float4 *a, const float4 *b, float4 *out, int64_t n4, int64_t bper4) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 x = a[i], y = b[bper4 ? i % bper4 : i];
+        out[i] = make_float4(binop(op, x.x, y.x), binop(op, x.y, y.y), binop(op, x.z, y.z), binop(op, x.w, y.w));
+    }
+}
+
 __global__ void binary_kernel(int op, Dk a, Dk b, Dk out, int64_t n) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         int64_t r = i;
@@ -476,6 +485,14 @@ __global__ void argmax_split_kernel(const float *x, int64_t ne0, int64_t ld, int
     }
 }
 
+__global__ void swiglu_f32x4_kernel(const float4 *g, const float4 *u, float4 *out, int64_t n4) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 a = g[i], b = u[i];
+        out[i] = make_float4(__fmul_rn(gc_silu(a.x), b.x), __fmul_rn(gc_silu(a.y), b.y), __fmul_rn(gc_silu(a.z), b.z),
+                             __fmul_rn(gc_silu(a.w), b.w));
+    }
+}
+
 __global__ void swiglu_kernel(Dk g, Dk u, Dk out, int64_t n) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const float a = ldf(at_lin(g, i), g.type), b = ldf(at_lin(u, i), u.type);
@@ -563,8 +580,23 @@ void copy(const TD &src, const TD &dst, cudaStream_t s) {
     check_launch("copy");
 }
 
+namespace {
+// Contiguous f32 with 16-byte aligned data and a multiple of 4 elements.
+bool f32x4_ok(const TD &t) { return t.type == T_F32 && t.contiguous() && (uintptr_t)t.data % 16 == 0 && t.nelements() % 4 == 0; }
+}  // namespace
+
 void binary(int op, const TD &a, const TD &b, const TD &out, cudaStream_t s) {
     const int64_t n = a.nelements();
+    if (f32x4_ok(a) && f32x4_ok(b) && f32x4_ok(out) && out.nelements() == n) {
+        const bool same = b.nelements() == n && b.ne[0] == a.ne[0] && b.ne[1] == a.ne[1] && b.ne[2] == a.ne[2];
+        const bool row = b.ne[0] == a.ne[0] && b.nelements() == b.ne[0];  // one row broadcast over a's rows
+        if (same || row) {
+            binary_f32x4_kernel<<<blocks_for(n / 4, 256), 256, 0, s>>>(op, (const float4 *)a.data, (const float4 *)b.data,
+                                                                       (float4 *)out.data, n / 4, same ? 0 : b.ne[0] / 4);
+            check_launch("binary");
+            return;
+        }
+    }
     binary_kernel<<<blocks_for(n, 256), 256, 0, s>>>(op, dk(a), dk(b), dk(out), n);
     check_launch("binary");
 }
@@ -639,6 +671,12 @@ void argmax_split(const TD &x, const TD &out, void *scratch, int *counters, cuda
 
 void swiglu(const TD &g, const TD &u, const TD &out, cudaStream_t s) {
     const int64_t n = g.nelements();
+    if (f32x4_ok(g) && f32x4_ok(u) && f32x4_ok(out) && u.nelements() == n && out.nelements() == n) {
+        swiglu_f32x4_kernel<<<blocks_for(n / 4, 256), 256, 0, s>>>((const float4 *)g.data, (const float4 *)u.data,
+                                                                  (float4 *)out.data, n / 4);
+        check_launch("swiglu");
+        return;
+    }
     swiglu_kernel<<<blocks_for(n, 256), 256, 0, s>>>(dk(g), dk(u), dk(out), n);
     check_launch("swiglu");
 }
