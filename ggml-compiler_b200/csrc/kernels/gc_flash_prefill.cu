@@ -92,7 +92,16 @@ __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) 
     const float ninf = -__int_as_float(0x7f800000);
     const char *kbase = a.k + hk * a.knb2 + b * a.knb3;
     const char *vbase = a.v + hk * a.vnb2 + b * a.vnb3;
-    auto valid = [&](int rh) { return row0 + rh / G < a.Sq; };
+    // per pair: in range, and the byte offset of its mask row (both without a division per use)
+    __shared__ int64_t mrow[PF_RH];
+    __shared__ unsigned char pvalid[PF_RH];
+    if (tid < PF_RH) {
+        const int64_t iq = row0 + tid / G, h = hk * G + tid % G;
+        pvalid[tid] = iq < a.Sq;
+        mrow[tid] = iq * a.mnb1 + (h % a.mne2) * a.mnb2 + (b % a.mne3) * a.mnb3;
+    }
+    __syncthreads();
+    auto valid = [&](int rh) { return pvalid[rh] != 0; };
 
     pdl_wait();  // q and the K/V cache rows of this call were written by earlier kernels
     if (tid == 0) {
@@ -132,10 +141,7 @@ __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) 
         for (int i = tid; i < PF_RH * KC; i += PF_NT) {
             const int rh = i / KC, j = i - rh * KC;
             float mv = 0.0f;
-            if (a.mask && j < n && valid(rh)) {
-                const int64_t iq = row0 + rh / G, h = hk * G + rh % G;
-                mv = __half2float(((const __half *)(a.mask + iq * a.mnb1 + (h % a.mne2) * a.mnb2 + (b % a.mne3) * a.mnb3))[j0 + j]);
-            }
+            if (a.mask && j < n && valid(rh)) mv = __half2float(((const __half *)(a.mask + mrow[rh]))[j0 + j]);
             Ms[i] = mv;
         }
         const bool got = __syncthreads_and(mbar_wait(&bar, phase));
