@@ -15,7 +15,7 @@ reference checkout; the GPU tests only read the files this writes).
    file), to pin this repository's Llama program emitter node for node.
 
     GGML_COMPILER_RT=ggml-compiler_b200/ggml_compiler_b200/lib/libggml_compiler_rt.so \
-        python tests/golden/make_llm_golden.py /root/reference
+        python tests/golden/make_llm_golden.py REFERENCE_CHECKOUT
 """
 
 from __future__ import annotations
@@ -109,4 +109,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_llm_golden.py REFERENCE_CHECKOUT (the ggml-compiler source tree)")
+    main(sys.argv[1])
