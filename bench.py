@@ -361,7 +361,9 @@ def prefill_bench(args) -> None:
                                        "(profiles/gemm_tc_q4_0_4096x4096_m512.md), scaled to this call's GEMMs",
                      "peak_source": "measured bf16_tflops (MEASURED_PEAKS.json); int8 nominal peak is 2x",
                      "gemm_flops_per_call": gemm_flops, "attn_flops_per_call": attn_flops,
-                     "gemm_share_of_call": mm["ms"] / total_ms if total_ms else None},
+                     "gemm_share_of_call": mm["ms"] / total_ms if total_ms else None,
+                     "call_tflops": (gemm_flops + attn_flops) / (pre_dev / n_seq / 1000.0) / 1e12,
+                     "call_frac": (gemm_flops + attn_flops) / (pre_dev / n_seq / 1000.0) / 1e12 / tflops_peak},
         "e2e": {"value": n_seq * plen / pre_wall, "unit": "tok/s", "h2d_bytes_per_step": plen * 8 + plen * plen * 4,
                 "d2h_bytes_per_step": 4 * sh.vocab},
         "decode_tok_s": n_seq * n_dec / (dec_dev / 1000.0),
@@ -383,7 +385,7 @@ def main() -> None:
     ap.add_argument("--wtype", default=None, choices=["q4_0", "q8_0"], help="sweep: one weight type")
     ap.add_argument("--parallel", default="replicas", choices=["tp", "replicas"],
                     help="N>1: N independent sequences (replicas), or one sequence tensor-parallel over the N GPUs (tp)")
-    ap.add_argument("--cpu-tokens", type=int, default=3)
+    ap.add_argument("--cpu-tokens", type=int, default=12)  # about 10 s of the oracle on 16 host threads
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
 
@@ -563,7 +565,8 @@ def main() -> None:
                      "mean_launch_us": 1000.0 * gemv_ms / max(1, gemv_launches),
                      "share_of_step": gemv_ms / total_ms if total_ms else None,
                      "step_weight_bytes": weight_bytes(sh) / (world if tp else 1),
-                     "step_hbm_frac": weight_bytes(sh) / (world if tp else 1) / (dev_ms / K / 1000.0) / 1e9 / peak},
+                     "step_hbm_frac": weight_bytes(sh) / (world if tp else 1) / (dev_ms / K / 1000.0) / 1e9 / peak,
+                     "frac_of_spec_8000_gbs": achieved / 8000.0},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4 + 4 + 4 * n_kv,
                 "d2h_bytes_per_step": 4 * sh.vocab, "wall_ms": wall * 1000.0},
         "gpu_launches": int(round(launches_per_step * K + 2 * K)),
