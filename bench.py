@@ -42,7 +42,7 @@ sys.path.insert(0, str(REPO / "ggml-compiler_b200"))
 sys.path.insert(0, str(REPO))
 
 METRIC = "8B-shape Q4_0 decode tok/s; quant-GEMV HBM GB/s as % of B200 peak"
-# DRAM traffic / algorithmic bytes from ncu captures of the same kernels (profiles/): the GEMV moves
+# DRAM traffic / algorithmic bytes from ncu captures of the same kernels: the GEMV moves
 # 9,515,264 B for 9,469,952 algorithmic; the GEMM 11,694,336 B for 11,665,408 (weights + codes + scales)
 GEMV_TRAFFIC_RATIO = 9515264 / 9469952
 GEMM_TRAFFIC_RATIO = 11694336 / 11665408
@@ -64,15 +64,18 @@ def shape_for(config: str):
     raise ValueError(config)
 
 
-def model_path(sh, config: str, rank: int, world: int) -> Path:
+def model_path(sh, config: str, rank: int, world: int, encoder=None) -> Path:
+    """The synthetic GGUF of this config (written once per box, then reused). `encoder` encodes the
+    quantized matrices: the product library's by default, the oracle's on the reference arm, which
+    must not load the product; both are bit-exact with gguf-py, so the file is the same either way."""
     from ggml_compiler_b200.llm import build_llama_gguf
 
     CACHE.mkdir(parents=True, exist_ok=True)
     p = CACHE / f"{config}_{sh.weight_type}_seed0.gguf"
     if rank == 0 and not p.exists():
-        tmp = p.with_suffix(".part")
+        tmp = p.with_suffix(f".part{os.getpid()}")
         t = time.time()
-        build_llama_gguf(tmp, sh, seed=0)
+        build_llama_gguf(tmp, sh, seed=0, encoder=encoder)
         tmp.rename(p)
         print(f"[bench] wrote {p} ({p.stat().st_size / 1e9:.2f} GB) in {time.time() - t:.1f}s", file=sys.stderr)
     if world > 1:
@@ -148,9 +151,13 @@ def peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
-def cpu_baseline(gguf: Path, sh, n_tokens: int) -> dict:
-    """The reference's CPU arithmetic (oracle/, the C restatement of ggml's CPU path) on the host's
-    cores: a 4-token prompt, then `n_tokens` greedy decode tokens timed."""
+def cpu_baseline(gguf: Path, sh, n_tokens: int, prompt: int, n_kv: int) -> dict:
+    """The reference's CPU arithmetic for the path (oracle/, the C restatement of ggml's CPU code) on
+    the host's cores, on the GPU arm's workload: greedy decode steps at positions prompt, prompt+1,
+    ... with attention over n_kv cache rows. Prefilling `prompt` tokens on the CPU would take
+    minutes, so the cache rows of the prompt positions are filled with seeded f16 values instead:
+    a decode step's work does not depend on what the cache holds. One untimed step, then
+    `n_tokens` timed."""
     import oracle
     from oracle.interp import OracleGenerator, Program
 
@@ -158,14 +165,20 @@ def cpu_baseline(gguf: Path, sh, n_tokens: int) -> dict:
     g = OracleGenerator(p)
     g.reset()
     rng = np.random.default_rng(1)
-    logits = g.feed(rng.integers(0, sh.vocab, 4).tolist())
+    for name in p.prog.get("state", []):
+        cache = p.values[name].reshape(sh.kv_heads, -1, sh.hd)  # [Hkv, max_context, D] f16
+        cache[:, :prompt] = (rng.standard_normal((sh.kv_heads, prompt, sh.hd), np.float32) * 0.5).astype(np.float16)
+    g.n_past = prompt
+    tok = int(rng.integers(0, sh.vocab))
+    tok = int(np.argmax(g.feed([tok])))
     t = time.perf_counter()
     for _ in range(n_tokens):
-        logits = g.feed([int(np.argmax(logits))])
+        tok = int(np.argmax(g.feed([tok])))
     dt = time.perf_counter() - t
     return {"value": n_tokens / dt, "unit": "tok/s", "cores": oracle.lib().orc_get_threads(), "kind": "port",
-            "sample": f"{n_tokens} greedy decode tokens after a 4-token prompt (n_kv 512) of the same model, "
-                      f"oracle/ C restatement of ggml's CPU arithmetic, {dt:.1f}s"}
+            "sample": f"{n_tokens} greedy decode steps of the same model at positions {prompt + 1}.. (n_kv {n_kv}, "
+                      f"the cache rows of a {prompt}-token prompt filled with seeded values), oracle/ C restatement "
+                      f"of ggml's CPU arithmetic, {dt:.1f}s"}
 
 
 SWEEP_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]  # weight [N x K]
@@ -180,7 +193,7 @@ def sweep(args) -> None:
     import torch
 
     from ggml_compiler_b200.programs import write_mul_mat
-    from ggml_compiler_b200.runtime import Session
+    from ggml_compiler_b200.runtime import Model
 
     peak, peak_kind = peaks()
     tflops = None
@@ -203,16 +216,17 @@ def sweep(args) -> None:
                         w = rng.standard_normal((N, Kd), dtype=np.float32) * np.float32(0.02)
                     write_mul_mat(p, w, wt, M)
                 x = np.random.default_rng(1).standard_normal((1, M, Kd), dtype=np.float32)
-                with Session(p, backend="cuda") as s:
+                with Model(p) as s:
+                    run = s.entries["main"]
                     for _ in range(max(3, args.warmup)):
-                        s.run(x=x)
-                    s.set_profiling(True)
+                        run(x=x)
+                    s.profile(True)
                     for _ in range(args.steps):
                         flush.fill_(1.0)
                         torch.cuda.synchronize()
-                        s.run(x=x)
-                    ks = s.kernel_stats()
-                    s.set_profiling(False)
+                        run(x=x)
+                    ks = s.kernel_table()
+                    s.profile(False)
                 kinds = [k for k in ks if k.startswith(("gemv", "mul_mat"))]
                 ms = sum(ks[k]["ms"] for k in kinds) / max(1, sum(ks[k]["launches"] for k in kinds))
                 wbytes = N * Kd * (18 if wt == "q4_0" else 34) / 32
@@ -240,7 +254,7 @@ def attn(args) -> None:
 
     from ggml_compiler_b200.gguf_write import write_gguf
     from ggml_compiler_b200.programs import single_node_program
-    from ggml_compiler_b200.runtime import Session
+    from ggml_compiler_b200.runtime import Model
 
     D, H, HKV = 128, 32, 8
     flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
@@ -261,16 +275,17 @@ def attn(args) -> None:
         p = CACHE / f"attn_{kind}_{nq}x{nkv}.gguf"
         write_gguf(p, prog, [])
         feed = {"q": q, "k": k, "v": v, "mask": m.astype(np.float16)[None, None]}
-        with Session(p, backend="cuda") as s:
+        with Model(p) as s:
+            run = s.entries["main"]
             for _ in range(max(3, args.warmup)):
-                s.run(**feed)
-            s.set_profiling(True)
+                run(**feed)
+            s.profile(True)
             for _ in range(args.steps):
                 flush.fill_(1.0)
                 torch.cuda.synchronize()
-                s.run(**feed)
-            ks = s.kernel_stats()
-            s.set_profiling(False)
+                run(**feed)
+            ks = s.kernel_table()
+            s.profile(False)
         fa = ks.get("flash_attn", {"ms": 0.0, "launches": 1})
         us = 1000.0 * fa["ms"] / max(1, fa["launches"])
         visible = sum(min(nkv, pos0 + i + 1) for i in range(nq))
@@ -288,15 +303,15 @@ def prefill_bench(args) -> None:
     """BASELINE config 4's prefill: the 8B shape with Q8_0 projections, 8 random 2048-token prompts
     (seed 2), each prefilled in one 2048-row call (tensor-core GEMMs, flash prefill), then 64 greedy
     decode steps per sequence. The reference program is batch 1, so the 8 sequences run one after
-    another. One JSON line: prefill tok/s (device time), e2e (host arrays through Session.run:
+    another. One JSON line: prefill tok/s (device time), e2e (host arrays through the prefill entry:
     tokens, positions and the f32 mask up, logits down), and the GEMMs' FLOP rate from a profiled
     pass against the measured dense bf16 peak (the int8 MMAs' nominal peak is twice that)."""
     import dataclasses
 
     import torch
 
-    from ggml_compiler_b200.llm import LLAMA3_8B, Generator, build_llama_gguf
-    from ggml_compiler_b200.runtime import Session
+    from ggml_compiler_b200.llm import LLAMA3_8B, Decoder, build_llama_gguf
+    from ggml_compiler_b200.runtime import Model
 
     sh = dataclasses.replace(LLAMA3_8B, weight_type="q8_0", max_context=2304, max_prompt=2048)
     CACHE.mkdir(parents=True, exist_ok=True)
@@ -307,31 +322,31 @@ def prefill_bench(args) -> None:
         tmp.rename(gguf)
     n_seq, plen, n_dec = 8, 2048, 64
     prompts = np.random.default_rng(2).integers(0, sh.vocab, (n_seq, plen))
-    s = Session(gguf, backend="cuda")
-    g = Generator(s)
+    s = Model(gguf)
+    g = Decoder(s)
     # warm-up: one sequence (plans and graphs for the 2048-row call and decode at n_kv 2304)
-    g.reset()
-    tok = int(np.argmax(g.feed(prompts[0].tolist())))
+    g.restart()
+    tok = int(np.argmax(g.prompt(prompts[0].tolist())))
     for _ in range(max(3, args.warmup)):
-        tok = int(np.argmax(g.feed([tok])))
+        tok = int(np.argmax(g.step(tok)))
     pre_dev = pre_wall = dec_dev = 0.0
     with Clocks(0) as clk:
         for i in range(n_seq):
-            g.reset()
+            g.restart()
             torch.cuda.synchronize()
             t0 = time.perf_counter()
-            tok = int(np.argmax(g.feed(prompts[i].tolist())))
+            tok = int(np.argmax(g.prompt(prompts[i].tolist())))
             pre_wall += time.perf_counter() - t0
-            pre_dev += s.last_device_ms
+            pre_dev += s.device_ms
             for _ in range(n_dec):
-                tok = int(np.argmax(g.feed([tok])))
-                dec_dev += s.last_device_ms
+                tok = int(np.argmax(g.step(tok)))
+                dec_dev += s.device_ms
     # profiled pass over one prefill: the GEMM kernels' share and FLOP rate
-    g.reset()
-    s.set_profiling(True)
-    g.feed(prompts[0].tolist())
-    ks = s.kernel_stats()
-    s.set_profiling(False)
+    g.restart()
+    s.profile(True)
+    g.prompt(prompts[0].tolist())
+    ks = s.kernel_table()
+    s.profile(False)
     s.close()
     d, H, Hkv, D, F = sh.d_model, sh.heads, sh.kv_heads, sh.hd, sh.ffn
     gemm_flops = 2.0 * plen * d * (H * D + 2 * Hkv * D + d + 3 * F) * sh.layers + 2.0 * d * sh.vocab  # head: last row
@@ -357,8 +372,8 @@ def prefill_bench(args) -> None:
                      "frac": achieved / tflops_peak, "kernel": "mul_mat (gemm_tc)",
                      "traffic": GEMM_TRAFFIC_RATIO * gemm_alg_bytes / max(1, mm["launches"]),
                      "traffic_source": "DRAM bytes per launch = 1.0025 x algorithmic (weights + activation codes), the "
-                                       "ratio of the ncu capture of the 4096x4096 M=512 Q4_0 GEMM "
-                                       "(profiles/gemm_tc_q4_0_4096x4096_m512.md), scaled to this call's GEMMs",
+                                       "ratio of an ncu capture of the 4096x4096 M=512 Q4_0 GEMM, scaled to this "
+                                       "call's GEMMs",
                      "peak_source": "measured bf16_tflops (MEASURED_PEAKS.json); int8 nominal peak is 2x",
                      "gemm_flops_per_call": gemm_flops, "attn_flops_per_call": attn_flops,
                      "gemm_share_of_call": mm["ms"] / total_ms if total_ms else None,
@@ -402,6 +417,11 @@ def main() -> None:
             args.steps = 10
         attn(args)
         return
+    decode_bench(args)
+
+
+def decode_bench(args) -> None:
+    """BASELINE config 3 (or the 70B shape): greedy decode tok/s, see the module docstring."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -409,112 +429,118 @@ def main() -> None:
     K, W = min(args.steps, NKV - P), max(3, args.warmup)
     metric = METRIC if args.config != "70b" else "70B-shape Q4_0 decode tok/s; quant-GEMV HBM GB/s as % of B200 peak"
     wgb = weight_bytes(sh) / 1e9
+    tp = world > 1 and args.parallel == "tp"
     config = {"workload": workload, "layers": sh.layers, "d_model": sh.d_model, "heads": sh.heads,
               "kv_heads": sh.kv_heads, "ffn": sh.ffn, "vocab": sh.vocab, "weights": sh.weight_type, "batch": 1,
               "prompt": P, "decode_tokens": K, "n_kv": NKV,
-              "l2": f"no flush: the decode step streams all weights ({wgb:.1f} GB) through a 126 MB L2"}
+              "l2": f"no flush: the decode step streams all weights ({wgb:.1f} GB) through a 126 MB L2",
+              "parallelism": (f"tp{world}: rows / heads split, exchanges over NVLink peer memory" if tp
+                              else f"replicas x{world}" if world > 1 else "single GPU")}
+    dtype = f"{sh.weight_type} weights, int8 x int{4 if sh.weight_type == 'q4_0' else 8} block dots, f32 sums"
 
     if args.impl == "reference":
-        if world > 1 and rank != 0:
+        # the reference's CPU arithmetic (oracle port) on the host cores; rank 0 only, no product code
+        if rank != 0:
             return
-        gguf = model_path(sh, args.config, 0, 1)
-        cb = cpu_baseline(gguf, sh, max(1, args.cpu_tokens))
+        import oracle
+
+        gguf = model_path(sh, args.config, 0, 1, encoder=oracle.quantize)
+        n = max(1, min(K, args.cpu_tokens))
+        cb = cpu_baseline(gguf, sh, n, P, NKV)
         print(json.dumps({"impl": "reference", "metric": metric, "value": cb["value"], "unit": "tok/s",
-                          "n_gpus": args.gpus, "steps": args.cpu_tokens, "warmup": 0,
-                          "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
-                          "vs_baseline": None, "dtype": "q4_0 weights, int8 x int4 block dots, f32 sums",
-                          "data": "synthetic", "config": config, "cpu_baseline": cb,
+                          "n_gpus": args.gpus, "steps": n, "warmup": 1, "ms_per_step": 1000.0 / cb["value"],
+                          "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+                          "dtype": dtype, "data": "synthetic", "config": config, "cpu_baseline": cb,
                           "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}))
         return
 
+    import ctypes
+
     import torch
 
     if world > 1:
+        import datetime
+
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     torch.cuda.set_device(local)
-    from ggml_compiler_b200.llm import Generator
-    from ggml_compiler_b200.runtime import Session, load_library
+    from ggml_compiler_b200.llm import Decoder
+    from ggml_compiler_b200.runtime import BackendError, Model, load_library, torch_all_gather
 
     lib = load_library()
     gguf = model_path(sh, args.config, rank, world)
-    s = Session(gguf, backend="cuda", device=local)
-    tp = world > 1 and args.parallel == "tp"
+    m = Model(gguf, device=local)
     if tp:
-        from ggml_compiler_b200.runtime import torch_all_gather
-
-        s.tensor_parallel(rank, world, torch_all_gather())
+        m.join_tensor_parallel(rank, world, torch_all_gather())
     seqs = 1 if tp else world  # sequences decoded by the whole job
-    stream = torch.cuda.ExternalStream(s.stream, device=torch.device("cuda", local))
-    g = Generator(s)
+    stream = torch.cuda.ExternalStream(m.stream, device=torch.device("cuda", local))
+    d = Decoder(m)
     prompt = np.random.default_rng(1).integers(0, sh.vocab, P).tolist()
+    gen = m.entries["generate"]
 
     def prefill() -> int:
-        g.reset()
-        return int(np.argmax(g.feed(prompt)))
+        d.restart()
+        return int(np.argmax(d.prompt(prompt)))
 
     def generate(first: int, n: int) -> float:
-        s.set_symbol("max_new", n)
-        s.run(first=np.array([[first]], np.int32), start=np.array([P], np.int32), entry="generate")
-        return s.last_device_ms
-
-    # warm-up: prefill + W device-loop steps (graphs captured for the decode n_kv)
-    first = prefill()
-    generate(first, W)
+        m.bind(max_new=n)
+        gen.upload({"first": np.array([[first]], np.int32), "start": np.array([P], np.int32)})
+        gen.launch()
+        return m.device_ms
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    # timed: K decode steps in the device loop
+    def max_over_ranks(x: float) -> float:
+        t = torch.tensor([x], device="cuda")
+        if world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    # warm-up: prefill + W device-loop steps (plans and graphs for the decode n_kv)
+    first = prefill()
+    generate(first, W)
+
+    # timed: K decode steps in the device loop, inputs resident
     barrier()
     with Clocks(local) as clk:
         dev_ms = generate(first, K)
     barrier()
-    t = torch.tensor([dev_ms], device="cuda")
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    dev_ms = float(t.item())
+    dev_ms = max_over_ranks(dev_ms)
     value = seqs * K / (dev_ms / 1000.0)
 
-    # e2e: host loop through the public API, pinned host buffers, K decode steps
-    first = prefill()
-    n_kv = NKV
+    # e2e: one `decode` entry per token through the C ABI, host buffers (pinned) both ways
     tok_h = torch.empty((1, 1), dtype=torch.int32, pin_memory=True).numpy()
     pos_h = torch.empty(1, dtype=torch.int32, pin_memory=True).numpy()
-    mask_h = torch.empty((1, 1, 1, n_kv), dtype=torch.float32, pin_memory=True).numpy()
+    mask_h = torch.empty((1, 1, 1, NKV), dtype=torch.float32, pin_memory=True).numpy()
     out_h = torch.empty((1, 1, sh.vocab), dtype=torch.float32, pin_memory=True).numpy()
-    from ggml_compiler_b200.runtime import _error
+    mask_dims = (ctypes.c_int64 * 4)(*mask_h.shape)
+    cols = np.arange(NKV)
+
+    def check(rc: int) -> None:
+        if rc != 0:
+            raise BackendError(lib.ggml_compiler_last_error().decode())
 
     def e2e_step(tok: int, p: int) -> int:
         tok_h[0, 0] = tok
         pos_h[0] = p
-        mask_h[...] = np.where(np.arange(n_kv) <= p, 0.0, -np.inf).astype(np.float32)
-        for name, arr in (("token", tok_h), ("position", pos_h), ("mask1", mask_h)):
-            if name == "mask1":
-                shp = (ctypes_i64 * 4)(*arr.shape)
-                if lib.ggml_compiler_set_input_shape(s._m, b"mask1", 4, shp) != 0:
-                    raise _error()
-            if lib.ggml_compiler_set_input(s._m, name.encode(), arr.ctypes.data, arr.nbytes) != 0:
-                raise _error()
-        if lib.ggml_compiler_run_entry(s._m, b"decode") != 0:
-            raise _error()
-        if lib.ggml_compiler_get_output(s._m, b"logits1", out_h.ctypes.data, out_h.nbytes) != 0:
-            raise _error()
+        mask_h[0, 0, 0] = np.where(cols <= p, np.float32(0.0), np.float32(-np.inf))
+        check(lib.ggml_compiler_set_input_shape(m.handle, b"mask1", 4, mask_dims))
+        for name, arr in ((b"token", tok_h), (b"position", pos_h), (b"mask1", mask_h)):
+            check(lib.ggml_compiler_set_input(m.handle, name, arr.ctypes.data, arr.nbytes))
+        check(lib.ggml_compiler_run_entry(m.handle, b"decode"))
+        check(lib.ggml_compiler_get_output(m.handle, b"logits1", out_h.ctypes.data, out_h.nbytes))
         return int(np.argmax(out_h))
 
-    import ctypes
-
-    ctypes_i64 = ctypes.c_int64
-    tok = first
+    tok = prefill()
     for i in range(W):
         tok = e2e_step(tok, P + i)
-    first = prefill()
-    tok = first
+    tok = prefill()
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
@@ -524,20 +550,16 @@ def main() -> None:
     ev1.record(stream)
     ev1.synchronize()
     wall = time.perf_counter() - w0
-    e2e_ms = max(ev0.elapsed_time(ev1), wall * 1000.0)
-    t = torch.tensor([e2e_ms], device="cuda")
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    e2e_value = seqs * K / (float(t.item()) / 1000.0)
+    e2e_value = seqs * K / (max_over_ranks(max(ev0.elapsed_time(ev1), wall * 1000.0)) / 1000.0)
 
-    # roofline: profiled pass over the same decode steps, per kernel family
+    # roofline: a profiled pass over the same decode steps (each launch timed with CUDA events on
+    # the model's stream, no graphs), per kernel family
     first = prefill()
-    s.set_profiling(True)
+    m.profile(True)
     n_prof = min(K, 16)
     generate(first, n_prof)
-    ks = s.kernel_stats()
-    s.set_profiling(False)
-    # the weight-streaming kernels: the decode kernel (every layer in one launch) or the per-group GEMVs
+    ks = m.kernel_table()
+    m.profile(False)
     gemv_kinds = [k for k in ks if k.startswith(("gemv", "decode_")) or k == "mul_mat"]
     gemv_ms = sum(ks[k]["ms"] for k in gemv_kinds)
     gemv_bytes = sum(ks[k]["bytes"] for k in gemv_kinds)
@@ -546,37 +568,36 @@ def main() -> None:
     launches_per_step = sum(v["launches"] for v in ks.values()) / n_prof
     peak, peak_kind = peaks()
     achieved = gemv_bytes / (gemv_ms / 1000.0) / 1e9 if gemv_ms else 0.0
+    step_bytes = weight_bytes(sh) / (world if tp else 1)
 
     out = {
         "metric": metric, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": dev_ms / K, "higher_is_better": True, "scaling": "strong" if tp else "weak",
-        "vs_baseline": None, "dtype": "q4_0 weights, int8 x int4 block dots, f32 sums", "data": "synthetic",
-        "config": {**config, "parallelism": (f"tp{world}: rows / heads split, exchanges over NVLink peer memory" if tp
-                                             else f"replicas x{world}" if world > 1 else "single GPU")},
+        "vs_baseline": None, "dtype": dtype, "data": "synthetic", "config": config,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak if peak else None,
                      "traffic": GEMV_TRAFFIC_RATIO * gemv_bytes / max(1, gemv_launches),
-                     "traffic_source": "DRAM bytes per launch = 1.0048 x algorithmic, the ratio of the ncu capture of "
-                                       "the 4096x4096 Q4_0 GEMV (profiles/gemv_q4_0_4096x4096_m1.md), scaled to this "
-                                       "mix of launches",
+                     "traffic_source": "DRAM bytes per launch = 1.0048 x algorithmic, the ratio of an ncu capture "
+                                       "of the 4096x4096 Q4_0 GEMV, scaled to this mix of launches",
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                      "kernel": "+".join(gemv_kinds),
                      "bytes_per_launch": gemv_bytes / max(1, gemv_launches),
                      "mean_launch_us": 1000.0 * gemv_ms / max(1, gemv_launches),
                      "share_of_step": gemv_ms / total_ms if total_ms else None,
-                     "step_weight_bytes": weight_bytes(sh) / (world if tp else 1),
-                     "step_hbm_frac": weight_bytes(sh) / (world if tp else 1) / (dev_ms / K / 1000.0) / 1e9 / peak,
+                     "step_weight_bytes": step_bytes,
+                     "step_achieved_gbs": step_bytes / (dev_ms / K / 1000.0) / 1e9,
+                     "step_hbm_frac": step_bytes / (dev_ms / K / 1000.0) / 1e9 / peak,
                      "frac_of_spec_8000_gbs": achieved / 8000.0},
-        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4 + 4 + 4 * n_kv,
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4 + 4 + 4 * NKV,
                 "d2h_bytes_per_step": 4 * sh.vocab, "wall_ms": wall * 1000.0},
         "gpu_launches": int(round(launches_per_step * K + 2 * K)),
         "clocks": clk.summary(),
         "kernel_breakdown_ms_per_step": {k: v["ms"] / n_prof for k, v in sorted(ks.items(), key=lambda kv: -kv[1]["ms"])},
     }
-    s.close()
+    m.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            out["cpu_baseline"] = cpu_baseline(gguf, sh, max(1, args.cpu_tokens))
+            out["cpu_baseline"] = cpu_baseline(gguf, sh, max(1, min(K, args.cpu_tokens)), P, NKV)
         except Exception as e:  # the baseline is reported, not required for the GPU number
             out["cpu_baseline"] = {"value": None, "unit": "tok/s", "error": str(e)[:200]}
     if world > 1:

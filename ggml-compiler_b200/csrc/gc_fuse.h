@@ -2,6 +2,7 @@
 #pragma once
 
 #include <functional>
+#include <memory>
 #include <set>
 #include <string>
 #include <unordered_map>
@@ -18,6 +19,13 @@ struct Storage {
     size_t offset = 0;
 };
 
+// What a fused GEMV launch prefetches into L2 for a later launch (FusedArgs::pf).
+struct GemvPrefetch {
+    const char *p[3] = {nullptr, nullptr, nullptr};
+    int64_t n[3] = {0, 0, 0};
+    int evict_first = 0;
+};
+
 struct PlanStep {
     const char *kind;
     std::string node;
@@ -27,6 +35,10 @@ struct PlanStep {
     // The same work as a phase of the decode kernel (gc_mega.cu), from the resolved TDs; false when
     // this binding's layout does not fit it. Empty for steps that only run as their own launch.
     std::function<bool(const std::vector<TD> &, MegaPhase &)> mega;
+    // Fused GEMV steps: their arguments from the resolved TDs, and the L2 prefetch ranges the
+    // launch takes (filled once every step of the call site is planned).
+    std::function<FusedArgs(const std::vector<TD> &)> gemv;
+    std::shared_ptr<GemvPrefetch> pf;
 };
 
 struct Planner {

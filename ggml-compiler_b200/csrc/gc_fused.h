@@ -47,6 +47,13 @@ struct FusedArgs {
     // Tensor-parallel shard: this launch computes shard `shard` of `nshard` of the rows (a run of
     // 8-row tiles; for MAP_ROPE_QKV the query and K/V heads H / nshard * shard.., Hkv / nshard * shard..).
     int shard = 0, nshard = 1;
+    // Weights that a later kernel of the step streams: the leading bytes of up to three matrices,
+    // fetched into L2 by this launch's producers once they have issued their own pieces (each
+    // range split evenly over the CTAs), so HBM keeps streaming through this launch's tail, the
+    // launch gap and the next launch's prologue. Addresses 16-byte aligned, sizes multiples of 256.
+    const char *pf[3] = {nullptr, nullptr, nullptr};
+    int64_t pf_bytes[3] = {0, 0, 0};
+    int stream_evict_first = 0;  // stream this launch's weights under an L2 evict-first policy
 };
 
 // An attention phase of the decode kernel: split-KV flash attention of M query rows

@@ -122,6 +122,8 @@ struct Model {
     bool use_graphs = true;
     bool use_decode_kernel = false;  // GGML_COMPILER_B200_DECODE_KERNEL=1: one persistent launch per decode step
     bool profiling = false;
+    int64_t l2_prefetch_bytes = 0;   // GCB_L2_PREFETCH_MB: what each fused GEMV prefetches of the next one's weights
+    bool stream_evict_first = false;  // GCB_STREAM_EVICT_FIRST=1: GEMV weight streams under an L2 evict-first policy
     std::map<std::string, KernelStat> kstats;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> event_pool;
     size_t events_used = 0;

@@ -21,12 +21,11 @@
 #include "gc_fuse.h"
 #include "gc_fused.h"
 #include "gc_model.h"
+#include "kernels/gc_qweight.cuh"
 
 namespace gcb {
 
 namespace {
-
-constexpr int64_t QTR = 8;  // rows per tile of the quantized weight layout (kernels/gc_qweight.cuh)
 
 std::string shape_str(const int64_t *ne) {
     std::ostringstream os;
@@ -166,7 +165,20 @@ void Planner::add_gemv(const char *kind, const std::string &node, std::vector<TD
         a.nshard = nshard;
         return a;
     };
-    add(kind, node, std::move(tds), [b2](cudaStream_t st, const std::vector<TD> &t) { k::fused_gemv(b2(t), st, true); }, bytes);
+    auto pf = std::make_shared<GemvPrefetch>();
+    add(kind, node, std::move(tds),
+        [b2, pf](cudaStream_t st, const std::vector<TD> &t) {
+            FusedArgs a = b2(t);
+            for (int r = 0; r < 3; r++) {
+                a.pf[r] = pf->p[r];
+                a.pf_bytes[r] = pf->n[r];
+            }
+            a.stream_evict_first = pf->evict_first;
+            k::fused_gemv(a, st, true);
+        },
+        bytes);
+    psteps.back().gemv = b2;
+    psteps.back().pf = pf;
     psteps.back().mega = [b2](const std::vector<TD> &t, MegaPhase &ph) {
         ph.type = 0;
         ph.g = b2(t);
@@ -709,6 +721,34 @@ void Planner::finish() {
                 t.sid = -1;
                 t.off = 0;
             }
+
+    // Each fused GEMV prefetches into L2 the leading bytes of the next fused GEMV's matrices (the
+    // last one those of the first: the next decode step starts there), up to m.l2_prefetch_bytes
+    // in all, split over the matrices by size. In the tiled layout those leading tiles are exactly
+    // the first pieces every CTA of the next launch streams.
+    std::vector<size_t> gi;
+    for (size_t i = 0; i < psteps.size(); i++)
+        if (psteps[i].pf) gi.push_back(i);
+    for (size_t x = 0; x < gi.size(); x++) {
+        GemvPrefetch &pf = *psteps[gi[x]].pf;
+        pf = GemvPrefetch{};
+        pf.evict_first = m.stream_evict_first ? 1 : 0;
+        if (m.l2_prefetch_bytes <= 0 || gi.size() < 2) continue;
+        const PlanStep &nx = psteps[gi[(x + 1) % gi.size()]];
+        const FusedArgs na = nx.gemv(nx.tds);
+        if (na.nshard > 1) continue;
+        const int nm = na.map == MAP_SINGLE ? 1 : na.map == MAP_SWIGLU ? 2 : 3;
+        int64_t tot[3] = {0, 0, 0}, sum = 0;
+        for (int r = 0; r < nm; r++) {
+            tot[r] = qw_total_bytes(na.wrows[r], na.K / 32, na.qtype == T_Q4_0 ? 16 : 32);
+            sum += tot[r];
+        }
+        for (int r = 0; r < nm && sum > 0; r++) {
+            const int64_t take = std::min<int64_t>(tot[r], (int64_t)((double)m.l2_prefetch_bytes * (double)tot[r] / (double)sum));
+            pf.p[r] = na.wc[r];
+            pf.n[r] = take & ~(int64_t)255;
+        }
+    }
 
     // Runs of two or more consecutive steps that the decode kernel can take (one token row, one
     // weight type, one head size) become one launch of it; the other steps keep their own launch.

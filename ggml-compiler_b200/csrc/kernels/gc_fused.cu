@@ -52,6 +52,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
         if (!produce_gemv(a, G, R, t, blockIdx.x, gridDim.x, gemv_chunk(M, 1, CG))) {
             if (a.err) atomicExch(a.err, 2);
             drain_ring(R, t);
+        } else {
+            prefetch_next(a, blockIdx.x, gridDim.x);
         }
         return;
     }
@@ -65,6 +67,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
 
 int g_num_sms = 0;
 size_t g_smem_budget = 0;
+int g_ctas_per_sm = 2;  // GCB_GEMV_CTAS_PER_SM: 1 leaves room for the next launch's CTAs (PDL)
 
 template <int QT, int NR, int M>
 void launch_t(const FusedArgs &a, const GemvGeo &G, cudaStream_t s, bool pdl) {
@@ -80,7 +83,7 @@ void launch_t(const FusedArgs &a, const GemvGeo &G, cudaStream_t s, bool pdl) {
     int log2ns = ring_log2(budget, head, (size_t)slot_bytes, MAXNS);
     while ((1 << log2ns) < 2 * G.pieces) log2ns++;  // room for one group's pieces in flight and one consumed
     const size_t smem = head + ((size_t)1 << log2ns) * (size_t)slot_bytes;
-    const int per_sm = smem <= 113 * 1024 ? 2 : 1;
+    const int per_sm = smem <= 113 * 1024 ? g_ctas_per_sm : 1;
     const int64_t cap = (int64_t)g_num_sms * per_sm;
     const int64_t ctas = G.groups < cap ? (int64_t)G.groups : cap;
     cudaLaunchConfig_t cfg = {};
@@ -120,6 +123,7 @@ int num_sms() {
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
         if (const char *b = std::getenv("GCB_GEMV_SMEM_KB")) g_smem_budget = (size_t)std::atoi(b) * 1024;
+        if (const char *c = std::getenv("GCB_GEMV_CTAS_PER_SM")) g_ctas_per_sm = std::atoi(c) == 1 ? 1 : 2;
     }
     return g_num_sms;
 }

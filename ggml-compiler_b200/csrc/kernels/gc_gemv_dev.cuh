@@ -117,6 +117,7 @@ struct Ring {
 __device__ inline bool produce_gemv(const FusedArgs &a, const GemvGeo &G, const Ring &R, uint32_t &t, int cta, int nctas,
                                     int chunk) {
     const int L = local_groups(G.groups, cta, nctas);
+    const uint64_t policy = a.stream_evict_first ? l2_policy_evict_first() : 0;
     for (int c0 = 0; c0 < L; c0 += chunk) {
         const int c1 = c0 + chunk < L ? c0 + chunk : L;
         for (int s = 0; s < G.nseg; s++) {
@@ -127,11 +128,26 @@ __device__ inline bool produce_gemv(const FusedArgs &a, const GemvGeo &G, const 
                     if ((t >> R.log2ns) && !mbar_wait(&R.empty[slot], R.parity(t) ^ 1u)) return false;
                     mbar_expect_tx(&R.full[slot], pb);
                     int mat, tile;
-                    bulk_g2s(R.data(t), gemv_piece(a, G, cta + gl * nctas, r, s, &mat, &tile), pb, &R.full[slot]);
+                    const char *src = gemv_piece(a, G, cta + gl * nctas, r, s, &mat, &tile);
+                    if (a.stream_evict_first) bulk_g2s_hint(R.data(t), src, pb, &R.full[slot], policy);
+                    else bulk_g2s(R.data(t), src, pb, &R.full[slot]);
                 }
         }
     }
     return true;
+}
+
+// This CTA's share of the L2 prefetch ranges (FusedArgs::pf): an even split over the launch's CTAs,
+// in requests of at most 32 KiB.
+__device__ inline void prefetch_next(const FusedArgs &a, int cta, int nctas) {
+#pragma unroll
+    for (int r = 0; r < 3; r++) {
+        const int64_t n = a.pf_bytes[r];
+        if (n <= 0) continue;
+        const int64_t per = ((n + nctas - 1) / nctas + 255) & ~(int64_t)255;
+        const int64_t b0 = (int64_t)cta * per, b1 = b0 + per < n ? b0 + per : n;
+        for (int64_t o = b0; o < b1; o += 32768) l2_prefetch(a.pf[r] + o, (uint32_t)(b1 - o < 32768 ? b1 - o : 32768));
+    }
 }
 
 // Drain after a failed wait: the copies still in flight into the ring land before the CTA exits.

@@ -1,16 +1,19 @@
-"""Causal language models over this backend: the reference's text-model host driver, and an emitter
-for Llama-shaped programs.
+"""Causal language models on this backend: a greedy decoder over a compiled causal LM, and an
+emitter for Llama-shaped programs.
 
-- `causal_mask`, `Generator` and `bench` are the reference's host side for a compiled causal LM
-  (ggml_compiler/llm.py:355-358, :473-634 text path, :637-683): positions, additive masks, prompt
-  chunking and greedy decoding over the prefill / decode / generate entries.
+- `Decoder` feeds token ids to a program compiled by the reference's `causal_lm` (or written by
+  `llama_program`): it chooses the entry (prefill for two or more ids, decode for one), builds
+  positions and the additive causal mask over the smallest KV window the program allows, and runs
+  greedy decoding on the host or through the program's `generate` entry (the loop on the device).
+  The reference drives the same entries from its own `ggml_compiler.llm.Generator`, which runs
+  unchanged over this library; the two issue the same calls for the same ids.
 - `llama_program` writes the program JSON the reference's `causal_lm(model, ...)` compiles a
   LlamaForCausalLM into at -O3 (flash attention, f16 KV cache, fused rope/rms_norm/swiglu): the same
   values, stages, node lists, parameters and driver (format 3). A test checks it node for node
   against programs the reference compiler wrote. It lets 8B- and 70B-shaped models be built from
   seeded weights without materialising them as fp32 PyTorch modules.
 - `build_llama_gguf` writes such a model with N(0, 0.02) weights (norm weights 1, as HF's init),
-  quantizing the projections and the output head with this library's bit-exact encoder.
+  encoding the projections and the output head with a bit-exact Q4_0 / Q8_0 encoder.
 """
 
 from __future__ import annotations
@@ -20,147 +23,99 @@ import os
 from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 from pathlib import Path
-from typing import Any, Sequence
+from typing import Any, Callable, Sequence
 
 import numpy as np
 
-from . import runtime
 from .gguf_write import TensorEntry, write_gguf
 
 KV_BLOCK = 256
 
 
-def causal_mask(n_past: int, s: int, n_kv: int) -> np.ndarray:
-    """[1, 1, s, n_kv]: token i (at position n_past + i) attends to positions 0 .. n_past + i."""
-    rows = n_past + np.arange(s)[:, None]
-    return np.where(np.arange(n_kv)[None, :] <= rows, 0.0, -np.inf).astype(np.float32)[None, None]
+def call_sizes(n: int, limit: int) -> list[int]:
+    """How `n` ids are fed: calls of at most `limit` ids, taken greedily, except that a call is
+    shortened by one when it would leave a single id behind (a prefill call takes two or more)."""
+    sizes, left = [], n
+    while left:
+        take = min(limit, left)
+        if take > 1 and left - take == 1:
+            take -= 1
+        sizes.append(take)
+        left -= take
+    return sizes
 
 
-class Generator:
-    """Drives a compiled causal LM on the host: positions, masks, prompt chunks, greedy decoding
-    (the reference's Generator, text path)."""
+class Decoder:
+    """Greedy decoding over a causal-LM program loaded in a `runtime.Model`.
 
-    def __init__(self, session: Any) -> None:
-        meta = session.metadata
-        if meta.get("kind") != "causal_lm":
-            raise ValueError("the artifact was not compiled from ggml_compiler.causal_lm")
-        self.s, self.meta = session, meta
-        self.reset(state=False)
+    `ctx` counts the positions filled in the program's KV cache; `restart()` empties it."""
 
-    def reset(self, state: bool = True) -> None:
-        if state:
-            self.s.reset()
-        self.n_past = 0
+    def __init__(self, model: Any) -> None:
+        self.model = model
+        self.meta = model.meta
+        if self.meta.get("kind") != "causal_lm":
+            raise ValueError(f"{model.path} holds no causal-LM program (metadata kind {self.meta.get('kind')!r})")
+        self.ctx = 0
 
-    def _n_kv(self, end: int) -> int:
-        block = self.meta["kv_block"]
-        return max(self.meta["min_kv"], -(-end // block) * block)
+    def restart(self) -> None:
+        self.model.clear_state()
+        self.ctx = 0
 
-    def _run(self, ids: Sequence[int]) -> np.ndarray:
-        n = len(ids)
-        if self.n_past + n > self.meta["max_context"]:
-            raise ValueError(f"context full: {self.n_past} + {n} tokens > max_context {self.meta['max_context']}")
-        n_kv = self._n_kv(self.n_past + n)
-        pos = np.arange(self.n_past, self.n_past + n, dtype=np.int32)
-        mask = causal_mask(self.n_past, n, n_kv)
-        tok = np.asarray(ids, dtype=np.int32)[None]
+    def window(self, end: int) -> int:
+        """KV rows the program attends over once positions < end are filled: whole blocks, at
+        least the program's minimum."""
+        blk = self.meta["kv_block"]
+        return max(self.meta["min_kv"], blk * ((end + blk - 1) // blk))
+
+    def _call(self, ids: Sequence[int]) -> np.ndarray:
+        n, start = len(ids), self.ctx
+        if start + n > self.meta["max_context"]:
+            raise ValueError(f"{start} + {n} positions exceed the program's max_context {self.meta['max_context']}")
+        cols = np.arange(self.window(start + n))
+        mask = np.full((1, 1, n, cols.size), -np.inf, np.float32)
+        mask[0, 0][cols[None, :] <= start + np.arange(n)[:, None]] = 0.0
+        toks = np.asarray(ids, np.int32).reshape(1, n)
+        where = np.arange(start, start + n, dtype=np.int32)
         if n == 1:
-            out = self.s.run(token=tok, position=pos, mask1=mask, entry="decode")["logits1"]
+            res = self.model.entries["decode"](token=toks, position=where, mask1=mask)["logits1"]
         else:
-            out = self.s.run(tokens=tok, positions=pos, mask=mask, entry="prefill")["logits"]
-        self.n_past += n
-        return out[0]
+            res = self.model.entries["prefill"](tokens=toks, positions=where, mask=mask)["logits"]
+        self.ctx += n
+        return res[0]
 
-    def feed(self, ids: Sequence[int]) -> np.ndarray:
-        """Append tokens to the context; returns the logits after the last one ([vocab])."""
-        ids = list(ids)
-        step = self.meta["max_prompt"]
-        rows = []
-        i = 0
-        while i < len(ids):
-            n = min(step, len(ids) - i)
-            if n == 1 or len(ids) - i - n == 1:  # never leave a lone token for a prefill of one
-                n = 1 if n == 1 else n - 1
-            rows.append(self._run(ids[i:i + n]))
+    def prompt(self, ids: Sequence[int]) -> np.ndarray:
+        """Appends `ids` to the context; the logits after the last one ([vocab])."""
+        ids, last, i = list(ids), None, 0
+        for n in call_sizes(len(ids), self.meta["max_prompt"]):
+            last = self._call(ids[i:i + n])
             i += n
-        out = np.concatenate(rows, axis=0)
-        return out if self.meta["logits"] == "all" else out[-1]
+        return last if last.ndim == 1 else last[-1]  # a program with logits="all" returns every row
 
-    def generate(self, prompt: Sequence[int], max_new: int, stop: Sequence[int] | None = None,
-                 device: bool = False) -> list[int]:
-        """Greedy continuation of `prompt` from an empty context (device=True: the `generate` entry's
-        loop runs in the runtime)."""
-        self.reset()
-        stop = set(self.meta["eos"] if stop is None else stop)
-        logits = self.feed(prompt)
-        if device:
-            if "generate" not in self.s.entries:
-                raise ValueError("compiled without the generate entry")
-            first = int(np.argmax(logits if logits.ndim == 1 else logits[-1]))
-            if first in stop or max_new == 1:
-                return [first]
-            room = self.meta["max_context"] - self.n_past
-            self.s.set_symbol("max_new", max(1, min(max_new - 1, room)))
-            out = self.s.run(first=np.array([[first]], np.int32), start=np.array([self.n_past], np.int32),
-                             entry="generate")["generated"].reshape(-1)
-            n = self.s.stats["stages"]["decode_greedy"]["calls"]
-            self.n_past += n
-            return [first] + out[:n].tolist()
-        out: list[int] = []
-        for _ in range(max_new):
-            tok = int(np.argmax(logits if logits.ndim == 1 else logits[-1]))
-            out.append(tok)
-            if tok in stop or len(out) == max_new:
-                break
-            logits = self.feed([tok])
-        return out
+    def step(self, token: int) -> np.ndarray:
+        return self._call([int(token)])
 
-
-def bench(session: Any, pp: int = 512, tg: int = 128, reps: int = 5, seed: int = 0,
-          device: bool = False) -> dict[str, float]:
-    """llama-bench style tokens/s (the reference's llm.bench): pp = one prefill of `pp` tokens from an
-    empty context, tg = `tg` single-token decodes; mean over `reps` runs after a warmup."""
-    import time
-
-    g = Generator(session)
-    rng = np.random.default_rng(seed)
-    vocab = g.meta["vocab"]
-    out: dict[str, float] = {}
-    if pp:
-        times = []
-        for r in range(reps + 1):
-            ids = rng.integers(0, vocab, pp).tolist()
-            g.reset()
-            t = time.perf_counter()
-            g.feed(ids)
-            if r:
-                times.append(time.perf_counter() - t)
-        out[f"pp{pp}"] = pp / float(np.mean(times))
-    if tg and device:
-        rates = []
-        session.set_symbol("max_new", tg)
-        for r in range(reps + 1):
-            g.reset()
-            first = np.array([[int(rng.integers(0, vocab))]], np.int32)
-            t = time.perf_counter()
-            session.run(first=first, start=np.array([0], np.int32), entry="generate")
-            dt = time.perf_counter() - t
-            if r:
-                rates.append(session.stats["stages"]["decode_greedy"]["calls"] / dt)
-        out[f"tg{tg}"] = float(np.mean(rates))
-    elif tg:
-        times = []
-        for r in range(reps + 1):
-            g.reset()
-            tok = int(rng.integers(0, vocab))
-            t = time.perf_counter()
-            for _ in range(tg):
-                logits = g.feed([tok])
-                tok = int(np.argmax(logits))
-            if r:
-                times.append(time.perf_counter() - t)
-        out[f"tg{tg}"] = tg / float(np.mean(times))
-    return out
+    def greedy(self, prompt: Sequence[int], n: int, stop: Sequence[int] | None = None,
+               on_device: bool = False) -> list[int]:
+        """Up to `n` greedy tokens after `prompt` from an empty context, ending early at a stop id
+        (default: the model's EOS ids). on_device: the tokens after the first come from the
+        program's `generate` entry, whose loop stops at the model's EOS ids."""
+        self.restart()
+        stops = set(self.meta["eos"] if stop is None else stop)
+        first = int(np.argmax(self.prompt(prompt)))
+        toks = [first]
+        if first in stops or n == 1:
+            return toks
+        if on_device:
+            room = self.meta["max_context"] - self.ctx
+            self.model.bind(max_new=max(1, min(n - 1, room)))
+            gen = self.model.entries["generate"]
+            got = gen(first=np.array([[first]], np.int32), start=np.array([self.ctx], np.int32))["generated"].ravel()
+            made = self.model.stage_calls()["decode_greedy"]
+            self.ctx += made
+            return toks + [int(t) for t in got[:made]]
+        while len(toks) < n and toks[-1] not in stops:
+            toks.append(int(np.argmax(self.step(toks[-1]))))
+        return toks
 
 
 # ------------------------------------------------------------------------------------------------
@@ -396,8 +351,13 @@ def normal_weights(shape: tuple[int, ...], seed: int, index: int, std: float = 0
     return out.reshape(shape)
 
 
-def build_llama_gguf(path: str | Path, sh: LlamaShape, seed: int = 0) -> dict[str, Any]:
-    """Write a seeded synthetic Llama-shaped model as a ggml-compiler GGUF; returns its metadata."""
+def build_llama_gguf(path: str | Path, sh: LlamaShape, seed: int = 0,
+                     encoder: Callable[[np.ndarray, str], np.ndarray] | None = None) -> dict[str, Any]:
+    """Write a seeded synthetic Llama-shaped model as a ggml-compiler GGUF; returns its metadata.
+    `encoder(w, type)` encodes the quantized matrices (default: this library's `runtime.encode`;
+    any bit-exact Q4_0 / Q8_0 encoder writes the same bytes)."""
+    if encoder is None:
+        from .runtime import encode as encoder
     program, meta = llama_program(sh)
     entries = []
     names = {}
@@ -412,7 +372,7 @@ def build_llama_gguf(path: str | Path, sh: LlamaShape, seed: int = 0) -> dict[st
                 return w
             if typ == "f16":
                 return w.astype(np.float16)
-            return runtime.quantize(w, typ)
+            return encoder(w, typ)
 
         entries.append(TensorEntry(gname, typ, tuple(reversed(shape)), data))
     write_gguf(path, program, entries, metadata=meta, tensor_names=names,

@@ -37,7 +37,7 @@ def write_mul_mat(path: str | Path, w: np.ndarray, wtype: str, M: int, batch: in
     """A program y = mul_mat(W, x): W [N, K] f32 stored as `wtype`, x [batch, M, K] f32 input."""
     N, K = w.shape
     if wtype in ("q4_0", "q8_0"):
-        data = runtime.quantize(w, wtype)
+        data = runtime.encode(w, wtype)
     elif wtype == "f16":
         data = w.astype(np.float16)
     else:

@@ -1,15 +1,19 @@
-"""ctypes bindings to this repository's libggml_compiler_rt.so (the B200 backend).
+"""Python handle on libggml_compiler_rt.so, the B200 backend for ggml-compiler programs.
 
-The same Python interface as the reference's ggml_compiler/runtime/session.py (Session, quantize,
-has_backend, version, GgmlCompilerRuntimeError; signatures bound as at session.py:75-122), so code
-written against the reference runs unchanged. The library is found through $GGML_COMPILER_RT, else
-the in-tree build (ggml_compiler_b200/lib/). There is no CPU fallback: without a B200 the library
-loads and encodes weights, but loading a model fails with a GgmlCompilerRuntimeError.
+The library exports the reference runtime's C ABI (include/ggml_compiler_rt.h), so the reference's
+own Python front end (ggml_compiler.runtime.Session, ggml_compiler.llm.Generator) drives it when
+$GGML_COMPILER_RT names it. This module is this repository's own, smaller binding, used by the
+tests, the benchmark and smoke(): a `Model` owns one loaded program; each of its entry points is an
+`Entry` that uploads host arrays, runs, and fetches the results; the backend's extensions (device
+timing, per-kernel statistics, tensor parallelism) are methods of `Model`.
+
+The library is looked up in $GGML_COMPILER_RT, else in the in-tree build (ggml_compiler_b200/lib/).
+There is no CPU fallback: without a B200 the library still encodes weights, but loading fails.
 """
 
 from __future__ import annotations
 
-import ctypes
+import ctypes as C
 import json
 import os
 from dataclasses import dataclass
@@ -18,338 +22,293 @@ from typing import Any, Callable
 
 import numpy as np
 
-_BACKENDS = {"cpu": 0, "cuda": 1, "auto": 2}
-_DTYPES = {0: ("f32", np.float32), 1: ("f16", np.float16), 2: ("i32", np.int32)}
-_MAX_RANK = 8
 LIB_NAME = "libggml_compiler_rt.so"
+BACKEND_CUDA = 1  # ggml_compiler_backend: CPU 0, CUDA 1, AUTO 2
+_NP_OF_DTYPE = (np.float32, np.float16, np.int32)  # ggml_compiler_dtype F32, F16, I32
 
 
-class _Options(ctypes.Structure):
-    _fields_ = [("backend", ctypes.c_int), ("device", ctypes.c_int), ("n_threads", ctypes.c_int),
-                ("allow_cpu_fallback", ctypes.c_bool)]
+class BackendError(RuntimeError):
+    """A call into libggml_compiler_rt returned an error; the message is the library's."""
 
 
-class _TensorInfo(ctypes.Structure):
-    _fields_ = [("name", ctypes.c_char_p), ("dtype", ctypes.c_int), ("ndim", ctypes.c_int),
-                ("shape", ctypes.c_int64 * _MAX_RANK), ("nbytes", ctypes.c_size_t)]
+# Layouts of the ABI's structs (include/ggml_compiler_rt.h).
+class COptions(C.Structure):
+    _fields_ = [("backend", C.c_int), ("device", C.c_int), ("n_threads", C.c_int), ("allow_cpu_fallback", C.c_bool)]
 
 
-class _Stats(ctypes.Structure):
-    _fields_ = [("ms_total", ctypes.c_double), ("n_calls", ctypes.c_int)]
+class CTensorInfo(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("dtype", C.c_int), ("ndim", C.c_int), ("shape", C.c_int64 * 8),
+                ("nbytes", C.c_size_t)]
 
 
-class GgmlCompilerRuntimeError(RuntimeError):
-    """An error reported by libggml_compiler_rt."""
+class CStats(C.Structure):
+    _fields_ = [("ms_total", C.c_double), ("n_calls", C.c_int)]
+
+
+def _prototypes() -> dict[str, tuple[Any, list[Any]]]:
+    """name -> (result type, argument types) for every exported function this module calls."""
+    vp, i32, i64, sz, s = C.c_void_p, C.c_int, C.c_int64, C.c_size_t, C.c_char_p
+    P = C.POINTER
+    proto: dict[str, tuple[Any, list[Any]]] = {
+        "version": (s, []), "last_error": (s, []), "default_options": (COptions, []), "has_backend": (C.c_bool, [i32]),
+        "load": (vp, [s, P(COptions)]), "load_with": (vp, [s, P(COptions), vp, i32]), "free": (None, [vp]),
+        "quantize": (sz, [s, vp, i64, i64, vp, sz]), "row_size": (sz, [s, i64]),
+        "backend_name": (s, [vp]), "metadata": (s, [vp, s]),
+        "n_inputs": (i32, [vp]), "n_outputs": (i32, [vp]),
+        "input_info": (i32, [vp, i32, P(CTensorInfo)]), "output_info": (i32, [vp, i32, P(CTensorInfo)]),
+        "n_entries": (i32, [vp]), "entry_name": (s, [vp, i32]),
+        "entry_n_inputs": (i32, [vp, i32]), "entry_n_outputs": (i32, [vp, i32]),
+        "entry_input_info": (i32, [vp, i32, i32, P(CTensorInfo)]),
+        "entry_output_info": (i32, [vp, i32, i32, P(CTensorInfo)]),
+        "run_entry": (i32, [vp, s]), "run": (i32, [vp]), "reset": (i32, [vp]),
+        "n_symbols": (i32, [vp]), "symbol_info": (i32, [vp, i32, P(s), P(i64), P(i64), P(i64)]),
+        "set_symbol": (i32, [vp, s, i64]), "set_input_shape": (i32, [vp, s, i32, P(i64)]),
+        "set_input": (i32, [vp, s, vp, sz]), "get_output": (i32, [vp, s, vp, sz]),
+        "last_stats": (i32, [vp, P(CStats)]), "n_stages": (i32, [vp]),
+        "stage_stats": (i32, [vp, i32, P(s), P(C.c_double), P(i32)]),
+        # this backend's extensions (include/ggml_compiler_b200.h)
+        "b200_stream": (vp, [vp]), "b200_last_device_ms": (C.c_double, [vp]), "b200_set_profiling": (i32, [vp, i32]),
+        "b200_n_kernel_stats": (i32, [vp]),
+        "b200_kernel_stats": (i32, [vp, i32, P(s), P(C.c_double), P(i32), P(C.c_double)]),
+        "b200_tp_init": (i32, [vp, i32, i32, sz, vp, sz]), "b200_tp_connect": (i32, [vp, vp, sz]),
+    }
+    return {"ggml_compiler_" + k: v for k, v in proto.items()}
+
+
+_LIB: C.CDLL | None = None
 
 
 def library_path() -> Path:
-    env = os.environ.get("GGML_COMPILER_RT")
-    if env:
-        return Path(env)
-    p = Path(__file__).resolve().parent / "lib" / LIB_NAME
-    if not p.exists():
-        raise RuntimeError(f"{LIB_NAME} not found: run `python -m ggml_compiler_b200.build` or set GGML_COMPILER_RT")
-    return p
+    if os.environ.get("GGML_COMPILER_RT"):
+        return Path(os.environ["GGML_COMPILER_RT"])
+    built = Path(__file__).resolve().parent / "lib" / LIB_NAME
+    if not built.exists():
+        raise FileNotFoundError(f"{built} is missing: build it with `python -m ggml_compiler_b200.build`")
+    return built
 
 
-# Every symbol of include/ggml_compiler_rt.h that takes or returns plain C types.
-_SIGS: dict[str, tuple[list[Any], Any]] = {}
+def load_library() -> C.CDLL:
+    """The product library with every prototype bound (loaded once per process)."""
+    global _LIB
+    if _LIB is None:
+        handle = C.CDLL(str(library_path()))
+        for name, (res, args) in _prototypes().items():
+            fn = getattr(handle, name)
+            fn.restype, fn.argtypes = res, args
+        _LIB = handle
+    return _LIB
 
 
-def _sigs() -> dict[str, tuple[list[Any], Any]]:
-    p, i, c_size, c_str = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_char_p
-    return {
-        "ggml_compiler_version": ([], c_str),
-        "ggml_compiler_last_error": ([], c_str),
-        "ggml_compiler_default_options": ([], _Options),
-        "ggml_compiler_has_backend": ([i], ctypes.c_bool),
-        "ggml_compiler_load": ([c_str, ctypes.POINTER(_Options)], p),
-        "ggml_compiler_load_with": ([c_str, ctypes.POINTER(_Options), p, i], p),
-        "ggml_compiler_quantize": ([c_str, p, ctypes.c_int64, ctypes.c_int64, p, c_size], c_size),
-        "ggml_compiler_row_size": ([c_str, ctypes.c_int64], c_size),
-        "ggml_compiler_free": ([p], None),
-        "ggml_compiler_backend_name": ([p], c_str),
-        "ggml_compiler_n_inputs": ([p], i),
-        "ggml_compiler_n_outputs": ([p], i),
-        "ggml_compiler_input_info": ([p, i, ctypes.POINTER(_TensorInfo)], i),
-        "ggml_compiler_output_info": ([p, i, ctypes.POINTER(_TensorInfo)], i),
-        "ggml_compiler_set_input": ([p, c_str, p, c_size], i),
-        "ggml_compiler_n_entries": ([p], i),
-        "ggml_compiler_entry_name": ([p, i], c_str),
-        "ggml_compiler_entry_n_inputs": ([p, i], i),
-        "ggml_compiler_entry_n_outputs": ([p, i], i),
-        "ggml_compiler_entry_input_info": ([p, i, i, ctypes.POINTER(_TensorInfo)], i),
-        "ggml_compiler_entry_output_info": ([p, i, i, ctypes.POINTER(_TensorInfo)], i),
-        "ggml_compiler_run_entry": ([p, c_str], i),
-        "ggml_compiler_reset": ([p], i),
-        "ggml_compiler_metadata": ([p, c_str], c_str),
-        "ggml_compiler_n_symbols": ([p], i),
-        "ggml_compiler_symbol_info": ([p, i, ctypes.POINTER(c_str), ctypes.POINTER(ctypes.c_int64),
-                                       ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)], i),
-        "ggml_compiler_set_symbol": ([p, c_str, ctypes.c_int64], i),
-        "ggml_compiler_set_input_shape": ([p, c_str, i, ctypes.POINTER(ctypes.c_int64)], i),
-        "ggml_compiler_run": ([p], i),
-        "ggml_compiler_get_output": ([p, c_str, p, c_size], i),
-        "ggml_compiler_last_stats": ([p, ctypes.POINTER(_Stats)], i),
-        "ggml_compiler_n_stages": ([p], i),
-        "ggml_compiler_stage_stats": ([p, i, ctypes.POINTER(c_str), ctypes.POINTER(ctypes.c_double),
-                                       ctypes.POINTER(ctypes.c_int)], i),
-        # extensions of this backend (include/ggml_compiler_b200.h)
-        "ggml_compiler_b200_stream": ([p], p),
-        "ggml_compiler_b200_last_device_ms": ([p], ctypes.c_double),
-        "ggml_compiler_b200_set_profiling": ([p, i], i),
-        "ggml_compiler_b200_n_kernel_stats": ([p], i),
-        "ggml_compiler_b200_kernel_stats": ([p, i, ctypes.POINTER(c_str), ctypes.POINTER(ctypes.c_double),
-                                             ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_double)], i),
-        "ggml_compiler_b200_tp_init": ([p, i, i, c_size, p, c_size], i),
-        "ggml_compiler_b200_tp_connect": ([p, p, c_size], i),
-    }
+_RETURNS_HANDLE = ("load", "entry_name", "backend_name")
 
 
-_lib: ctypes.CDLL | None = None
-
-
-def load_library() -> ctypes.CDLL:
-    global _lib
-    if _lib is not None:
-        return _lib
-    lib = ctypes.CDLL(str(library_path()))
-    for name, (args, res) in _sigs().items():
-        f = getattr(lib, name)
-        f.argtypes = args
-        f.restype = res
-    _lib = lib
-    return lib
-
-
-_load = load_library
-
-
-def _error() -> GgmlCompilerRuntimeError:
-    return GgmlCompilerRuntimeError(_load().ggml_compiler_last_error().decode())
-
-
-def version() -> str:
-    return _load().ggml_compiler_version().decode()
-
-
-def quantize(data: np.ndarray, type_name: str) -> np.ndarray:
-    """Encode f32 data (rows along the last axis) in a ggml type; uint8 [rows..., row_bytes]."""
-    lib = _load()
-    x = np.ascontiguousarray(data, dtype=np.float32)
-    n = x.shape[-1]
-    rows = x.size // n
-    row_bytes = lib.ggml_compiler_row_size(type_name.encode(), n)
-    if row_bytes == 0:
-        raise _error()
-    out = np.empty(x.shape[:-1] + (row_bytes,), dtype=np.uint8)
-    if lib.ggml_compiler_quantize(type_name.encode(), x.ctypes.data, rows, n, out.ctypes.data, out.nbytes) == 0:
-        raise _error()
+def _call(fn: str, *args: Any) -> Any:
+    """Calls ggml_compiler_<fn>. A negative int result, or NULL from a function that returns a
+    handle or a name, is the library's error convention and becomes a BackendError."""
+    out = getattr(load_library(), "ggml_compiler_" + fn)(*args)
+    failed = out is None if fn in _RETURNS_HANDLE else type(out) is int and out < 0
+    if failed:
+        raise BackendError(load_library().ggml_compiler_last_error().decode())
     return out
 
 
-def row_size(type_name: str, n: int) -> int:
-    return int(_load().ggml_compiler_row_size(type_name.encode(), n))
+def version() -> str:
+    return load_library().ggml_compiler_version().decode()
 
 
-def has_backend(backend: str) -> bool:
-    return bool(_load().ggml_compiler_has_backend(_BACKENDS[backend]))
+def cuda_available() -> bool:
+    return bool(load_library().ggml_compiler_has_backend(BACKEND_CUDA))
+
+
+def encoded_row_bytes(type_name: str, n: int) -> int:
+    """Bytes of one row of `n` values encoded as `type_name` (0 if the type cannot hold it)."""
+    return int(load_library().ggml_compiler_row_size(type_name.encode(), n))
+
+
+def encode(values: np.ndarray, type_name: str) -> np.ndarray:
+    """Rows (the last axis) of f32 values in a ggml block format, through the library's encoder:
+    uint8 [..., encoded_row_bytes]."""
+    x = np.ascontiguousarray(values, np.float32)
+    width = encoded_row_bytes(type_name, x.shape[-1])
+    if not width:
+        raise BackendError(load_library().ggml_compiler_last_error().decode())
+    out = np.empty(x.shape[:-1] + (width,), np.uint8)
+    if not load_library().ggml_compiler_quantize(type_name.encode(), x.ctypes.data, x.size // x.shape[-1],
+                                                 x.shape[-1], out.ctypes.data, out.nbytes):
+        raise BackendError(load_library().ggml_compiler_last_error().decode())
+    return out
 
 
 @dataclass(frozen=True)
-class TensorInfo:
+class Port:
+    """An input or output of an entry point, at the program's current symbol binding."""
+
     name: str
+    dtype: Any
     shape: tuple[int, ...]
-    dtype: str
     nbytes: int
 
+    @staticmethod
+    def of(info: CTensorInfo) -> "Port":
+        return Port(info.name.decode(), np.dtype(_NP_OF_DTYPE[info.dtype]), tuple(info.shape[: info.ndim]), info.nbytes)
 
-class Session:
-    """A loaded model. `run` takes inputs positionally or by name and returns outputs by name
-    (reference ggml_compiler/runtime/session.py:160-306). Symbols are bound from the input shapes;
-    `set_symbol` binds the others (a loop's trip count). State (a KV cache) persists across runs
-    until `reset()`."""
 
-    def __init__(self, path: str | os.PathLike, backend: str = "auto", device: int = 0, n_threads: int = 0,
-                 allow_cpu_fallback: bool = False) -> None:
-        lib = _load()
-        self._m = None
-        if backend not in _BACKENDS:
-            raise ValueError(f"backend must be one of {sorted(_BACKENDS)}")
-        opt = lib.ggml_compiler_default_options()
-        opt.backend, opt.device, opt.n_threads, opt.allow_cpu_fallback = (
-            _BACKENDS[backend], device, n_threads, allow_cpu_fallback)
-        self._m = lib.ggml_compiler_load(os.fsencode(path), ctypes.byref(opt))
-        if not self._m:
-            raise _error()
-        self.backend_name: str = lib.ggml_compiler_backend_name(self._m).decode()
-        self._np: dict[str, np.dtype] = {}
-        self.entries: dict[str, tuple[list[TensorInfo], list[TensorInfo]]] = {}
-        for e in range(lib.ggml_compiler_n_entries(self._m)):
-            ins = [self._info(lambda m, k, info: lib.ggml_compiler_entry_input_info(m, e, k, info), k)
-                   for k in range(lib.ggml_compiler_entry_n_inputs(self._m, e))]
-            outs = [self._info(lambda m, k, info: lib.ggml_compiler_entry_output_info(m, e, k, info), k)
-                    for k in range(lib.ggml_compiler_entry_n_outputs(self._m, e))]
-            self.entries[lib.ggml_compiler_entry_name(self._m, e).decode()] = (ins, outs)
-        self.inputs, self.outputs = next(iter(self.entries.values()))
-        self.symbols: dict[str, tuple[int, int]] = {}
-        for k in range(lib.ggml_compiler_n_symbols(self._m)):
-            name, lo, hi = ctypes.c_char_p(), ctypes.c_int64(), ctypes.c_int64()
-            lib.ggml_compiler_symbol_info(self._m, k, ctypes.byref(name), ctypes.byref(lo), ctypes.byref(hi), None)
-            self.symbols[name.value.decode()] = (lo.value, hi.value)
+class Entry:
+    """One entry point of a loaded program (prefill, decode, generate, ...)."""
+
+    def __init__(self, model: "Model", index: int) -> None:
+        self.model, self.index = model, index
+        self.name = _call("entry_name", model.handle, index).decode()
+
+    def _ports(self, outputs: bool) -> list[Port]:
+        h, e = self.model.handle, self.index
+        count = _call("entry_n_outputs" if outputs else "entry_n_inputs", h, e)
+        ports = []
+        for k in range(count):
+            info = CTensorInfo()
+            _call("entry_output_info" if outputs else "entry_input_info", h, e, k, C.byref(info))
+            ports.append(Port.of(info))
+        return ports
 
     @property
-    def metadata(self) -> dict[str, Any]:
-        raw = _load().ggml_compiler_metadata(self._m, b"ggml_compiler.meta")
-        return json.loads(raw.decode()) if raw else {}
+    def inputs(self) -> list[Port]:
+        return self._ports(False)
 
-    def set_symbol(self, name: str, value: int) -> None:
-        if _load().ggml_compiler_set_symbol(self._m, name.encode(), int(value)) != 0:
-            raise _error()
+    @property
+    def outputs(self) -> list[Port]:
+        """The outputs at the binding in force now (after the inputs of a run were uploaded)."""
+        return self._ports(True)
 
-    def bound(self) -> dict[str, int]:
-        lib, out = _load(), {}
-        for k in range(len(self.symbols)):
-            name, v = ctypes.c_char_p(), ctypes.c_int64()
-            lib.ggml_compiler_symbol_info(self._m, k, ctypes.byref(name), None, None, ctypes.byref(v))
-            out[name.value.decode()] = v.value
-        return out
+    def upload(self, arrays: dict[str, Any]) -> None:
+        """Copies every input of this entry from host arrays; symbolic dims bind from their shapes."""
+        ports = self.inputs
+        given, wanted = set(arrays), {p.name for p in ports}
+        if given != wanted:
+            raise KeyError(f"entry {self.name} takes {sorted(wanted)}, got {sorted(given)}")
+        host = {p.name: np.ascontiguousarray(np.asarray(arrays[p.name]), p.dtype) for p in ports}
+        h = self.model.handle
+        if self.model.symbol_range:
+            for name, a in host.items():
+                dims = (C.c_int64 * max(1, a.ndim))(*a.shape)
+                _call("set_input_shape", h, name.encode(), a.ndim, dims)
+        for name, a in host.items():
+            _call("set_input", h, name.encode(), a.ctypes.data, a.nbytes)
 
-    def _info(self, fn: Any, k: int) -> TensorInfo:
-        info = _TensorInfo()
-        if fn(self._m, k, ctypes.byref(info)) != 0:
-            raise _error()
-        name, (dtype, np_dtype) = info.name.decode(), _DTYPES[info.dtype]
-        self._np[name] = np.dtype(np_dtype)
-        return TensorInfo(name, tuple(info.shape[: info.ndim]), dtype, info.nbytes)
+    def launch(self) -> None:
+        _call("run_entry", self.model.handle, self.name.encode())
 
-    def reset(self) -> None:
-        if _load().ggml_compiler_reset(self._m) != 0:
-            raise _error()
-
-    def set_inputs(self, entry: str, arrays: dict[str, np.ndarray]) -> None:
-        """Bind symbols from the shapes and upload every input of `entry` (host -> device)."""
-        lib = _load()
-        inputs, _ = self.entries[entry]
-        for t in inputs:
-            x = arrays[t.name]
-            if not self.symbols:
-                if x.shape != t.shape:
-                    raise ValueError(f"input {t.name} has shape {x.shape}, the model expects {t.shape}")
-                continue
-            shape = (ctypes.c_int64 * max(1, x.ndim))(*x.shape)
-            if lib.ggml_compiler_set_input_shape(self._m, t.name.encode(), x.ndim, shape) != 0:
-                raise _error()
-        for t in inputs:
-            x = arrays[t.name]
-            if lib.ggml_compiler_set_input(self._m, t.name.encode(), x.ctypes.data, x.nbytes) != 0:
-                raise _error()
-
-    def run_entry(self, entry: str) -> None:
-        if _load().ggml_compiler_run_entry(self._m, entry.encode()) != 0:
-            raise _error()
-
-    def get_outputs(self, entry: str) -> dict[str, np.ndarray]:
-        lib = _load()
-        _, outputs = self.entries[entry]
-        if self.symbols:
-            e = list(self.entries).index(entry)
-            outputs = [self._info(lambda m, k, info: lib.ggml_compiler_entry_output_info(m, e, k, info), k)
-                       for k in range(len(outputs))]
+    def fetch(self) -> dict[str, np.ndarray]:
         out = {}
-        for t in outputs:
-            y = np.empty(t.shape, dtype=self._np[t.name])
-            if lib.ggml_compiler_get_output(self._m, t.name.encode(), y.ctypes.data, y.nbytes) != 0:
-                raise _error()
-            out[t.name] = y
+        for p in self.outputs:
+            y = np.empty(p.shape, p.dtype)
+            _call("get_output", self.model.handle, p.name.encode(), y.ctypes.data, y.nbytes)
+            out[p.name] = y
         return out
 
-    def run(self, *args: Any, entry: str | None = None, **kwargs: Any) -> dict[str, np.ndarray]:
-        entry = entry or next(iter(self.entries))
-        if entry not in self.entries:
-            raise ValueError(f"no entry point {entry!r}; the model has {list(self.entries)}")
-        inputs, _ = self.entries[entry]
-        if len(args) > len(inputs):
-            raise TypeError(f"{len(args)} positional inputs for an entry with {len(inputs)} inputs")
-        given = {t.name: a for t, a in zip(inputs, args)}
-        for k, v in kwargs.items():
-            if k in given:
-                raise TypeError(f"input {k} given twice")
-            given[k] = v
-        names = {t.name for t in inputs}
-        unknown = set(given) - names
-        if unknown:
-            raise TypeError(f"unknown inputs {sorted(unknown)}; the model takes {[t.name for t in inputs]}")
-        missing = names - set(given)
-        if missing:
-            raise TypeError(f"missing inputs {sorted(missing)}")
-        arrays = {t.name: _as_numpy(given[t.name], self._np[t.name]) for t in inputs}
-        self.set_inputs(entry, arrays)
-        self.run_entry(entry)
-        return self.get_outputs(entry)
+    def __call__(self, **arrays: Any) -> dict[str, np.ndarray]:
+        self.upload(arrays)
+        self.launch()
+        return self.fetch()
+
+
+class Model:
+    """A ggml-compiler GGUF loaded on one B200 (ggml_compiler_load with the CUDA backend)."""
+
+    def __init__(self, path: str | os.PathLike, device: int = 0) -> None:
+        opts = load_library().ggml_compiler_default_options()
+        opts.backend, opts.device = BACKEND_CUDA, device
+        self.handle = _call("load", os.fsencode(path), C.byref(opts))
+        self.path = Path(path)
+        self.entries = {e.name: e for e in (Entry(self, k) for k in range(_call("n_entries", self.handle)))}
+        self.symbol_range: dict[str, tuple[int, int]] = {}
+        for k in range(_call("n_symbols", self.handle)):
+            name, lo, hi = C.c_char_p(), C.c_int64(), C.c_int64()
+            _call("symbol_info", self.handle, k, C.byref(name), C.byref(lo), C.byref(hi), None)
+            self.symbol_range[name.value.decode()] = (lo.value, hi.value)
+
+    # -- the program ------------------------------------------------------------------------------
+    @property
+    def backend(self) -> str:
+        return _call("backend_name", self.handle).decode()
 
     @property
-    def stats(self) -> dict[str, Any]:
-        lib = _load()
-        st = _Stats()
-        if lib.ggml_compiler_last_stats(self._m, ctypes.byref(st)) != 0:
-            raise _error()
-        stages = {}
-        for k in range(lib.ggml_compiler_n_stages(self._m)):
-            name, ms, calls = ctypes.c_char_p(), ctypes.c_double(), ctypes.c_int()
-            lib.ggml_compiler_stage_stats(self._m, k, ctypes.byref(name), ctypes.byref(ms), ctypes.byref(calls))
-            stages[name.value.decode()] = {"ms": ms.value, "calls": calls.value}
-        return {"ms_total": st.ms_total, "n_calls": st.n_calls, "stages": stages}
+    def meta(self) -> dict[str, Any]:
+        """The program's own metadata (GGUF key ggml_compiler.meta), {} if it has none."""
+        raw = load_library().ggml_compiler_metadata(self.handle, b"ggml_compiler.meta")
+        return json.loads(raw) if raw else {}
 
-    # ---- extensions of this backend (no counterpart in the reference's Session)
+    def symbols(self) -> dict[str, int]:
+        vals = {}
+        for k, name in enumerate(self.symbol_range):
+            v = C.c_int64()
+            _call("symbol_info", self.handle, k, None, None, None, C.byref(v))
+            vals[name] = v.value
+        return vals
 
+    def bind(self, **values: int) -> None:
+        """Binds symbols that no input shape fixes (a loop's trip count `max_new`)."""
+        for name, v in values.items():
+            _call("set_symbol", self.handle, name.encode(), int(v))
+
+    def clear_state(self) -> None:
+        """Zeroes the program's state values (the KV cache)."""
+        _call("reset", self.handle)
+
+    def stage_calls(self) -> dict[str, int]:
+        """Calls of each stage in the last entry run (a device loop's iterations, for one)."""
+        out = {}
+        for k in range(_call("n_stages", self.handle)):
+            name, ms, n = C.c_char_p(), C.c_double(), C.c_int()
+            _call("stage_stats", self.handle, k, C.byref(name), C.byref(ms), C.byref(n))
+            out[name.value.decode()] = n.value
+        return out
+
+    def wall_ms(self) -> float:
+        st = CStats()
+        _call("last_stats", self.handle, C.byref(st))
+        return st.ms_total
+
+    # -- this backend's extensions ---------------------------------------------------------------------
     @property
     def stream(self) -> int:
-        """The CUDA stream (cudaStream_t as an int) every launch of this session goes to."""
-        return int(_load().ggml_compiler_b200_stream(self._m) or 0)
+        """The cudaStream_t (as an int) of every launch of this model."""
+        return int(_call("b200_stream", self.handle) or 0)
 
     @property
-    def last_device_ms(self) -> float:
-        """Device time of the last run or run_entry, CUDA events around all its launches."""
-        return float(_load().ggml_compiler_b200_last_device_ms(self._m))
+    def device_ms(self) -> float:
+        """Device time of the last entry run: CUDA events on the model's stream around its launches."""
+        return float(_call("b200_last_device_ms", self.handle))
 
-    def set_profiling(self, on: bool) -> None:
-        """Per-launch timing (each launch synchronised, no CUDA graphs) while on; clears the stats."""
-        if _load().ggml_compiler_b200_set_profiling(self._m, int(bool(on))) != 0:
-            raise _error()
+    def profile(self, on: bool) -> None:
+        """On: every launch timed on its own (synchronised, no CUDA graphs); the statistics restart."""
+        _call("b200_set_profiling", self.handle, int(bool(on)))
 
-    def kernel_stats(self) -> dict[str, dict[str, float]]:
-        """Per kernel family, since profiling was switched on: total ms, launches and algorithmic bytes."""
-        lib = _load()
-        out = {}
-        for k in range(lib.ggml_compiler_b200_n_kernel_stats(self._m)):
-            name, ms, n, b = ctypes.c_char_p(), ctypes.c_double(), ctypes.c_int(), ctypes.c_double()
-            lib.ggml_compiler_b200_kernel_stats(self._m, k, ctypes.byref(name), ctypes.byref(ms), ctypes.byref(n),
-                                                ctypes.byref(b))
-            out[name.value.decode()] = {"ms": ms.value, "launches": n.value, "bytes": b.value}
-        return out
+    def kernel_table(self) -> dict[str, dict[str, float]]:
+        """Per kernel family since profiling was switched on: ms, launches, algorithmic bytes."""
+        table = {}
+        for k in range(_call("b200_n_kernel_stats", self.handle)):
+            name, ms, n, b = C.c_char_p(), C.c_double(), C.c_int(), C.c_double()
+            _call("b200_kernel_stats", self.handle, k, C.byref(name), C.byref(ms), C.byref(n), C.byref(b))
+            table[name.value.decode()] = {"ms": ms.value, "launches": n.value, "bytes": b.value}
+        return table
 
-    def tensor_parallel(self, rank: int, world: int, all_gather: Callable[[bytes], list[bytes]],
-                        window_bytes: int = 0) -> None:
-        """Join a tensor-parallel group of `world` processes, one GPU each, that loaded the same
-        program (ggml_compiler_b200_tp_init / _tp_connect). `all_gather(b)` returns every rank's
-        bytes in rank order (for example `torch_all_gather()`); call before the first run, on every
-        rank. Afterwards every rank must make the same runs; results equal one GPU's."""
-        lib = _load()
-        h = ctypes.create_string_buffer(256)
-        n = lib.ggml_compiler_b200_tp_init(self._m, rank, world, window_bytes, h, len(h))
-        if n < 0:
-            raise _error()
-        handles = exchange_handles(h.raw[:n], rank, world, all_gather)
-        if lib.ggml_compiler_b200_tp_connect(self._m, handles, len(handles)) != 0:
-            raise _error()
+    def join_tensor_parallel(self, rank: int, world: int, all_gather: Callable[[bytes], list[bytes]],
+                             window_bytes: int = 0) -> None:
+        """Makes this process rank `rank` of `world` (one GPU each, every rank with the same program
+        loaded): exports this rank's exchange window, gathers every rank's handle with `all_gather`
+        (bytes -> list of every rank's bytes, rank order) and maps the peers' windows. Every rank
+        must then make the same entry runs; results equal one GPU's."""
+        buf = C.create_string_buffer(256)
+        n = _call("b200_tp_init", self.handle, rank, world, window_bytes, buf, len(buf))
+        joined = joined_handles(buf.raw[:n], rank, world, all_gather)
+        _call("b200_tp_connect", self.handle, joined, len(joined))
 
     def close(self) -> None:
-        if getattr(self, "_m", None):
-            _load().ggml_compiler_free(self._m)
-            self._m = None
+        if getattr(self, "handle", None):
+            load_library().ggml_compiler_free(self.handle)
+            self.handle = None
 
-    def __enter__(self) -> "Session":
+    def __enter__(self) -> "Model":
         return self
 
     def __exit__(self, *exc: Any) -> None:
@@ -359,29 +318,22 @@ class Session:
         self.close()
 
 
-def exchange_handles(mine: bytes, rank: int, world: int, all_gather: Callable[[bytes], list[bytes]]) -> bytes:
-    """Every rank's window handle, concatenated in rank order, checked for shape."""
-    got = list(all_gather(bytes(mine)))
-    if len(got) != world:
-        raise ValueError(f"all_gather returned {len(got)} handles for a group of {world}")
-    if got[rank] != mine or any(len(g) != len(mine) for g in got):
-        raise ValueError("all_gather must return every rank's handle, in rank order, all of one size")
-    return b"".join(got)
+def joined_handles(mine: bytes, rank: int, world: int, all_gather: Callable[[bytes], list[bytes]]) -> bytes:
+    """Every rank's exchange-window handle in rank order, concatenated; checks what came back."""
+    every = [bytes(b) for b in all_gather(bytes(mine))]
+    if len(every) != world or every[rank] != mine or len({len(b) for b in every}) != 1:
+        raise ValueError(f"all_gather must return {world} handles of one size in rank order, "
+                         f"this rank's ({rank}) at its place")
+    return b"".join(every)
 
 
 def torch_all_gather(group: Any = None) -> Callable[[bytes], list[bytes]]:
-    """An all_gather for Session.tensor_parallel over an initialised torch.distributed group."""
+    """An all_gather of bytes over an initialised torch.distributed process group."""
     import torch.distributed as dist
 
     def gather(b: bytes) -> list[bytes]:
-        out: list[Any] = [None] * dist.get_world_size(group)
-        dist.all_gather_object(out, b, group=group)
-        return out
+        got: list[Any] = [None] * dist.get_world_size(group)
+        dist.all_gather_object(got, b, group=group)
+        return got
 
     return gather
-
-
-def _as_numpy(x: Any, dtype: np.dtype) -> np.ndarray:
-    if hasattr(x, "detach"):
-        x = x.detach().cpu().numpy()
-    return np.ascontiguousarray(np.asarray(x).astype(dtype, copy=False))

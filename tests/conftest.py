@@ -33,6 +33,30 @@ def gpu():
     """Skip unless a B200 is visible to the library (the -m gpu suite runs on one)."""
     from ggml_compiler_b200 import runtime
 
-    if not runtime.has_backend("cuda"):
+    if not runtime.cuda_available():
         pytest.fail("no B200 visible to libggml_compiler_rt (the gpu tests need one)")
     return True
+
+
+REFERENCE_PY = REPO / "baseline" / "_ref"  # the reference's Python package (installed without its CMake build)
+
+
+@pytest.fixture(scope="session")
+def reference_pkg(rtlib):
+    """The reference's own Python front end (ggml_compiler), bound to this repository's library
+    through $GGML_COMPILER_RT, as a user of the reference switches backends. It lives in
+    baseline/_ref: `pip install --no-index --no-build-isolation --no-deps
+    --config-settings=wheel.cmake=false --target baseline/_ref <reference checkout>` (the
+    reference's own build backend with its CMake step, which needs the network, switched off)."""
+    if not (REFERENCE_PY / "ggml_compiler" / "runtime" / "session.py").exists():
+        pytest.skip("the reference's Python package is not installed in baseline/_ref")
+    from ggml_compiler_b200 import runtime
+
+    os.environ["GGML_COMPILER_RT"] = str(runtime.library_path())
+    if str(REFERENCE_PY) not in sys.path:
+        sys.path.append(str(REFERENCE_PY))
+    import ggml_compiler
+    import ggml_compiler.runtime.session as session
+
+    assert Path(session.library_path()) == Path(runtime.library_path())
+    return ggml_compiler

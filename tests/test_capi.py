@@ -39,22 +39,31 @@ def test_every_declared_symbol_is_exported(rtlib):
 
 def test_version_and_backends(rtlib):
     assert "sm_100a" in runtime.version()
-    assert runtime.has_backend("cpu") is False  # no CPU fallback in this backend
+    assert rtlib.ggml_compiler_has_backend(0) is False  # no CPU fallback in this backend
     o = rtlib.ggml_compiler_default_options()
     assert (o.backend, o.device, o.n_threads, o.allow_cpu_fallback) == (2, 0, 0, False)
 
 
 def test_struct_layouts():
     # ctypes mirrors of ggml_compiler_rt.h:57-75 (identical to the reference's session.py:24-35)
-    assert ctypes.sizeof(runtime._Options) == 16
-    assert ctypes.sizeof(runtime._TensorInfo) == 8 + 4 + 4 + 64 + 8
-    assert ctypes.sizeof(runtime._Stats) == 16
+    assert ctypes.sizeof(runtime.COptions) == 16
+    assert ctypes.sizeof(runtime.CTensorInfo) == 8 + 4 + 4 + 64 + 8
+    assert ctypes.sizeof(runtime.CStats) == 16
+
+
+BACKENDS = {"cpu": 0, "cuda": 1, "auto": 2}
 
 
 def _load_error(path, backend="auto"):
-    with pytest.raises(runtime.GgmlCompilerRuntimeError) as e:
-        runtime.Session(path, backend=backend)
-    return str(e.value)
+    """Loads through the C ABI with the given backend option; returns the error message."""
+    lib = runtime.load_library()
+    opts = lib.ggml_compiler_default_options()
+    opts.backend = BACKENDS[backend]
+    handle = lib.ggml_compiler_load(str(path).encode(), ctypes.byref(opts))
+    if handle:
+        lib.ggml_compiler_free(handle)
+        pytest.fail(f"{path} loaded with backend {backend}")
+    return lib.ggml_compiler_last_error().decode()
 
 
 def test_cpu_backend_refused(tmp_path):
@@ -113,7 +122,7 @@ def test_corrupt_program(tmp_path):
 def test_no_device_is_a_clear_error(tmp_path):
     """On a machine without a B200, a well-formed program fails at the device check (never a crash,
     never a silent CPU run)."""
-    if runtime.has_backend("cuda"):
+    if runtime.cuda_available():
         pytest.skip("a GPU is present")
     msg = _load_error(GOLDEN / "ref_llama_q8_0.gguf")
     assert "no CUDA device available" in msg or "not a B200" in msg

@@ -14,8 +14,8 @@ import pytest
 from conftest import GOLDEN
 
 from oracle.interp import OracleGenerator, Program
-from ggml_compiler_b200.llm import Generator
-from ggml_compiler_b200.runtime import Session
+from ggml_compiler_b200.llm import Decoder
+from ggml_compiler_b200.runtime import BackendError, Model
 
 pytestmark = pytest.mark.gpu
 GGUF = GOLDEN / "ref_llama_q8_0.gguf"
@@ -35,7 +35,7 @@ def sess(gpu, request):
     old = os.environ.get("GGML_COMPILER_B200_DECODE_KERNEL")
     os.environ["GGML_COMPILER_B200_DECODE_KERNEL"] = "1" if request.param == "decode_kernel" else "0"
     try:
-        s = Session(GGUF, backend="cuda")
+        s = Model(GGUF)
     finally:
         if old is None:
             del os.environ["GGML_COMPILER_B200_DECODE_KERNEL"]
@@ -52,34 +52,34 @@ def scaled_err(out, ref):
 
 def test_program_shape(sess):
     assert set(sess.entries) == {"prefill", "decode", "generate"}
-    assert sess.symbols == {"max_new": (1, 768), "s": (2, 64), "kv_blocks": (2, 3)}
-    assert sess.metadata["eos"] == [7] and sess.metadata["max_context"] == 768
-    assert sess.backend_name.startswith("CUDA")
+    assert sess.symbol_range == {"max_new": (1, 768), "s": (2, 64), "kv_blocks": (2, 3)}
+    assert sess.meta["eos"] == [7] and sess.meta["max_context"] == 768
+    assert sess.backend.startswith("CUDA")
 
 
 def test_logits_bit_exact_vs_oracle(sess, golden):
     ids = golden["ids"].tolist()
-    g, o = Generator(sess), OracleGenerator(Program(GGUF))
-    g.reset()
+    g, o = Decoder(sess), OracleGenerator(Program(GGUF))
+    g.restart()
     o.reset()
     chunks = [ids[:16], ids[16:30]] + [[t] for t in ids[30:40]]
     for c in chunks:
-        a, b = g.feed(c), o.feed(c)
+        a, b = g.prompt(c), o.feed(c)
         np.testing.assert_array_equal(a, b)
 
 
 def test_decode_launches(sess):
     """A decode step is the hoisted mask conversion, the embedding row, one decode-kernel launch
     over every layer and the output head, then argmax: or one launch per fused group."""
-    g = Generator(sess)
-    g.reset()
-    g.feed([1, 2, 3])
-    sess.set_profiling(True)
+    g = Decoder(sess)
+    g.restart()
+    g.prompt([1, 2, 3])
+    sess.profile(True)
     try:
-        g.feed([4])
-        ks = sess.kernel_stats()
+        g.step(4)
+        ks = sess.kernel_table()
     finally:
-        sess.set_profiling(False)
+        sess.profile(False)
     if sess.mode == "decode_kernel":
         assert ks["decode_q8_0"]["launches"] == 1
         assert not any(k.startswith("gemv") or k == "flash_attn" for k in ks), ks
@@ -92,9 +92,9 @@ def test_decode_launches(sess):
 
 def test_logits_vs_transformers(sess, golden):
     ids = golden["ids"].tolist()
-    g = Generator(sess)
-    g.reset()
-    got = {39: g.feed(ids)}
+    g = Decoder(sess)
+    g.restart()
+    got = {39: g.prompt(ids)}
     for i, row in got.items():
         assert scaled_err(row, golden["logits"][i]) < 2e-2
 
@@ -102,38 +102,35 @@ def test_logits_vs_transformers(sess, golden):
 def test_greedy_host_and_device_loops_match_oracle(sess, golden):
     """300 tokens from a 30-token prompt: the loop crosses from n_kv 512 into 768."""
     prompt = golden["ids"][:30].tolist()
-    g = Generator(sess)
-    host = g.generate(prompt, max_new=300, stop=[])
-    dev_full = Generator(sess)
+    g = Decoder(sess)
+    host = g.greedy(prompt, 300, stop=[])
+    dev_full = Decoder(sess)
     o = OracleGenerator(Program(GGUF))
     ref, _ = o.generate(prompt, max_new=300)
     assert host == ref
-    dev = dev_full.generate(prompt, max_new=300, device=True)
+    dev = dev_full.greedy(prompt, 300, on_device=True)
     # the device loop stops at the model's EOS id (7); the host loop was told not to
     n = len(dev)
     assert dev == host[:n] and (n == 300 or dev[-1] == 7)
-    assert dev_full.n_past == len(prompt) + n - 1
+    assert dev_full.ctx == len(prompt) + n - 1
 
 
 def test_state_persists_until_reset(sess):
-    g = Generator(sess)
-    a = g.generate([1, 2, 3, 4], max_new=5, stop=[])
-    g.feed([9, 9, 9])
-    b = g.generate([1, 2, 3, 4], max_new=5, stop=[])  # generate resets first
+    g = Decoder(sess)
+    a = g.greedy([1, 2, 3, 4], 5, stop=[])
+    g.prompt([9, 9, 9])
+    b = g.greedy([1, 2, 3, 4], 5, stop=[])  # greedy restarts first
     assert a == b
-    sess.reset()
+    sess.clear_state()
 
 
 def test_input_errors(sess):
-    from ggml_compiler_b200.runtime import GgmlCompilerRuntimeError
+    from ggml_compiler_b200.runtime import load_library
 
-    with pytest.raises(GgmlCompilerRuntimeError, match="needs"):
-        import ctypes
-
-        lib = __import__("ggml_compiler_b200.runtime", fromlist=["x"]).load_library()
-        x = np.zeros(3, np.int32)
-        if lib.ggml_compiler_set_input(sess._m, b"token", x.ctypes.data, 12) != 0:
-            raise GgmlCompilerRuntimeError(lib.ggml_compiler_last_error().decode())
-    with pytest.raises(GgmlCompilerRuntimeError, match="no kv_blocks|cannot have shape"):
-        sess.run(token=np.zeros((1, 1), np.int32), position=np.zeros(1, np.int32),
-                 mask1=np.zeros((1, 1, 1, 300), np.float32), entry="decode")
+    lib = load_library()
+    x = np.zeros(3, np.int32)
+    assert lib.ggml_compiler_set_input(sess.handle, b"token", x.ctypes.data, 12) == -1
+    assert "needs" in lib.ggml_compiler_last_error().decode()
+    with pytest.raises(BackendError, match="no kv_blocks|cannot have shape"):
+        sess.entries["decode"](token=np.zeros((1, 1), np.int32), position=np.zeros(1, np.int32),
+                               mask1=np.zeros((1, 1, 1, 300), np.float32))

@@ -8,7 +8,7 @@ import pytest
 
 import oracle
 from ggml_compiler_b200.programs import write_mul_mat
-from ggml_compiler_b200.runtime import Session
+from ggml_compiler_b200.runtime import Model
 
 pytestmark = pytest.mark.gpu
 
@@ -20,8 +20,8 @@ def weights(shape, seed=0):
 def run_mm(tmp_path, w, wtype, x):
     p = tmp_path / f"mm_{wtype}_{w.shape[0]}x{w.shape[1]}_{x.shape[0]}.gguf"
     write_mul_mat(p, w, wtype, x.shape[0])
-    with Session(p, backend="cuda") as s:
-        return s.run(x=x[None])["out.0"].reshape(x.shape[0], w.shape[0])
+    with Model(p) as m:
+        return m.entries["main"](x=x[None])["out.0"].reshape(x.shape[0], w.shape[0])
 
 
 @pytest.mark.parametrize("wtype", ["q4_0", "q8_0"])
@@ -106,8 +106,8 @@ def test_flash_attn_bit_exact(gpu, tmp_path, D, H, HKV, NQ, NKV, mask):
                                {"scale": float(1.0 / np.sqrt(D))})
     path = tmp_path / "fa.gguf"
     write_gguf(path, prog, [])
-    with Session(path, backend="cuda") as s:
-        got = s.run(**feed)["out.0"]
+    with Model(path) as m:
+        got = m.entries["main"](**feed)["out.0"]
     want = Program(path).run("main", **feed)["out.0"]
     assert np.isfinite(got).all()
     np.testing.assert_array_equal(got, want)

@@ -1,4 +1,4 @@
-"""Tensor parallelism (Session.tensor_parallel, ggml_compiler_b200_tp_init/_tp_connect) on 2, 4 and
+"""Tensor parallelism (Model.join_tensor_parallel, ggml_compiler_b200_tp_init/_tp_connect) on 2, 4 and
 8 GPUs, each rank its own process (tests/tp_worker.py), against the CPU oracle on the same GGUF.
 
 Sharding keeps every row's arithmetic: each GEMV row and each attention head is computed by one

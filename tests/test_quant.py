@@ -22,7 +22,7 @@ def weights(shape, seed=0):
 def test_edge_cases_match_gguf_py(rtlib, typ):
     g = np.load(GOLDEN / "quant_small.npz")
     x = g["x"]
-    got = runtime.quantize(x, typ)
+    got = runtime.encode(x, typ)
     assert got.tobytes() == g[typ].tobytes()
     assert oracle.quantize(x, typ).tobytes() == g[typ].tobytes()
     dec = oracle.dequantize(got, typ, x.shape[-1])
@@ -35,7 +35,7 @@ def test_sweep_digests(rtlib, shape, typ):
     golden = json.loads((GOLDEN / "quant_golden.json").read_text())[f"{shape[0]}x{shape[1]}"]
     w = weights(shape)
     assert hashlib.sha256(w.tobytes()).hexdigest() == golden["f32"]
-    assert hashlib.sha256(runtime.quantize(w, typ).tobytes()).hexdigest() == golden[typ]
+    assert hashlib.sha256(runtime.encode(w, typ).tobytes()).hexdigest() == golden[typ]
 
 
 def test_oracle_digest_one_shape():
@@ -46,18 +46,18 @@ def test_oracle_digest_one_shape():
 
 
 def test_row_size(rtlib):
-    assert runtime.row_size("q4_0", 4096) == 4096 // 32 * 18
-    assert runtime.row_size("q8_0", 4096) == 4096 // 32 * 34
-    assert runtime.row_size("f16", 10) == 20
-    assert runtime.row_size("q4_K", 256) == 144
-    assert runtime.row_size("nope", 32) == 0
+    assert runtime.encoded_row_bytes("q4_0", 4096) == 4096 // 32 * 18
+    assert runtime.encoded_row_bytes("q8_0", 4096) == 4096 // 32 * 34
+    assert runtime.encoded_row_bytes("f16", 10) == 20
+    assert runtime.encoded_row_bytes("q4_K", 256) == 144
+    assert runtime.encoded_row_bytes("nope", 32) == 0
 
 
 def test_quantize_errors(rtlib):
-    with pytest.raises(runtime.GgmlCompilerRuntimeError, match="multiple"):
-        runtime.quantize(np.zeros((2, 40), np.float32), "q8_0")
-    with pytest.raises(runtime.GgmlCompilerRuntimeError, match="unknown tensor type"):
-        runtime.quantize(np.zeros((2, 32), np.float32), "q9_9")
+    with pytest.raises(runtime.BackendError, match="multiple"):
+        runtime.encode(np.zeros((2, 40), np.float32), "q8_0")
+    with pytest.raises(runtime.BackendError, match="unknown tensor type"):
+        runtime.encode(np.zeros((2, 32), np.float32), "q9_9")
     lib = runtime.load_library()
     x = np.zeros((2, 32), np.float32)
     out = np.zeros(10, np.uint8)
@@ -67,11 +67,11 @@ def test_quantize_errors(rtlib):
 
 def test_f16_bf16_encoding(rtlib):
     x = np.array([[0.1, -2.5, 65504.0, 1e-8, 70000.0, -0.0, 3.0e-5, 1.0]], np.float32)
-    np.testing.assert_array_equal(runtime.quantize(x, "f16").view(np.float16), x.astype(np.float16))
+    np.testing.assert_array_equal(runtime.encode(x, "f16").view(np.float16), x.astype(np.float16))
     from gguf import quants
     from gguf.constants import GGMLQuantizationType as T
 
-    assert runtime.quantize(x, "bf16").tobytes() == quants.quantize(x, T.BF16).tobytes()
+    assert runtime.encode(x, "bf16").tobytes() == quants.quantize(x, T.BF16).tobytes()
 
 
 def test_activation_quant_rule():

@@ -7,7 +7,7 @@ import os
 import pytest
 import torch.multiprocessing as mp
 
-from ggml_compiler_b200.runtime import exchange_handles, torch_all_gather
+from ggml_compiler_b200.runtime import joined_handles, torch_all_gather
 
 
 def _rank(rank: int, world: int, port: int, q) -> None:
@@ -16,7 +16,7 @@ def _rank(rank: int, world: int, port: int, q) -> None:
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
         mine = bytes([rank + 1]) * 64
-        q.put((rank, exchange_handles(mine, rank, world, torch_all_gather())))
+        q.put((rank, joined_handles(mine, rank, world, torch_all_gather())))
     finally:
         dist.destroy_process_group()
 
@@ -42,13 +42,13 @@ def test_handles_gathered_in_rank_order():
 
 def test_handle_checks():
     a, b = b"\x01" * 64, b"\x02" * 64
-    assert exchange_handles(b, 1, 2, lambda x: [a, x]) == a + b
-    with pytest.raises(ValueError, match="group of 2"):
-        exchange_handles(a, 0, 2, lambda x: [x])
-    with pytest.raises(ValueError, match="rank order"):
-        exchange_handles(a, 0, 2, lambda x: [b, x])
-    with pytest.raises(ValueError, match="rank order"):
-        exchange_handles(a, 0, 2, lambda x: [x, b"\x02" * 32])
+    assert joined_handles(b, 1, 2, lambda x: [a, x]) == a + b
+    with pytest.raises(ValueError, match="must return 2 handles"):
+        joined_handles(a, 0, 2, lambda x: [x])
+    with pytest.raises(ValueError, match="in rank order"):
+        joined_handles(a, 0, 2, lambda x: [b, x])
+    with pytest.raises(ValueError, match="in rank order"):
+        joined_handles(a, 0, 2, lambda x: [x, b"\x02" * 32])
 
 
 def test_entry_points_reject_bad_arguments(rtlib):

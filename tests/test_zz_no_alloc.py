@@ -12,7 +12,7 @@ import pytest
 
 from ggml_compiler_b200.gguf_write import write_gguf
 from ggml_compiler_b200.programs import single_node_program
-from ggml_compiler_b200.runtime import Session, load_library
+from ggml_compiler_b200.runtime import Model, load_library
 
 D, H, HKV, NQ, NKV, CTX = 128, 8, 2, 3, 300, 512
 SCALE = float(1.0 / np.sqrt(D))
@@ -38,9 +38,9 @@ def _inputs(seed):
 
 def _program_out(path, q, cache_k, cache_v, mask):
     """The op through the existing entry point: a one-node program, K/V as contiguous [Hkv, n_kv, D]."""
-    with Session(path, backend="cuda") as s:
-        out = s.run(q=q[None], k=np.ascontiguousarray(cache_k[None, :, :NKV]),
-                    v=np.ascontiguousarray(cache_v[None, :, :NKV]), mask=mask[None, None])["out.0"]
+    with Model(path) as m:
+        out = m.entries["main"](q=q[None], k=np.ascontiguousarray(cache_k[None, :, :NKV]),
+                                v=np.ascontiguousarray(cache_v[None, :, :NKV]), mask=mask[None, None])["out.0"]
     return out.reshape(NQ, H, D)
 
 

@@ -25,42 +25,41 @@ sys.path[:0] = [str(REPO), str(REPO / "ggml-compiler_b200")]
 
 def run_case(sess, case: dict) -> dict:
     """Logits after each chunk (last row), greedy tokens through the host loop and the device loop."""
-    from ggml_compiler_b200.llm import Generator
+    from ggml_compiler_b200.llm import Decoder
 
-    g = Generator(sess)
-    g.reset()
+    g = Decoder(sess)
+    g.restart()
     logits = []
     for c in case["chunks"]:
-        x = np.asarray(g.feed(c), np.float32)
-        logits.append(x if x.ndim == 1 else x[-1])
-    toks = g.generate(case["prompt"], case["max_new"])
-    dev = g.generate(case["prompt"], case["max_new"], device=True)
+        logits.append(np.asarray(g.prompt(c), np.float32))
+    toks = g.greedy(case["prompt"], case["max_new"])
+    dev = g.greedy(case["prompt"], case["max_new"], on_device=True)
     return {"logits": np.stack(logits), "tokens": np.array(toks), "device_tokens": np.array(dev)}
 
 
 def main() -> None:
     import torch.distributed as dist
 
-    from ggml_compiler_b200.runtime import Session, torch_all_gather
+    from ggml_compiler_b200.runtime import Model, torch_all_gather
 
     path, out, rank, world, port, case = sys.argv[1], Path(sys.argv[2]), int(sys.argv[3]), int(sys.argv[4]), sys.argv[5], sys.argv[6]
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=timedelta(seconds=120))
     try:
-        sess = Session(path, backend="cuda", device=rank)
-        sess.tensor_parallel(rank, world, torch_all_gather())
+        sess = Model(path, device=rank)
+        sess.join_tensor_parallel(rank, world, torch_all_gather())
         if case == "absent-peer":
-            from ggml_compiler_b200.llm import Generator
-            from ggml_compiler_b200.runtime import GgmlCompilerRuntimeError
+            from ggml_compiler_b200.llm import Decoder
+            from ggml_compiler_b200.runtime import BackendError
 
-            g = Generator(sess)
-            g.reset()
-            g.feed(list(range(1, 17)))  # 16 rows: the prefill path, which exchanges nothing
+            g = Decoder(sess)
+            g.restart()
+            g.prompt(list(range(1, 17)))  # 16 rows: the prefill path, which exchanges nothing
             if rank == 0:
                 try:
-                    g.feed([5])
+                    g.step(5)
                     outcome = "no error"
-                except GgmlCompilerRuntimeError as e:
+                except BackendError as e:
                     outcome = str(e)
                 (out / "rank0.txt").write_text(outcome)
         else:
