@@ -11,12 +11,13 @@ are timed (one step = one token through all 32 layers; n_kv = 768).
 - e2e: the same decode through the public C API from host buffers, one `decode` entry per token
   (host -> device copies of token/position/mask from pinned memory, device -> host logits, host
   argmax), timed with CUDA events on the same stream.
-- roofline: the weight-streaming kernel (the decode kernel, one launch per token running every
-  layer's fused GEMVs and attention; or, with GGML_COMPILER_B200_DECODE_KERNEL=0, the per-group
-  GEMV launches), algorithmic bytes per launch (Q4_0 weight bytes + activation bytes + the K/V rows
-  attention reads) / mean launch time from a profiled pass of the same steps.
+- roofline: the weight-streaming kernels (the fused GEMV launches), algorithmic bytes per launch
+  (Q4_0 weight bytes + activation bytes) / mean launch time from a profiled pass of the same steps
+  (each launch timed with CUDA events on the model's stream); `step_hbm_frac` is the same weight
+  bytes over the timed step itself.
 - cpu_baseline / --impl reference: the reference's CPU arithmetic (this repository's C
-  restatement of ggml's CPU path, oracle/) timed on the host's cores on a few decode tokens.
+  restatement of ggml's CPU path, oracle/) timed on the host's cores on decode steps of the same
+  model at the same n_kv. The reference arm loads no product code.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 8b|tiny|sweep]
     python bench.py --config sweep [--shape NxK] [--m M] [--wtype q4_0|q8_0]   # config 2, one line per case

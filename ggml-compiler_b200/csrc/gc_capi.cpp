@@ -53,7 +53,7 @@ int fill_info(const ggml_compiler_model *mm, const gcb::TensorSpec &v, const std
         set_error("info is NULL");
         return -1;
     }
-    const auto shape = gcb::eval_shape(v, b);
+    const auto shape = v.shape_at(b);
     switch (v.type) {
         case gcb::T_F32: info->dtype = GGML_COMPILER_DTYPE_F32; break;
         case gcb::T_F16: info->dtype = GGML_COMPILER_DTYPE_F16; break;
@@ -71,43 +71,37 @@ int fill_info(const ggml_compiler_model *mm, const gcb::TensorSpec &v, const std
     return 0;
 }
 
-// Bind the symbols an input's shape fixes: a dim with one unknown symbol is solved by bisection over
-// the symbol's range (dims are monotone in it), then the whole shape is checked
-// (reference ggml_compiler_rt.cpp:761-808).
+// Binds the symbols an input's shape fixes. Each dim that reads exactly one symbol not yet fixed
+// pins it: dims are nondecreasing in their symbol, so the smallest value in the symbol's range
+// whose dim reaches the given size is found by bisection and must hit it exactly. Two passes let a
+// symbol fixed by one dim settle another dim's expression; the whole shape is then re-checked.
 void solve_shape(Model &m, const gcb::TensorSpec &v, const std::vector<int64_t> &shape) {
-    if (shape.size() != v.shape_x.size())
-        throw std::runtime_error("input '" + v.name + "' has rank " + std::to_string(v.shape_x.size()) + ", got " +
+    if (shape.size() != v.shape_expr.size())
+        throw std::runtime_error("input '" + v.name + "' has rank " + std::to_string(v.shape_expr.size()) + ", got " +
                                  std::to_string(shape.size()));
     std::vector<int64_t> b = m.binding;
-    std::vector<bool> known(b.size(), false);
-    for (int pass = 0; pass < 2; pass++) {
+    uint64_t fixed = 0;
+    for (int pass = 0; pass < 2; pass++)
         for (size_t i = 0; i < shape.size(); i++) {
-            std::vector<bool> used(b.size(), false);
-            v.shape_x[i].symbols(used);
-            int unknown = -1, n_unknown = 0;
-            for (size_t k = 0; k < used.size(); k++)
-                if (used[k] && !known[k]) {
-                    unknown = (int)k;
-                    n_unknown++;
-                }
-            if (n_unknown != 1) continue;
-            const gcb::Symbol &sy = m.prog.symbols[(size_t)unknown];
+            const gcb::DimExpr &dim = v.shape_expr[i];
+            const uint64_t open = dim.reads() & ~fixed;
+            if (!open || (open & (open - 1))) continue;  // no unknown symbol, or more than one
+            const int k = __builtin_ctzll(open);
+            const gcb::Symbol &sy = m.prog.symbols[(size_t)k];
             int64_t lo = sy.min, hi = sy.max;
             while (lo < hi) {
-                const int64_t mid = lo + (hi - lo) / 2;
-                b[(size_t)unknown] = mid;
-                if (v.shape_x[i].eval(b) < shape[i]) lo = mid + 1;
-                else hi = mid;
+                b[(size_t)k] = lo + (hi - lo) / 2;
+                if (dim.eval(b) < shape[i]) lo = b[(size_t)k] + 1;
+                else hi = b[(size_t)k];
             }
-            b[(size_t)unknown] = lo;
-            if (v.shape_x[i].eval(b) != shape[i])
+            b[(size_t)k] = lo;
+            if (dim.eval(b) != shape[i])
                 throw std::runtime_error("input '" + v.name + "': no " + sy.name + " in [" + std::to_string(sy.min) + ", " +
                                          std::to_string(sy.max) + "] gives dim " + std::to_string(i) + " = " +
                                          std::to_string(shape[i]));
-            known[(size_t)unknown] = true;
+            fixed |= 1ull << k;
         }
-    }
-    const auto got = gcb::eval_shape(v, b);
+    const auto got = v.shape_at(b);
     if (got != shape) {
         std::string want, have;
         for (auto d : shape) want += (want.empty() ? "" : ", ") + std::to_string(d);
@@ -373,7 +367,7 @@ int ggml_compiler_get_output(ggml_compiler_model *mm, const char *name, void *ds
             for (const auto &e : mm->m.entries) {
                 for (const gcb::TensorSpec *v : e.outputs) {
                     if (v->name != name) continue;
-                    const size_t have = mm->m.nbytes_of(*v, mm->m.built);
+                    const size_t have = mm->m.nbytes_of(*v, mm->m.binding);
                     if (nbytes != have)
                         throw std::runtime_error("output '" + std::string(name) + "' has " + std::to_string(have) +
                                                  " bytes, buffer has " + std::to_string(nbytes));
@@ -468,6 +462,45 @@ int ggml_compiler_b200_tp_connect(ggml_compiler_model *mm, const void *handles, 
         set_error(e.what());
         return -1;
     }
+}
+
+int64_t ggml_compiler_b200_value_bytes(const ggml_compiler_model *mm, const char *name) {
+    return guarded(
+        [&]() -> int64_t {
+            if (!mm || !name) throw std::runtime_error("NULL argument");
+            auto it = mm->m.values.find(name);
+            if (it == mm->m.values.end()) throw std::runtime_error("no value named '" + std::string(name) + "'");
+            return (int64_t)it->second.buf.size();
+        },
+        (int64_t)-1);
+}
+
+static int copy_value(ggml_compiler_model *mm, const char *name, void *host, size_t nbytes, bool to_host) {
+    return guarded(
+        [&]() {
+            if (!mm || !name || !host) throw std::runtime_error("NULL argument");
+            auto it = mm->m.values.find(name);
+            if (it == mm->m.values.end()) throw std::runtime_error("no value named '" + std::string(name) + "'");
+            gcb::DevBuf &b = it->second.buf;
+            if (nbytes != b.size())
+                throw std::runtime_error("value '" + std::string(name) + "' holds " + std::to_string(b.size()) +
+                                         " bytes, buffer has " + std::to_string(nbytes));
+            gcb::cuda_check(cudaSetDevice(mm->m.device), "cudaSetDevice");
+            gcb::cuda_check(cudaMemcpyAsync(to_host ? host : b.get(), to_host ? (const void *)b.get() : host, nbytes,
+                                            to_host ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice, mm->m.stream),
+                            "value copy");
+            gcb::cuda_check(cudaStreamSynchronize(mm->m.stream), "value copy");
+            return 0;
+        },
+        -1);
+}
+
+int ggml_compiler_b200_read_value(ggml_compiler_model *mm, const char *name, void *dst, size_t nbytes) {
+    return copy_value(mm, name, dst, nbytes, true);
+}
+
+int ggml_compiler_b200_write_value(ggml_compiler_model *mm, const char *name, const void *src, size_t nbytes) {
+    return copy_value(mm, name, const_cast<void *>(src), nbytes, false);
 }
 
 int ggml_compiler_b200_n_kernel_stats(const ggml_compiler_model *mm) { return mm ? (int)mm->m.kstats.size() : -1; }

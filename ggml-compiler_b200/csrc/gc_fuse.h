@@ -32,9 +32,6 @@ struct PlanStep {
     std::vector<TD> tds;  // arena TDs are resolved to pointers before the launch closure is made
     std::function<void(cudaStream_t, const std::vector<TD> &)> fn;
     double bytes;
-    // The same work as a phase of the decode kernel (gc_mega.cu), from the resolved TDs; false when
-    // this binding's layout does not fit it. Empty for steps that only run as their own launch.
-    std::function<bool(const std::vector<TD> &, MegaPhase &)> mega;
     // Fused GEMV steps: their arguments from the resolved TDs, and the L2 prefetch ranges the
     // launch takes (filled once every step of the call site is planned).
     std::function<FusedArgs(const std::vector<TD> &)> gemv;
@@ -42,10 +39,10 @@ struct PlanStep {
 };
 
 struct Planner {
-    Planner(Model &m, CallSite &cs, const DriverOp &d);
+    Planner(Model &m, SitePlan &plan, const CallSite &site);
     Model &m;
-    CallSite &cs;
-    const DriverOp &d;
+    SitePlan &plan;
+    const DriverStep &d;
     const StageSpec &s;
     std::unordered_map<std::string, TD> env;  // node ids and stage params -> views
     std::vector<Storage> storages;

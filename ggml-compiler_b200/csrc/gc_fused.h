@@ -56,40 +56,11 @@ struct FusedArgs {
     int stream_evict_first = 0;  // stream this launch's weights under an L2 evict-first policy
 };
 
-// An attention phase of the decode kernel: split-KV flash attention of M query rows
-// (q [D, H, M] f32) over the first nkv rows of an f16 KV cache (rows contiguous), f16 mask rows
-// [nkv] per query row (broadcast over heads), output [D, H, M] f32.
-struct MegaAttn {
-    const float *q = nullptr;
-    int64_t D = 0, H = 0, Hkv = 0, M = 1, ldq = 0;
-    const char *k = nullptr, *v = nullptr;
-    int64_t knb1 = 0, knb2 = 0, vnb1 = 0, vnb2 = 0, nkv = 0;
-    const __half *mask = nullptr;
-    int64_t mask_ld = 0;  // halves between mask rows
-    float scale = 1.0f;
-    float *part = nullptr;  // [M][H][nchunks][D + 2]
-    float *out = nullptr;
-    int *counters = nullptr;  // [M][Hkv], zero between launches
-};
-
-struct MegaPhase {
-    int type = 0;  // 0: fused GEMV, 1: attention
-    FusedArgs g;
-    MegaAttn at;
-};
-
 namespace k {
 bool fused_gemv_supported(int64_t K, int64_t M, int map);
 // Shape preconditions of one set of arguments (the rope map needs head sizes that are multiples of 16).
 bool fused_gemv_args_ok(const FusedArgs &a);
 void fused_gemv(const FusedArgs &a, cudaStream_t s, bool pdl);
-// The decode step kernel (gc_mega.cu): one cooperative launch over a device array of phases.
-bool mega_supported(int qtype, int M, int64_t kmax, int attn_d);
-// `trace`, when not null, receives [CTA][phase][4] %globaltimer stamps: phase start (after the grid
-// barrier), activation ready, consumers done, producer done issuing the phase's weights.
-void mega_step(const MegaPhase *phases_dev, int nph, int qtype, int M, int64_t kmax, int attn_d, int *gbar, int *err,
-               uint64_t *trace, cudaStream_t s);
-int mega_ctas();  // CTAs of one decode-kernel launch
 }  // namespace k
 
 }  // namespace gcb

@@ -82,7 +82,41 @@ void repeat(const TD &x, const TD &out, cudaStream_t s);
 void concat(const TD &a, const TD &b, const TD &out, int dim, cudaStream_t s);
 void arange(const TD &out, float start, float step, cudaStream_t s);
 void fill_f32(float *dst, int64_t n, float v, cudaStream_t s);
-void causal_mask_row(float *dst, int64_t n_total, int64_t row_len, const int32_t *pos, cudaStream_t s);
+
+// A driver loop's per-iteration bookkeeping on the device (gc_loop.cu). Pointers are device
+// memory; `iter` is the index of the iteration about to run, `start` the counters' start values.
+constexpr int LOOP_MAX = 4;      // counters, masks, scalars, slices, collects and stop tests per loop
+constexpr int LOOP_MAX_IDS = 8;  // stop ids per test
+struct LoopDev {
+    int32_t *iter = nullptr, *stop = nullptr, *end = nullptr;  // end: iterations to run before pausing
+    const int32_t *start = nullptr;
+    int n_counters = 0;
+    int32_t *counter[LOOP_MAX] = {};
+    int n_masks = 0;
+    float *mask[LOOP_MAX] = {};
+    int64_t mask_n[LOOP_MAX] = {}, mask_row[LOOP_MAX] = {};
+    int mask_counter[LOOP_MAX] = {};
+    int n_scalars = 0;
+    float *scalar[LOOP_MAX] = {};
+    int64_t scalar_n[LOOP_MAX] = {};
+    const float *scalar_vals[LOOP_MAX] = {};  // [trips] per scalar
+    int n_slices = 0;
+    char *slice_dst[LOOP_MAX] = {};
+    const char *slice_src[LOOP_MAX] = {};
+    int64_t slice_bytes[LOOP_MAX] = {};
+    int n_collect = 0;
+    char *collect_dst[LOOP_MAX] = {};
+    const char *collect_src[LOOP_MAX] = {};
+    int64_t collect_bytes[LOOP_MAX] = {};
+    int n_until = 0;
+    const int32_t *until_val[LOOP_MAX] = {};
+    int32_t until_ids[LOOP_MAX][LOOP_MAX_IDS] = {};
+    int n_ids[LOOP_MAX] = {};
+};
+void loop_begin(const LoopDev &L, cudaStream_t s);
+// `use_cond`: also set `cond` (the loop's WHILE node) for the next iteration.
+void loop_end(const LoopDev &L, cudaGraphConditionalHandle cond, bool use_cond, cudaStream_t s);
+void loop_guard(const LoopDev &L, cudaGraphConditionalHandle cond, cudaStream_t s);
 
 // mul_mat(a, b): out[n, m, i2, i3] = sum_k a[k, n, i2/r2, i3/r3] * b[k, m, i2, i3].
 // `scratch` must hold mul_mat_scratch_bytes(a, b) bytes.

@@ -43,11 +43,6 @@ void DevBuf::release() {
 
 namespace {
 
-bool symbolic(const TensorSpec &v) {
-    for (const auto &d : v.ne_x)
-        if (!d.is_const()) return true;
-    return false;
-}
 
 struct FileCloser {
     void operator()(FILE *f) const { std::fclose(f); }
@@ -60,8 +55,7 @@ __global__ void set_i32_kernel(int32_t *p, int32_t v) { *p = v; }
 Model::~Model() {
     if (device >= 0) cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
-    for (auto &c : calls)
-        if (c.graph) cudaGraphExecDestroy(c.graph);
+    loops.clear();
     for (size_t r = 0; r < tp.win.size(); r++)
         if ((int)r != tp.rank && tp.win[r]) cudaIpcCloseMemHandle(tp.win[r]);
     for (auto &e : event_pool) {
@@ -80,7 +74,7 @@ Model::~Model() {
 }
 
 size_t Model::nbytes_of(const TensorSpec &v, const std::vector<int64_t> &b) const {
-    const auto ne = eval_ne(v, b);
+    const auto ne = v.ne_at(b);
     return row_size(v.type, ne[0]) * (size_t)(ne[1] * ne[2] * ne[3]);
 }
 
@@ -119,9 +113,8 @@ void Model::load(const char *path, int backend, int dev, bool allow_cpu_fallback
     cuda_check(cudaMalloc(&d_err, sizeof(int)), "cudaMalloc");
     cuda_check(cudaMemset(d_err, 0, sizeof(int)), "cudaMemset");
     if (const char *p = std::getenv("GGML_COMPILER_PROFILE")) profile_path = p;
-    if (const char *p = std::getenv("GGML_COMPILER_B200_TRACE")) trace_path = p;
     if (const char *g = std::getenv("GGML_COMPILER_B200_GRAPHS")) use_graphs = std::atoi(g) != 0;
-    if (const char *g = std::getenv("GGML_COMPILER_B200_DECODE_KERNEL")) use_decode_kernel = std::atoi(g) != 0;
+    if (const char *g = std::getenv("GGML_COMPILER_B200_DEVICE_LOOPS")) use_device_loops = std::atoi(g) != 0;
     if (const char *g = std::getenv("GCB_L2_PREFETCH_MB")) l2_prefetch_bytes = (int64_t)(std::atof(g) * (1 << 20));
     if (const char *g = std::getenv("GCB_STREAM_EVICT_FIRST")) stream_evict_first = std::atoi(g) != 0;
 
@@ -136,8 +129,8 @@ void Model::load(const char *path, int backend, int dev, bool allow_cpu_fallback
         const auto &v = values.at(name);
         rope_positions = std::max<int64_t>(rope_positions, v.spec->ne[1]);
     }
-    for (auto &e : prog.entries) build_ops(e.driver);
-    built = binding;
+    bound = binding;
+    for (auto &e : prog.entries) prepare(e.driver);
     cuda_check(cudaStreamSynchronize(stream), "load");
 }
 
@@ -206,19 +199,17 @@ void Model::load_weights() {
 void Model::alloc_values() {
     for (const auto &v : prog.values) {
         int64_t most = 1;
-        if (!symbolic(v)) {
+        if (!v.reads) {
             most = v.ne[0] * v.ne[1] * v.ne[2] * v.ne[3];
-        } else {  // the largest size over the corners of the symbols it uses
-            std::vector<bool> used(prog.symbols.size(), false);
-            for (const auto &d : v.ne_x) d.symbols(used);
+        } else {  // the largest size over the corners of the box of the symbols it reads
             std::vector<size_t> idx;
-            for (size_t k = 0; k < used.size(); k++)
-                if (used[k]) idx.push_back(k);
+            for (size_t k = 0; k < prog.symbols.size(); k++)
+                if ((v.reads >> k) & 1u) idx.push_back(k);
             std::vector<int64_t> b = binding;
-            for (size_t mask = 0; mask < ((size_t)1 << idx.size()); mask++) {
+            for (size_t corner = 0; corner < ((size_t)1 << idx.size()); corner++) {
                 for (size_t k = 0; k < idx.size(); k++)
-                    b[idx[k]] = (mask >> k) & 1 ? prog.symbols[idx[k]].max : prog.symbols[idx[k]].min;
-                const auto ne = eval_ne(v, b);
+                    b[idx[k]] = (corner >> k) & 1 ? prog.symbols[idx[k]].max : prog.symbols[idx[k]].min;
+                const auto ne = v.ne_at(b);
                 most = std::max(most, ne[0] * ne[1] * ne[2] * ne[3]);
             }
         }
@@ -261,66 +252,80 @@ void Model::bind_values() {
     }
 }
 
-void Model::build_ops(std::vector<DriverOp> &ops) {
-    for (auto &d : ops) {
-        if (d.kind == DriverOp::Kind::Call) {
-            if (d.call_site >= 0) {
-                // rebinding: a stage is replanned only if it reads a symbol whose value changed
-                CallSite &c = calls[(size_t)d.call_site];
-                for (size_t k = 0; k < binding.size() && k < built.size(); k++)
-                    if (binding[k] != built[k] && c.stage->uses[k]) c.stale = true;
-                continue;
+// Every call of every entry gets its call site, planned once at load for the load binding, so a
+// node this backend cannot run fails the load and names itself. Loops are checked here too.
+void Model::prepare(std::vector<DriverStep> &steps) {
+    for (DriverStep &d : steps) {
+        if (d.is_loop) {
+            const LoopSpec &L = *d.loop;
+            auto val = [&](const std::string &name) -> const Value & {
+                auto it = values.find(name);
+                if (it == values.end()) throw std::runtime_error("loop uses undeclared value '" + name + "'");
+                return it->second;
+            };
+            auto typed = [&](const std::string &name, Type t, const char *what) {
+                if (val(name).spec->type != t)
+                    throw std::runtime_error(std::string("loop ") + what + " '" + name + "' must be " + type_name(t));
+            };
+            for (const auto &c : L.carry) {
+                const TD &x = val(c.dst).td, &y = val(c.src).td;
+                if (x.type != y.type || x.ne[0] != y.ne[0] || x.ne[1] != y.ne[1] || x.ne[2] != y.ne[2] || x.ne[3] != y.ne[3])
+                    throw std::runtime_error("loop carry '" + c.dst + "' does not match its initial value '" + c.src + "'");
             }
-            CallSite c;
-            for (size_t i = 0; i < prog.stages.size(); i++) {
-                if (prog.stages[i].name == d.stage) {
-                    c.stage = &prog.stages[i];
-                    c.stage_index = (int)i;
-                }
+            for (const auto &c : L.counters) typed(c.value, T_I32, "counter"), typed(c.start, T_I32, "counter start");
+            for (const auto &mk : L.masks) typed(mk.value, T_F32, "mask");
+            for (const auto &sc : L.scalars) typed(sc.value, T_F32, "scalar");
+            for (const auto &u : L.until) typed(u.value, T_I32, "stop value");
+            for (const auto &sl : L.slices) {
+                const TD &x = val(sl.dst).td, &y = val(sl.src).td;
+                if (x.type != y.type || y.nelements() != x.nelements() * L.trips)
+                    throw std::runtime_error("loop slice '" + sl.dst + "' does not match its source '" + sl.src + "'");
             }
-            if (!c.stage) throw std::runtime_error("driver calls unknown stage '" + d.stage + "'");
-            d.call_site = (int)calls.size();
-            calls.push_back(std::move(c));
-            plan_call_site(*this, calls.back(), d);  // plan now: unsupported nodes fail the load
+            for (const auto &c : L.collect) (void)val(c.dst), (void)val(c.src);
+            prepare(d.loop->body);
             continue;
         }
-        auto val = [&](const std::string &name) -> Value & {
-            auto it = values.find(name);
-            if (it == values.end()) throw std::runtime_error("loop uses undeclared value '" + name + "'");
-            return it->second;
-        };
-        for (const auto &cp : d.carry) {
-            const Value &a = val(cp.first), &b = val(cp.second);
-            if (a.spec->type != b.spec->type || a.td.ne[0] != b.td.ne[0] || a.td.ne[1] != b.td.ne[1] ||
-                a.td.ne[2] != b.td.ne[2] || a.td.ne[3] != b.td.ne[3])
-                throw std::runtime_error("loop carry '" + cp.first + "' does not match its initial value '" + cp.second + "'");
-        }
-        for (const auto &sc : d.scalars)
-            if (val(sc.first).spec->type != T_F32) throw std::runtime_error("loop scalar '" + sc.first + "' must be f32");
-        for (const auto &sl : d.slices) {
-            const Value &a = val(sl.first), &b = val(sl.second);
-            if (a.spec->type != b.spec->type || b.td.nelements() != a.td.nelements() * d.n)
-                throw std::runtime_error("loop slice '" + sl.first + "' does not match its source '" + sl.second + "'");
-        }
-        for (const auto &c : d.counters) {
-            if (val(c.first).spec->type != T_I32 || val(c.second).spec->type != T_I32)
-                throw std::runtime_error("loop counter '" + c.first + "' must be i32");
-        }
-        for (const auto &mk : d.masks)
-            if (val(mk.first).spec->type != T_F32) throw std::runtime_error("loop mask '" + mk.first + "' must be f32");
-        for (const auto &u : d.until)
-            if (val(u.first).spec->type != T_I32) throw std::runtime_error("loop stop value '" + u.first + "' must be i32");
-        for (const auto &c : d.collect) (void)val(c.first), (void)val(c.second);
-        build_ops(d.body);
+        if (d.call_site >= 0) continue;
+        CallSite site;
+        site.stage = &prog.stages[(size_t)d.stage];
+        site.stage_index = d.stage;
+        site.step = &d;
+        d.call_site = (int)calls.size();
+        calls.push_back(std::move(site));
+        plan_for(calls.back());
     }
 }
 
 void Model::rebind() {
-    if (binding == built) return;
+    if (binding == bound) return;
     prog.bind(binding);
     bind_values();
-    for (auto &e : prog.entries) build_ops(e.driver);
-    built = binding;
+    bound = binding;
+}
+
+SitePlan &Model::plan_for(CallSite &site) {
+    rebind();
+    std::vector<int64_t> key;
+    for (size_t k = 0; k < binding.size(); k++)
+        if (site.stage->reads_symbol(k)) key.push_back(binding[k]);
+    for (auto &p : site.plans)
+        if (p->key == key) {
+            p->last_use = ++plan_clock;
+            return *p;
+        }
+    if (site.plans.size() >= CallSite::kPlansPerSite) {
+        // the plan least recently used goes; launches already queued may still read its arena
+        cuda_check(cudaStreamSynchronize(stream), "dropping a plan");
+        auto old = std::min_element(site.plans.begin(), site.plans.end(),
+                                    [](const auto &x, const auto &y) { return x->last_use < y->last_use; });
+        site.plans.erase(old);
+    }
+    auto p = std::make_unique<SitePlan>();
+    p->key = key;
+    plan_call_site(*this, site, *p);
+    p->last_use = ++plan_clock;
+    site.plans.push_back(std::move(p));
+    return *site.plans.back();
 }
 
 std::pair<cudaEvent_t, cudaEvent_t> Model::events() {
@@ -337,151 +342,340 @@ void Model::collect_times() {
     for (const auto &p : pending) {
         float ms = 0;
         cuda_check(cudaEventElapsedTime(&ms, p.a, p.b), "cudaEventElapsedTime");
-        stage_stats[(size_t)p.stage].ms += ms;
+        for (int st : p.stages) stage_stats[(size_t)st].ms += ms / (double)p.stages.size();
     }
     pending.clear();
     events_used = 0;
 }
 
-void Model::run_call(const DriverOp &d) {
-    CallSite &c = calls[(size_t)d.call_site];
-    if (c.stale) plan_call_site(*this, c, d);
-    const bool per_step = profiling || !profile_path.empty();
-    if (events_used > 4096) {  // long loops: fold finished timings so the event pool stays small
-        cuda_check(cudaStreamSynchronize(stream), "stage timing");
-        collect_times();
+// Records a timed region on the stream around `body`, charged to `stages` (split evenly).
+template <class F>
+static void timed(Model &m, std::vector<int> stages, F &&body) {
+    if (m.events_used > 4096) {  // long host loops: fold finished timings so the event pool stays small
+        cuda_check(cudaStreamSynchronize(m.stream), "stage timing");
+        m.collect_times();
     }
-    auto ev = events();
-    cuda_check(cudaEventRecord(ev.first, stream), "cudaEventRecord");
-    if (per_step) {
-        for (const auto &st : c.steps) {
-            cudaEvent_t a, b;
-            cuda_check(cudaEventCreate(&a), "cudaEventCreate");
-            cuda_check(cudaEventCreate(&b), "cudaEventCreate");
-            cuda_check(cudaEventRecord(a, stream), "cudaEventRecord");
-            st.run(stream);
-            cuda_check(cudaEventRecord(b, stream), "cudaEventRecord");
-            cuda_check(cudaEventSynchronize(b), "step");
-            float ms = 0;
-            cudaEventElapsedTime(&ms, a, b);
-            cudaEventDestroy(a);
-            cudaEventDestroy(b);
-            KernelStat &ks = kstats[st.kind];
-            ks.ms += ms;
-            ks.bytes += st.bytes;
-            ks.launches++;
-            if (!profile_path.empty())
-                profile_lines.push_back(c.stage->name + "\t" + st.node + "\t" + st.kind + "\t" + std::to_string(ms));
-        }
-    } else if (use_graphs) {
-        if (!c.graph_ok) {
-            if (c.graph) {
-                cudaGraphExecDestroy(c.graph);
-                c.graph = nullptr;
+    auto ev = m.events();
+    cuda_check(cudaEventRecord(ev.first, m.stream), "cudaEventRecord");
+    body();
+    cuda_check(cudaEventRecord(ev.second, m.stream), "cudaEventRecord");
+    m.pending.push_back({std::move(stages), ev.first, ev.second});
+}
+
+void Model::launch_plan(SitePlan &p, int stage_index) {
+    timed(*this, {stage_index}, [&] {
+        if (profiling || !profile_path.empty()) {  // each launch on its own, timed
+            for (const auto &st : p.steps) {
+                cudaEvent_t a, b;
+                cuda_check(cudaEventCreate(&a), "cudaEventCreate");
+                cuda_check(cudaEventCreate(&b), "cudaEventCreate");
+                cuda_check(cudaEventRecord(a, stream), "cudaEventRecord");
+                st.run(stream);
+                cuda_check(cudaEventRecord(b, stream), "cudaEventRecord");
+                cuda_check(cudaEventSynchronize(b), "step");
+                float ms = 0;
+                cudaEventElapsedTime(&ms, a, b);
+                cudaEventDestroy(a);
+                cudaEventDestroy(b);
+                KernelStat &ks = kstats[st.kind];
+                ks.ms += ms;
+                ks.bytes += st.bytes;
+                ks.launches++;
+                if (!profile_path.empty())
+                    profile_lines.push_back(prog.stages[(size_t)stage_index].name + "\t" + st.node + "\t" + st.kind + "\t" +
+                                            std::to_string(ms));
             }
-            cudaGraph_t g = nullptr;
-            cuda_check(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
-            try {
-                for (const auto &st : c.steps) st.run(stream);
-            } catch (...) {
-                cudaStreamEndCapture(stream, &g);
-                if (g) cudaGraphDestroy(g);
-                throw;
+        } else if (use_graphs) {
+            if (!p.graph) {
+                cudaGraph_t g = nullptr;
+                cuda_check(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+                try {
+                    for (const auto &st : p.steps) st.run(stream);
+                } catch (...) {
+                    cudaStreamEndCapture(stream, &g);
+                    if (g) cudaGraphDestroy(g);
+                    throw;
+                }
+                cuda_check(cudaStreamEndCapture(stream, &g), "cudaStreamEndCapture");
+                const cudaError_t e = cudaGraphInstantiate(&p.graph, g, 0);
+                cudaGraphDestroy(g);
+                cuda_check(e, "cudaGraphInstantiate");
             }
-            cuda_check(cudaStreamEndCapture(stream, &g), "cudaStreamEndCapture");
-            cuda_check(cudaGraphInstantiate(&c.graph, g, 0), "cudaGraphInstantiate");
-            cudaGraphDestroy(g);
-            c.graph_ok = true;
+            cuda_check(cudaGraphLaunch(p.graph, stream), "cudaGraphLaunch");
+        } else {
+            for (const auto &st : p.steps) st.run(stream);
         }
-        cuda_check(cudaGraphLaunch(c.graph, stream), "cudaGraphLaunch");
-    } else {
-        for (const auto &st : c.steps) st.run(stream);
-    }
-    cuda_check(cudaEventRecord(ev.second, stream), "cudaEventRecord");
-    pending.push_back({c.stage_index, ev.first, ev.second});
-    stage_stats[(size_t)c.stage_index].calls++;
+    });
+    stage_stats[(size_t)stage_index].calls++;
     last_calls++;
 }
 
-void Model::run_ops(const std::vector<DriverOp> &ops) {
-    for (const auto &d : ops) {
-        if (d.kind == DriverOp::Kind::Call) {
-            run_call(d);
-            continue;
-        }
-        for (const auto &cp : d.carry) {
-            const Value &src = values.at(cp.second);
-            Value &dst = values.at(cp.first);
-            cuda_check(cudaMemcpyAsync(dst.td.data, src.td.data, src.td.nbytes(), cudaMemcpyDeviceToDevice, stream), "carry");
-        }
-        const int n = d.n_symbol >= 0 ? (int)binding[(size_t)d.n_symbol] : d.n;
-        std::vector<int32_t> starts;
-        for (const auto &c : d.counters) {
-            int32_t v = 0;
-            cuda_check(cudaMemcpyAsync(&v, values.at(c.second).td.data, 4, cudaMemcpyDeviceToHost, stream), "counter");
-            cuda_check(cudaStreamSynchronize(stream), "counter");
-            starts.push_back(v);
-        }
-        for (const auto &c : d.collect) {
-            Value &dst = values.at(c.first);
-            cuda_check(cudaMemsetAsync(dst.buf.get(), 0, dst.buf.size(), stream), "collect");
-        }
-        std::vector<int64_t> ext;
-        for (int i = 0; i < n; i++) {
-            for (const auto &sc : d.scalars) {
-                Value &v = values.at(sc.first);
-                k::fill_f32((float *)v.td.data, v.td.nelements(), sc.second[(size_t)i], stream);
-            }
-            for (const auto &sl : d.slices) {
-                Value &dst = values.at(sl.first);
-                const Value &src = values.at(sl.second);
-                const size_t nb = dst.td.nbytes();
-                cuda_check(cudaMemcpyAsync(dst.td.data, src.td.data + (size_t)i * nb, nb, cudaMemcpyDeviceToDevice, stream),
-                           "slice");
-            }
-            for (size_t k = 0; k < d.counters.size(); k++) {
-                set_i32_kernel<<<1, 1, 0, stream>>>((int32_t *)values.at(d.counters[k].first).td.data, starts[k] + i);
-                cuda_check(cudaGetLastError(), "counter");
-            }
-            if (!d.bind.empty()) {
-                ext = binding;
-                for (int32_t v : starts) ext.push_back((int64_t)v + i);
-                for (const auto &b : d.bind) {
-                    const int64_t v = b.second.eval(ext);
-                    const Symbol &sy = prog.symbols[(size_t)b.first];
-                    if (v < sy.min || v > sy.max)
-                        throw std::runtime_error("loop binds " + sy.name + " = " + std::to_string(v) + ", outside its range");
-                    binding[(size_t)b.first] = v;
-                }
-                rebind();
-            }
-            for (const auto &mk : d.masks) {
-                Value &v = values.at(mk.first);
-                const int64_t pos = (int64_t)starts[(size_t)mk.second] + i;
-                // the mask is written through a device copy of its counter value: graphs stay valid
-                k::causal_mask_row((float *)v.buf.get(), v.td.nelements(), v.td.ne[0],
-                                   (const int32_t *)values.at(d.counters[(size_t)mk.second].first).td.data, stream);
-                (void)pos;
-            }
-            run_ops(d.body);
-            for (const auto &c : d.collect) {
-                Value &dst = values.at(c.first);
-                const Value &src = values.at(c.second);
-                const size_t nb = nbytes_of(*src.spec, binding);
-                cuda_check(cudaMemcpyAsync(dst.buf.get() + (size_t)i * nb, src.td.data, nb, cudaMemcpyDeviceToDevice, stream),
-                           "collect");
-            }
-            bool stop = false;
-            for (const auto &u : d.until) {
-                int32_t v = 0;
-                cuda_check(cudaMemcpyAsync(&v, values.at(u.first).td.data, 4, cudaMemcpyDeviceToHost, stream), "until");
-                cuda_check(cudaStreamSynchronize(stream), "until");
-                stop = stop || std::find(u.second.begin(), u.second.end(), v) != u.second.end();
-            }
-            if (stop) break;
-        }
+void Model::run_call(const DriverStep &d) {
+    CallSite &site = calls[(size_t)d.call_site];
+    launch_plan(plan_for(site), site.stage_index);
+}
+
+void Model::run_steps(const std::vector<DriverStep> &steps) {
+    for (const DriverStep &d : steps) {
+        if (d.is_loop) run_loop(*d.loop);
+        else run_call(d);
     }
 }
+
+// ----------------------------------------------------------------------------------------- loops
+//
+// A loop runs on the device. Its per-iteration bookkeeping is two small kernels (gc_loop.cu) that
+// take the iteration index from device memory, so the iterations between two changes of the
+// symbol binding (a KV window growing by a block) are one CUDA graph: a guard kernel, then a
+// conditional WHILE node whose body is loop_begin, the body's launches and loop_end, which
+// decides whether the body runs again (no stop id seen, iterations left in the stretch). The host
+// computes the binding of every iteration first (the counters' start values are read once), plans
+// each stretch's calls before the loop starts, and launches one graph per stretch without waiting.
+// A stop id ends the loop on the device; the remaining stretches' guards see it and run nothing.
+// With graphs off, under profiling, for nested loops, or if the conditional graph cannot be made,
+// the same kernels run iteration by iteration with the stop flag read back each time.
+
+namespace {
+
+void set_word(int32_t *p, int32_t v, cudaStream_t s) {
+    set_i32_kernel<<<1, 1, 0, s>>>(p, v);
+    cuda_check(cudaGetLastError(), "loop word");
+}
+
+}  // namespace
+
+LoopRuntime &Model::loop_runtime(const LoopSpec &L) {
+    auto &slot = loops[&L];
+    if (slot) return *slot;
+    if (L.counters.size() > (size_t)k::LOOP_MAX || L.masks.size() > (size_t)k::LOOP_MAX ||
+        L.scalars.size() > (size_t)k::LOOP_MAX || L.slices.size() > (size_t)k::LOOP_MAX ||
+        L.collect.size() > (size_t)k::LOOP_MAX || L.until.size() > (size_t)k::LOOP_MAX)
+        throw std::runtime_error("loop has more than " + std::to_string(k::LOOP_MAX) +
+                                 " counters, masks, scalars, slices, collects or stop values");
+    for (const auto &u : L.until)
+        if (u.ids.size() > (size_t)k::LOOP_MAX_IDS)
+            throw std::runtime_error("loop stop value '" + u.value + "' has more than " + std::to_string(k::LOOP_MAX_IDS) + " ids");
+    auto rt = std::make_unique<LoopRuntime>();
+    rt->words.alloc((3 + k::LOOP_MAX) * sizeof(int32_t));
+    int32_t *w = (int32_t *)rt->words.get();
+    k::LoopDev &D = rt->dev;
+    D.iter = w;
+    D.stop = w + 1;
+    D.end = w + 2;
+    D.start = w + 3;
+    if (!L.scalars.empty()) {
+        std::vector<float> host;
+        for (const auto &sc : L.scalars) host.insert(host.end(), sc.per_iteration.begin(), sc.per_iteration.end());
+        rt->scalars.alloc(host.size() * sizeof(float));
+        cuda_check(cudaMemcpy(rt->scalars.get(), host.data(), host.size() * sizeof(float), cudaMemcpyHostToDevice), "loop scalars");
+    }
+    slot = std::move(rt);
+    return *slot;
+}
+
+// The value pointers of the loop's kernels at the current binding.
+void Model::loop_bind(LoopRuntime &rt, const LoopSpec &L) {
+    k::LoopDev &D = rt.dev;
+    auto td = [&](const std::string &name) -> const TD & { return values.at(name).td; };
+    D.n_counters = (int)L.counters.size();
+    for (int k = 0; k < D.n_counters; k++) D.counter[k] = (int32_t *)td(L.counters[(size_t)k].value).data;
+    D.n_masks = (int)L.masks.size();
+    for (int k = 0; k < D.n_masks; k++) {
+        const TD &m = td(L.masks[(size_t)k].value);
+        D.mask[k] = (float *)m.data;
+        D.mask_n[k] = m.nelements();
+        D.mask_row[k] = m.ne[0];
+        D.mask_counter[k] = L.masks[(size_t)k].counter;
+    }
+    D.n_scalars = (int)L.scalars.size();
+    for (int k = 0; k < D.n_scalars; k++) {
+        const TD &v = td(L.scalars[(size_t)k].value);
+        D.scalar[k] = (float *)v.data;
+        D.scalar_n[k] = v.nelements();
+        D.scalar_vals[k] = (const float *)rt.scalars.get() + (size_t)k * (size_t)L.trips;
+    }
+    D.n_slices = (int)L.slices.size();
+    for (int k = 0; k < D.n_slices; k++) {
+        const TD &dst = td(L.slices[(size_t)k].dst);
+        D.slice_dst[k] = dst.data;
+        D.slice_src[k] = td(L.slices[(size_t)k].src).data;
+        D.slice_bytes[k] = (int64_t)dst.nbytes();
+    }
+    D.n_collect = (int)L.collect.size();
+    for (int k = 0; k < D.n_collect; k++) {
+        const Value &src = values.at(L.collect[(size_t)k].src);
+        D.collect_dst[k] = values.at(L.collect[(size_t)k].dst).buf.get();
+        D.collect_src[k] = src.td.data;
+        D.collect_bytes[k] = (int64_t)nbytes_of(*src.spec, binding);
+    }
+    D.n_until = (int)L.until.size();
+    for (int k = 0; k < D.n_until; k++) {
+        D.until_val[k] = (const int32_t *)td(L.until[(size_t)k].value).data;
+        D.n_ids[k] = (int)L.until[(size_t)k].ids.size();
+        for (int t = 0; t < D.n_ids[k]; t++) D.until_ids[k][t] = L.until[(size_t)k].ids[(size_t)t];
+    }
+}
+
+// The stretch graph for the current binding: guard, then WHILE { loop_begin, body, loop_end }.
+// Null if this loop cannot run as a conditional graph.
+cudaGraphExec_t Model::loop_graph(LoopRuntime &rt, const LoopSpec &L, const std::vector<SitePlan *> &body) {
+    for (auto &g : rt.graphs)
+        if (g.key == binding) return g.exec;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t e = cudaGraphCreate(&g, 0);
+    auto fail = [&](const char *what) {
+        if (std::getenv("GGML_COMPILER_B200_LOOP_DEBUG"))
+            std::fprintf(stderr, "[ggml_compiler_b200] loop runs on the host: %s: %s\n", what, cudaGetErrorString(e));
+        cudaGetLastError();
+        if (g) cudaGraphDestroy(g);
+        rt.device_ok = false;
+        return (cudaGraphExec_t) nullptr;
+    };
+    if (e != cudaSuccess) return fail("cudaGraphCreate");
+    cudaGraphConditionalHandle cond = 0;
+    if ((e = cudaGraphConditionalHandleCreate(&cond, g, 0, 0)) != cudaSuccess) return fail("conditional handle");
+    // the guard, captured into g, then the WHILE node after it
+    if ((e = cudaStreamBeginCaptureToGraph(stream, g, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
+        return fail("capture of the guard");
+    k::loop_guard(rt.dev, cond, stream);
+    cudaGraph_t got = nullptr;
+    if ((e = cudaStreamEndCapture(stream, &got)) != cudaSuccess) return fail("capture of the guard");
+    cudaGraphNode_t guard = nullptr;
+    size_t nn = 1;
+    if ((e = cudaGraphGetNodes(g, &guard, &nn)) != cudaSuccess || nn != 1) return fail("guard node");
+    cudaGraphNodeParams cp = {};
+    cp.type = cudaGraphNodeTypeConditional;
+    cp.conditional.handle = cond;
+    cp.conditional.type = cudaGraphCondTypeWhile;
+    cp.conditional.size = 1;
+    cudaGraphNode_t wnode = nullptr;
+    if ((e = cudaGraphAddNode(&wnode, g, &guard, 1, &cp)) != cudaSuccess) return fail("conditional node");
+    cudaGraph_t bodyg = cp.conditional.phGraph_out[0];
+    if ((e = cudaStreamBeginCaptureToGraph(stream, bodyg, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
+        return fail("capture of the body");
+    try {
+        k::loop_begin(rt.dev, stream);
+        for (SitePlan *p : body)
+            for (const auto &st : p->steps) st.run(stream);
+        k::loop_end(rt.dev, cond, true, stream);
+    } catch (...) {
+        cudaGraph_t junk = nullptr;
+        cudaStreamEndCapture(stream, &junk);
+        e = cudaErrorUnknown;
+        return fail("a launch of the body");
+    }
+    if ((e = cudaStreamEndCapture(stream, &got)) != cudaSuccess) return fail("capture of the body");
+    if ((e = cudaGraphInstantiate(&exec, g, 0)) != cudaSuccess) return fail("instantiation");
+    cudaGraphDestroy(g);
+    rt.graphs.push_back({binding, exec});
+    return exec;
+}
+
+void Model::run_loop(const LoopSpec &L) {
+    LoopRuntime &rt = loop_runtime(L);
+    const int64_t trips = L.trip_symbol >= 0 ? binding[(size_t)L.trip_symbol] : L.trips;
+    for (const auto &c : L.carry) {
+        const Value &src = values.at(c.src);
+        cuda_check(cudaMemcpyAsync(values.at(c.dst).td.data, src.td.data, src.td.nbytes(), cudaMemcpyDeviceToDevice, stream),
+                   "loop carry");
+    }
+    for (size_t k = 0; k < L.counters.size(); k++)
+        cuda_check(cudaMemcpyAsync((int32_t *)rt.dev.start + k, values.at(L.counters[k].start).td.data, 4,
+                                   cudaMemcpyDeviceToDevice, stream),
+                   "loop counter start");
+    cuda_check(cudaMemsetAsync(rt.dev.iter, 0, 2 * sizeof(int32_t), stream), "loop words");
+    for (const auto &c : L.collect) {
+        Value &dst = values.at(c.dst);
+        cuda_check(cudaMemsetAsync(dst.buf.get(), 0, dst.buf.size(), stream), "loop collect");
+    }
+    if (trips <= 0) return;
+
+    // the binding of every iteration: stretches of iterations that share one
+    std::vector<int32_t> start(L.counters.size(), 0);
+    if (!L.rebind.empty() && !L.counters.empty()) {
+        cuda_check(cudaMemcpyAsync(start.data(), rt.dev.start, start.size() * 4, cudaMemcpyDeviceToHost, stream), "loop starts");
+        cuda_check(cudaStreamSynchronize(stream), "loop starts");
+    }
+    struct Stretch {
+        int64_t first, count;
+        std::vector<int64_t> binding;
+    };
+    std::vector<Stretch> stretches;
+    std::vector<int64_t> scope = binding;
+    scope.resize(binding.size() + L.counters.size());
+    for (int64_t i = 0; i < trips; i++) {
+        std::vector<int64_t> b = binding;
+        for (size_t k = 0; k < L.counters.size(); k++) scope[binding.size() + k] = (int64_t)start[k] + i;
+        for (size_t k = 0; k < binding.size(); k++) scope[k] = stretches.empty() ? binding[k] : stretches.back().binding[k];
+        for (const auto &rb : L.rebind) {
+            const int64_t v = rb.value.eval(scope);
+            const Symbol &sy = prog.symbols[(size_t)rb.symbol];
+            if (v < sy.min || v > sy.max)
+                throw std::runtime_error("loop sets " + sy.name + " to " + std::to_string(v) + " at iteration " +
+                                         std::to_string(i) + ", outside [" + std::to_string(sy.min) + ", " +
+                                         std::to_string(sy.max) + "]");
+            b[(size_t)rb.symbol] = v;
+            scope[(size_t)rb.symbol] = v;
+        }
+        if (stretches.empty() || stretches.back().binding != b) stretches.push_back({i, 0, b});
+        stretches.back().count++;
+    }
+
+    bool device = use_graphs && use_device_loops && !profiling && profile_path.empty() && rt.device_ok;
+    for (const auto &st : L.body) device = device && !st.is_loop;
+    std::vector<int> body_stages;
+    for (const auto &st : L.body)
+        if (!st.is_loop) body_stages.push_back(st.stage);
+    // every stretch's plans (and graphs) first: nothing is planned while the loop runs
+    std::vector<std::vector<SitePlan *>> plans(stretches.size());
+    std::vector<cudaGraphExec_t> graphs(stretches.size(), nullptr);
+    for (size_t s = 0; s < stretches.size(); s++) {
+        binding = stretches[s].binding;
+        for (const auto &st : L.body)
+            if (!st.is_loop) plans[s].push_back(&plan_for(calls[(size_t)st.call_site]));
+        if (device) {
+            loop_bind(rt, L);
+            graphs[s] = loop_graph(rt, L, plans[s]);
+            device = graphs[s] != nullptr;
+        }
+    }
+
+    int64_t done = 0;
+    if (device) {
+        for (size_t s = 0; s < stretches.size(); s++) {
+            set_word(rt.dev.end, (int32_t)(stretches[s].first + stretches[s].count), stream);
+            timed(*this, body_stages, [&] { cuda_check(cudaGraphLaunch(graphs[s], stream), "loop graph"); });
+        }
+        int32_t ran = 0;
+        cuda_check(cudaMemcpyAsync(&ran, rt.dev.iter, 4, cudaMemcpyDeviceToHost, stream), "loop iterations");
+        cuda_check(cudaStreamSynchronize(stream), "loop");
+        done = ran;
+        for (int st : body_stages) stage_stats[(size_t)st].calls += (int)done;
+        last_calls += (int)(done * (int64_t)body_stages.size());
+    } else {
+        for (size_t s = 0; s < stretches.size() && done == stretches[s].first; s++) {
+            binding = stretches[s].binding;
+            rebind();
+            loop_bind(rt, L);
+            for (int64_t i = 0; i < stretches[s].count; i++) {
+                k::loop_begin(rt.dev, stream);
+                run_steps(L.body);
+                k::loop_end(rt.dev, 0, false, stream);
+                int32_t stop = 0;
+                cuda_check(cudaMemcpyAsync(&stop, rt.dev.stop, 4, cudaMemcpyDeviceToHost, stream), "loop stop");
+                cuda_check(cudaStreamSynchronize(stream), "loop stop");
+                done++;
+                if (stop) break;
+            }
+        }
+    }
+    // the binding of the last iteration that ran stays in force, as after a host-driven loop
+    for (const auto &st : stretches)
+        if (done > st.first) binding = st.binding;
+    rebind();
+}
+
 
 void Model::run_entry(const std::string &name) {
     const Entry *e = nullptr;
@@ -502,7 +696,7 @@ void Model::run_entry(const std::string &name) {
         cuda_check(cudaEventCreate(&run_ev[1]), "cudaEventCreate");
     }
     cuda_check(cudaEventRecord(run_ev[0], stream), "cudaEventRecord");
-    run_ops(e->spec->driver);
+    run_steps(e->spec->driver);
     cuda_check(cudaEventRecord(run_ev[1], stream), "cudaEventRecord");
     cuda_check(cudaStreamSynchronize(stream), ("entry '" + name + "'").c_str());
     last_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
@@ -523,7 +717,6 @@ void Model::run_entry(const std::string &name) {
                                      "(results are invalid)");
         throw std::runtime_error("entry '" + name + "': a set_rows index was outside its destination (row skipped)");
     }
-    if (!trace_path.empty()) write_trace();
     if (!profile_path.empty() && !profile_lines.empty()) {
         if (FILE *f = std::fopen(profile_path.c_str(), "a")) {
             for (const auto &l : profile_lines) std::fprintf(f, "%s\n", l.c_str());
@@ -577,10 +770,10 @@ void Model::tp_connect(const cudaIpcMemHandle_t *handles) {
         tp.win[(size_t)r] = (char *)p;
     }
     tp.connected = true;
-    for (auto &c : calls) {
-        c.stale = true;
-        c.graph_ok = false;
-    }
+    // every plan is made again with this rank's share of the work and the exchanges
+    cuda_check(cudaStreamSynchronize(stream), "tensor parallel");
+    for (auto &c : calls) c.plans.clear();
+    loops.clear();
 }
 
 int *Model::counters(const std::string &key, size_t n) {
@@ -621,35 +814,6 @@ const float *Model::rope_table(int n_dims, float base, float scale, float attn, 
     const float *p = (const float *)buf.get();
     rope_tables.emplace(key, std::move(buf));
     return p;
-}
-
-// One text line per traced phase and CTA: label, CTA, then the four stamps in ns relative to the
-// earliest phase start of the call site.
-void Model::write_trace() {
-    FILE *f = std::fopen(trace_path.c_str(), "w");
-    if (!f) return;
-    const int nctas = k::mega_ctas();
-    for (auto &c : calls) {
-        if (!c.trace.size() || c.trace_labels.empty()) continue;
-        std::vector<uint64_t> h(c.trace.size() / 8);
-        cuda_check(cudaMemcpy(h.data(), c.trace.get(), c.trace.size(), cudaMemcpyDeviceToHost), "trace");
-        uint64_t t0 = ~0ull;
-        for (size_t i = 0; i < h.size(); i += 4)
-            if (h[i]) t0 = std::min(t0, h[i]);
-        std::fprintf(f, "# stage %s ctas %d phases %zu\n", c.stage->name.c_str(), nctas, c.trace_labels.size());
-        for (const auto &r : c.trace_runs) {
-            const uint64_t *run = &h[(size_t)nctas * r.first * 4];  // [CTA][phase of the run][4]
-            for (size_t p = 0; p < r.second; p++)
-                for (int cta = 0; cta < nctas; cta++) {
-                    const uint64_t *st = run + ((size_t)cta * r.second + p) * 4;
-                    std::fprintf(f, "%s\t%d", c.trace_labels[r.first + p].c_str(), cta);
-                    for (int k = 0; k < 4; k++) std::fprintf(f, "\t%lld", st[k] ? (long long)(st[k] - t0) : -1ll);
-                    std::fprintf(f, "\n");
-                }
-        }
-        cuda_check(cudaMemset(c.trace.get(), 0, c.trace.size()), "trace");
-    }
-    std::fclose(f);
 }
 
 }  // namespace gcb

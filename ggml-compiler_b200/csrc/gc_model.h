@@ -47,18 +47,52 @@ struct Step {
     double bytes = 0;       // algorithmic bytes moved (weights, activations, KV)
 };
 
-struct CallSite {
-    const StageSpec *stage = nullptr;
-    int stage_index = 0;
+// One call site planned for one binding of the symbols its stage reads: its launches with every
+// pointer resolved, the arena holding its intermediates, and the CUDA graph that replays them.
+struct SitePlan {
+    std::vector<int64_t> key;  // the stage's symbols, in symbol order, at this binding
     std::vector<Step> steps;
     DevBuf arena;
-    DevBuf phases;  // decode-kernel phase lists (MegaPhase arrays) of the planned steps
-    DevBuf trace;   // decode-kernel phase stamps [run][CTA][phase][4] (GGML_COMPILER_B200_TRACE)
-    std::vector<std::string> trace_labels;  // "<kind> <node>" per traced phase, all runs in order
-    std::vector<std::pair<size_t, size_t>> trace_runs;  // (first phase, phases) per run
-    bool stale = true;
     cudaGraphExec_t graph = nullptr;
-    bool graph_ok = false;
+    uint64_t last_use = 0;
+    SitePlan() = default;
+    SitePlan(const SitePlan &) = delete;
+    SitePlan &operator=(const SitePlan &) = delete;
+    ~SitePlan() {
+        if (graph) cudaGraphExecDestroy(graph);
+    }
+};
+
+// A `call` step of an entry's driver. Its plans are kept per binding (up to kPlansPerSite, the
+// least recently used is dropped), so a loop that moves between KV windows switches plans without
+// planning again.
+struct CallSite {
+    static constexpr size_t kPlansPerSite = 4;
+    const StageSpec *stage = nullptr;
+    int stage_index = 0;
+    const DriverStep *step = nullptr;
+    std::vector<std::unique_ptr<SitePlan>> plans;
+};
+
+// The device state of one loop of the program (gc_model.cu, kernels/gc_loop.cu) and the stretch
+// graphs made for it, one per binding.
+struct LoopRuntime {
+    DevBuf words;    // iter, stop, end, then the counters' start values
+    DevBuf scalars;  // per-iteration scalar values, [scalar][trips]
+    k::LoopDev dev;
+    struct Graph {
+        std::vector<int64_t> key;
+        cudaGraphExec_t exec = nullptr;
+    };
+    std::vector<Graph> graphs;
+    bool device_ok = true;  // false once a conditional graph could not be built
+    LoopRuntime() = default;
+    LoopRuntime(const LoopRuntime &) = delete;
+    LoopRuntime &operator=(const LoopRuntime &) = delete;
+    ~LoopRuntime() {
+        for (auto &g : graphs)
+            if (g.exec) cudaGraphExecDestroy(g.exec);
+    }
 };
 
 struct Weight {
@@ -107,7 +141,7 @@ struct Model {
     std::vector<Entry> entries;
     std::map<std::string, bool> input_set;
     std::vector<CallSite> calls;
-    std::vector<int64_t> binding, built;
+    std::vector<int64_t> binding;
     struct StageStat {
         double ms = 0;
         int calls = 0;
@@ -120,21 +154,21 @@ struct Model {
     int64_t rope_positions = 4096;
     std::map<std::string, DevBuf> rope_tables;
     bool use_graphs = true;
-    bool use_decode_kernel = false;  // GGML_COMPILER_B200_DECODE_KERNEL=1: one persistent launch per decode step
+    bool use_device_loops = true;  // GGML_COMPILER_B200_DEVICE_LOOPS=0: loops checked on the host every iteration
     bool profiling = false;
     int64_t l2_prefetch_bytes = 0;   // GCB_L2_PREFETCH_MB: what each fused GEMV prefetches of the next one's weights
-    bool stream_evict_first = false;  // GCB_STREAM_EVICT_FIRST=1: GEMV weight streams under an L2 evict-first policy
+    bool stream_evict_first = true;  // GCB_STREAM_EVICT_FIRST=0: GEMV weight streams without the L2 evict-first policy
     std::map<std::string, KernelStat> kstats;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> event_pool;
     size_t events_used = 0;
     struct PendingTime {
-        int stage;
+        std::vector<int> stages;  // the stages the timed region is charged to, evenly
         cudaEvent_t a, b;
     };
     std::vector<PendingTime> pending;
     std::string profile_path;  // GGML_COMPILER_PROFILE
-    std::string trace_path;    // GGML_COMPILER_B200_TRACE: decode-kernel phase stamps, rewritten per entry run
     std::vector<std::string> profile_lines;
+    uint64_t plan_clock = 0;  // orders plan uses (least recently used plan of a site is dropped)
     TpGroup tp;
 
     ~Model();
@@ -143,7 +177,7 @@ struct Model {
     void tp_init(int rank, int world, size_t window_bytes, cudaIpcMemHandle_t *handle);
     void tp_connect(const cudaIpcMemHandle_t *handles);
     void load(const char *path, int backend, int device, bool allow_cpu_fallback);
-    void rebind();
+    void rebind();  // the spec's dims and the values' views follow `binding`
     void run_entry(const std::string &name);
     void reset_state();
     size_t nbytes_of(const TensorSpec &v, const std::vector<int64_t> &b) const;
@@ -152,22 +186,30 @@ struct Model {
     // Zeroed device ints that persist across launches (arrival counters), one buffer per key.
     int *counters(const std::string &key, size_t n);
     std::map<std::string, DevBuf> counter_bufs;
+    // The plan of `site` for the current binding, made if missing.
+    SitePlan &plan_for(CallSite &site);
+
+    std::pair<cudaEvent_t, cudaEvent_t> events();
+    void collect_times();
 
   private:
+    std::vector<int64_t> bound;  // the binding the spec and the value views were last bound to
+    std::map<const LoopSpec *, std::unique_ptr<LoopRuntime>> loops;
+    LoopRuntime &loop_runtime(const LoopSpec &L);
+    void loop_bind(LoopRuntime &rt, const LoopSpec &L);
+    cudaGraphExec_t loop_graph(LoopRuntime &rt, const LoopSpec &L, const std::vector<SitePlan *> &body);
     void load_weights();
     void alloc_values();
     void bind_values();
-    void build_ops(std::vector<DriverOp> &ops);
-    void build_site(const DriverOp &d);
-    void run_ops(const std::vector<DriverOp> &ops);
-    void run_call(const DriverOp &d);
-    std::pair<cudaEvent_t, cudaEvent_t> events();
-    void collect_times();
-    void write_trace();
+    void prepare(std::vector<DriverStep> &steps);  // call sites for every call, checks of every loop
+    void run_steps(const std::vector<DriverStep> &steps);
+    void run_call(const DriverStep &d);
+    void launch_plan(SitePlan &p, int stage_index);
+    void run_loop(const LoopSpec &loop);
 };
 
-// Plans one stage call into kernel launches (gc_plan.cpp).
-void plan_call_site(Model &m, CallSite &cs, const DriverOp &d);
+// Plans one stage call for the current binding into kernel launches (gc_plan.cpp).
+void plan_call_site(Model &m, const CallSite &cs, SitePlan &plan);
 
 void cuda_check(cudaError_t e, const char *what);
 

@@ -65,42 +65,9 @@ const std::map<std::string, int> &unary_ops() {
     return m;
 }
 
-// One query row of split-KV attention as a decode-kernel phase (MegaAttn): the query's heads
-// contiguous, K/V rows contiguous with 16-byte aligned heads, one mask row broadcast over heads.
-bool attn_phase(const std::vector<TD> &t, float scale, int *counters, MegaPhase &ph) {
-    const TD &q = t[0], &kk = t[1], &v = t[2], &mk = t[3], &y = t[4];
-    const int64_t D = q.ne[0];
-    if (q.ne[1] != 1 || q.ne[3] != 1 || q.nb[0] != 4 || q.nb[2] != 4 * D || !y.contiguous()) return false;
-    if (kk.nb[1] != 2 * D || v.nb[1] != 2 * D || kk.ne[3] != 1 || mk.ne[2] != 1 || mk.ne[3] != 1) return false;
-    if (q.ne[2] % kk.ne[2] || q.ne[2] / kk.ne[2] > 4) return false;  // up to 4 query heads per K/V head
-    if (((uintptr_t)kk.data | (uintptr_t)v.data | (uintptr_t)kk.nb[2] | (uintptr_t)v.nb[2]) % 16) return false;
-    ph.type = 1;
-    MegaAttn &a = ph.at;
-    a.q = (const float *)q.data;
-    a.D = D;
-    a.H = q.ne[2];
-    a.Hkv = kk.ne[2];
-    a.M = 1;
-    a.ldq = D * q.ne[2];
-    a.k = kk.data;
-    a.v = v.data;
-    a.knb1 = kk.nb[1];
-    a.knb2 = kk.nb[2];
-    a.vnb1 = v.nb[1];
-    a.vnb2 = v.nb[2];
-    a.nkv = kk.ne[1];
-    a.mask = (const __half *)mk.data;
-    a.mask_ld = mk.nb[1] / 2;
-    a.scale = scale;
-    a.part = (float *)t[5].data;
-    a.out = (float *)y.data;
-    a.counters = counters;
-    return true;
-}
-
 }  // namespace
 
-Planner::Planner(Model &m, CallSite &cs, const DriverOp &d) : m(m), cs(cs), d(d), s(*cs.stage) {}
+Planner::Planner(Model &m, SitePlan &plan, const CallSite &site) : m(m), plan(plan), d(*site.step), s(*site.stage) {}
 
 TD Planner::alloc(Type t, const int64_t *ne) {
     TD o;
@@ -179,11 +146,6 @@ void Planner::add_gemv(const char *kind, const std::string &node, std::vector<TD
         bytes);
     psteps.back().gemv = b2;
     psteps.back().pf = pf;
-    psteps.back().mega = [b2](const std::vector<TD> &t, MegaPhase &ph) {
-        ph.type = 0;
-        ph.g = b2(t);
-        return ph.g.M == 1 && ph.g.nshard == 1 && k::fused_gemv_args_ok(ph.g);
-    };
     if (nshard > 1 && !col.empty()) add_exchange(node, out, rows, ld, col);
 }
 
@@ -496,7 +458,6 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
                         k::flash_attn_split(t[0], t[1], t[2], &t[3], t[4], scale, t[5].data, cnt, err, st);
                     },
                     bytes);
-                psteps.back().mega = [scale, cnt](const std::vector<TD> &t, MegaPhase &ph) { return attn_phase(t, scale, cnt, ph); };
                 return y;
             }
             add("flash_attn", n.id, {q, kk, v, mk, y},
@@ -709,11 +670,11 @@ void Planner::finish() {
         for (int sid : starts[i]) storages[(size_t)sid].offset = take(storages[(size_t)sid].bytes);
         for (int sid : ends[i]) give(storages[(size_t)sid].offset, storages[(size_t)sid].bytes);
     }
-    if (cs.arena.size() < top) {
+    if (plan.arena.size() < top) {
         cuda_check(cudaStreamSynchronize(m.stream), "arena");
-        cs.arena.alloc(top);
+        plan.arena.alloc(top);
     }
-    char *base = cs.arena.get();
+    char *base = plan.arena.get();
     for (auto &ps : psteps)
         for (auto &t : ps.tds)
             if (t.sid >= 0) {
@@ -750,90 +711,8 @@ void Planner::finish() {
         }
     }
 
-    // Runs of two or more consecutive steps that the decode kernel can take (one token row, one
-    // weight type, one head size) become one launch of it; the other steps keep their own launch.
-    struct Run {
-        size_t begin = 0, end = 0, phase0 = 0;
-        int qtype = -1;
-        int64_t kmax = 0;
-        int attn_d = 0;
-        double bytes = 0;
-    };
-    std::vector<MegaPhase> phases;
-    std::vector<Run> runs;
-    for (size_t i = 0; m.use_decode_kernel && !m.tp.active() && i < psteps.size();) {
-        Run r;
-        r.begin = i;
-        r.phase0 = phases.size();
-        bool gemv = false;
-        size_t j = i;
-        for (; j < psteps.size() && psteps[j].mega; j++) {
-            MegaPhase ph;
-            if (!psteps[j].mega(psteps[j].tds, ph)) break;
-            int qt = r.qtype, d = r.attn_d;
-            int64_t km = r.kmax;
-            if (ph.type == 0) {
-                if (qt >= 0 && ph.g.qtype != qt) break;
-                qt = ph.g.qtype;
-                km = std::max<int64_t>(km, ph.g.K);
-            } else {
-                if (d && ph.at.D != d) break;
-                d = (int)ph.at.D;
-            }
-            if (!k::mega_supported(qt < 0 ? T_Q4_0 : qt, 1, km, d)) break;
-            r.qtype = qt, r.attn_d = d, r.kmax = km;
-            r.bytes += psteps[j].bytes;
-            gemv = gemv || ph.type == 0;
-            phases.push_back(ph);
-        }
-        if (j - i >= 2 && gemv) {
-            r.end = j;
-            runs.push_back(r);
-            i = j;
-        } else {
-            phases.resize(r.phase0);
-            i = std::max(j, i + 1);
-        }
-    }
-    const size_t pbytes = phases.size() * sizeof(MegaPhase);
-    if (pbytes) {
-        cuda_check(cudaStreamSynchronize(m.stream), "decode kernel phases");  // an earlier plan's launches may read them
-        if (cs.phases.size() < pbytes) cs.phases.alloc(pbytes);
-        cuda_check(cudaMemcpy(cs.phases.get(), phases.data(), pbytes, cudaMemcpyHostToDevice), "decode kernel phases");
-    }
-    int *gbar = runs.empty() ? nullptr : m.counters(s.name + "/decode_kernel", 1);
-    int *err = m.d_err;
-    cs.trace_labels.clear();
-    cs.trace_runs.clear();
-    if (!m.trace_path.empty() && !phases.empty()) {
-        const size_t tb = (size_t)k::mega_ctas() * phases.size() * 4 * sizeof(uint64_t);
-        if (cs.trace.size() < tb) cs.trace.alloc(tb);
-        for (const Run &r : runs) {
-            cs.trace_runs.emplace_back(r.phase0, r.end - r.begin);
-            for (size_t j = r.begin; j < r.end; j++) cs.trace_labels.push_back(std::string(psteps[j].kind) + " " + psteps[j].node);
-        }
-    }
-    uint64_t *trace = cs.trace_labels.empty() ? nullptr : (uint64_t *)cs.trace.get();
-    cs.steps.clear();
-    size_t ri = 0;
-    for (size_t i = 0; i < psteps.size();) {
-        if (ri < runs.size() && runs[ri].begin == i) {
-            const Run r = runs[ri++];
-            const MegaPhase *dev = (const MegaPhase *)cs.phases.get() + r.phase0;
-            const int nph = (int)(r.end - r.begin);
-            Step st;
-            st.kind = r.qtype == T_Q4_0 ? "decode_q4_0" : "decode_q8_0";
-            st.node = psteps[r.begin].node + ".." + psteps[r.end - 1].node;
-            st.bytes = r.bytes;
-            uint64_t *tr = trace ? trace + (size_t)k::mega_ctas() * r.phase0 * 4 : nullptr;
-            st.run = [dev, nph, r, gbar, err, tr](cudaStream_t stream) {
-                k::mega_step(dev, nph, r.qtype, 1, r.kmax, r.attn_d, gbar, err, tr, stream);
-            };
-            cs.steps.push_back(std::move(st));
-            i = r.end;
-            continue;
-        }
-        PlanStep &ps = psteps[i++];
+    plan.steps.clear();
+    for (PlanStep &ps : psteps) {
         Step st;
         st.kind = ps.kind;
         st.node = ps.node;
@@ -841,15 +720,16 @@ void Planner::finish() {
         auto fn = std::move(ps.fn);
         auto tds = std::move(ps.tds);
         st.run = [fn, tds](cudaStream_t stream) { fn(stream, tds); };
-        cs.steps.push_back(std::move(st));
+        plan.steps.push_back(std::move(st));
     }
 }
 
-void plan_call_site(Model &m, CallSite &cs, const DriverOp &d) {
-    const StageSpec &s = *cs.stage;
+void plan_call_site(Model &m, const CallSite &site, SitePlan &plan) {
+    const StageSpec &s = *site.stage;
+    const DriverStep &d = *site.step;
     if (d.args.size() != s.params.size() || d.out.size() != s.outputs.size())
         throw std::runtime_error("call to stage '" + s.name + "' has the wrong number of arguments or results");
-    Planner p(m, cs, d);
+    Planner p(m, plan, site);
     for (size_t i = 0; i < s.params.size(); i++) {
         auto it = m.values.find(d.args[i]);
         if (it == m.values.end()) throw std::runtime_error("driver value '" + d.args[i] + "' is not declared");
@@ -927,8 +807,6 @@ void plan_call_site(Model &m, CallSite &cs, const DriverOp &d) {
         p.env[n.id] = t;
     }
     p.finish();
-    cs.stale = false;
-    cs.graph_ok = false;
 }
 
 }  // namespace gcb

@@ -556,13 +556,6 @@ __global__ void fill_kernel(float *out, int64_t n, float v) {
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) out[t] = v;
 }
 
-// Loop masks: element j of every row is 0 where (j % row_len) <= pos, -inf elsewhere.
-__global__ void causal_mask_kernel(float *out, int64_t n, int64_t row_len, const int32_t *pos) {
-    const int64_t p = *pos;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x)
-        out[t] = (t % row_len) <= p ? 0.0f : -__int_as_float(0x7f800000);
-}
-
 }  // namespace
 
 void repack_quant(Type t, const uint8_t *raw, int64_t nrows, int64_t K, char *dst, cudaStream_t s) {
@@ -710,11 +703,6 @@ void fill_f32(float *dst, int64_t n, float v, cudaStream_t s) {
     check_launch("fill");
 }
 
-void causal_mask_row(float *dst, int64_t n_total, int64_t row_len, const int32_t *pos, cudaStream_t s) {
-    if (n_total <= 0) return;
-    causal_mask_kernel<<<blocks_for(n_total, 256), 256, 0, s>>>(dst, n_total, row_len, pos);
-    check_launch("causal_mask");
-}
 
 }  // namespace k
 }  // namespace gcb

@@ -119,6 +119,12 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
         for (int i = threadIdx.x; !live && i < (int)G * CH; i += blockDim.x) live = (i % CH) < n && ms[i] != ninf;
         live = __syncthreads_or(live);
         if (iq == iq0 && rows_contig && !__syncthreads_and(mbar_wait(&bar, 0))) {  // every thread leaves together
+            // the error word, and NaN in the output rows of this CTA's heads (this chunk's partials
+            // never arrive, so nothing else writes them): a caller that cannot read the error word
+            // (the allocation-free entry point) still sees the failure
+            for (int64_t r = iq0; r < iq1; r++)
+                for (int64_t i = threadIdx.x; i < G * a.D; i += blockDim.x)
+                    a.out[a.D * (hk * G + i / a.D + a.oH * (r + a.Sq * b)) + i % a.D] = __int_as_float(0x7fc00000);
             if (threadIdx.x == 0 && a.err) atomicExch(a.err, 2);
             return;
         }

@@ -102,6 +102,17 @@ __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) 
     }
     __syncthreads();
     auto valid = [&](int rh) { return pvalid[rh] != 0; };
+    // After a timed-out wait: the error word, and NaN in every output row of this CTA, so that a
+    // caller that cannot read the error word (the allocation-free entry point) still sees it.
+    auto give_up = [&]() {
+        for (int i = tid; i < PF_RH * D; i += PF_NT) {
+            const int rh = i / D;
+            if (!valid(rh)) continue;
+            const int64_t iq = row0 + rh / G, h = hk * G + rh % G;
+            a.out[(int64_t)D * (h + a.oH * (iq + a.Sq * b)) + i % D] = __int_as_float(0x7fc00000);
+        }
+        if (tid == 0 && a.err) atomicExch(a.err, 2);
+    };
 
     pdl_wait();  // q and the K/V cache rows of this call were written by earlier kernels
     if (tid == 0) {
@@ -285,7 +296,7 @@ __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) 
         __syncthreads();  // Kt and Ms are rewritten by the next chunk
     }
     if (!ok) {
-        if (tid == 0 && a.err) atomicExch(a.err, 2);
+        give_up();
         return;
     }
     if (tid < PF_RH) {
@@ -378,7 +389,7 @@ __global__ void __launch_bounds__(PF_NT, 1) flash_prefill_kernel(PrefillArgs a) 
         __syncthreads();  // Kt, Vs, Ms and Ps are rewritten by the next chunk
     }
     if (!ok) {
-        if (tid == 0 && a.err) atomicExch(a.err, 2);
+        give_up();
         return;
     }
 #pragma unroll

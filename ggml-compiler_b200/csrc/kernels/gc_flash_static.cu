@@ -14,9 +14,10 @@
 //                            written before they are read, no initial value needed
 //   [4 MiB, 4 MiB + 16 KiB)  up to 4096 arrival counters, one per (query row, K/V head): these must be
 //                            zero when a launch starts; each call zeroes them on its stream first
-//   [4 MiB + 16 KiB, +256 B) the error word the kernel sets when a bounded wait expires (2 s): the
-//                            call's output is then undefined; the call zeroes it first and does not
-//                            read it back
+//   [4 MiB + 16 KiB, +256 B) the error word the kernel sets when a bounded wait expires (2 s); the
+//                            call zeroes it first and does not read it back (that would synchronise):
+//                            the kernel also writes NaN into the output rows it could not compute,
+//                            which is how a caller sees the failure
 // The first call on each device does the set-up: with that device current it looks up the array's
 // device address (cudaGetSymbolAddress), which also makes the driver load the library's device
 // code there if it has not yet; make that first call before any stream capture on that device.
@@ -117,8 +118,11 @@ extern "C" GGML_COMPILER_API int ggml_compiler_b200_flash_attn_static(const floa
         for (int i = 0; i < 4; i++) to.ne[i] = one[i];
         gcb::set_contiguous(to);
 
-        const size_t part = gcb::k::flash_split_scratch_bytes(tq, tk);
-        const size_t ncnt = gcb::k::flash_split_counters(tq, tk);
+        // calls the prefill kernel takes (16+ query rows, head size 64 or 128) merge inside each CTA
+        // and use no partials or counters; the limits bind the split kernel's calls only
+        const bool in_cta = gcb::k::flash_prefill_ok(tq, tk, tv, to);
+        const size_t part = in_cta ? 0 : gcb::k::flash_split_scratch_bytes(tq, tk);
+        const size_t ncnt = in_cta ? 0 : gcb::k::flash_split_counters(tq, tk);
         if (part > kPartBytes)
             throw std::runtime_error("flash_attn_static: n_q " + std::to_string(n_q) + ", n_head " + std::to_string(n_head) +
                                      ", n_kv " + std::to_string(n_kv) + " need " + mib(part) +

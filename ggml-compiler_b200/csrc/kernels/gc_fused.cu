@@ -24,7 +24,7 @@ constexpr int MAXNS = 16;
 constexpr int CG = 2;  // row groups per chunk with one activation row (gc_gemv_dev.cuh)
 
 template <int QT, int NR, int M>
-__global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, GemvGeo G, int log2ns, int slot_bytes) {
+__global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, GemvGeo G, int ns, uint32_t magic, int slot_bytes) {
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t *full = (uint64_t *)smem;
     uint64_t *empty = full + MAXNS;
@@ -33,11 +33,11 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
     float *sdf = (float *)(sq + (size_t)M * a.K);
     int *ss8 = (int *)(sdf + (size_t)M * G.nb);
     unsigned char *slots = (unsigned char *)(red + 256) + gemv_act_bytes(M, a.K);
-    const Ring R{full, empty, slots, log2ns, slot_bytes};
+    const Ring R{full, empty, slots, (uint32_t)ns, magic, slot_bytes};
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < (1 << log2ns); s++) {
+        for (int s = 0; s < ns; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], NCW);
         }
@@ -79,10 +79,10 @@ void launch_t(const FusedArgs &a, const GemvGeo &G, cudaStream_t s, bool pdl) {
     }
     const int slot_bytes = (int)qw_piece_bytes(G.nb, G.cb, 0);
     const size_t head = (size_t)(2 * MAXNS) * 8 + 256 * 8 + gemv_act_bytes(M, a.K);
-    const size_t budget = g_smem_budget ? g_smem_budget : 110 * 1024;
-    int log2ns = ring_log2(budget, head, (size_t)slot_bytes, MAXNS);
-    while ((1 << log2ns) < 2 * G.pieces) log2ns++;  // room for one group's pieces in flight and one consumed
-    const size_t smem = head + ((size_t)1 << log2ns) * (size_t)slot_bytes;
+    const size_t budget = g_smem_budget ? g_smem_budget : (g_ctas_per_sm == 2 ? 113 * 1024 : 224 * 1024);
+    int ns = ring_slots(budget, head, (size_t)slot_bytes, MAXNS);
+    if (ns < 2 * G.pieces) ns = 2 * G.pieces;  // room for one group's pieces in flight and one consumed
+    const size_t smem = head + (size_t)ns * (size_t)slot_bytes;
     const int per_sm = smem <= 113 * 1024 ? g_ctas_per_sm : 1;
     const int64_t cap = (int64_t)g_num_sms * per_sm;
     const int64_t ctas = G.groups < cap ? (int64_t)G.groups : cap;
@@ -96,7 +96,7 @@ void launch_t(const FusedArgs &a, const GemvGeo &G, cudaStream_t s, bool pdl) {
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, G, log2ns, slot_bytes);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, G, ns, ring_magic((uint32_t)ns), slot_bytes);
     if (e != cudaSuccess) throw std::runtime_error(std::string("CUDA launch of gemv_tma failed: ") + cudaGetErrorString(e));
 }
 

@@ -102,15 +102,21 @@ __device__ __forceinline__ const char *gemv_piece(const FusedArgs &a, const Gemv
     return a.wc[m] + qw_piece_off(G.nb, G.cb, t, s);
 }
 
+// Piece t lives in slot t mod ns; its fill is phase floor(t / ns) of that slot's barriers. The
+// quotient comes from a multiply-high by magic = ceil(2^32 / ns), exact for t < 2^32 / ns (a CTA
+// streams far fewer pieces in one launch), so any slot count fits the shared-memory budget.
 struct Ring {
     uint64_t *full, *empty;
     unsigned char *slots;
-    int log2ns;  // slots = 1 << log2ns
+    uint32_t ns, magic;
     int slot_bytes;
-    __device__ __forceinline__ int slot(uint32_t t) const { return (int)(t & ((1u << log2ns) - 1)); }
-    __device__ __forceinline__ uint32_t parity(uint32_t t) const { return (t >> log2ns) & 1u; }
+    __device__ __forceinline__ uint32_t round(uint32_t t) const { return __umulhi(t, magic); }
+    __device__ __forceinline__ int slot(uint32_t t) const { return (int)(t - round(t) * ns); }
+    __device__ __forceinline__ uint32_t parity(uint32_t t) const { return round(t) & 1u; }
     __device__ __forceinline__ unsigned char *data(uint32_t t) const { return slots + (size_t)slot(t) * slot_bytes; }
 };
+
+__host__ inline uint32_t ring_magic(uint32_t ns) { return (uint32_t)((((uint64_t)1 << 32) + ns - 1) / ns); }
 
 // Producer: put this CTA's pieces of one GEMV into the ring, continuing the piece count `t`.
 // Returns false if a slot was never released (bounded wait).
@@ -125,7 +131,7 @@ __device__ inline bool produce_gemv(const FusedArgs &a, const GemvGeo &G, const 
             for (int gl = c0; gl < c1; gl++)
                 for (int r = 0; r < G.pieces; r++, t++) {
                     const int slot = R.slot(t);
-                    if ((t >> R.log2ns) && !mbar_wait(&R.empty[slot], R.parity(t) ^ 1u)) return false;
+                    if (t >= R.ns && !mbar_wait(&R.empty[slot], R.parity(t) ^ 1u)) return false;
                     mbar_expect_tx(&R.full[slot], pb);
                     int mat, tile;
                     const char *src = gemv_piece(a, G, cta + gl * nctas, r, s, &mat, &tile);
@@ -152,7 +158,7 @@ __device__ inline void prefetch_next(const FusedArgs &a, int cta, int nctas) {
 
 // Drain after a failed wait: the copies still in flight into the ring land before the CTA exits.
 __device__ inline void drain_ring(const Ring &R, uint32_t t) {
-    const uint32_t ns = 1u << R.log2ns;
+    const uint32_t ns = R.ns;
     for (uint32_t u = t > ns ? t - ns : 0; u < t; u++) mbar_wait(&R.full[R.slot(u)], R.parity(u), 100000000ull);
 }
 
@@ -611,11 +617,10 @@ __host__ __device__ inline size_t gemv_act_bytes(int M, int64_t K) {
     return ((size_t)M * (size_t)K + (size_t)M * (size_t)(K / 32) * 8 + 127) / 128 * 128;
 }
 
-// Ring slots for a shared-memory budget: the largest power of two that fits, at most `maxns`.
-__host__ inline int ring_log2(size_t budget, size_t head, size_t slot_bytes, int maxns) {
-    int l = 0;
-    while ((2 << l) <= maxns && head + ((size_t)2 << l) * slot_bytes <= budget) l++;
-    return l;
+// Ring slots for a shared-memory budget: as many as fit, at most `maxns`.
+__host__ inline int ring_slots(size_t budget, size_t head, size_t slot_bytes, int maxns) {
+    int n = budget > head ? (int)((budget - head) / slot_bytes) : 0;
+    return n < maxns ? n : maxns;
 }
 
 }  // namespace k

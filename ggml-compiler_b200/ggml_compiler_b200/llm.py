@@ -352,10 +352,12 @@ def normal_weights(shape: tuple[int, ...], seed: int, index: int, std: float = 0
 
 
 def build_llama_gguf(path: str | Path, sh: LlamaShape, seed: int = 0,
-                     encoder: Callable[[np.ndarray, str], np.ndarray] | None = None) -> dict[str, Any]:
-    """Write a seeded synthetic Llama-shaped model as a ggml-compiler GGUF; returns its metadata.
-    `encoder(w, type)` encodes the quantized matrices (default: this library's `runtime.encode`;
-    any bit-exact Q4_0 / Q8_0 encoder writes the same bytes)."""
+                     encoder: Callable[[np.ndarray, str], np.ndarray] | None = None,
+                     weights: dict[str, np.ndarray] | None = None) -> dict[str, Any]:
+    """Write a Llama-shaped model as a ggml-compiler GGUF; returns its metadata. The weights are
+    `weights` (f32 arrays by Hugging Face name, e.g. a LlamaForCausalLM's state dict) or, without
+    it, seeded synthetic ones. `encoder(w, type)` encodes the quantized matrices (default: this
+    library's `runtime.encode`; any bit-exact Q4_0 / Q8_0 encoder writes the same bytes)."""
     if encoder is None:
         from .runtime import encode as encoder
     program, meta = llama_program(sh)
@@ -365,9 +367,12 @@ def build_llama_gguf(path: str | Path, sh: LlamaShape, seed: int = 0,
         names[gname] = hf
 
         def data(shape=shape, typ=typ, idx=idx, hf=hf) -> np.ndarray:
-            if hf.endswith("norm.weight"):
+            if weights is not None:
+                w = np.ascontiguousarray(weights[hf], np.float32).reshape(shape)
+            elif hf.endswith("norm.weight"):
                 return np.ones(shape, np.float32)
-            w = normal_weights(shape, seed, idx)
+            else:
+                w = normal_weights(shape, seed, idx)
             if typ == "f32":
                 return w
             if typ == "f16":

@@ -71,6 +71,8 @@ def _prototypes() -> dict[str, tuple[Any, list[Any]]]:
         "b200_n_kernel_stats": (i32, [vp]),
         "b200_kernel_stats": (i32, [vp, i32, P(s), P(C.c_double), P(i32), P(C.c_double)]),
         "b200_tp_init": (i32, [vp, i32, i32, sz, vp, sz]), "b200_tp_connect": (i32, [vp, vp, sz]),
+        "b200_value_bytes": (i64, [vp, s]), "b200_read_value": (i32, [vp, s, vp, sz]),
+        "b200_write_value": (i32, [vp, s, vp, sz]),
     }
     return {"ggml_compiler_" + k: v for k, v in proto.items()}
 
@@ -291,6 +293,17 @@ class Model:
             _call("b200_kernel_stats", self.handle, k, C.byref(name), C.byref(ms), C.byref(n), C.byref(b))
             table[name.value.decode()] = {"ms": ms.value, "launches": n.value, "bytes": b.value}
         return table
+
+    def read_value(self, name: str) -> np.ndarray:
+        """The whole device storage of value `name` (a KV cache, for one) as bytes."""
+        out = np.empty(int(_call("b200_value_bytes", self.handle, name.encode())), np.uint8)
+        _call("b200_read_value", self.handle, name.encode(), out.ctypes.data, out.nbytes)
+        return out
+
+    def write_value(self, name: str, data: np.ndarray) -> None:
+        """Overwrites the whole device storage of value `name` with `data`'s bytes."""
+        a = np.ascontiguousarray(data)
+        _call("b200_write_value", self.handle, name.encode(), a.ctypes.data, a.nbytes)
 
     def join_tensor_parallel(self, rank: int, world: int, all_gather: Callable[[bytes], list[bytes]],
                              window_bytes: int = 0) -> None:

@@ -29,6 +29,16 @@ GGML_COMPILER_API int ggml_compiler_b200_n_kernel_stats(const ggml_compiler_mode
 GGML_COMPILER_API int ggml_compiler_b200_kernel_stats(const ggml_compiler_model * m, int i, const char ** kind,
                                                       double * ms, int * launches, double * bytes);
 
+/* Snapshots of driver values, typically state values such as a KV cache: the whole storage of
+   value `name` (sized for the value's largest binding, ggml_compiler_b200_value_bytes) copied to or
+   from host memory, after the model's queued work. nbytes must equal that size. Saving and
+   restoring a sequence's cache, or handing a cache to another process, uses these. No counterpart
+   in the reference, whose state is reachable only through reset (ggml_compiler_rt.h:152-153). */
+GGML_COMPILER_API int64_t ggml_compiler_b200_value_bytes(const ggml_compiler_model * m, const char * name);
+GGML_COMPILER_API int ggml_compiler_b200_read_value(ggml_compiler_model * m, const char * name, void * dst, size_t nbytes);
+GGML_COMPILER_API int ggml_compiler_b200_write_value(ggml_compiler_model * m, const char * name, const void * src,
+                                                     size_t nbytes);
+
 /* Tensor parallelism over NVLink peer memory. No counterpart in the reference, which runs on one
    device (ggml_compiler_rt.h:57-62, options.device). Processes 0 .. world-1 (2..8), one GPU each,
    load the same program. Each calls tp_init before its first run; it exports this rank's exchange
@@ -56,9 +66,13 @@ GGML_COMPILER_API int ggml_compiler_b200_tp_connect(ggml_compiler_model * m, con
      mask  f16 [n_q][n_kv], added to the scaled scores, the same for every head; NULL for none
      out   f32 [n_q][n_head][head_dim]                  (ggml ne {head_dim, n_head, n_q, 1})
    head_dim a multiple of 32 up to 256, n_head a multiple of n_head_kv, kv_head_stride >= n_kv.
-   Limit: the chunk partials of one launch (n_q x n_head x ceil(n_kv / 64) x (head_dim + 2) floats,
-   with n_q capped where 64 MiB would be exceeded) must fit 4 MiB, and n_q x n_head_kv must be at most
-   4096; larger calls are rejected (-1, ggml_compiler_last_error()).
+   Limit: a call that the per-chunk kernel runs (fewer than 16 query rows, or a head_dim other than
+   64 and 128) needs n_q x n_head x ceil(n_kv / 64) x (head_dim + 2) x 4 bytes <= 4 MiB of chunk
+   partials and n_q x n_head_kv <= 4096 arrival counters; larger calls are rejected (-1,
+   ggml_compiler_last_error()). Calls of 16+ rows with head_dim 64 or 128 merge inside each CTA and
+   need no scratch, so no size limit applies to them.
+   A bounded wait in the kernel that expires (2 s) leaves NaN in the output rows it could not
+   compute: check the output for NaN to detect it.
    Asynchronous on `stream` (a cudaStream_t; NULL: the legacy default stream) of the current device.
    The arrival counters in the scratch must be zero when the kernel starts: each call zeroes them on
    `stream` first. The first call on a device does the set-up (looks up the scratch's device address);

@@ -105,6 +105,9 @@ class Program:
         self.entries = {e["name"]: e for e in self.prog["entries"]}
         self.calls: dict[str, int] = {}
         self._rope_cache: dict[tuple, np.ndarray] = {}
+        # (stage, node id) pairs whose values the next stage runs record in `taps` (copies)
+        self.tap_ids: set[tuple[str, str]] = set()
+        self.taps: dict[tuple[str, str], np.ndarray] = {}
 
     # -- values ---------------------------------------------------------------------------------
     def _max_elems(self, v: dict[str, Any]) -> int:
@@ -339,6 +342,8 @@ class Program:
             env[prm["name"]] = self.value(arg)
         for n in st["nodes"]:
             env[n["id"]] = self._node(n, [self._src(x, env) for x in n["src"]])
+            if (st["name"], n["id"]) in self.tap_ids:
+                self.taps[(st["name"], n["id"])] = np.array(env[n["id"]], copy=True)
         results = [env[o] for o in st["outputs"]]
         for res, out in zip(results, call["out"]):
             dst = self.value(out)

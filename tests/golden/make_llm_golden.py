@@ -13,6 +13,10 @@ reference checkout; the GPU tests only read the files this writes).
    per-model oracle (tests/unit/test_llm.py:81-145).
 3. ref_program_gqa2.json: the program the reference writes for a 2-layer GQA Llama (config in the
    file), to pin this repository's Llama program emitter node for node.
+4. ref_program_config1.json: the same for BASELINE config 1's shape (4 layers, d_model 512, 8/8
+   heads, FFN 1408, vocab 32000, Q8_0 projections and head). The GGUF itself (f32 embeddings,
+   65 MB) is not kept: the tests rebuild it from the same seeded transformers model with this
+   repository's writer, whose program this file pins.
 
     GGML_COMPILER_RT=ggml-compiler_b200/ggml_compiler_b200/lib/libggml_compiler_rt.so \
         python tests/golden/make_llm_golden.py REFERENCE_CHECKOUT
@@ -31,6 +35,11 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
+
+
+# tiny Llama-architecture decoder (the EOS id is transformers' Llama default)
+CONFIG1 = dict(vocab_size=32000, hidden_size=512, intermediate_size=1408, num_hidden_layers=4, num_attention_heads=8,
+               num_key_value_heads=8, eos_token_id=2, rope_theta=10000.0, rms_norm_eps=1e-5)
 
 
 def _program(gguf_path: str) -> tuple[dict, dict]:
@@ -103,6 +112,23 @@ def main(ref_root: str) -> None:
                 n.pop("scope", None)
         (HERE / "ref_program_gqa2.json").write_text(json.dumps(
             {"config": {**cfg2, "max_context": 1024, "max_prompt": 32, "weights": "q4_0"}, "meta": meta,
+             "program": prog}, separators=(",", ":")))
+
+        # 4: BASELINE config 1's shape
+        cfg1 = CONFIG1
+        torch.manual_seed(0)
+        m1 = transformers.LlamaForCausalLM(transformers.LlamaConfig(**cfg1)).float().eval()
+        m1.config._attn_implementation = "eager"
+        pol1 = DTypePolicy(rules=[("*_proj.weight", "q8_0"), ("lm_head.weight", "q8_0")], float="f32", fallback=[])
+        art1 = ggml_compiler.compile(ggml_compiler.causal_lm(m1, max_context=768, max_prompt=64), opt="O3",
+                                     out_dir=tmp / "config1", dtype_policy=pol1)
+        prog, meta = _program(art1.gguf)
+        for s in prog["stages"]:
+            for n in s["nodes"]:
+                n.pop("loc", None)
+                n.pop("scope", None)
+        (HERE / "ref_program_config1.json").write_text(json.dumps(
+            {"config": {**cfg1, "max_context": 768, "max_prompt": 64, "weights": "q8_0"}, "meta": meta,
              "program": prog}, separators=(",", ":")))
     finally:
         shutil.rmtree(tmp, ignore_errors=True)

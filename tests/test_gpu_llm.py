@@ -26,21 +26,21 @@ def golden():
     return np.load(GOLDEN / "ref_llama_q8_0.npz")
 
 
-@pytest.fixture(scope="module", params=["decode_kernel", "per_group"])
+@pytest.fixture(scope="module", params=["device_loops", "host_loops"])
 def sess(gpu, request):
-    """Every test runs twice: decode steps as one persistent kernel (GGML_COMPILER_B200_DECODE_KERNEL=1,
-    read when a session loads), and with one launch per fused group (=0)."""
+    """Every test runs twice: loops run on the device as conditional CUDA graphs, and iteration by
+    iteration from the host (GGML_COMPILER_B200_DEVICE_LOOPS=0, read when a model loads)."""
     import os
 
-    old = os.environ.get("GGML_COMPILER_B200_DECODE_KERNEL")
-    os.environ["GGML_COMPILER_B200_DECODE_KERNEL"] = "1" if request.param == "decode_kernel" else "0"
+    old = os.environ.get("GGML_COMPILER_B200_DEVICE_LOOPS")
+    os.environ["GGML_COMPILER_B200_DEVICE_LOOPS"] = "1" if request.param == "device_loops" else "0"
     try:
         s = Model(GGUF)
     finally:
         if old is None:
-            del os.environ["GGML_COMPILER_B200_DECODE_KERNEL"]
+            del os.environ["GGML_COMPILER_B200_DEVICE_LOOPS"]
         else:
-            os.environ["GGML_COMPILER_B200_DECODE_KERNEL"] = old
+            os.environ["GGML_COMPILER_B200_DEVICE_LOOPS"] = old
     s.mode = request.param
     yield s
     s.close()
@@ -69,8 +69,9 @@ def test_logits_bit_exact_vs_oracle(sess, golden):
 
 
 def test_decode_launches(sess):
-    """A decode step is the hoisted mask conversion, the embedding row, one decode-kernel launch
-    over every layer and the output head, then argmax: or one launch per fused group."""
+    """A decode step is the hoisted mask conversion, the embedding row, one launch per fused group
+    (norm + QKV + RoPE + KV write, attention, o + residual, norm + gate/up + SwiGLU, down +
+    residual) and the output head, then argmax."""
     g = Decoder(sess)
     g.restart()
     g.prompt([1, 2, 3])
@@ -80,14 +81,26 @@ def test_decode_launches(sess):
         ks = sess.kernel_table()
     finally:
         sess.profile(False)
-    if sess.mode == "decode_kernel":
-        assert ks["decode_q8_0"]["launches"] == 1
-        assert not any(k.startswith("gemv") or k == "flash_attn" for k in ks), ks
-    else:
-        assert "decode_q8_0" not in ks
-        assert ks["gemv_q8_0_qkv"]["launches"] == ks["flash_attn"]["launches"] == ks["gemv_q8_0_glu"]["launches"]
+    assert ks["gemv_q8_0_qkv"]["launches"] == ks["flash_attn"]["launches"] == ks["gemv_q8_0_glu"]["launches"]
     # the per-layer mask conversion is planned once
     assert ks.get("unary", {"launches": 0})["launches"] <= 1 and ks.get("copy", {"launches": 0})["launches"] <= 2
+
+
+def test_generate_counts_and_stops(sess):
+    """The generate entry's loop: the iterations run (its stage calls) and the collected tokens
+    match the host loop's; with a stop id the loop ends on it and later rows stay zero."""
+    prompt = [3, 1, 4, 1, 5, 9, 2, 6]
+    g = Decoder(sess)
+    host = g.greedy(prompt, 40, stop=[])
+    g.restart()
+    first = int(np.argmax(g.prompt(prompt)))
+    sess.bind(max_new=39)
+    out = sess.entries["generate"](first=np.array([[first]], np.int32), start=np.array([g.ctx], np.int32))
+    gen = out["generated"].ravel()
+    n = sess.stage_calls()["decode_greedy"]
+    assert [first] + gen[:n].tolist() == host[:n + 1]
+    if n < 39:  # stopped at the model's EOS id: the token is collected, the rest stays zero
+        assert gen[n - 1] == 7 and not gen[n:].any()
 
 
 def test_logits_vs_transformers(sess, golden):

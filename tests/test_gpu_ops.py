@@ -1,5 +1,5 @@
-"""Isolated quantized mul_mat on the B200 against the CPU oracle (BASELINE config 2's op sweep at
-sizes the oracle finishes in seconds): single-stage programs through the C ABI, as the reference's
+"""Isolated quantized mul_mat on the B200 against the CPU oracle (BASELINE config 2's op sweep, every
+shape, M up to 2048): single-stage programs through the C ABI, as the reference's
 op tests run them (tests/unit/test_runtime_ops.py:86-102). The backend follows the oracle's reduction
 order, so results are compared bit for bit."""
 
@@ -24,12 +24,16 @@ def run_mm(tmp_path, w, wtype, x):
         return m.entries["main"](x=x[None])["out.0"].reshape(x.shape[0], w.shape[0])
 
 
+# the three weight shapes at M = 1, 8, 64, 512 (and 2048 on the square one),
+# plus small and ragged shapes (a row of 1000 tiles' worth, K not a multiple of the 128-block segment)
+SWEEP = ([(4096, 4096, m) for m in (1, 8, 64, 512, 2048)] + [(14336, 4096, m) for m in (1, 8, 64, 512)] +
+         [(4096, 14336, m) for m in (1, 8, 64, 512)] + [(256, 512, m) for m in (1, 8, 64)] +
+         [(1000, 14336, m) for m in (1, 9, 64)])
+
+
 @pytest.mark.parametrize("wtype", ["q4_0", "q8_0"])
-@pytest.mark.parametrize("N,K", [(256, 512), (4096, 4096), (1000, 14336)])
-@pytest.mark.parametrize("M", [1, 8, 64])
+@pytest.mark.parametrize("N,K,M", SWEEP)
 def test_quant_mul_mat_bit_exact(gpu, tmp_path, wtype, N, K, M):
-    if N * K * M > 4096 * 4096 * 8:
-        pytest.skip("oracle time")
     w = weights((N, K))
     x = np.random.default_rng(1).standard_normal((M, K), dtype=np.float32)
     got = run_mm(tmp_path, w, wtype, x)

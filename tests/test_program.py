@@ -32,6 +32,16 @@ def test_emitter_matches_reference_program():
     assert prog == g["program"]
 
 
+def test_emitter_matches_reference_config1_program():
+    """BASELINE config 1's shape, as the reference compiler wrote it (tests/golden/make_llm_golden.py)."""
+    from llm_models import config1, config1_shape
+
+    g = config1()
+    prog, meta = llama_program(config1_shape())
+    assert meta == g["meta"]
+    assert prog == g["program"]
+
+
 def test_emitter_matches_reference_fixture_gguf():
     import gguf
 
