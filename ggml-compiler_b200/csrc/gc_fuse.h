@@ -49,6 +49,15 @@ struct Planner {
     std::vector<PlanStep> psteps;
     int cur = 0;
     std::set<int> head_sharded;  // tensor parallel: storages holding only this rank's query heads
+    // GGML_COMPILER_B200_TRACE: launches that record per-CTA stamps, and where (filled by finish)
+    struct TraceReq {
+        const char *kind;
+        std::string node;
+        size_t ctas;
+        std::shared_ptr<uint64_t *> slot;
+    };
+    std::vector<TraceReq> traces;
+    std::shared_ptr<uint64_t *> trace_slot(const char *kind, const std::string &node, size_t ctas);
 
     TD alloc(Type t, const int64_t *ne);          // a fresh arena tensor written at `cur`
     void *scratch_marker(size_t bytes, TD *out);  // scratch arena space for the launch at `cur`

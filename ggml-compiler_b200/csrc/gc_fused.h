@@ -54,9 +54,14 @@ struct FusedArgs {
     const char *pf[3] = {nullptr, nullptr, nullptr};
     int64_t pf_bytes[3] = {0, 0, 0};
     int stream_evict_first = 0;  // stream this launch's weights under an L2 evict-first policy
+    // GGML_COMPILER_B200_TRACE: %globaltimer stamps per CTA, [CTA][8] (k::kTraceSlots): producer
+    // start, producer done issuing, consumers past the dependent-launch wait, prologue done,
+    // consumers done (epilogue included). Null: no stamps.
+    uint64_t *trace = nullptr;
 };
 
 namespace k {
+int num_sms();  // of the current device
 bool fused_gemv_supported(int64_t K, int64_t M, int map);
 // Shape preconditions of one set of arguments (the rope map needs head sizes that are multiples of 16).
 bool fused_gemv_args_ok(const FusedArgs &a);

@@ -134,7 +134,8 @@ bool flash_split_ok(const TD &q);
 size_t flash_split_scratch_bytes(const TD &q, const TD &k);
 size_t flash_split_counters(const TD &q, const TD &k);
 void flash_attn_split(const TD &q, const TD &k, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
-                      int *counters, int *err, cudaStream_t s);
+                      int *counters, int *err, cudaStream_t s, uint64_t *trace = nullptr);
+size_t flash_split_ctas(const TD &q, const TD &k);  // CTAs of one split launch (trace slots)
 // The same result for prefill calls (16+ query rows, head size 64 or 128, K/V rows contiguous):
 // one CTA per 64 (row, head) pairs over every chunk, merge in the CTA (gc_flash_prefill.cu).
 bool flash_prefill_ok(const TD &q, const TD &k, const TD &v, const TD &out);

@@ -115,6 +115,7 @@ void Model::load(const char *path, int backend, int dev, bool allow_cpu_fallback
     if (const char *p = std::getenv("GGML_COMPILER_PROFILE")) profile_path = p;
     if (const char *g = std::getenv("GGML_COMPILER_B200_GRAPHS")) use_graphs = std::atoi(g) != 0;
     if (const char *g = std::getenv("GGML_COMPILER_B200_DEVICE_LOOPS")) use_device_loops = std::atoi(g) != 0;
+    if (const char *p = std::getenv("GGML_COMPILER_B200_TRACE")) trace_path = p;
     if (const char *g = std::getenv("GCB_L2_PREFETCH_MB")) l2_prefetch_bytes = (int64_t)(std::atof(g) * (1 << 20));
     if (const char *g = std::getenv("GCB_STREAM_EVICT_FIRST")) stream_evict_first = std::atoi(g) != 0;
 
@@ -717,6 +718,7 @@ void Model::run_entry(const std::string &name) {
                                      "(results are invalid)");
         throw std::runtime_error("entry '" + name + "': a set_rows index was outside its destination (row skipped)");
     }
+    if (!trace_path.empty()) write_trace();
     if (!profile_path.empty() && !profile_lines.empty()) {
         if (FILE *f = std::fopen(profile_path.c_str(), "a")) {
             for (const auto &l : profile_lines) std::fprintf(f, "%s\n", l.c_str());
@@ -724,6 +726,42 @@ void Model::run_entry(const std::string &name) {
         }
         profile_lines.clear();
     }
+}
+
+// One line per CTA of every traced launch of every current plan, in plan order: stage, launch
+// index, kind, node, CTA, then the stamps in ns relative to the earliest stamp of the file (-1:
+// not recorded). A plan's stamps are those of its latest launch (a loop's last iteration).
+void Model::write_trace() {
+    FILE *f = std::fopen(trace_path.c_str(), "w");
+    if (!f) return;
+    std::vector<std::pair<const CallSite *, std::vector<uint64_t>>> all;
+    uint64_t t0 = ~0ull;
+    for (const auto &c : calls)
+        for (const auto &p : c.plans) {
+            if (!p->trace.size()) continue;
+            std::vector<uint64_t> h(p->trace.size() / 8);
+            cuda_check(cudaMemcpy(h.data(), p->trace.get(), p->trace.size(), cudaMemcpyDeviceToHost), "trace");
+            for (uint64_t v : h)
+                if (v) t0 = std::min(t0, v);
+            all.emplace_back(&c, std::move(h));
+        }
+    size_t k = 0;
+    for (const auto &c : calls)
+        for (const auto &p : c.plans) {
+            if (!p->trace.size()) continue;
+            const auto &h = all[k++].second;
+            for (size_t li = 0; li < p->trace_index.size(); li++) {
+                const auto &e = p->trace_index[li];
+                for (size_t cta = 0; cta < e.ctas; cta++) {
+                    const uint64_t *st = &h[e.offset + cta * 8];
+                    if (!st[0] && !st[2]) continue;  // a CTA the launch did not have
+                    std::fprintf(f, "%s\t%zu\t%s\t%s\t%zu", c.stage->name.c_str(), li, e.kind.c_str(), e.node.c_str(), cta);
+                    for (int s = 0; s < 5; s++) std::fprintf(f, "\t%lld", st[s] ? (long long)(st[s] - t0) : -1ll);
+                    std::fprintf(f, "\n");
+                }
+            }
+        }
+    std::fclose(f);
 }
 
 void Model::reset_state() {

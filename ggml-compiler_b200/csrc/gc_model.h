@@ -55,6 +55,13 @@ struct SitePlan {
     DevBuf arena;
     cudaGraphExec_t graph = nullptr;
     uint64_t last_use = 0;
+    // GGML_COMPILER_B200_TRACE: per-CTA stamps of the traced launches, [launch][CTA][8]
+    struct TraceEntry {
+        std::string kind, node;
+        size_t offset, ctas;
+    };
+    DevBuf trace;
+    std::vector<TraceEntry> trace_index;
     SitePlan() = default;
     SitePlan(const SitePlan &) = delete;
     SitePlan &operator=(const SitePlan &) = delete;
@@ -167,6 +174,7 @@ struct Model {
     };
     std::vector<PendingTime> pending;
     std::string profile_path;  // GGML_COMPILER_PROFILE
+    std::string trace_path;    // GGML_COMPILER_B200_TRACE: per-CTA stamps of the last run's launches
     std::vector<std::string> profile_lines;
     uint64_t plan_clock = 0;  // orders plan uses (least recently used plan of a site is dropped)
     TpGroup tp;
@@ -206,6 +214,7 @@ struct Model {
     void run_call(const DriverStep &d);
     void launch_plan(SitePlan &p, int stage_index);
     void run_loop(const LoopSpec &loop);
+    void write_trace();
 };
 
 // Plans one stage call for the current binding into kernel launches (gc_plan.cpp).

@@ -133,20 +133,28 @@ void Planner::add_gemv(const char *kind, const std::string &node, std::vector<TD
         return a;
     };
     auto pf = std::make_shared<GemvPrefetch>();
+    auto tr = trace_slot(kind, node, (size_t)(2 * k::num_sms()));
     add(kind, node, std::move(tds),
-        [b2, pf](cudaStream_t st, const std::vector<TD> &t) {
+        [b2, pf, tr](cudaStream_t st, const std::vector<TD> &t) {
             FusedArgs a = b2(t);
             for (int r = 0; r < 3; r++) {
                 a.pf[r] = pf->p[r];
                 a.pf_bytes[r] = pf->n[r];
             }
             a.stream_evict_first = pf->evict_first;
+            a.trace = *tr;
             k::fused_gemv(a, st, true);
         },
         bytes);
     psteps.back().gemv = b2;
     psteps.back().pf = pf;
     if (nshard > 1 && !col.empty()) add_exchange(node, out, rows, ld, col);
+}
+
+std::shared_ptr<uint64_t *> Planner::trace_slot(const char *kind, const std::string &node, size_t ctas) {
+    auto slot = std::make_shared<uint64_t *>(nullptr);
+    if (!m.trace_path.empty()) traces.push_back({kind, node, ctas, slot});
+    return slot;
 }
 
 k::TpExchange Planner::exchange_args(int64_t rows, int64_t ld, const std::vector<int64_t> &col) const {
@@ -453,9 +461,10 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
                 scratch_marker(k::flash_split_scratch_bytes(q, kk), &scratch);
                 int *cnt = m.counters(s.name + "/" + n.id, k::flash_split_counters(q, kk));
                 int *err = m.d_err;
+                auto tr = trace_slot("flash_attn", n.id, k::flash_split_ctas(q, kk));
                 add("flash_attn", n.id, {q, kk, v, mk, y, scratch},
-                    [scale, cnt, err](cudaStream_t st, const std::vector<TD> &t) {
-                        k::flash_attn_split(t[0], t[1], t[2], &t[3], t[4], scale, t[5].data, cnt, err, st);
+                    [scale, cnt, err, tr](cudaStream_t st, const std::vector<TD> &t) {
+                        k::flash_attn_split(t[0], t[1], t[2], &t[3], t[4], scale, t[5].data, cnt, err, st, *tr);
                     },
                     bytes);
                 return y;
@@ -711,6 +720,19 @@ void Planner::finish() {
         }
     }
 
+    if (!traces.empty()) {
+        size_t words = 0;
+        for (const auto &t : traces) words += t.ctas * 8;
+        cuda_check(cudaStreamSynchronize(m.stream), "trace");
+        plan.trace.alloc(words * sizeof(uint64_t));
+        size_t off = 0;
+        plan.trace_index.clear();
+        for (auto &t : traces) {
+            *t.slot = (uint64_t *)plan.trace.get() + off;
+            plan.trace_index.push_back({t.kind, t.node, off, t.ctas});
+            off += t.ctas * 8;
+        }
+    }
     plan.steps.clear();
     for (PlanStep &ps : psteps) {
         Step st;

@@ -48,6 +48,7 @@ struct SplitArgs {
     int *counters;   // [B][Sq][Hkv], zero between launches
     int *err;
     int64_t nch;
+    uint64_t *trace;  // [CTA][8] %globaltimer stamps, or null: start, past the wait, K/V landed, done
 };
 
 template <int MAXD>
@@ -73,8 +74,12 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
     const int64_t G = a.H / a.Hkv;
     const float ninf = -__int_as_float(0x7f800000);
 
+    const int64_t cta_id = blockIdx.x + (int64_t)gridDim.x * (blockIdx.y + (int64_t)gridDim.y * blockIdx.z);
+    uint64_t *stamps = a.trace && threadIdx.x == 0 ? a.trace + cta_id * 8 : nullptr;
+    if (stamps) stamps[0] = global_ns();
     pdl_trigger();  // the next GEMV may start streaming its weights now; it waits for this grid to finish before reading
     pdl_wait();     // the KV cache row of this step was written by the previous kernel
+    if (stamps) stamps[2] = global_ns();
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         mbar_fence_init();
@@ -128,6 +133,7 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
             if (threadIdx.x == 0 && a.err) atomicExch(a.err, 2);
             return;
         }
+        if (stamps && iq == iq0) stamps[3] = global_ns();
         if (live) {
             const int nslots = (int)(blockDim.x / 32) / WPH;
             flash_chunk<WPH, MAXD>(fc, Ks, Vs, qs, ms, sc, ps, nslots, SyncCta());  // MAXD is the head size
@@ -156,6 +162,7 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
             }
         __syncthreads();  // qs / ms / sc / ps and `last` are reused by the next row
     }
+    if (stamps) stamps[4] = global_ns();
 }
 
 constexpr size_t kMaxPartBytes = 256u << 20;  // scratch for chunk partials per row group
@@ -177,8 +184,12 @@ size_t flash_split_counters(const TD &q, const TD &kk) {
     return (size_t)(q.ne[3] * std::min<int64_t>(rows_per, q.ne[1]) * kk.ne[2]);
 }
 
+size_t flash_split_ctas(const TD &q, const TD &kk) {
+    return (size_t)((kk.ne[1] + CH - 1) / CH) * (size_t)(kk.ne[2] * q.ne[3]) * (size_t)((q.ne[1] + RQ - 1) / RQ);
+}
+
 void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
-                      int *counters, int *err, cudaStream_t s) {
+                      int *counters, int *err, cudaStream_t s, uint64_t *trace) {
     if (flash_prefill_ok(q, kk, v, out)) {
         flash_prefill(q, kk, v, mask, out, scale, err, s);
         return;
@@ -218,6 +229,7 @@ void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, co
     a.part = (float *)scratch;
     a.counters = counters;
     a.err = err;
+    a.trace = trace;
     const int64_t G = a.H / a.Hkv;
     const int hslots = (int)std::min<int64_t>(G, MAXG);
     const int threads = hslots * WPH * 32;

@@ -48,11 +48,13 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
 
     if (warp == NCW) {  // producer
         if (lane != 0) return;
+        if (a.trace) a.trace[blockIdx.x * 8 + 0] = global_ns();
         uint32_t t = 0;
         if (!produce_gemv(a, G, R, t, blockIdx.x, gridDim.x, gemv_chunk(M, 1, CG))) {
             if (a.err) atomicExch(a.err, 2);
             drain_ring(R, t);
         } else {
+            if (a.trace) a.trace[blockIdx.x * 8 + 1] = global_ns();
             prefetch_next(a, blockIdx.x, gridDim.x);
         }
         return;
@@ -60,9 +62,13 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
     float4 wpre[GEMV_UB];
     gemv_norm_prefetch<NCW * 32>(a, wpre);
     pdl_wait();
+    const bool stamp = a.trace && threadIdx.x == 0;
+    if (stamp) a.trace[blockIdx.x * 8 + 2] = global_ns();
     gemv_prologue<M, NCW * 32>(a, sq, sdf, ss8, red, 1, wpre);
+    if (stamp) a.trace[blockIdx.x * 8 + 3] = global_ns();
     if (!consume_gemv<QT, NR, M, CG>(a, G, R, 0, blockIdx.x, gridDim.x, 0, 1, warp, sq, sdf, ss8))
         if (a.err) atomicExch(a.err, 2);
+    if (stamp) a.trace[blockIdx.x * 8 + 4] = global_ns();
 }
 
 int g_num_sms = 0;

@@ -81,7 +81,7 @@ class Decoder:
         else:
             res = self.model.entries["prefill"](tokens=toks, positions=where, mask=mask)["logits"]
         self.ctx += n
-        return res[0]
+        return res.reshape(-1, res.shape[-1])  # [rows, vocab]: the last row, or every row (logits="all")
 
     def prompt(self, ids: Sequence[int]) -> np.ndarray:
         """Appends `ids` to the context; the logits after the last one ([vocab])."""
@@ -89,10 +89,11 @@ class Decoder:
         for n in call_sizes(len(ids), self.meta["max_prompt"]):
             last = self._call(ids[i:i + n])
             i += n
-        return last if last.ndim == 1 else last[-1]  # a program with logits="all" returns every row
+        return last[-1]
 
     def step(self, token: int) -> np.ndarray:
-        return self._call([int(token)])
+        """Appends one token; the logits after it ([vocab])."""
+        return self._call([int(token)])[-1]
 
     def greedy(self, prompt: Sequence[int], n: int, stop: Sequence[int] | None = None,
                on_device: bool = False) -> list[int]:
