@@ -19,11 +19,19 @@ struct Storage {
     size_t offset = 0;
 };
 
-// What a fused GEMV launch prefetches into L2 for a later launch (FusedArgs::pf).
-struct GemvPrefetch {
+// Per-launch settings of a fused GEMV step that depend on the steps around it, filled once the
+// whole call site is planned: L2 prefetch of a later launch's weights (FusedArgs::pf), the
+// stream's cache policy, and the Q8_0 activation hand-off (FusedArgs::xq / act_*).
+struct GemvExtras {
     const char *p[3] = {nullptr, nullptr, nullptr};
     int64_t n[3] = {0, 0, 0};
     int evict_first = 0;
+    const char *xq = nullptr;  // non-null: the input row comes staged (PRO_Q8)
+    int act_mode = 0;
+    char *act_out = nullptr;
+    const float *act_norm_w = nullptr;
+    float act_eps = 0.0f;
+    int *act_cnt = nullptr;
 };
 
 struct PlanStep {
@@ -35,7 +43,12 @@ struct PlanStep {
     // Fused GEMV steps: their arguments from the resolved TDs, and the L2 prefetch ranges the
     // launch takes (filled once every step of the call site is planned).
     std::function<FusedArgs(const std::vector<TD> &)> gemv;
-    std::shared_ptr<GemvPrefetch> pf;
+    std::shared_ptr<GemvExtras> pf;
+    // A one-row split attention step: its output row (`attn_out`, H x D floats) and where its merge
+    // writes that row's Q8_0 blocks for the GEMV that reads it (null: nowhere).
+    std::shared_ptr<char *> attn_act;
+    const float *attn_out = nullptr;
+    int64_t attn_k = 0;
 };
 
 struct Planner {

@@ -10,7 +10,13 @@
 
 namespace gcb {
 
-enum { PRO_ACT = 0, PRO_NORM = 1 };
+// The activation prologue: quantize the f32 row(s) (PRO_ACT), rms_norm x weight first (PRO_NORM),
+// or take Q8_0 blocks a kernel before wrote in the staging layout (PRO_Q8, one row).
+enum { PRO_ACT = 0, PRO_NORM = 1, PRO_Q8 = 2 };
+// What a launch emits for the GEMV after it (one row): nothing, the rms_norm-ed output row's Q8_0
+// blocks (written by the launch's last CTA), or the output's own Q8_0 blocks (each written by the
+// CTA that stores the block's last 8-row tile).
+enum { ACT8_NONE = 0, ACT8_NORM = 1, ACT8_BLOCKS = 2 };
 enum { MAP_SINGLE = 0, MAP_ROPE_QKV = 1, MAP_SWIGLU = 2 };
 
 struct FusedArgs {
@@ -24,6 +30,17 @@ struct FusedArgs {
     int64_t K = 0;
     const float *norm_w = nullptr;  // PRO_NORM
     float eps = 0.0f;
+    // PRO_Q8: the row in the consumers' staging layout (gemv_act_bytes(1, K) bytes: int8 codes [K],
+    // f32 block scales [K / 32], int 8 x code sums [K / 32]), written by the kernel before
+    const char *xq = nullptr;
+    // ACT8_NORM / ACT8_BLOCKS: where this launch writes the next GEMV's row in that layout, the
+    // next GEMV's norm weight and eps (ACT8_NORM), and zeroed counters the launch leaves zero (one
+    // for ACT8_NORM, one per 32-row block for ACT8_BLOCKS)
+    int act_mode = ACT8_NONE;
+    char *act_out = nullptr;
+    const float *act_norm_w = nullptr;
+    float act_eps = 0.0f;
+    int *act_cnt = nullptr;
     // weights: repacked codes + fp16 scales, rows of K
     const char *wc[3] = {nullptr, nullptr, nullptr};
     const uint16_t *ws[3] = {nullptr, nullptr, nullptr};

@@ -134,8 +134,10 @@ bool flash_split_ok(const TD &q);
 size_t flash_split_scratch_bytes(const TD &q, const TD &k);
 size_t flash_split_counters(const TD &q, const TD &k);
 void flash_attn_split(const TD &q, const TD &k, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
-                      int *counters, int *err, cudaStream_t s, uint64_t *trace = nullptr);
+                      int *counters, int *err, cudaStream_t s, uint64_t *trace = nullptr, char *act_out = nullptr);
 size_t flash_split_ctas(const TD &q, const TD &k);  // CTAs of one split launch (trace slots)
+// act_out (one query row, one batch): the merged row's Q8_0 blocks in the GEMV staging layout
+// (gemv_act_bytes(1, H x D) bytes) for the GEMV that reads it (FusedArgs::PRO_Q8).
 // The same result for prefill calls (16+ query rows, head size 64 or 128, K/V rows contiguous):
 // one CTA per 64 (row, head) pairs over every chunk, merge in the CTA (gc_flash_prefill.cu).
 bool flash_prefill_ok(const TD &q, const TD &k, const TD &v, const TD &out);

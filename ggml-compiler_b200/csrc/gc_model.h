@@ -62,6 +62,7 @@ struct SitePlan {
     };
     DevBuf trace;
     std::vector<TraceEntry> trace_index;
+    DevBuf act;  // Q8_0 activation rows handed between fused steps, and their counters
     SitePlan() = default;
     SitePlan(const SitePlan &) = delete;
     SitePlan &operator=(const SitePlan &) = delete;
@@ -164,6 +165,7 @@ struct Model {
     bool use_device_loops = true;  // GGML_COMPILER_B200_DEVICE_LOOPS=0: loops checked on the host every iteration
     bool profiling = false;
     int64_t l2_prefetch_bytes = 0;   // GCB_L2_PREFETCH_MB: what each fused GEMV prefetches of the next one's weights
+    bool act_handoff = true;  // GCB_ACT_HANDOFF=0: every GEMV quantizes its own input row
     bool stream_evict_first = true;  // GCB_STREAM_EVICT_FIRST=0: GEMV weight streams without the L2 evict-first policy
     std::map<std::string, KernelStat> kstats;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> event_pool;

@@ -132,7 +132,7 @@ void Planner::add_gemv(const char *kind, const std::string &node, std::vector<TD
         a.nshard = nshard;
         return a;
     };
-    auto pf = std::make_shared<GemvPrefetch>();
+    auto pf = std::make_shared<GemvExtras>();
     auto tr = trace_slot(kind, node, (size_t)(2 * k::num_sms()));
     add(kind, node, std::move(tds),
         [b2, pf, tr](cudaStream_t st, const std::vector<TD> &t) {
@@ -143,6 +143,15 @@ void Planner::add_gemv(const char *kind, const std::string &node, std::vector<TD
             }
             a.stream_evict_first = pf->evict_first;
             a.trace = *tr;
+            if (pf->xq) {
+                a.pro = PRO_Q8;
+                a.xq = pf->xq;
+            }
+            a.act_mode = pf->act_mode;
+            a.act_out = pf->act_out;
+            a.act_norm_w = pf->act_norm_w;
+            a.act_eps = pf->act_eps;
+            a.act_cnt = pf->act_cnt;
             k::fused_gemv(a, st, true);
         },
         bytes);
@@ -462,11 +471,16 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
                 int *cnt = m.counters(s.name + "/" + n.id, k::flash_split_counters(q, kk));
                 int *err = m.d_err;
                 auto tr = trace_slot("flash_attn", n.id, k::flash_split_ctas(q, kk));
+                auto act = std::make_shared<char *>(nullptr);
                 add("flash_attn", n.id, {q, kk, v, mk, y, scratch},
-                    [scale, cnt, err, tr](cudaStream_t st, const std::vector<TD> &t) {
-                        k::flash_attn_split(t[0], t[1], t[2], &t[3], t[4], scale, t[5].data, cnt, err, st, *tr);
+                    [scale, cnt, err, tr, act](cudaStream_t st, const std::vector<TD> &t) {
+                        k::flash_attn_split(t[0], t[1], t[2], &t[3], t[4], scale, t[5].data, cnt, err, st, *tr, *act);
                     },
                     bytes);
+                if (q.ne[1] == 1 && q.ne[3] == 1) {
+                    psteps.back().attn_act = act;
+                    psteps.back().attn_k = q.ne[0] * q.ne[2];
+                }
                 return y;
             }
             add("flash_attn", n.id, {q, kk, v, mk, y},
@@ -700,8 +714,8 @@ void Planner::finish() {
     for (size_t i = 0; i < psteps.size(); i++)
         if (psteps[i].pf) gi.push_back(i);
     for (size_t x = 0; x < gi.size(); x++) {
-        GemvPrefetch &pf = *psteps[gi[x]].pf;
-        pf = GemvPrefetch{};
+        GemvExtras &pf = *psteps[gi[x]].pf;
+        pf = GemvExtras{};
         pf.evict_first = m.stream_evict_first ? 1 : 0;
         if (m.l2_prefetch_bytes <= 0 || gi.size() < 2) continue;
         const PlanStep &nx = psteps[gi[(x + 1) % gi.size()]];
@@ -717,6 +731,61 @@ void Planner::finish() {
             const int64_t take = std::min<int64_t>(tot[r], (int64_t)((double)m.l2_prefetch_bytes * (double)tot[r] / (double)sum));
             pf.p[r] = na.wc[r];
             pf.n[r] = take & ~(int64_t)255;
+        }
+    }
+
+    // Q8_0 activation hand-off (one activation row, one GPU). A fused GEMV whose input row is the
+    // whole output of the step right before it takes the row already quantized, in its staging
+    // layout (PRO_Q8), and that step writes it: a split attention step from its merge; a residual
+    // GEMV from its last CTA, with the rms_norm x weight the next GEMV applies; the SwiGLU GEMV per
+    // 32-row block. The quantization rule is the prologue's, so results do not change; the
+    // consumers' prologue shrinks to one copy into shared memory.
+    if (m.act_handoff) {
+        struct Link {
+            size_t from, to;
+            int mode;  // 0: attention merge, else an ACT8_* mode
+            int64_t K;
+        };
+        std::vector<Link> links;
+        for (size_t i = 1; i < psteps.size(); i++) {
+            const PlanStep &B = psteps[i], &A = psteps[i - 1];
+            if (!B.pf) continue;
+            const FusedArgs b = B.gemv(B.tds);
+            if (b.M != 1 || b.nshard != 1 || b.K % 32 || b.pro == PRO_Q8) continue;
+            if (A.attn_act && b.pro == PRO_ACT && (const char *)b.x == A.tds[4].data && b.K == A.attn_k) {
+                links.push_back({i - 1, i, 0, b.K});
+            } else if (A.pf) {
+                const FusedArgs a = A.gemv(A.tds);
+                if (a.M != 1 || a.nshard != 1 || (const float *)a.out != b.x || a.wrows[0] != b.K) continue;
+                if (a.map == MAP_SINGLE && b.pro == PRO_NORM) links.push_back({i - 1, i, ACT8_NORM, b.K});
+                else if (a.map == MAP_SWIGLU && b.pro == PRO_ACT) links.push_back({i - 1, i, ACT8_BLOCKS, b.K});
+            }
+        }
+        auto staged = [](int64_t K) { return (size_t)((K + K / 32 * 8 + 127) / 128 * 128); };
+        size_t bytes = 0;
+        for (const Link &l : links) bytes += staged(l.K) + (size_t)((l.K / 32 + 32) * 4 + 127) / 128 * 128;
+        if (bytes) {
+            cuda_check(cudaStreamSynchronize(m.stream), "activation hand-off");
+            plan.act.alloc(bytes);  // zero-filled: the counters start at zero
+            char *p = plan.act.get();
+            for (const Link &l : links) {
+                char *act = p;
+                int *cnt = (int *)(p + staged(l.K));
+                p += staged(l.K) + (size_t)((l.K / 32 + 32) * 4 + 127) / 128 * 128;
+                GemvExtras &to = *psteps[l.to].pf;
+                to.xq = act;
+                if (l.mode == 0) {
+                    *psteps[l.from].attn_act = act;
+                    continue;
+                }
+                const FusedArgs b = psteps[l.to].gemv(psteps[l.to].tds);
+                GemvExtras &from = *psteps[l.from].pf;
+                from.act_mode = l.mode;
+                from.act_out = act;
+                from.act_cnt = cnt;
+                from.act_norm_w = b.norm_w;
+                from.act_eps = b.eps;
+            }
         }
     }
 

@@ -49,6 +49,7 @@ struct SplitArgs {
     int *err;
     int64_t nch;
     uint64_t *trace;  // [CTA][8] %globaltimer stamps, or null: start, past the wait, K/V landed, done
+    char *act_out;    // one query row: its Q8_0 blocks in the GEMV staging layout (K = H x D), or null
 };
 
 template <int MAXD>
@@ -157,8 +158,12 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
         if (last)
             for (int64_t g = warp; g < G; g += blockDim.x / 32) {
                 const int64_t h = hk * G + g;
+                const int64_t K = a.H * a.D;
+                int8_t *qc = a.act_out ? (int8_t *)a.act_out + h * a.D : nullptr;
+                float *qd = a.act_out ? (float *)(a.act_out + K) + h * a.D / 32 : nullptr;
+                int *qs = a.act_out ? (int *)((float *)(a.act_out + K) + K / 32) + h * a.D / 32 : nullptr;
                 flash_merge<MAXD>(a.part + (((b * a.Sq + iq) * a.H + h) * a.nch) * (a.D + 2), (int)a.nch,
-                                  a.out + a.D * (h + a.oH * (iq + a.Sq * b)));
+                                  a.out + a.D * (h + a.oH * (iq + a.Sq * b)), qc, qd, qs);
             }
         __syncthreads();  // qs / ms / sc / ps and `last` are reused by the next row
     }
@@ -189,7 +194,7 @@ size_t flash_split_ctas(const TD &q, const TD &kk) {
 }
 
 void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
-                      int *counters, int *err, cudaStream_t s, uint64_t *trace) {
+                      int *counters, int *err, cudaStream_t s, uint64_t *trace, char *act_out) {
     if (flash_prefill_ok(q, kk, v, out)) {
         flash_prefill(q, kk, v, mask, out, scale, err, s);
         return;
@@ -230,6 +235,7 @@ void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, co
     a.counters = counters;
     a.err = err;
     a.trace = trace;
+    a.act_out = q.ne[1] == 1 && q.ne[3] == 1 ? act_out : nullptr;
     const int64_t G = a.H / a.Hkv;
     const int hslots = (int)std::min<int64_t>(G, MAXG);
     const int threads = hslots * WPH * 32;

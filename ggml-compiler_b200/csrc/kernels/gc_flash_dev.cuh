@@ -206,7 +206,8 @@ struct SyncCta {
 // partials were written by other CTAs: they are read from L2 (ld.global.cg), all of a batch of
 // chunks at once.
 template <int D, int BATCH = (D <= 128 ? 16 : 8)>  // BATCH: chunks fetched at once (registers: BATCH x D/32)
-__device__ inline void flash_merge(const float *pp, int nch, float *orow) {
+__device__ inline void flash_merge(const float *pp, int nch, float *orow, int8_t *qcodes = nullptr, float *qd = nullptr,
+                                   int *qs8 = nullptr) {
     constexpr int MAXD = D;
     const int lane = threadIdx.x & 31, cpl = D / 32;
     const float ninf = -__int_as_float(0x7f800000);
@@ -247,6 +248,31 @@ __device__ inline void flash_merge(const float *pp, int nch, float *orow) {
 #pragma unroll
     for (int e = 0; e < MAXD / 32; e++)
         if (e < cpl) orow[lane * cpl + e] = __fmul_rn(O[e], inv);
+    if (qcodes) {
+        // the row's Q8_0 blocks for the GEMV that reads it (the GEMV prologue's rule: d = amax / 127
+        // in fp16, codes = nearest-even(v * 127 / amax), 8 x the code sum); a block of 32 values is
+        // 32 / cpl consecutive lanes
+        constexpr int LPB = 32 / (MAXD / 32);
+        float amax = 0.0f;
+#pragma unroll
+        for (int e = 0; e < MAXD / 32; e++) amax = fmaxf(amax, fabsf(__fmul_rn(O[e], inv)));
+#pragma unroll
+        for (int off = LPB / 2; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        int sum = 0;
+#pragma unroll
+        for (int e = 0; e < MAXD / 32; e++) {
+            const int q = __float2int_rn(__fmul_rn(__fmul_rn(O[e], inv), id));
+            qcodes[lane * cpl + e] = (int8_t)q;
+            sum += q;
+        }
+#pragma unroll
+        for (int off = LPB / 2; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        if (lane % LPB == 0) {
+            qd[lane / LPB] = h2f(f2h(__fdiv_rn(amax, 127.0f)));
+            qs8[lane / LPB] = 8 * sum;
+        }
+    }
 }
 
 }  // namespace k

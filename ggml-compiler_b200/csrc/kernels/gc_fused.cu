@@ -64,10 +64,12 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
     pdl_wait();
     const bool stamp = a.trace && threadIdx.x == 0;
     if (stamp) a.trace[blockIdx.x * 8 + 2] = global_ns();
-    gemv_prologue<M, NCW * 32>(a, sq, sdf, ss8, red, 1, wpre);
+    if (M == 1 && a.pro == PRO_Q8) gemv_stage_q8<NCW * 32>(a, sq, 1);
+    else gemv_prologue<M, NCW * 32>(a, sq, sdf, ss8, red, 1, wpre);
     if (stamp) a.trace[blockIdx.x * 8 + 3] = global_ns();
     if (!consume_gemv<QT, NR, M, CG>(a, G, R, 0, blockIdx.x, gridDim.x, 0, 1, warp, sq, sdf, ss8))
         if (a.err) atomicExch(a.err, 2);
+    if (M == 1 && a.act_mode != ACT8_NONE) gemv_emit_act8<NCW * 32>(a, G, red, 1);
     if (stamp) a.trace[blockIdx.x * 8 + 4] = global_ns();
 }
 

@@ -28,6 +28,12 @@ namespace k {
 
 constexpr int GEMV_MAXM = 8;
 
+// Shared-memory staging of M activation rows of K values: int8 codes [M][K], f32 block scales
+// [M][K / 32], int 8 x code sums [M][K / 32], rounded up to 128 bytes.
+__host__ __device__ inline size_t gemv_act_bytes(int M, int64_t K) {
+    return ((size_t)M * (size_t)K + (size_t)M * (size_t)(K / 32) * 8 + 127) / 128 * 128;
+}
+
 // Geometry of one GEMV over the tiled weights. With a.nshard > 1 the groups are this shard's: a
 // contiguous run of tiles (MAP_SINGLE, MAP_SWIGLU) or this shard's query and K/V heads (MAP_ROPE_QKV);
 // gemv_piece maps them back to the global tiles, so every row keeps its single-shard arithmetic.
@@ -201,7 +207,7 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
                 for (int i0 = tid; i0 < K; i0 += 256 * U) {
                     float v[U];
 #pragma unroll
-                    for (int u = 0; u < U; u++) v[u] = i0 + 256 * u < K ? x[i0 + 256 * u] : 0.0f;
+                    for (int u = 0; u < U; u++) v[u] = i0 + 256 * u < K ? __ldcg(x + i0 + 256 * u) : 0.0f;
 #pragma unroll
                     for (int u = 0; u < U; u++)
                         if (i0 + 256 * u < K) p = __dadd_rn(p, (double)__fmul_rn(v[u], v[u]));
@@ -239,7 +245,7 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
 #pragma unroll
             for (int u = 0; u < UB; u++) {
                 const int b = b0 + u * NW * 4 + sub;
-                v[u] = b < nb ? *(const float4 *)(x + b * 32 + e) : zero;
+                v[u] = b < nb ? __ldcg((const float4 *)(x + b * 32 + e)) : zero;
                 w[u] = (wpre && b0 == warp * 4) ? wpre[u]  // first round, loaded before the wait
                                                 : (a.pro == PRO_NORM && b < nb) ? *(const float4 *)(a.norm_w + b * 32 + e) : zero;
             }
@@ -274,6 +280,90 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
         }
     }
     named_bar(bar, NCT);
+}
+
+// PRO_Q8: the row's staged blocks (a.xq, gemv_act_bytes(1, K) bytes) copied into shared memory by
+// the NCT consumer threads.
+template <int NCT>
+__device__ inline void gemv_stage_q8(const FusedArgs &a, int8_t *sq, int bar) {
+    const int n = (int)(gemv_act_bytes(1, a.K) / 16);
+    const int4 *src = (const int4 *)a.xq;
+    int4 *dst = (int4 *)sq;
+    for (int i = threadIdx.x; i < n; i += NCT) dst[i] = __ldcg(src + i);
+    named_bar(bar, NCT);
+}
+
+// One warp: the Q8_0 block of 32 consecutive f32 values at x (written by other CTAs: read through
+// L2) into the staging layout at (codes, d, s8), with the prologue's rule: d = amax / 127 in fp16,
+// codes = nearest-even(x * 127 / amax), s8 = 8 x the code sum.
+__device__ inline void quantize_block_warp(const float *x, int8_t *codes, float *d, int *s8) {
+    const int lane = threadIdx.x & 31;
+    const float v = __ldcg(x + lane);
+    const float amax = warp_max(fabsf(v));
+    const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    const int q = __float2int_rn(__fmul_rn(v, id));
+    int sum = q;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    codes[lane] = (int8_t)q;
+    if (lane == 0) {
+        *d = h2f(f2h(__fdiv_rn(amax, 127.0f)));
+        *s8 = 8 * sum;
+    }
+}
+
+// After the CTA's consumers stored their rows (one activation row): what the launch emits for the
+// next GEMV (FusedArgs::act_mode). `red` is the prologue's shared scratch, free by now.
+template <int NCT>
+__device__ inline void gemv_emit_act8(const FusedArgs &a, const GemvGeo &G, double *red, int bar) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    named_bar(bar, NCT);  // every consumer warp's rows are stored
+    const int64_t N = a.wrows[0];
+    int8_t *codes = (int8_t *)a.act_out;
+    float *d = (float *)(a.act_out + N);
+    int *s8 = (int *)(d + N / 32);
+    if (a.act_mode == ACT8_NORM) {
+        int *flag = (int *)red;
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const bool last = atomicAdd(a.act_cnt, 1) == (int)gridDim.x - 1;
+            if (last) {
+                *a.act_cnt = 0;
+                __threadfence();
+            }
+            *flag = last ? 1 : 0;
+        }
+        named_bar(bar, NCT);
+        const int last = *flag;
+        named_bar(bar, NCT);  // `red` is the norm's scratch next
+        if (!last) return;
+        FusedArgs na = a;
+        na.x = a.out;
+        na.ldx = a.ldo;
+        na.K = N;
+        na.M = 1;
+        na.pro = PRO_NORM;
+        na.norm_w = a.act_norm_w;
+        na.eps = a.act_eps;
+        gemv_prologue<1, NCT>(na, codes, d, s8, red, bar);
+    } else {
+        // each 32-row block is quantized by the CTA that stores its last 8-row tile
+        const int L = local_groups(G.groups, blockIdx.x, gridDim.x);
+        for (int gl = warp; gl < L; gl += NCT / 32) {
+            const int blk = (G.gbase + (int)blockIdx.x + gl * (int)gridDim.x) / (32 / QTR);
+            int done = 0;
+            if (lane == 0) {
+                __threadfence();
+                done = atomicAdd(a.act_cnt + blk, 1) == 32 / QTR - 1;
+                if (done) {
+                    a.act_cnt[blk] = 0;
+                    __threadfence();
+                }
+            }
+            if (__shfl_sync(0xffffffffu, done, 0))
+                quantize_block_warp(a.out + (int64_t)blk * 32, codes + (int64_t)blk * 32, d + blk, s8 + blk);
+        }
+    }
 }
 
 // Epilogue operands of row `row0` (loaded by lane 0 before the row's pieces arrive): the residual
@@ -611,10 +701,6 @@ __device__ inline bool consume_gemv(const FusedArgs &a, const GemvGeo &G, const 
         }
         return true;
     }
-}
-
-__host__ __device__ inline size_t gemv_act_bytes(int M, int64_t K) {
-    return ((size_t)M * (size_t)K + (size_t)M * (size_t)(K / 32) * 8 + 127) / 128 * 128;
 }
 
 // Ring slots for a shared-memory budget: as many as fit, at most `maxns`.
