@@ -165,7 +165,9 @@ struct Model {
     bool use_device_loops = true;  // GGML_COMPILER_B200_DEVICE_LOOPS=0: loops checked on the host every iteration
     bool profiling = false;
     int64_t l2_prefetch_bytes = 0;   // GCB_L2_PREFETCH_MB: what each fused GEMV prefetches of the next one's weights
-    bool act_handoff = true;  // GCB_ACT_HANDOFF=0: every GEMV quantizes its own input row
+    // GCB_ACT_HANDOFF: which producers hand the next GEMV its row quantized (bit 0: the attention
+    // merge; bit 1: a residual GEMV's last CTA, normed; bit 2: the SwiGLU GEMV per block)
+    int act_handoff = 1;
     bool stream_evict_first = true;  // GCB_STREAM_EVICT_FIRST=0: GEMV weight streams without the L2 evict-first policy
     std::map<std::string, KernelStat> kstats;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> event_pool;

@@ -753,12 +753,14 @@ void Planner::finish() {
             const FusedArgs b = B.gemv(B.tds);
             if (b.M != 1 || b.nshard != 1 || b.K % 32 || b.pro == PRO_Q8) continue;
             if (A.attn_act && b.pro == PRO_ACT && (const char *)b.x == A.tds[4].data && b.K == A.attn_k) {
-                links.push_back({i - 1, i, 0, b.K});
+                if (m.act_handoff & 1) links.push_back({i - 1, i, 0, b.K});
             } else if (A.pf) {
                 const FusedArgs a = A.gemv(A.tds);
                 if (a.M != 1 || a.nshard != 1 || (const float *)a.out != b.x || a.wrows[0] != b.K) continue;
-                if (a.map == MAP_SINGLE && b.pro == PRO_NORM) links.push_back({i - 1, i, ACT8_NORM, b.K});
-                else if (a.map == MAP_SWIGLU && b.pro == PRO_ACT) links.push_back({i - 1, i, ACT8_BLOCKS, b.K});
+                if (a.map == MAP_SINGLE && b.pro == PRO_NORM && (m.act_handoff & 2))
+                    links.push_back({i - 1, i, ACT8_NORM, b.K});
+                else if (a.map == MAP_SWIGLU && b.pro == PRO_ACT && (m.act_handoff & 4))
+                    links.push_back({i - 1, i, ACT8_BLOCKS, b.K});
             }
         }
         auto staged = [](int64_t K) { return (size_t)((K + K / 32 * 8 + 127) / 128 * 128); };
