@@ -59,16 +59,12 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
         }
         return;
     }
-    const bool row = M == 1 && gemv_row_prologue_ok(a);
     float4 wpre[GEMV_UB];
-    float wrow[GEMV_PU];
-    if (row) gemv_row_norm_prefetch(a, wrow);
-    else gemv_norm_prefetch<NCW * 32>(a, wpre);
+    gemv_norm_prefetch<NCW * 32>(a, wpre);
     pdl_wait();
     const bool stamp = a.trace && threadIdx.x == 0;
     if (stamp) a.trace[blockIdx.x * 8 + 2] = global_ns();
     if (M == 1 && a.pro == PRO_Q8) gemv_stage_q8<NCW * 32>(a, sq, 1);
-    else if (row) gemv_row_prologue(a, sq, sdf, ss8, red, 1, wrow);
     else gemv_prologue<M, NCW * 32>(a, sq, sdf, ss8, red, 1, wpre);
     if (stamp) a.trace[blockIdx.x * 8 + 3] = global_ns();
     if (!consume_gemv<QT, NR, M, CG>(a, G, R, 0, blockIdx.x, gridDim.x, 0, 1, warp, sq, sdf, ss8))

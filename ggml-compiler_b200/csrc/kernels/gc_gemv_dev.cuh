@@ -240,8 +240,9 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
         }
         const int sub = lane >> 3, e = (lane & 7) * 4;
         const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int b0 = warp * 4; b0 < nb; b0 += NW * 4 * UB) {
-            float4 v[UB], w[UB];
+        constexpr int STRIDE = NW * 4 * UB;  // blocks of one round (UB 4-block groups per warp)
+        // a round's loads: the activation values and, for PRO_NORM, the norm weights
+        auto load = [&](int b0, float4 (&v)[UB], float4 (&w)[UB]) {
 #pragma unroll
             for (int u = 0; u < UB; u++) {
                 const int b = b0 + u * NW * 4 + sub;
@@ -249,6 +250,11 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
                 w[u] = (wpre && b0 == warp * 4) ? wpre[u]  // first round, loaded before the wait
                                                 : (a.pro == PRO_NORM && b < nb) ? *(const float4 *)(a.norm_w + b * 32 + e) : zero;
             }
+        };
+        float4 v[UB], w[UB], vn[UB], wn[UB];
+        load(warp * 4, v, w);
+        for (int b0 = warp * 4; b0 < nb; b0 += STRIDE) {
+            if (b0 + STRIDE < nb) load(b0 + STRIDE, vn, wn);  // the next round's loads first
 #pragma unroll
             for (int u = 0; u < UB; u++) {
                 const int b = b0 + u * NW * 4 + sub;
@@ -277,104 +283,11 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
                     }
                 }
             }
-        }
-    }
-    named_bar(bar, NCT);
-}
-
-// One activation row with 256 consumer threads, every value loaded once. Thread t = 32 w + j holds
-// x[256 u + t], u = 0, 1, ...: for rms_norm these are exactly the elements of the checker's partial
-// t, in its order; for the quantization, value u is element j of block 8 u + w, so each warp
-// quantizes whole blocks from registers (amax and the code sum across its 32 lanes). A row of at
-// most 256 x GEMV_PU values is loaded in one round; a longer one (PRO_ACT only) in rounds, the next
-// round's loads issued before the current round's arithmetic. Same arithmetic as gemv_prologue.
-constexpr int GEMV_PU = 16;
-
-// The norm weights of the row prologue (PRO_NORM): loaded before griddepcontrol.wait (weights
-// are written by no kernel of the step), so the load latency overlaps the previous kernel's tail.
-__device__ __forceinline__ void gemv_row_norm_prefetch(const FusedArgs &a, float (&w)[GEMV_PU]) {
 #pragma unroll
-    for (int u = 0; u < GEMV_PU; u++) {
-        const int i = 256 * u + (int)threadIdx.x;
-        w[u] = (a.pro == PRO_NORM && i < a.K) ? a.norm_w[i] : 0.0f;
-    }
-}
-
-__host__ __device__ inline bool gemv_row_prologue_ok(const FusedArgs &a) {
-    return a.M == 1 && (a.pro == PRO_ACT || (a.pro == PRO_NORM && a.K <= 256 * GEMV_PU));
-}
-
-// Block b's Q8_0 form from lane j's value v (one warp per block).
-__device__ __forceinline__ void row_quant_block(float v, int b, int j, int8_t *sq, float *sdf, int *ss8) {
-    const float amax = warp_max(fabsf(v));
-    const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-    const int q = __float2int_rn(__fmul_rn(v, id));
-    int sum = q;
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    sq[b * 32 + j] = (int8_t)q;
-    if (j == 0) {
-        sdf[b] = h2f(f2h(__fdiv_rn(amax, 127.0f)));
-        ss8[b] = 8 * sum;
-    }
-}
-
-__device__ inline void gemv_row_prologue(const FusedArgs &a, int8_t *sq, float *sdf, int *ss8, double *red, int bar,
-                                         const float (&wpre)[GEMV_PU]) {
-    constexpr int NCT = 256;
-    const int K = (int)a.K, nb = K / 32;
-    const int t = threadIdx.x, w = t >> 5, j = t & 31;
-    const float *x = a.x;
-    if (a.pro == PRO_NORM) {
-        float v[GEMV_PU];
-#pragma unroll
-        for (int u = 0; u < GEMV_PU; u++) v[u] = 256 * u + t < K ? __ldcg(x + 256 * u + t) : 0.0f;
-        double p = 0.0;
-#pragma unroll
-        for (int u = 0; u < GEMV_PU; u++)
-            if (256 * u + t < K) p = __dadd_rn(p, (double)__fmul_rn(v[u], v[u]));
-        red[t] = p;
-        named_bar(bar, NCT);
-#pragma unroll
-        for (int off = 128; off >= 32; off >>= 1) {
-            if (t < off) red[t] = __dadd_rn(red[t], red[t + off]);
-            named_bar(bar, NCT);
-        }
-        if (t < 32) {
-            double s = red[t];
-#pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) s = __dadd_rn(s, __shfl_down_sync(0xffffffffu, s, off));
-            if (t == 0) red[0] = s;
-        }
-        named_bar(bar, NCT);
-        const double tot = red[0];
-        const float mean = __double2float_rn(__ddiv_rn(tot, (double)K));
-        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
-#pragma unroll
-        for (int u = 0; u < GEMV_PU; u++) {
-            const int b = 8 * u + w;
-            if (b < nb) row_quant_block(__fmul_rn(__fmul_rn(v[u], scale), wpre[u]), b, j, sq, sdf, ss8);
-        }
-    } else {
-        const int rounds = (K + 256 * GEMV_PU - 1) / (256 * GEMV_PU);
-        float cur[GEMV_PU], nxt[GEMV_PU];
-#pragma unroll
-        for (int u = 0; u < GEMV_PU; u++) cur[u] = u * 256 + t < K ? __ldcg(x + u * 256 + t) : 0.0f;
-        for (int r = 0; r < rounds; r++) {
-            const int base = r * GEMV_PU * 256;
-            if (r + 1 < rounds)
-#pragma unroll
-                for (int u = 0; u < GEMV_PU; u++) {
-                    const int i = base + GEMV_PU * 256 + u * 256 + t;
-                    nxt[u] = i < K ? __ldcg(x + i) : 0.0f;
-                }
-#pragma unroll
-            for (int u = 0; u < GEMV_PU; u++) {
-                const int b = 8 * (r * GEMV_PU + u) + w;
-                if (b < nb) row_quant_block(cur[u], b, j, sq, sdf, ss8);
+            for (int u = 0; u < UB; u++) {
+                v[u] = vn[u];
+                w[u] = wn[u];
             }
-#pragma unroll
-            for (int u = 0; u < GEMV_PU; u++) cur[u] = nxt[u];
         }
     }
     named_bar(bar, NCT);
