@@ -32,6 +32,7 @@ struct GemvExtras {
     const float *act_norm_w = nullptr;
     float act_eps = 0.0f;
     int *act_cnt = nullptr;
+    int hold_pieces = 0;
 };
 
 struct PlanStep {

@@ -75,6 +75,10 @@ struct FusedArgs {
     // start, producer done issuing, consumers past the dependent-launch wait, prologue done,
     // consumers done (epilogue included). Null: no stamps.
     uint64_t *trace = nullptr;
+    // The producer issues this many pieces, then waits (bounded) until the consumers' prologue is
+    // done before issuing the rest, so that the prologue's loads do not queue behind the ring's
+    // fill. 0: no wait.
+    int hold_pieces = 0;
 };
 
 namespace k {

@@ -166,8 +166,11 @@ struct Model {
     bool profiling = false;
     int64_t l2_prefetch_bytes = 0;   // GCB_L2_PREFETCH_MB: what each fused GEMV prefetches of the next one's weights
     // GCB_ACT_HANDOFF: which producers hand the next GEMV its row quantized (bit 0: the attention
-    // merge; bit 1: a residual GEMV's last CTA, normed; bit 2: the SwiGLU GEMV per block)
-    int act_handoff = 1;
+    // merge; bit 1: a residual GEMV's last CTA, normed; bit 2: the SwiGLU GEMV per block). Bit 1
+    // measured slower (its serial tail), so the default is 5.
+    int act_handoff = 5;
+    int prologue_hold = 0;    // GCB_PROLOGUE_HOLD: FusedArgs::hold_pieces of the single-row GEMVs
+    bool kv_prefetch = false;  // GCB_KV_PREFETCH=1: a GEMV before one-row attention prefetches its K/V into L2
     bool stream_evict_first = true;  // GCB_STREAM_EVICT_FIRST=0: GEMV weight streams without the L2 evict-first policy
     std::map<std::string, KernelStat> kstats;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> event_pool;

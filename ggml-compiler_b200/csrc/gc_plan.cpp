@@ -152,6 +152,7 @@ void Planner::add_gemv(const char *kind, const std::string &node, std::vector<TD
             a.act_norm_w = pf->act_norm_w;
             a.act_eps = pf->act_eps;
             a.act_cnt = pf->act_cnt;
+            a.hold_pieces = pf->hold_pieces;
             k::fused_gemv(a, st, true);
         },
         bytes);
@@ -717,6 +718,18 @@ void Planner::finish() {
         GemvExtras &pf = *psteps[gi[x]].pf;
         pf = GemvExtras{};
         pf.evict_first = m.stream_evict_first ? 1 : 0;
+        pf.hold_pieces = m.prologue_hold;
+        // a one-row attention step right after: its K and V cache rows into L2 while this GEMV
+        // streams (the attention's bulk copies then read L2)
+        if (m.kv_prefetch && gi[x] + 1 < psteps.size() && psteps[gi[x] + 1].attn_act) {
+            const PlanStep &at = psteps[gi[x] + 1];
+            for (int r = 0; r < 2; r++) {
+                const TD &kv = at.tds[(size_t)(1 + r)];
+                pf.p[r] = kv.data;
+                pf.n[r] = (int64_t)((kv.ne[2] - 1) * kv.nb[2] + kv.ne[1] * kv.nb[1]) & ~(int64_t)255;
+            }
+            continue;
+        }
         if (m.l2_prefetch_bytes <= 0 || gi.size() < 2) continue;
         const PlanStep &nx = psteps[gi[(x + 1) % gi.size()]];
         const FusedArgs na = nx.gemv(nx.tds);

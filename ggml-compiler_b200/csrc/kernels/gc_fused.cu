@@ -28,7 +28,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t *full = (uint64_t *)smem;
     uint64_t *empty = full + MAXNS;
-    double *red = (double *)(empty + MAXNS);  // [256]
+    uint64_t *hold = empty + MAXNS;          // the consumers' prologue is done (FusedArgs::hold_pieces)
+    double *red = (double *)(hold + 2);      // [256]
     int8_t *sq = (int8_t *)(red + 256);
     float *sdf = (float *)(sq + (size_t)M * a.K);
     int *ss8 = (int *)(sdf + (size_t)M * G.nb);
@@ -41,6 +42,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], NCW);
         }
+        mbar_init(hold, 1);
         mbar_fence_init();
     }
     __syncthreads();
@@ -50,7 +52,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
         if (lane != 0) return;
         if (a.trace) a.trace[blockIdx.x * 8 + 0] = global_ns();
         uint32_t t = 0;
-        if (!produce_gemv(a, G, R, t, blockIdx.x, gridDim.x, gemv_chunk(M, 1, CG))) {
+        if (!produce_gemv(a, G, R, t, blockIdx.x, gridDim.x, gemv_chunk(M, 1, CG), a.hold_pieces > 0 ? hold : nullptr)) {
             if (a.err) atomicExch(a.err, 2);
             drain_ring(R, t);
         } else {
@@ -67,6 +69,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
     if (M == 1 && a.pro == PRO_Q8) gemv_stage_q8<NCW * 32>(a, sq, 1);
     else gemv_prologue<M, NCW * 32>(a, sq, sdf, ss8, red, 1, wpre);
     if (stamp) a.trace[blockIdx.x * 8 + 3] = global_ns();
+    if (threadIdx.x == 0) mbar_arrive(hold);
     if (!consume_gemv<QT, NR, M, CG>(a, G, R, 0, blockIdx.x, gridDim.x, 0, 1, warp, sq, sdf, ss8))
         if (a.err) atomicExch(a.err, 2);
     if (M == 1 && a.act_mode != ACT8_NONE) gemv_emit_act8<NCW * 32>(a, G, red, 1);
@@ -86,7 +89,7 @@ void launch_t(const FusedArgs &a, const GemvGeo &G, cudaStream_t s, bool pdl) {
         attr = true;
     }
     const int slot_bytes = (int)qw_piece_bytes(G.nb, G.cb, 0);
-    const size_t head = (size_t)(2 * MAXNS) * 8 + 256 * 8 + gemv_act_bytes(M, a.K);
+    const size_t head = (size_t)(2 * MAXNS + 2) * 8 + 256 * 8 + gemv_act_bytes(M, a.K);
     const size_t budget = g_smem_budget ? g_smem_budget : (g_ctas_per_sm == 2 ? 113 * 1024 : 224 * 1024);
     int ns = ring_slots(budget, head, (size_t)slot_bytes, MAXNS);
     if (ns < 2 * G.pieces) ns = 2 * G.pieces;  // room for one group's pieces in flight and one consumed

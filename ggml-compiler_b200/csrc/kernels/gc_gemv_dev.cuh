@@ -127,7 +127,7 @@ __host__ inline uint32_t ring_magic(uint32_t ns) { return (uint32_t)((((uint64_t
 // Producer: put this CTA's pieces of one GEMV into the ring, continuing the piece count `t`.
 // Returns false if a slot was never released (bounded wait).
 __device__ inline bool produce_gemv(const FusedArgs &a, const GemvGeo &G, const Ring &R, uint32_t &t, int cta, int nctas,
-                                    int chunk) {
+                                    int chunk, uint64_t *hold = nullptr) {
     const int L = local_groups(G.groups, cta, nctas);
     const uint64_t policy = a.stream_evict_first ? l2_policy_evict_first() : 0;
     for (int c0 = 0; c0 < L; c0 += chunk) {
@@ -137,6 +137,7 @@ __device__ inline bool produce_gemv(const FusedArgs &a, const GemvGeo &G, const 
             for (int gl = c0; gl < c1; gl++)
                 for (int r = 0; r < G.pieces; r++, t++) {
                     const int slot = R.slot(t);
+                    if (hold && t == (uint32_t)a.hold_pieces) mbar_wait(hold, 0);  // a late prologue only delays
                     if (t >= R.ns && !mbar_wait(&R.empty[slot], R.parity(t) ^ 1u)) return false;
                     mbar_expect_tx(&R.full[slot], pb);
                     int mat, tile;
