@@ -759,7 +759,7 @@ void Model::write_trace() {
                     const uint64_t *st = &h[e.offset + cta * 8];
                     if (!st[0] && !st[2]) continue;  // a CTA the launch did not have
                     std::fprintf(f, "%s\t%zu\t%s\t%s\t%zu", c.stage->name.c_str(), li, e.kind.c_str(), e.node.c_str(), cta);
-                    for (int s = 0; s < 5; s++) std::fprintf(f, "\t%lld", st[s] ? (long long)(st[s] - t0) : -1ll);
+                    for (int s = 0; s < 8; s++) std::fprintf(f, "\t%lld", st[s] ? (long long)(st[s] - t0) : -1ll);
                     std::fprintf(f, "\n");
                 }
             }

@@ -48,7 +48,8 @@ struct SplitArgs {
     int *counters;   // [B][Sq][Hkv], zero between launches
     int *err;
     int64_t nch;
-    uint64_t *trace;  // [CTA][8] %globaltimer stamps, or null: start, past the wait, K/V landed, done
+    uint64_t *trace;  // [CTA][8] %globaltimer stamps, or null: start, staged, past the wait, K/V landed,
+                      // done, chunk computed, past the arrival counter
     char *act_out;    // one query row: its Q8_0 blocks in the GEMV staging layout (K = H x D), or null
 };
 
@@ -119,6 +120,7 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
         fc.part = a.part + ((((b * a.Sq + iq) * a.H + hk * G) * a.nch + ch) * (a.D + 2));
         fc.pstride = a.nch * (a.D + 2);
         flash_stage(fc, qs, ms, threadIdx.x, blockDim.x);  // the first row: while the copies are in flight
+        if (stamps && iq == iq0) stamps[1] = global_ns();
         // a chunk whose keys the mask hides from every head of this row contributes nothing: its
         // partial is (m = -inf, l = 0), which the merge skips, without the arithmetic
         int live = !fc.mask;
@@ -144,6 +146,7 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
         }
 
         // the last CTA of this (batch, query row, K/V head) merges every chunk of its heads
+        if (stamps && iq == iq0) stamps[5] = global_ns();
         __syncthreads();
         if (threadIdx.x == 0) {
             __threadfence();  // this CTA's partials (ordered before by the barrier) are visible first
@@ -155,6 +158,7 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
             }
         }
         __syncthreads();
+        if (stamps && iq == iq0) stamps[6] = global_ns();
         if (last)
             for (int64_t g = warp; g < G; g += blockDim.x / 32) {
                 const int64_t h = hk * G + g;
