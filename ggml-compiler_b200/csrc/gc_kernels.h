@@ -136,6 +136,10 @@ size_t flash_split_counters(const TD &q, const TD &k);
 void flash_attn_split(const TD &q, const TD &k, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
                       int *counters, int *err, cudaStream_t s, uint64_t *trace = nullptr, char *act_out = nullptr);
 size_t flash_split_ctas(const TD &q, const TD &k);  // CTAs of one split launch (trace slots)
+// One decode row of 2-16 chunks runs as thread-block clusters (one per K/V head, chunk partials
+// merged through distributed shared memory) when such clusters fit; this asks once, outside any
+// stream capture, and says whether they do. GCB_ATTN_CLUSTER=0 keeps the split kernel.
+bool flash_split_prepare(const TD &q, const TD &k, const TD &v, const TD &out);
 // act_out (one query row, one batch): the merged row's Q8_0 blocks in the GEMV staging layout
 // (gemv_act_bytes(1, H x D) bytes) for the GEMV that reads it (FusedArgs::PRO_Q8).
 // The same result for prefill calls (16+ query rows, head size 64 or 128, K/V rows contiguous):

@@ -471,7 +471,9 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
                 scratch_marker(k::flash_split_scratch_bytes(q, kk), &scratch);
                 int *cnt = m.counters(s.name + "/" + n.id, k::flash_split_counters(q, kk));
                 int *err = m.d_err;
-                auto tr = trace_slot("flash_attn", n.id, k::flash_split_ctas(q, kk));
+                const bool cluster = k::flash_split_prepare(q, kk, v, y);
+                auto tr = trace_slot("flash_attn", n.id, cluster ? (size_t)(((kk.ne[1] + 63) / 64) * kk.ne[2] * q.ne[3])
+                                                                  : k::flash_split_ctas(q, kk));
                 auto act = std::make_shared<char *>(nullptr);
                 add("flash_attn", n.id, {q, kk, v, mk, y, scratch},
                     [scale, cnt, err, tr, act](cudaStream_t st, const std::vector<TD> &t) {

@@ -13,8 +13,14 @@
 // The CTA writes its chunk partial (m, l, o[D]) to scratch; the last CTA to finish for a
 // (query row, K/V head) merges every chunk in chunk order (an atomic arrival counter, reset by that
 // CTA), so no second kernel is needed. Waits are bounded; a timeout sets the error word.
+#include <cooperative_groups.h>
+
+#include <cstdlib>
+#include <map>
+#include <mutex>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 #include "../gc_kernels.h"
 #include "gc_flash_dev.cuh"
@@ -174,7 +180,172 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
     if (stamps) stamps[4] = global_ns();
 }
 
+// One query row of decode (Sq == 1, K/V rows contiguous, at most FL_CLUSTER_MAX chunks): one thread
+// block cluster per (K/V head, batch), one CTA per 64-key chunk. Each CTA computes its chunk
+// partials exactly as the split kernel does, but writes them into the shared memory of the
+// cluster's rank-0 CTA (distributed shared memory); after a cluster barrier rank 0 merges them in
+// chunk order from its own shared memory. No global scratch, counters or fences: the cross-CTA
+// merge costs one cluster barrier. A chunk whose K/V copy timed out writes a NaN partial (the
+// merged rows come out NaN) and sets the error word; every CTA still reaches both barriers.
+constexpr int FL_CLUSTER_MAX = 16;
+
+template <int MAXD>
+__global__ void __launch_bounds__(MAXG * WPH * 32) flash_cluster_kernel(SplitArgs a) {
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(128) unsigned char smem[];
+    const cg::cluster_group cluster = cg::this_cluster();
+    const int D = (int)a.D;
+    __shared__ uint64_t bar;
+    __half *Ks = (__half *)smem;
+    __half *Vs = Ks + CH * D;
+    float *sc = (float *)(Vs + CH * D);
+    float *ps = sc + MAXG * CH;
+    const int64_t G = a.H / a.Hkv;
+    float *qs = ps + MAXG * WPH * CH;
+    float *ms = qs + G * D;
+    float *parts = ms + G * CH;  // rank 0: [G][nch][D + 2] partials of every chunk
+    const int64_t ch = blockIdx.x;
+    const int64_t hk = blockIdx.y % a.Hkv, b = blockIdx.y / a.Hkv;
+    const int64_t j0 = ch * CH;
+    const int n = (int)min((int64_t)CH, a.nkv - j0);
+    const int warp = threadIdx.x >> 5;
+    const float ninf = -__int_as_float(0x7f800000);
+    const int64_t cta_id = blockIdx.x + (int64_t)gridDim.x * blockIdx.y;
+    uint64_t *stamps = a.trace && threadIdx.x == 0 ? a.trace + cta_id * 8 : nullptr;
+    if (stamps) stamps[0] = global_ns();
+    pdl_trigger();
+    pdl_wait();
+    if (stamps) stamps[2] = global_ns();
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+        const uint32_t bytes = (uint32_t)(n * D * 2);
+        mbar_expect_tx(&bar, 2 * bytes);
+        bulk_g2s(Ks, a.k + hk * a.knb2 + b * a.knb3 + j0 * a.knb1, bytes, &bar);
+        bulk_g2s(Vs, a.v + hk * a.vnb2 + b * a.vnb3 + j0 * a.vnb1, bytes, &bar);
+    }
+    cluster.sync();  // every CTA of the cluster has started: its shared memory may be written
+    FlashChunk fc;
+    fc.q = a.q + (hk * G) * a.qnb2 + b * a.qnb3;
+    fc.qnb0 = a.qnb0;
+    fc.qnbh = a.qnb2;
+    fc.mask = a.mask ? a.mask + ((hk * G) % a.mne2) * a.mnb2 + (b % a.mne3) * a.mnb3 + j0 * 2 : nullptr;
+    fc.mne2 = a.mne2;
+    fc.mnbh = a.mnb2;
+    fc.hbase = (int)(hk * G);
+    fc.scale = a.scale;
+    fc.D = D;
+    fc.n = n;
+    fc.G = (int)G;
+    fc.part = cluster.map_shared_rank(parts, 0) + ch * (a.D + 2);
+    fc.pstride = a.nch * (a.D + 2);
+    flash_stage(fc, qs, ms, threadIdx.x, blockDim.x);
+    if (stamps) stamps[1] = global_ns();
+    int live = !fc.mask;
+    for (int i = threadIdx.x; !live && i < (int)G * CH; i += blockDim.x) live = (i % CH) < n && ms[i] != ninf;
+    live = __syncthreads_or(live);
+    const bool landed = __syncthreads_and(mbar_wait(&bar, 0));
+    if (stamps) stamps[3] = global_ns();
+    if (!landed) {
+        if (threadIdx.x < G) {
+            fc.part[threadIdx.x * fc.pstride] = __int_as_float(0x7fc00000);
+            fc.part[threadIdx.x * fc.pstride + 1] = 0.0f;
+        }
+        if (threadIdx.x == 0 && a.err) atomicExch(a.err, 2);
+    } else if (live) {
+        const int nslots = (int)(blockDim.x / 32) / WPH;
+        flash_chunk<WPH, MAXD>(fc, Ks, Vs, qs, ms, sc, ps, nslots, SyncCta());
+    } else if (threadIdx.x < G) {
+        fc.part[threadIdx.x * fc.pstride] = ninf;
+        fc.part[threadIdx.x * fc.pstride + 1] = 0.0f;
+    }
+    if (stamps) stamps[5] = global_ns();
+    cluster.sync();  // every partial is in rank 0's shared memory
+    if (stamps) stamps[6] = global_ns();
+    if (cluster.block_rank() == 0)
+        for (int64_t g = warp; g < G; g += blockDim.x / 32) {
+            const int64_t h = hk * G + g;
+            const int64_t K = a.H * a.D;
+            int8_t *qc = a.act_out ? (int8_t *)a.act_out + h * a.D : nullptr;
+            float *qd = a.act_out ? (float *)(a.act_out + K) + h * a.D / 32 : nullptr;
+            int *qs8 = a.act_out ? (int *)((float *)(a.act_out + K) + K / 32) + h * a.D / 32 : nullptr;
+            flash_merge<MAXD, true>(parts + g * a.nch * (a.D + 2), (int)a.nch, a.out + a.D * (h + a.oH * b * a.Sq), qc, qd,
+                                    qs8);
+        }
+    if (stamps) stamps[4] = global_ns();
+}
+
 constexpr size_t kMaxPartBytes = 256u << 20;  // scratch for chunk partials per row group
+
+bool flash_cluster_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("GCB_ATTN_CLUSTER");
+        return !e || std::atoi(e) != 0;
+    }();
+    return on;
+}
+
+// Whether clusters of `size` CTAs of this kernel with this shared memory can be resident (asked
+// once per kernel, size and shared-memory size; sizes above 8 need the non-portable attribute).
+bool flash_cluster_fits(void (*kern)(SplitArgs), cudaLaunchConfig_t cfg, size_t smem, int size) {
+    static std::mutex mu;
+    static std::map<std::pair<void *, std::pair<size_t, int>>, bool> known;
+    std::lock_guard<std::mutex> lk(mu);
+    const auto key = std::make_pair((void *)kern, std::make_pair(smem, size));
+    auto it = known.find(key);
+    if (it != known.end()) return it->second;
+    bool ok = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess;
+    if (ok && size > 8) ok = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+    int clusters = 0;
+    cfg.numAttrs = 2;
+    if (ok) ok = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) == cudaSuccess && clusters >= 1;
+    cudaGetLastError();
+    known[key] = ok;
+    return ok;
+}
+
+// The cluster kernel for one decode row, if it applies and clusters of a.nch CTAs fit: launched
+// (launch) or only checked, which caches the occupancy answer outside any stream capture.
+bool cluster_decode(const SplitArgs &a, size_t smem, int threads, cudaStream_t s, bool launch) {
+    const bool rows_contig = a.knb1 == 2 * a.D && a.vnb1 == 2 * a.D &&
+                             (((uintptr_t)a.k | (uintptr_t)a.v | (uintptr_t)a.knb2 | (uintptr_t)a.vnb2) % 16) == 0;
+    if (a.nch < 2 || a.nch > FL_CLUSTER_MAX || !rows_contig || !flash_cluster_enabled()) return false;
+    void (*ck)(SplitArgs) = nullptr;
+    switch (a.D) {
+        case 32: ck = flash_cluster_kernel<32>; break;
+        case 64: ck = flash_cluster_kernel<64>; break;
+        case 96: ck = flash_cluster_kernel<96>; break;
+        case 128: ck = flash_cluster_kernel<128>; break;
+        case 160: ck = flash_cluster_kernel<160>; break;
+        case 192: ck = flash_cluster_kernel<192>; break;
+        case 224: ck = flash_cluster_kernel<224>; break;
+        case 256: ck = flash_cluster_kernel<256>; break;
+        default: return false;
+    }
+    const int64_t G = a.H / a.Hkv;
+    const size_t csmem = smem + (size_t)G * a.nch * (a.D + 2) * 4;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)a.nch, (unsigned)(a.Hkv * a.B), 1);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = csmem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = (unsigned)a.nch;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    if (!flash_cluster_fits(ck, cfg, csmem, (int)a.nch)) return false;
+    if (!launch) return true;
+    SplitArgs g = a;
+    g.Sq = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, ck, g);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("CUDA launch of flash_cluster failed: ") + cudaGetErrorString(e));
+    return true;
+}
 
 }  // namespace
 
@@ -195,6 +366,28 @@ size_t flash_split_counters(const TD &q, const TD &kk) {
 
 size_t flash_split_ctas(const TD &q, const TD &kk) {
     return (size_t)((kk.ne[1] + CH - 1) / CH) * (size_t)(kk.ne[2] * q.ne[3]) * (size_t)((q.ne[1] + RQ - 1) / RQ);
+}
+
+bool flash_split_prepare(const TD &q, const TD &kk, const TD &v, const TD &out) {
+    if (q.ne[1] != 1 || flash_prefill_ok(q, kk, v, out) || !flash_split_ok(q)) return false;
+    SplitArgs a{};
+    a.D = q.ne[0];
+    a.H = q.ne[2];
+    a.B = q.ne[3];
+    a.k = kk.data;
+    a.v = v.data;
+    a.nkv = kk.ne[1];
+    a.Hkv = kk.ne[2];
+    a.knb1 = kk.nb[1];
+    a.knb2 = kk.nb[2];
+    a.vnb1 = v.nb[1];
+    a.vnb2 = v.nb[2];
+    a.nch = (a.nkv + CH - 1) / CH;
+    const int64_t G = a.H / a.Hkv;
+    const int threads = (int)std::min<int64_t>(G, MAXG) * WPH * 32;
+    const size_t smem = (size_t)CH * a.D * 2 * 2 + (size_t)MAXG * CH * 4 + (size_t)MAXG * WPH * CH * 4 +
+                        (size_t)G * (a.D + CH) * 4;
+    return cluster_decode(a, smem, threads, nullptr, false);
 }
 
 void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
@@ -259,6 +452,12 @@ void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, co
     }
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     const int64_t Sq = q.ne[1];
+    if (Sq == 1) {
+        SplitArgs c = a;
+        c.mask = mask ? mask->data : nullptr;
+        c.out = (float *)out.data;
+        if (cluster_decode(c, smem, threads, s, true)) return;
+    }
     const size_t per_row = (size_t)(a.H * a.B * a.nch * (a.D + 2)) * 4;
     const int64_t rows_per = std::max<int64_t>(1, (int64_t)(kMaxPartBytes / per_row));
     if (a.B != 1 && rows_per < Sq) throw std::runtime_error("flash_split: batched prefill needs one row group");

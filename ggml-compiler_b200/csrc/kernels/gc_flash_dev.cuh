@@ -205,9 +205,12 @@ struct SyncCta {
 // One warp: merge head partials pp[c * (D + 2)], c < nch, in chunk order into orow[D]. The
 // partials were written by other CTAs: they are read from L2 (ld.global.cg), all of a batch of
 // chunks at once.
-template <int D, int BATCH = (D <= 128 ? 16 : 8)>  // BATCH: chunks fetched at once (registers: BATCH x D/32)
+// LOCAL: the partials are in this CTA's shared memory (plain loads) rather than global memory
+// written by other CTAs (L2 loads).
+template <int D, bool LOCAL = false, int BATCH = (D <= 128 ? 16 : 8)>  // BATCH: chunks fetched at once
 __device__ inline void flash_merge(const float *pp, int nch, float *orow, int8_t *qcodes = nullptr, float *qd = nullptr,
                                    int *qs8 = nullptr) {
+    auto ld = [](const float *p) { return LOCAL ? *p : __ldcg(p); };
     constexpr int MAXD = D;
     const int lane = threadIdx.x & 31, cpl = D / 32;
     const float ninf = -__int_as_float(0x7f800000);
@@ -217,7 +220,7 @@ __device__ inline void flash_merge(const float *pp, int nch, float *orow, int8_t
     // the overall max first (one load per lane per 32 chunks), unless one batch holds every chunk
     if (nch > BATCH) {
         for (int c0 = 0; c0 < nch; c0 += 32)
-            if (c0 + lane < nch) M = fmaxf(M, __ldcg(pp + (int64_t)(c0 + lane) * (D + 2)));
+            if (c0 + lane < nch) M = fmaxf(M, ld(pp + (int64_t)(c0 + lane) * (D + 2)));
         M = warp_max(M);
     }
     for (int c0 = 0; c0 < nch; c0 += BATCH) {
@@ -226,10 +229,10 @@ __device__ inline void flash_merge(const float *pp, int nch, float *orow, int8_t
         for (int u = 0; u < BATCH; u++) {
             const bool ok = c0 + u < nch;
             const float *pc = pp + (int64_t)(c0 + u) * (D + 2);
-            bm[u] = ok ? __ldcg(pc) : ninf;
-            bl[u] = ok ? __ldcg(pc + 1) : 0.0f;
+            bm[u] = ok ? ld(pc) : ninf;
+            bl[u] = ok ? ld(pc + 1) : 0.0f;
 #pragma unroll
-            for (int e = 0; e < MAXD / 32; e++) bo[u][e] = (ok && e < cpl) ? __ldcg(pc + 2 + lane * cpl + e) : 0.0f;
+            for (int e = 0; e < MAXD / 32; e++) bo[u][e] = (ok && e < cpl) ? ld(pc + 2 + lane * cpl + e) : 0.0f;
         }
         if (nch <= BATCH)
 #pragma unroll
