@@ -79,6 +79,10 @@ def test_quant_gemm_bit_exact(gpu, tmp_path, wtype, N, K, M):
     (64, 16, 2, 40, 260, "inf"),       # prefill kernel: GQA 8, -inf above the diagonal
     (64, 4, 4, 70, 64, "random"),      # prefill kernel: one chunk, finite random mask
     (128, 32, 8, 9, 700, "causal"),    # split-KV kernel (fewer than 16 rows)
+    (128, 32, 8, 1, 768, "causal"),    # one decode row: clusters of 12 chunks, merged in shared memory
+    (64, 8, 2, 1, 130, "inf"),         # one row, 3 chunks (ragged), hidden keys
+    (128, 8, 8, 1, 1024, "none"),      # one row, 16 chunks: the largest cluster
+    (128, 32, 8, 1, 1100, "causal"),   # one row, 18 chunks: the split-KV kernel's global merge
 ])
 def test_flash_attn_bit_exact(gpu, tmp_path, D, H, HKV, NQ, NKV, mask):
     """flash_attn as a one-node program against the oracle, bit for bit, through the prefill kernel
@@ -102,8 +106,8 @@ def test_flash_attn_bit_exact(gpu, tmp_path, D, H, HKV, NQ, NKV, mask):
             m = rng.standard_normal((NQ, NKV), dtype=np.float32) * 2
         else:
             hide = np.float32(-65504.0) if mask == "causal" else np.float32(-np.inf)
-            for i in range(NQ):
-                m[i, NKV - NQ + i + 1:] = hide
+            for i in range(NQ):  # a decode row sees the first two thirds of the cache
+                m[i, (NKV - NQ + i if NQ > 1 else 2 * NKV // 3) + 1:] = hide
         ins.append(("mask", "f16", [NKV, NQ, 1, 1], [1, 1, NQ, NKV]))
         feed["mask"] = m.astype(np.float16)[None, None]
     prog = single_node_program("flash_attn", ins, [n for n, *_ in ins], "f32", [D, H, NQ, 1], [1, NQ, H, D],
