@@ -294,7 +294,9 @@ bool flash_cluster_fits(void (*kern)(SplitArgs), cudaLaunchConfig_t cfg, size_t 
     const auto key = std::make_pair((void *)kern, std::make_pair(smem, size));
     auto it = known.find(key);
     if (it != known.end()) return it->second;
-    bool ok = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess;
+    // the kernel's limit, not this size: one instantiation serves configurations of several sizes
+    bool ok = smem <= 227 * 1024 &&
+              cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) == cudaSuccess;
     if (ok && size > 8) ok = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
     int clusters = 0;
     cfg.numAttrs = 2;
