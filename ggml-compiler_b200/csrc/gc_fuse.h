@@ -33,6 +33,7 @@ struct GemvExtras {
     float act_eps = 0.0f;
     int *act_cnt = nullptr;
     int hold_pieces = 0;
+    int producer_waits = 0;
 };
 
 struct PlanStep {

@@ -79,6 +79,9 @@ struct FusedArgs {
     // done before issuing the rest, so that the prologue's loads do not queue behind the ring's
     // fill. 0: no wait.
     int hold_pieces = 0;
+    // The producer waits for the previous kernel to complete (griddepcontrol.wait) before it
+    // streams, instead of streaming during that kernel's latency-bound tail.
+    int producer_waits = 0;
 };
 
 namespace k {

@@ -120,6 +120,7 @@ void Model::load(const char *path, int backend, int dev, bool allow_cpu_fallback
     if (const char *g = std::getenv("GCB_STREAM_EVICT_FIRST")) stream_evict_first = std::atoi(g) != 0;
     if (const char *g = std::getenv("GCB_ACT_HANDOFF")) act_handoff = std::atoi(g);
     if (const char *g = std::getenv("GCB_PROLOGUE_HOLD")) prologue_hold = std::atoi(g);
+    if (const char *g = std::getenv("GCB_PRODUCER_WAIT_AFTER_ATTN")) producer_wait_after_attn = std::atoi(g);
     if (const char *g = std::getenv("GCB_KV_PREFETCH")) kv_prefetch = std::atoi(g) != 0;
 
     load_weights();

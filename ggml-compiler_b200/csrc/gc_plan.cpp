@@ -153,6 +153,7 @@ void Planner::add_gemv(const char *kind, const std::string &node, std::vector<TD
             a.act_eps = pf->act_eps;
             a.act_cnt = pf->act_cnt;
             a.hold_pieces = pf->hold_pieces;
+            a.producer_waits = pf->producer_waits;
             k::fused_gemv(a, st, true);
         },
         bytes);
@@ -721,6 +722,7 @@ void Planner::finish() {
         pf = GemvExtras{};
         pf.evict_first = m.stream_evict_first ? 1 : 0;
         pf.hold_pieces = m.prologue_hold;
+        if (gi[x] > 0 && std::string(psteps[gi[x] - 1].kind) == "flash_attn") pf.producer_waits = m.producer_wait_after_attn;
         // a one-row attention step right after: its K and V cache rows into L2 while this GEMV
         // streams (the attention's bulk copies then read L2)
         if (m.kv_prefetch && gi[x] + 1 < psteps.size() && psteps[gi[x] + 1].attn_act) {

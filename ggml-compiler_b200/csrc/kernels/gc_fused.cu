@@ -51,6 +51,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
     if (warp == NCW) {  // producer
         if (lane != 0) return;
         if (a.trace) a.trace[blockIdx.x * 8 + 0] = global_ns();
+        if (a.producer_waits) pdl_wait();
         uint32_t t = 0;
         if (!produce_gemv(a, G, R, t, blockIdx.x, gridDim.x, gemv_chunk(M, 1, CG), a.hold_pieces > 0 ? hold : nullptr)) {
             if (a.err) atomicExch(a.err, 2);
