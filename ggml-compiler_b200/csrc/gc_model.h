@@ -169,8 +169,10 @@ struct Model {
     // merge; bit 1: a residual GEMV's last CTA, normed; bit 2: the SwiGLU GEMV per block). Bit 1
     // measured slower (its serial tail), so the default is 5.
     int act_handoff = 5;
-    int prologue_hold = 0;
-    int producer_wait_after_attn = 0;  // GCB_PRODUCER_WAIT_AFTER_ATTN=1: FusedArgs::producer_waits after attention    // GCB_PROLOGUE_HOLD: FusedArgs::hold_pieces of the single-row GEMVs
+    int prologue_hold = 3;
+    // GCB_PRODUCER_WAIT_AFTER_ATTN: the GEMV after attention streams only once attention completed
+    // (1), or is launched without programmatic dependent launch at all (2)
+    int producer_wait_after_attn = 0;    // GCB_PROLOGUE_HOLD: FusedArgs::hold_pieces of the single-row GEMVs
     bool kv_prefetch = false;  // GCB_KV_PREFETCH=1: a GEMV before one-row attention prefetches its K/V into L2
     bool stream_evict_first = true;  // GCB_STREAM_EVICT_FIRST=0: GEMV weight streams without the L2 evict-first policy
     std::map<std::string, KernelStat> kstats;

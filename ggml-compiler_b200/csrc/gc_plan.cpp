@@ -154,7 +154,7 @@ void Planner::add_gemv(const char *kind, const std::string &node, std::vector<TD
             a.act_cnt = pf->act_cnt;
             a.hold_pieces = pf->hold_pieces;
             a.producer_waits = pf->producer_waits;
-            k::fused_gemv(a, st, true);
+            k::fused_gemv(a, st, pf->producer_waits < 2);
         },
         bytes);
     psteps.back().gemv = b2;
