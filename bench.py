@@ -403,6 +403,9 @@ def main() -> None:
                     help="N>1: N independent sequences (replicas), or one sequence tensor-parallel over the N GPUs (tp)")
     ap.add_argument("--cpu-tokens", type=int, default=12)  # about 10 s of the oracle on 16 host threads
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="decode only: prefill and warm up, then run this many device-loop decode steps between "
+                         "cudaProfilerStart/Stop (for `ncu --profile-from-start off`) and exit without a JSON line")
     args = ap.parse_args()
 
     if args.config == "sweep":
@@ -506,6 +509,14 @@ def decode_bench(args) -> None:
     # warm-up: prefill + W device-loop steps (plans and graphs for the decode n_kv)
     first = prefill()
     generate(first, W)
+    if args.profile_steps:
+        first = prefill()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        generate(first, args.profile_steps)
+        torch.cuda.profiler.stop()
+        m.close()
+        return
 
     # timed: K decode steps in the device loop, inputs resident
     barrier()
