@@ -503,6 +503,48 @@ int ggml_compiler_b200_write_value(ggml_compiler_model *mm, const char *name, co
     return copy_value(mm, name, const_cast<void *>(src), nbytes, false);
 }
 
+int ggml_compiler_b200_seq_slots(ggml_compiler_model *mm, int n) {
+    return guarded(
+        [&]() {
+            if (!mm) throw std::runtime_error("NULL model");
+            mm->m.seq_slots(n);
+            return 0;
+        },
+        -1);
+}
+
+int ggml_compiler_b200_seq_copy(ggml_compiler_model *mm, int dst, int src) {
+    return guarded(
+        [&]() {
+            if (!mm) throw std::runtime_error("NULL model");
+            mm->m.seq_copy(dst, src);
+            return 0;
+        },
+        -1);
+}
+
+int ggml_compiler_b200_decode_batch(ggml_compiler_model *mm, const char *entry, int n, const int32_t *tokens,
+                                    const int32_t *positions, float *logits, int32_t *next) {
+    return guarded(
+        [&]() {
+            if (!mm || !entry) throw std::runtime_error("NULL argument");
+            mm->m.decode_batch(entry, n, tokens, positions, logits, next);
+            return 0;
+        },
+        -1);
+}
+
+int ggml_compiler_b200_generate_batch(ggml_compiler_model *mm, const char *entry, int n, const int32_t *first,
+                                      const int32_t *start, int steps, int32_t *out) {
+    return guarded(
+        [&]() {
+            if (!mm || !entry) throw std::runtime_error("NULL argument");
+            mm->m.generate_batch(entry, n, first, start, steps, out);
+            return 0;
+        },
+        -1);
+}
+
 int ggml_compiler_b200_n_kernel_stats(const ggml_compiler_model *mm) { return mm ? (int)mm->m.kstats.size() : -1; }
 
 int ggml_compiler_b200_kernel_stats(const ggml_compiler_model *mm, int i, const char **kind, double *ms, int *launches,

@@ -188,7 +188,7 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
     fp.group_of.assign(s.nodes.size(), -1);
     if (std::getenv("GGML_COMPILER_B200_NOFUSE")) return fp;
     Graph g(s);
-    auto claim = [&](std::vector<int> nodes, std::function<void(Planner &)> emit) {
+    auto claim = [&](std::vector<int> nodes, std::function<void(Planner &)> emit, std::shared_ptr<GroupDesc> desc) {
         for (int x : nodes)
             if (fp.group_of[(size_t)x] >= 0) return false;
         FusionGroup grp;
@@ -197,6 +197,7 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
         for (int x : nodes) grp.nodes.push_back((size_t)x);
         grp.anchor = (size_t)nodes.front();
         grp.emit = std::move(emit);
+        grp.desc = std::move(desc);
         const int gid = (int)fp.groups.size();
         for (int x : nodes) fp.group_of[(size_t)x] = gid;
         fp.groups.push_back(std::move(grp));
@@ -351,7 +352,20 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
                 pl.env[qid] = qb;
                 pl.env[kid] = tkc;
                 pl.env[vid] = tvc;
-            });
+            }, [&] {
+                auto ds = std::make_shared<GroupDesc>();
+                ds->kind = GroupDesc::QKV;
+                ds->x = xname;
+                ds->norm_w = wname;
+                ds->w[0] = wqn, ds->w[1] = wkn, ds->w[2] = wvn;
+                ds->pos = pos;
+                ds->kc = kc, ds->vc = vc;
+                ds->out[0] = qid, ds->out[1] = kid, ds->out[2] = vid;
+                ds->eps = eps, ds->base = base;
+                ds->d = d, ds->N = (H + 2 * Hkv) * D;
+                ds->D = D, ds->H = H, ds->Hkv = Hkv;
+                return ds;
+            }());
             continue;
         }
 
@@ -417,7 +431,17 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
                        },
                        bytes);
                 pl.env[swid] = hb;
-            });
+            }, [&] {
+                auto ds = std::make_shared<GroupDesc>();
+                ds->kind = GroupDesc::GLU;
+                ds->x = xname;
+                ds->norm_w = wname;
+                ds->w[0] = wgn, ds->w[1] = wun;
+                ds->out[0] = swid;
+                ds->eps = eps;
+                ds->d = d, ds->N = F;
+                return ds;
+            }());
             continue;
         }
 
@@ -452,7 +476,17 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
                        },
                        bytes);
                 pl.env[mid] = yb;
-            });
+            }, [&] {
+                auto ds = std::make_shared<GroupDesc>();
+                ds->kind = GroupDesc::HEAD;
+                ds->x = xname;
+                ds->norm_w = wname;
+                ds->w[0] = wn;
+                ds->out[0] = mid;
+                ds->eps = eps;
+                ds->d = d, ds->N = N;
+                return ds;
+            }());
         }
     }
 
@@ -505,7 +539,16 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
                    },
                    bytes);
             pl.env[aid] = yb;
-        });
+        }, [&] {
+            auto ds = std::make_shared<GroupDesc>();
+            ds->kind = GroupDesc::RESID;
+            ds->x = xn;
+            ds->res = resn;
+            ds->w[0] = wn;
+            ds->out[0] = aid;
+            ds->d = K, ds->N = N;
+            return ds;
+        }());
     }
     return fp;
 }

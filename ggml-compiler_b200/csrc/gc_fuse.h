@@ -63,6 +63,7 @@ struct Planner {
     std::vector<Storage> storages;
     std::vector<PlanStep> psteps;
     int cur = 0;
+    bool copy_results = true;  // finish() copies the stage's results into their driver values
     std::set<int> head_sharded;  // tensor parallel: storages holding only this rank's query heads
     // GGML_COMPILER_B200_TRACE: launches that record per-CTA stamps, and where (filled by finish)
     struct TraceReq {
@@ -94,11 +95,29 @@ struct Planner {
     void finish();
 };
 
+// What a matched group computes, by the names of what it reads and defines, independent of the
+// token count it was matched at (the batched decode step re-plans groups for several sequences).
+struct GroupDesc {
+    enum Kind { QKV, GLU, HEAD, RESID } kind = RESID;
+    std::string x;         // activation rows (a node id or stage parameter)
+    std::string norm_w;    // QKV / GLU / HEAD: the rms_norm weight
+    std::string w[3];      // weights: q, k, v / gate, up / the one matrix
+    std::string res;       // RESID: the residual rows
+    std::string pos;       // QKV: the positions parameter
+    std::string kc, vc;    // QKV: the K and V cache parameters
+    std::string out[3];    // QKV: rope(q), set_rows(k), set_rows(v); otherwise out[0]
+    float eps = 0.0f, base = 0.0f;
+    int64_t d = 0;         // input width
+    int64_t N = 0;         // output width
+    int64_t D = 0, H = 0, Hkv = 0;
+};
+
 // A set of node groups, each emitted as fused launches at its anchor (its last node).
 struct FusionGroup {
     std::vector<size_t> nodes;
     size_t anchor = 0;
     std::function<void(Planner &)> emit;  // plans the launches and defines the group's visible outputs
+    std::shared_ptr<GroupDesc> desc;
 };
 
 struct FusionPlan {

@@ -56,6 +56,9 @@ struct FusedArgs {
     int64_t ldq = 0;
     char *kcache = nullptr, *vcache = nullptr;
     int64_t cache_nb1 = 0, cache_nb2 = 0, cache_rows = 0;
+    // bytes between the caches of consecutive activation rows: 0 when every row is a token of one
+    // sequence; a sequence slot's size when row m is sequence m of a batched decode step
+    int64_t cache_nb3 = 0;
     const int32_t *pos = nullptr;
     const float *table = nullptr;
     int64_t npos = 0;

@@ -7,6 +7,7 @@
 // are only viewed row for row).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -117,6 +118,11 @@ void loop_begin(const LoopDev &L, cudaStream_t s);
 // `use_cond`: also set `cond` (the loop's WHILE node) for the next iteration.
 void loop_end(const LoopDev &L, cudaGraphConditionalHandle cond, bool use_cond, cudaStream_t s);
 void loop_guard(const LoopDev &L, cudaGraphConditionalHandle cond, cudaStream_t s);
+// Batched decode bookkeeping (kernels/gc_loop.cu): the causal mask of each sequence's row
+// ([n][window] f16: 0 for keys up to pos[i], -inf after), and one greedy step's hand-over (tok :=
+// next, pos += 1, out[step][i] := next, step += 1).
+void batch_mask(__half *mask, const int32_t *pos, int n, int64_t window, cudaStream_t s);
+void batch_advance(int32_t *tok, int32_t *pos, const int32_t *next, int32_t *out, int32_t *step, int n, cudaStream_t s);
 
 // mul_mat(a, b): out[n, m, i2, i3] = sum_k a[k, n, i2/r2, i3/r3] * b[k, m, i2, i3].
 // `scratch` must hold mul_mat_scratch_bytes(a, b) bytes.

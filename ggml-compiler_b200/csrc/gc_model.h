@@ -103,6 +103,33 @@ struct LoopRuntime {
     }
 };
 
+// Batched decode (gc_batch.cpp; an extension: the reference decodes one sequence). Sequence slots
+// hold copies of the program's state values (its KV caches); one batched step runs the decode
+// stage's fused groups for n sequences at once, sequence i in slot i at its own position, so each
+// weight stream serves up to 8 rows. Plans are kept per (entry, n, attention window).
+struct BatchRuntime {
+    static constexpr int kMaxSeq = 16;
+    static constexpr size_t kMaxPlans = 8;
+    int n_seq = 0;
+    std::unordered_map<std::string, DevBuf> slots;  // state value -> n_seq copies, back to back
+    DevBuf io;       // tok[16], pos[16], next[16], step, then the mask rows
+    int32_t *tok = nullptr, *pos = nullptr, *next = nullptr, *step = nullptr;
+    __half *mask = nullptr;   // [kMaxSeq][max_window]
+    int64_t max_window = 0;   // rows of the smallest KV cache
+    DevBuf logits_buf;        // [kMaxSeq][vocab] f32, made with the first plan
+    int64_t vocab = 0;
+    DevBuf gen;  // generated tokens, [steps][n]
+    struct Plan {
+        std::string entry;
+        int n = 0;
+        int64_t window = 0;
+        std::unique_ptr<SitePlan> site;
+        uint64_t last_use = 0;
+    };
+    std::vector<Plan> plans;
+    uint64_t clock = 0;
+};
+
 struct Weight {
     TD td;
     DevBuf data, scales;
@@ -188,6 +215,18 @@ struct Model {
     std::vector<std::string> profile_lines;
     uint64_t plan_clock = 0;  // orders plan uses (least recently used plan of a site is dropped)
     TpGroup tp;
+    std::unique_ptr<BatchRuntime> batch;
+
+    // Batched decode (gc_batch.cpp). seq_slots allocates n zeroed slots (dropping earlier ones);
+    // seq_copy copies the state between slots, -1 naming the model's own state (what the entries
+    // read and write). decode_batch runs one step for sequences 0..n-1 (tok / pos host arrays):
+    // logits [n][vocab] and greedy tokens [n] to host memory when non-null. generate_batch runs
+    // `steps` greedy steps from first / start, with no host round trip between steps, and writes
+    // the tokens [steps][n].
+    void seq_slots(int n);
+    void seq_copy(int dst, int src);
+    void decode_batch(const std::string &entry, int n, const int32_t *tok, const int32_t *pos, float *logits, int32_t *next);
+    void generate_batch(const std::string &entry, int n, const int32_t *first, const int32_t *start, int steps, int32_t *out);
 
     ~Model();
     // Tensor parallelism: allocate and export this rank's window (before any run), then map every
@@ -225,6 +264,9 @@ struct Model {
     void launch_plan(SitePlan &p, int stage_index);
     void run_loop(const LoopSpec &loop);
     void write_trace();
+    BatchRuntime::Plan &batch_plan(const std::string &entry, int n, int64_t window);
+    void batch_launch(SitePlan &p);
+    void batch_check_error(const char *what);
 };
 
 // Plans one stage call for the current binding into kernel launches (gc_plan.cpp).

@@ -639,7 +639,7 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
 void Planner::finish() {
     // stage results into their driver values, after every other launch
     cur = (int)s.nodes.size();
-    for (size_t i = 0; i < s.outputs.size(); i++) {
+    for (size_t i = 0; copy_results && i < s.outputs.size(); i++) {
         auto it = env.find(s.outputs[i]);
         if (it == env.end()) throw std::runtime_error("stage '" + s.name + "' returns unknown value '" + s.outputs[i] + "'");
         const TD r = it->second;

@@ -439,7 +439,7 @@ __device__ __forceinline__ void gemv_epi_store(const FusedArgs &a, int mat, int 
                 qo[i] = y0;
                 qo[i + half] = y1;
             } else if (p >= 0 && p < a.cache_rows) {
-                char *base = (mat == 1 ? a.kcache : a.vcache) + p * a.cache_nb1 + h * a.cache_nb2;
+                char *base = (mat == 1 ? a.kcache : a.vcache) + m * a.cache_nb3 + p * a.cache_nb1 + h * a.cache_nb2;
                 ((__half *)base)[i] = __float2half_rn(y0);
                 ((__half *)base)[i + half] = __float2half_rn(y1);
             } else if (a.err) {

@@ -9,8 +9,13 @@
 //                and, inside a conditional WHILE graph node, the node's condition for the next
 //                iteration: not stopped and i below LoopDev::end.
 // loop_guard sets the condition before the WHILE node runs its first iteration.
+//
+// The batched decode step's two kernels live here too: the per-sequence causal mask rows, built
+// from the positions at the start of each step, and the greedy hand-over between steps.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <stdexcept>
 #include <string>
 
@@ -67,7 +72,41 @@ __global__ void loop_guard_kernel(const int32_t *iter, const int32_t *stop, cons
     cudaGraphSetConditional(cond, *stop == 0 && *iter < *end ? 1u : 0u);
 }
 
+__global__ void batch_mask_kernel(__half *mask, const int32_t *pos, int n, int64_t window) {
+    const __half zero = __float2half_rn(0.0f), ninf = __ushort_as_half((unsigned short)0xfc00u);
+    for (int b = blockIdx.y; b < n; b += gridDim.y) {
+        const int64_t p = pos[b];
+        for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < window; j += (int64_t)gridDim.x * blockDim.x)
+            mask[(int64_t)b * window + j] = j <= p ? zero : ninf;
+    }
+}
+
+__global__ void batch_advance_kernel(int32_t *tok, int32_t *pos, const int32_t *next, int32_t *out, int32_t *step, int n) {
+    const int i = threadIdx.x;
+    const int32_t s = *step;
+    __syncthreads();  // every thread has read the step before thread 0 moves it
+    if (i < n) {
+        tok[i] = next[i];
+        pos[i] += 1;
+        if (out) out[(int64_t)s * n + i] = next[i];
+    }
+    if (i == 0) *step = s + 1;
+}
+
 }  // namespace
+
+void batch_mask(__half *mask, const int32_t *pos, int n, int64_t window, cudaStream_t s) {
+    const unsigned bx = (unsigned)std::min<int64_t>((window + 255) / 256, 16);
+    batch_mask_kernel<<<dim3(bx, (unsigned)n), 256, 0, s>>>(mask, pos, n, window);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) throw std::runtime_error(std::string("batch_mask launch: ") + cudaGetErrorString(e));
+}
+
+void batch_advance(int32_t *tok, int32_t *pos, const int32_t *next, int32_t *out, int32_t *step, int n, cudaStream_t s) {
+    batch_advance_kernel<<<1, 32, 0, s>>>(tok, pos, next, out, step, n);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) throw std::runtime_error(std::string("batch_advance launch: ") + cudaGetErrorString(e));
+}
 
 void loop_begin(const LoopDev &L, cudaStream_t s) {
     loop_begin_kernel<<<1, 256, 0, s>>>(L);

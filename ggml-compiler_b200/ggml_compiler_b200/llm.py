@@ -95,6 +95,19 @@ class Decoder:
         """Appends one token; the logits after it ([vocab])."""
         return self._call([int(token)])[-1]
 
+    def fill_slots(self, prompts: Sequence[Sequence[int]]) -> tuple[np.ndarray, np.ndarray]:
+        """Batched decode set-up: gives the model one sequence slot per prompt, prefills prompt i in
+        the model's own state and copies that state into slot i. Returns each sequence's greedy
+        first token and its next position (the inputs of `Model.generate_batch`)."""
+        self.model.seq_slots(len(prompts))
+        first, start = [], []
+        for i, p in enumerate(prompts):
+            self.restart()
+            first.append(int(np.argmax(self.prompt(p))))
+            start.append(self.ctx)
+            self.model.seq_copy(i, -1)
+        return np.asarray(first, np.int32), np.asarray(start, np.int32)
+
     def greedy(self, prompt: Sequence[int], n: int, stop: Sequence[int] | None = None,
                on_device: bool = False) -> list[int]:
         """Up to `n` greedy tokens after `prompt` from an empty context, ending early at a stop id

@@ -73,6 +73,9 @@ def _prototypes() -> dict[str, tuple[Any, list[Any]]]:
         "b200_tp_init": (i32, [vp, i32, i32, sz, vp, sz]), "b200_tp_connect": (i32, [vp, vp, sz]),
         "b200_value_bytes": (i64, [vp, s]), "b200_read_value": (i32, [vp, s, vp, sz]),
         "b200_write_value": (i32, [vp, s, vp, sz]),
+        "b200_seq_slots": (i32, [vp, i32]), "b200_seq_copy": (i32, [vp, i32, i32]),
+        "b200_decode_batch": (i32, [vp, s, i32, vp, vp, vp, vp]),
+        "b200_generate_batch": (i32, [vp, s, i32, vp, vp, i32, vp]),
     }
     return {"ggml_compiler_" + k: v for k, v in proto.items()}
 
@@ -304,6 +307,51 @@ class Model:
         """Overwrites the whole device storage of value `name` with `data`'s bytes."""
         a = np.ascontiguousarray(data)
         _call("b200_write_value", self.handle, name.encode(), a.ctypes.data, a.nbytes)
+
+    # ---- batched decode (several sequences per decode step; include/ggml_compiler_b200.h)
+
+    def seq_slots(self, n: int) -> None:
+        """Gives the model n (1..16) sequence slots, each a zeroed copy of its state (the KV caches)."""
+        _call("b200_seq_slots", self.handle, n)
+
+    def seq_copy(self, dst: int, src: int) -> None:
+        """Copies the whole state from slot src to slot dst; -1 is the model's own state (the one the
+        entries use)."""
+        _call("b200_seq_copy", self.handle, dst, src)
+
+    def decode_batch(self, tokens: Any, positions: Any, entry: str = "decode") -> tuple[np.ndarray, np.ndarray]:
+        """One decode step for the sequences in slots 0..n-1: token i at position i of sequence i.
+        Returns (logits [n, vocab], greedy tokens [n])."""
+        tok = np.ascontiguousarray(np.asarray(tokens, np.int32).reshape(-1))
+        pos = np.ascontiguousarray(np.asarray(positions, np.int32).reshape(-1))
+        if tok.shape != pos.shape:
+            raise ValueError("one position per token")
+        n = tok.size
+        vocab = self._vocab()
+        logits = np.empty((n, vocab), np.float32)
+        nxt = np.empty(n, np.int32)
+        _call("b200_decode_batch", self.handle, entry.encode(), n, tok.ctypes.data, pos.ctypes.data, logits.ctypes.data,
+              nxt.ctypes.data)
+        return logits, nxt
+
+    def generate_batch(self, first: Any, start: Any, steps: int, entry: str = "decode") -> np.ndarray:
+        """`steps` greedy steps for the sequences in slots 0..n-1 from token first[i] at position
+        start[i], each step's tokens fed back on the device. Returns the tokens [steps, n]."""
+        f = np.ascontiguousarray(np.asarray(first, np.int32).reshape(-1))
+        st = np.ascontiguousarray(np.asarray(start, np.int32).reshape(-1))
+        if f.shape != st.shape:
+            raise ValueError("one start position per sequence")
+        out = np.empty((steps, f.size), np.int32)
+        _call("b200_generate_batch", self.handle, entry.encode(), f.size, f.ctypes.data, st.ctypes.data, steps,
+              out.ctypes.data)
+        return out
+
+    def _vocab(self) -> int:
+        """Rows of the decode entry's logits output."""
+        if getattr(self, "_vocab_rows", None) is None:
+            e = self.entries["decode"]
+            self._vocab_rows = int(np.prod(e.outputs[0].shape))
+        return self._vocab_rows
 
     def join_tensor_parallel(self, rank: int, world: int, all_gather: Callable[[bytes], list[bytes]],
                              window_bytes: int = 0) -> None:

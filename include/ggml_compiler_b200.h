@@ -54,6 +54,33 @@ GGML_COMPILER_API int ggml_compiler_b200_tp_init(ggml_compiler_model * m, int ra
                                                  void * handle, size_t cap);
 GGML_COMPILER_API int ggml_compiler_b200_tp_connect(ggml_compiler_model * m, const void * handles, size_t nbytes);
 
+/* Batched decode: one decode step for up to 16 sequences, each weight matrix streamed once per 8
+   sequences instead of once per sequence. No counterpart in the reference, which decodes one
+   sequence per model (ggml_compiler/llm.py:64 builds the decode entry for batch 1).
+   seq_slots gives model m n (1..16) sequence slots, each a zeroed copy of every state value (the KV
+   caches); calling it again drops the earlier slots. seq_copy copies the whole state from slot src
+   to slot dst, -1 naming the model's own state, the one the program's entries read and write: run
+   a prompt through the `prefill` entry, then copy the state into the sequence's slot.
+   decode_batch runs the stage of `entry` (normally "decode": fused decode layers, an output head)
+   for sequences 0..n-1 at once: token tokens[i] at position positions[i] of the sequence in slot i,
+   whose K/V rows are written there and whose keys 0..positions[i] are attended (the causal mask
+   the single-sequence entry takes from its caller). logits: host f32 [n][vocab] or NULL; next:
+   host i32 [n], each row's argmax, or NULL. Row i equals, bit for bit, what `entry` gives for that
+   sequence alone. Positions must lie inside the KV cache; a stage with nodes outside the fused
+   decode layer is refused.
+   generate_batch runs `steps` greedy steps from tokens first[i] at positions start[i]: every step
+   feeds each sequence's argmax back on the device, with no host round trip in between; out: host
+   i32 [steps][n] (NULL: not copied). No stop tokens: every sequence runs all steps.
+   ggml_compiler_b200_last_device_ms gives the device time of the last call. */
+GGML_COMPILER_API int ggml_compiler_b200_seq_slots(ggml_compiler_model * m, int n);
+GGML_COMPILER_API int ggml_compiler_b200_seq_copy(ggml_compiler_model * m, int dst, int src);
+GGML_COMPILER_API int ggml_compiler_b200_decode_batch(ggml_compiler_model * m, const char * entry, int n,
+                                                      const int32_t * tokens, const int32_t * positions,
+                                                      float * logits, int32_t * next);
+GGML_COMPILER_API int ggml_compiler_b200_generate_batch(ggml_compiler_model * m, const char * entry, int n,
+                                                        const int32_t * first, const int32_t * start, int steps,
+                                                        int32_t * out);
+
 /* Split-KV flash attention on caller-owned device buffers that allocates no device memory: the
    kernel the flash_attn node runs (reference: runtime/src/ops.cpp:217-240 -> ggml_flash_attn_ext,
    runtime/include/ggml_compiler_ops.h:133-135), with its scratch in a static device array of the
