@@ -331,6 +331,8 @@ def prefill_bench(args) -> None:
     for _ in range(max(3, args.warmup)):
         tok = int(np.argmax(g.step(tok)))
     pre_dev = pre_wall = dec_dev = 0.0
+    s.seq_slots(n_seq)
+    first, single = [], []
     with Clocks(0) as clk:
         for i in range(n_seq):
             g.restart()
@@ -339,9 +341,24 @@ def prefill_bench(args) -> None:
             tok = int(np.argmax(g.prompt(prompts[i].tolist())))
             pre_wall += time.perf_counter() - t0
             pre_dev += s.device_ms
+            first.append(tok)
+            s.seq_copy(i, -1)  # the sequence's prefilled state into its slot for the batched decode
+            toks = []
             for _ in range(n_dec):
                 tok = int(np.argmax(g.step(tok)))
+                toks.append(tok)
                 dec_dev += s.device_ms
+            single.append(toks)
+        # batched decode (include/ggml_compiler_b200.h): the 8 sequences in one step, greedy on the
+        # device; a warm-up call first (plans and graphs; it writes the same cache rows again)
+        start = np.full(n_seq, plen, np.int32)
+        s.generate_batch(first, start, 3)
+        got = s.generate_batch(first, start, n_dec)
+        bat_dev = s.device_ms
+    s.profile(True)  # the batched step's launches one by one, timed
+    s.generate_batch(first, start, 4)
+    kb = s.kernel_table()
+    s.profile(False)
     # profiled pass over one prefill: the GEMM kernels' share and FLOP rate
     g.restart()
     s.profile(True)
@@ -383,6 +400,15 @@ def prefill_bench(args) -> None:
         "e2e": {"value": n_seq * plen / pre_wall, "unit": "tok/s", "h2d_bytes_per_step": plen * 8 + plen * plen * 4,
                 "d2h_bytes_per_step": 4 * sh.vocab},
         "decode_tok_s": n_seq * n_dec / (dec_dev / 1000.0),
+        "batched_decode": {
+            "value": n_seq * n_dec / (bat_dev / 1000.0), "unit": "tok/s", "batch": n_seq, "steps": n_dec,
+            "ms_per_step": bat_dev / n_dec,
+            "weight_gb_s": weight_bytes(sh) / (bat_dev / n_dec / 1000.0) / 1e9,
+            "vs_batch1": (n_seq * n_dec / (bat_dev / 1000.0)) / (n_seq * n_dec / (dec_dev / 1000.0)),
+            "tokens_equal_batch1": bool(np.array_equal(np.asarray(got).T, np.asarray(single))),
+            "kernel_breakdown_ms_per_step": {k: v["ms"] / 4 for k, v in sorted(kb.items(), key=lambda kv: -kv[1]["ms"])},
+            "how": "generate_batch: one step decodes all 8 sequences (8-row GEMVs, attention over 8 KV slots), "
+                   "greedy tokens fed back on the device; device time of the 64 steps"},
         "gpu_launches": int(sum(v["launches"] for v in ks.values()) * n_seq),
         "clocks": clk.summary(),
         "kernel_breakdown_ms_per_call": {k: v["ms"] for k, v in sorted(ks.items(), key=lambda kv: -kv[1]["ms"])},

@@ -62,6 +62,10 @@ void put_weight(FusedArgs &a, int slot, const TD &w) {
     a.qtype = w.type;
 }
 
+// Bytes of M activation rows of K values in the GEMV's Q8_0 staging layout (codes, f32 block
+// scales, 8 x code sums; rounded to 128), as kernels/gc_gemv_dev.cuh gemv_act_bytes lays them out.
+size_t act_bytes(int64_t M, int64_t K) { return (size_t)((M * K + M * (K / 32) * 8 + 127) / 128 * 128); }
+
 // A value of the decode stage as the batched step holds it.
 struct BV {
     enum Kind { ROWS, CACHE, MASK, INDEX, TOKENS } kind = ROWS;
@@ -271,6 +275,32 @@ struct BatchPlanner {
         bv[x.id] = r;
     }
 
+    // Two or more rows: one launch quantizes them (normed for norm_w) into the staging layout the
+    // GEMV then copies (PRO_Q8), instead of every CTA of the GEMV repeating that work. Returns the
+    // staging buffer, or an empty descriptor for one row (the GEMV's own prologue does it).
+    TD stage_rows(const std::string &node, const TD &x, const TD *nw, float eps, int64_t K, int r0, int r1) {
+        TD act;
+        if (r1 - r0 < 2) return act;
+        p.scratch_marker(act_bytes(r1 - r0, K), &act);
+        std::vector<TD> tds = {x, act};
+        if (nw) tds.push_back(*nw);
+        const bool norm = nw != nullptr;
+        p.add("act_rows", node, tds,
+              [=](cudaStream_t st, const std::vector<TD> &td) {
+                  FusedArgs a;
+                  a.pro = norm ? PRO_NORM : PRO_ACT;
+                  a.x = (const float *)td[0].data + (int64_t)r0 * K;
+                  a.ldx = K;
+                  a.M = r1 - r0;
+                  a.K = K;
+                  if (norm) a.norm_w = (const float *)td[2].data;
+                  a.eps = eps;
+                  k::act_rows(a, td[1].data, st);
+              },
+              (double)(r1 - r0) * K * 5.25);
+        return act;
+    }
+
     // The row chunks of one fused GEMV: [r0, r1) with at most GEMV rows each.
     template <class F>
     void chunks(F &&f) {
@@ -299,10 +329,13 @@ struct BatchPlanner {
                 const char *kind = tq.type == T_Q4_0 ? "gemv_q4_0_qkv" : "gemv_q8_0_qkv";
                 chunks([&](int r0, int r1) {
                     const double bytes = qweight_bytes(tq) + qweight_bytes(tk) + qweight_bytes(tv) + 4.0 * d * (r1 - r0);
-                    p.add_gemv(kind, g.out[0], {xr.td, nw, tq, tk, tv, qb},
+                    const TD act = stage_rows(g.out[0], xr.td, &nw, eps, d, r0, r1);
+                    const bool staged = act.sid >= 0;
+                    p.add_gemv(kind, g.out[0], {xr.td, nw, tq, tk, tv, qb, act},
                                [=](const std::vector<TD> &td) {
                                    FusedArgs a;
-                                   a.pro = PRO_NORM;
+                                   a.pro = staged ? PRO_Q8 : PRO_NORM;
+                                   a.xq = staged ? td[6].data : nullptr;
                                    a.map = MAP_ROPE_QKV;
                                    a.x = (const float *)td[0].data + (int64_t)r0 * d;
                                    a.ldx = d;
@@ -367,13 +400,14 @@ struct BatchPlanner {
                                        : (w0.type == T_Q4_0 ? "gemv_q4_0_head" : "gemv_q8_0_head");
                 chunks([&](int r0, int r1) {
                     const double bytes = qweight_bytes(w0) + (glu ? qweight_bytes(w1) : 0.0) + 4.0 * (d + N) * (r1 - r0);
-                    std::vector<TD> tds = {xr.td, nw, w0};
-                    if (glu) tds.push_back(w1);
-                    tds.push_back(out);
+                    const TD act = stage_rows(g.out[0], xr.td, &nw, eps, d, r0, r1);
+                    const bool staged = act.sid >= 0;
+                    std::vector<TD> tds = {xr.td, nw, w0, glu ? w1 : w0, out, act};
                     p.add_gemv(kind, g.out[0], tds,
                                [=](const std::vector<TD> &td) {
                                    FusedArgs a;
-                                   a.pro = PRO_NORM;
+                                   a.pro = staged ? PRO_Q8 : PRO_NORM;
+                                   a.xq = staged ? td[5].data : nullptr;
                                    a.map = glu ? MAP_SWIGLU : MAP_SINGLE;
                                    a.x = (const float *)td[0].data + (int64_t)r0 * d;
                                    a.ldx = d;
@@ -383,7 +417,7 @@ struct BatchPlanner {
                                    a.eps = eps;
                                    put_weight(a, 0, td[2]);
                                    if (glu) put_weight(a, 1, td[3]);
-                                   a.out = (float *)td.back().data + (int64_t)r0 * N;
+                                   a.out = (float *)td[4].data + (int64_t)r0 * N;
                                    a.ldo = N;
                                    return a;
                                },
@@ -399,10 +433,13 @@ struct BatchPlanner {
                 TD out = alloc_rows(N);
                 const char *kind = w.type == T_Q4_0 ? "gemv_q4_0_res" : "gemv_q8_0_res";
                 chunks([&](int r0, int r1) {
-                    p.add_gemv(kind, g.out[0], {xr.td, res.td, w, out},
+                    const TD act = stage_rows(g.out[0], xr.td, nullptr, 0.0f, K, r0, r1);
+                    const bool staged = act.sid >= 0;
+                    p.add_gemv(kind, g.out[0], {xr.td, res.td, w, out, act},
                                [=](const std::vector<TD> &td) {
                                    FusedArgs a;
-                                   a.pro = PRO_ACT;
+                                   a.pro = staged ? PRO_Q8 : PRO_ACT;
+                                   a.xq = staged ? td[4].data : nullptr;
                                    a.map = MAP_SINGLE;
                                    a.x = (const float *)td[0].data + (int64_t)r0 * K;
                                    a.ldx = K;
@@ -578,6 +615,26 @@ BatchRuntime::Plan &Model::batch_plan(const std::string &entry, int n, int64_t w
 }
 
 void Model::batch_launch(SitePlan &p) {
+    if (profiling) {  // each launch on its own, timed (ggml_compiler_b200_set_profiling)
+        for (const auto &st : p.steps) {
+            cudaEvent_t a, b;
+            cuda_check(cudaEventCreate(&a), "cudaEventCreate");
+            cuda_check(cudaEventCreate(&b), "cudaEventCreate");
+            cuda_check(cudaEventRecord(a, stream), "cudaEventRecord");
+            st.run(stream);
+            cuda_check(cudaEventRecord(b, stream), "cudaEventRecord");
+            cuda_check(cudaEventSynchronize(b), "step");
+            float ms = 0;
+            cudaEventElapsedTime(&ms, a, b);
+            cudaEventDestroy(a);
+            cudaEventDestroy(b);
+            KernelStat &ks = kstats[std::string("batch_") + st.kind];
+            ks.ms += ms;
+            ks.bytes += st.bytes;
+            ks.launches++;
+        }
+        return;
+    }
     if (!use_graphs) {
         for (const auto &st : p.steps) st.run(stream);
         return;
@@ -654,6 +711,7 @@ void Model::decode_batch(const std::string &entry, int n, const int32_t *tok, co
     cuda_check(cudaEventElapsedTime(&dms, run_ev[0], run_ev[1]), "cudaEventElapsedTime");
     last_device_ms = dms;
     batch_check_error("batched decode");
+    if (!trace_path.empty()) write_trace();
 }
 
 void Model::generate_batch(const std::string &entry, int n, const int32_t *first, const int32_t *start, int steps,
@@ -700,6 +758,7 @@ void Model::generate_batch(const std::string &entry, int n, const int32_t *first
     cuda_check(cudaEventElapsedTime(&dms, run_ev[0], run_ev[1]), "cudaEventElapsedTime");
     last_device_ms = dms;
     batch_check_error("batched generate");
+    if (!trace_path.empty()) write_trace();
 }
 
 }  // namespace gcb

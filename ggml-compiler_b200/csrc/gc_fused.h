@@ -11,7 +11,7 @@
 namespace gcb {
 
 // The activation prologue: quantize the f32 row(s) (PRO_ACT), rms_norm x weight first (PRO_NORM),
-// or take Q8_0 blocks a kernel before wrote in the staging layout (PRO_Q8, one row).
+// or take Q8_0 blocks a kernel before wrote in the staging layout (PRO_Q8).
 enum { PRO_ACT = 0, PRO_NORM = 1, PRO_Q8 = 2 };
 // What a launch emits for the GEMV after it (one row): nothing, the rms_norm-ed output row's Q8_0
 // blocks (written by the launch's last CTA), or the output's own Q8_0 blocks (each written by the
@@ -30,8 +30,8 @@ struct FusedArgs {
     int64_t K = 0;
     const float *norm_w = nullptr;  // PRO_NORM
     float eps = 0.0f;
-    // PRO_Q8: the row in the consumers' staging layout (gemv_act_bytes(1, K) bytes: int8 codes [K],
-    // f32 block scales [K / 32], int 8 x code sums [K / 32]), written by the kernel before
+    // PRO_Q8: the M rows in the consumers' staging layout (gemv_act_bytes(M, K) bytes: int8 codes
+    // [M][K], f32 block scales [M][K / 32], int 8 x code sums [M][K / 32]), written by the kernel before
     const char *xq = nullptr;
     // ACT8_NORM / ACT8_BLOCKS: where this launch writes the next GEMV's row in that layout, the
     // next GEMV's norm weight and eps (ACT8_NORM), and zeroed counters the launch leaves zero (one
@@ -93,6 +93,10 @@ bool fused_gemv_supported(int64_t K, int64_t M, int map);
 // Shape preconditions of one set of arguments (the rope map needs head sizes that are multiples of 16).
 bool fused_gemv_args_ok(const FusedArgs &a);
 void fused_gemv(const FusedArgs &a, cudaStream_t s, bool pdl);
+// a's M activation rows (x, ldx, K; normed for PRO_NORM) into the PRO_Q8 staging layout for M
+// rows at dst (gemv_act_bytes(M, K) bytes), one CTA per row: the launch that reads them then only
+// copies them into shared memory.
+void act_rows(const FusedArgs &a, char *dst, cudaStream_t s);
 }  // namespace k
 
 }  // namespace gcb

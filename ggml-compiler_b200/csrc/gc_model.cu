@@ -738,33 +738,37 @@ void Model::run_entry(const std::string &name) {
 void Model::write_trace() {
     FILE *f = std::fopen(trace_path.c_str(), "w");
     if (!f) return;
-    std::vector<std::pair<const CallSite *, std::vector<uint64_t>>> all;
+    std::vector<std::pair<std::string, const SitePlan *>> plans;  // every current plan with stamps
+    for (const auto &c : calls)
+        for (const auto &p : c.plans)
+            if (p->trace.size()) plans.emplace_back(c.stage->name, p.get());
+    if (batch)
+        for (const auto &bp : batch->plans)
+            if (bp.site->trace.size())
+                plans.emplace_back("batch:" + bp.entry + "/" + std::to_string(bp.n) + "x" + std::to_string(bp.window), bp.site.get());
+    std::vector<std::vector<uint64_t>> stamps;
     uint64_t t0 = ~0ull;
-    for (const auto &c : calls)
-        for (const auto &p : c.plans) {
-            if (!p->trace.size()) continue;
-            std::vector<uint64_t> h(p->trace.size() / 8);
-            cuda_check(cudaMemcpy(h.data(), p->trace.get(), p->trace.size(), cudaMemcpyDeviceToHost), "trace");
-            for (uint64_t v : h)
-                if (v) t0 = std::min(t0, v);
-            all.emplace_back(&c, std::move(h));
-        }
-    size_t k = 0;
-    for (const auto &c : calls)
-        for (const auto &p : c.plans) {
-            if (!p->trace.size()) continue;
-            const auto &h = all[k++].second;
-            for (size_t li = 0; li < p->trace_index.size(); li++) {
-                const auto &e = p->trace_index[li];
-                for (size_t cta = 0; cta < e.ctas; cta++) {
-                    const uint64_t *st = &h[e.offset + cta * 8];
-                    if (!st[0] && !st[2]) continue;  // a CTA the launch did not have
-                    std::fprintf(f, "%s\t%zu\t%s\t%s\t%zu", c.stage->name.c_str(), li, e.kind.c_str(), e.node.c_str(), cta);
-                    for (int s = 0; s < 8; s++) std::fprintf(f, "\t%lld", st[s] ? (long long)(st[s] - t0) : -1ll);
-                    std::fprintf(f, "\n");
-                }
+    for (const auto &pp : plans) {
+        std::vector<uint64_t> h(pp.second->trace.size() / 8);
+        cuda_check(cudaMemcpy(h.data(), pp.second->trace.get(), pp.second->trace.size(), cudaMemcpyDeviceToHost), "trace");
+        for (uint64_t v : h)
+            if (v) t0 = std::min(t0, v);
+        stamps.push_back(std::move(h));
+    }
+    for (size_t k = 0; k < plans.size(); k++) {
+        const SitePlan &p = *plans[k].second;
+        const auto &h = stamps[k];
+        for (size_t li = 0; li < p.trace_index.size(); li++) {
+            const auto &e = p.trace_index[li];
+            for (size_t cta = 0; cta < e.ctas; cta++) {
+                const uint64_t *st = &h[e.offset + cta * 8];
+                if (!st[0] && !st[2]) continue;  // a CTA the launch did not have
+                std::fprintf(f, "%s\t%zu\t%s\t%s\t%zu", plans[k].first.c_str(), li, e.kind.c_str(), e.node.c_str(), cta);
+                for (int s = 0; s < 8; s++) std::fprintf(f, "\t%lld", st[s] ? (long long)(st[s] - t0) : -1ll);
+                std::fprintf(f, "\n");
             }
         }
+    }
     std::fclose(f);
 }
 

@@ -495,9 +495,12 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
             scratch_marker(k::flash_split_scratch_bytes(q, kk), &scratch);
             int *cnt = m.counters(s.name + "/" + n.id, k::flash_split_counters(q, kk));
             int *err = m.d_err;
+            const bool cluster = k::flash_split_prepare(q, kk, v, y);
+            auto tr = trace_slot("flash_attn", n.id, cluster ? (size_t)(((kk.ne[1] + 63) / 64) * kk.ne[2] * q.ne[3])
+                                                              : k::flash_split_ctas(q, kk));
             add("flash_attn", n.id, {q, kk, v, y, scratch},
-                [scale, cnt, err](cudaStream_t st, const std::vector<TD> &t) {
-                    k::flash_attn_split(t[0], t[1], t[2], nullptr, t[3], scale, t[4].data, cnt, err, st);
+                [scale, cnt, err, tr](cudaStream_t st, const std::vector<TD> &t) {
+                    k::flash_attn_split(t[0], t[1], t[2], nullptr, t[3], scale, t[4].data, cnt, err, st, *tr, nullptr);
                 },
                 bytes);
         } else {

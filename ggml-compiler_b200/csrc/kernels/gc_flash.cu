@@ -15,6 +15,7 @@
 // CTA), so no second kernel is needed. Waits are bounded; a timeout sets the error word.
 #include <cooperative_groups.h>
 
+#include <cstdio>
 #include <cstdlib>
 #include <map>
 #include <mutex>
@@ -55,12 +56,13 @@ struct SplitArgs {
     int *err;
     int64_t nch;
     uint64_t *trace;  // [CTA][8] %globaltimer stamps, or null: start, staged, past the wait, K/V landed,
-                      // done, chunk computed, past the arrival counter
+                      // done, chunk computed, past the arrival counter (the cluster kernel: past the
+                      // cluster barrier), and done again in the cluster kernel only
     char *act_out;    // one query row: its Q8_0 blocks in the GEMV staging layout (K = H x D), or null
 };
 
 template <int MAXD>
-__global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs a) {
+__global__ void __launch_bounds__(MAXG * WPH * 32, 2) flash_split_kernel(SplitArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int D = (int)a.D;
     __shared__ uint64_t bar;
@@ -190,7 +192,7 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_split_kernel(SplitArgs 
 constexpr int FL_CLUSTER_MAX = 16;
 
 template <int MAXD>
-__global__ void __launch_bounds__(MAXG * WPH * 32) flash_cluster_kernel(SplitArgs a) {
+__global__ void __launch_bounds__(MAXG * WPH * 32, 2) flash_cluster_kernel(SplitArgs a) {
     namespace cg = cooperative_groups;
     extern __shared__ __align__(128) unsigned char smem[];
     const cg::cluster_group cluster = cg::this_cluster();
@@ -272,7 +274,7 @@ __global__ void __launch_bounds__(MAXG * WPH * 32) flash_cluster_kernel(SplitArg
             flash_merge<MAXD, true>(parts + g * a.nch * (a.D + 2), (int)a.nch, a.out + a.D * (h + a.oH * b * a.Sq), qc, qd,
                                     qs8);
         }
-    if (stamps) stamps[4] = global_ns();
+    if (stamps) stamps[4] = stamps[7] = global_ns();  // [7]: set only by the cluster kernel
 }
 
 constexpr size_t kMaxPartBytes = 256u << 20;  // scratch for chunk partials per row group
@@ -294,13 +296,38 @@ bool flash_cluster_fits(void (*kern)(SplitArgs), cudaLaunchConfig_t cfg, size_t 
     const auto key = std::make_pair((void *)kern, std::make_pair(smem, size));
     auto it = known.find(key);
     if (it != known.end()) return it->second;
-    // the kernel's limit, not this size: one instantiation serves configurations of several sizes
-    bool ok = smem <= 227 * 1024 &&
-              cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) == cudaSuccess;
-    if (ok && size > 8) ok = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+    // the kernel's limit, not this size: one instantiation serves configurations of several sizes.
+    // The limit is the device's opt-in maximum less the kernel's static shared memory (asking for
+    // the whole 227 KiB fails, and the cluster kernel then never ran).
+    cudaFuncAttributes fa{};
+    int dev = 0, optin = 0;
+    bool ok = cudaFuncGetAttributes(&fa, kern) == cudaSuccess && cudaGetDevice(&dev) == cudaSuccess &&
+              cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) == cudaSuccess;
+    const size_t maxdyn = ok && (size_t)optin > fa.sharedSizeBytes ? (size_t)optin - fa.sharedSizeBytes : 0;
+    ok = ok && smem <= maxdyn;
+    if (ok) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)maxdyn);
+        if (e == cudaSuccess && size > 8) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess)
+            std::fprintf(stderr, "ggml_compiler_b200: cluster attention (%d CTAs) unavailable: %s\n", size, cudaGetErrorString(e));
+        ok = e == cudaSuccess;
+    }
+    // the occupancy query takes the cluster shape alone (with the launch's programmatic-serialization
+    // attribute in the list it fails, which read as "does not fit")
+    cudaLaunchAttribute ca[1];
+    ca[0].id = cudaLaunchAttributeClusterDimension;
+    ca[0].val.clusterDim.x = (unsigned)size;
+    ca[0].val.clusterDim.y = 1;
+    ca[0].val.clusterDim.z = 1;
+    cfg.attrs = ca;
+    cfg.numAttrs = 1;
     int clusters = 0;
-    cfg.numAttrs = 2;
-    if (ok) ok = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) == cudaSuccess && clusters >= 1;
+    if (ok) {
+        const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+        if (e != cudaSuccess)  // not a "does not fit" answer: say why the split kernel runs instead
+            std::fprintf(stderr, "ggml_compiler_b200: cluster attention (%d CTAs) unavailable: %s\n", size, cudaGetErrorString(e));
+        ok = e == cudaSuccess && clusters >= 1;
+    }
     cudaGetLastError();
     known[key] = ok;
     return ok;

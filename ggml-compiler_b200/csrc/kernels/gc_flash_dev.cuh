@@ -207,7 +207,7 @@ struct SyncCta {
 // chunks at once.
 // LOCAL: the partials are in this CTA's shared memory (plain loads) rather than global memory
 // written by other CTAs (L2 loads).
-template <int D, bool LOCAL = false, int BATCH = (D <= 128 ? 16 : 8)>  // BATCH: chunks fetched at once
+template <int D, bool LOCAL = false, int BATCH = 4>  // BATCH: chunks fetched at once
 __device__ inline void flash_merge(const float *pp, int nch, float *orow, int8_t *qcodes = nullptr, float *qd = nullptr,
                                    int *qs8 = nullptr) {
     auto ld = [](const float *p) { return LOCAL ? *p : __ldcg(p); };

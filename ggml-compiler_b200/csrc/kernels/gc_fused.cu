@@ -23,8 +23,11 @@ constexpr int NTHREADS = (NCW + 1) * 32;
 constexpr int MAXNS = 16;
 constexpr int CG = 2;  // row groups per chunk with one activation row (gc_gemv_dev.cuh)
 
+// One activation row: two CTAs per SM (96 registers). More rows: one CTA per SM, so the M x NR
+// accumulators and the rows' operands stay in registers (at two per SM they spilled to local
+// memory), with the whole shared memory for the staged rows and the ring.
 template <int QT, int NR, int M>
-__global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, GemvGeo G, int ns, uint32_t magic, int slot_bytes) {
+__global__ void __launch_bounds__(NTHREADS, M == 1 ? 2 : 1) gemv_tma_kernel(FusedArgs a, GemvGeo G, int ns, uint32_t magic, int slot_bytes) {
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t *full = (uint64_t *)smem;
     uint64_t *empty = full + MAXNS;
@@ -67,7 +70,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
     pdl_wait();
     const bool stamp = a.trace && threadIdx.x == 0;
     if (stamp) a.trace[blockIdx.x * 8 + 2] = global_ns();
-    if (M == 1 && a.pro == PRO_Q8) gemv_stage_q8<NCW * 32>(a, sq, 1);
+    if (a.pro == PRO_Q8) gemv_stage_q8<NCW * 32>(a, sq, 1, M);
     else gemv_prologue<M, NCW * 32>(a, sq, sdf, ss8, red, 1, wpre);
     if (stamp) a.trace[blockIdx.x * 8 + 3] = global_ns();
     if (threadIdx.x == 0) mbar_arrive(hold);
@@ -75,6 +78,24 @@ __global__ void __launch_bounds__(NTHREADS, 2) gemv_tma_kernel(FusedArgs a, Gemv
         if (a.err) atomicExch(a.err, 2);
     if (M == 1 && a.act_mode != ACT8_NONE) gemv_emit_act8<NCW * 32>(a, G, red, 1);
     if (stamp) a.trace[blockIdx.x * 8 + 4] = global_ns();
+}
+
+// Activation rows -> Q8_0 blocks in the GEMV staging layout for M rows (gemv_act_bytes(M, K) bytes
+// at dst: codes [M][K], f32 block scales [M][K / 32], 8 x code sums [M][K / 32]), with rms_norm x
+// weight first for PRO_NORM: the consumers' prologue arithmetic, one CTA per row, done once for
+// the launch that reads it (PRO_Q8) instead of in each of its CTAs.
+__global__ void __launch_bounds__(256) act_rows_kernel(FusedArgs a, char *dst) {
+    __shared__ double red[256];
+    pdl_trigger();
+    pdl_wait();  // the rows were written by the kernel before
+    const int m = blockIdx.x, nb = (int)(a.K / 32);
+    FusedArgs r = a;
+    r.x = a.x + (int64_t)m * a.ldx;
+    r.M = 1;
+    int8_t *codes = (int8_t *)dst;
+    float *d = (float *)(dst + (size_t)a.M * a.K);
+    int *s8 = (int *)(d + (size_t)a.M * nb);
+    gemv_prologue<1, 256>(r, codes + (size_t)m * a.K, d + (size_t)m * nb, s8 + (size_t)m * nb, red, 1);
 }
 
 int g_num_sms = 0;
@@ -91,11 +112,11 @@ void launch_t(const FusedArgs &a, const GemvGeo &G, cudaStream_t s, bool pdl) {
     }
     const int slot_bytes = (int)qw_piece_bytes(G.nb, G.cb, 0);
     const size_t head = (size_t)(2 * MAXNS + 2) * 8 + 256 * 8 + gemv_act_bytes(M, a.K);
-    const size_t budget = g_smem_budget ? g_smem_budget : (g_ctas_per_sm == 2 ? 113 * 1024 : 224 * 1024);
+    const size_t budget = g_smem_budget ? g_smem_budget : (M == 1 && g_ctas_per_sm == 2 ? 113 * 1024 : 224 * 1024);
     int ns = ring_slots(budget, head, (size_t)slot_bytes, MAXNS);
     if (ns < 2 * G.pieces) ns = 2 * G.pieces;  // room for one group's pieces in flight and one consumed
     const size_t smem = head + (size_t)ns * (size_t)slot_bytes;
-    const int per_sm = smem <= 113 * 1024 ? g_ctas_per_sm : 1;
+    const int per_sm = M == 1 && smem <= 113 * 1024 ? g_ctas_per_sm : 1;
     const int64_t cap = (int64_t)g_num_sms * per_sm;
     const int64_t ctas = G.groups < cap ? (int64_t)G.groups : cap;
     cudaLaunchConfig_t cfg = {};
@@ -144,6 +165,21 @@ bool fused_gemv_supported(int64_t K, int64_t M, int map) {
     (void)map;
     if (K % 32 || M < 1 || M > GEMV_MAXM) return false;
     return gemv_act_bytes((int)M, K) <= 64 * 1024;
+}
+
+void act_rows(const FusedArgs &a, char *dst, cudaStream_t s) {
+    if (a.pro != PRO_ACT && a.pro != PRO_NORM) throw std::runtime_error("act_rows: f32 rows in (ACT or NORM prologue)");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)a.M);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, act_rows_kernel, a, dst);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("CUDA launch of act_rows failed: ") + cudaGetErrorString(e));
 }
 
 bool fused_gemv_args_ok(const FusedArgs &a) { return a.map != MAP_ROPE_QKV || (a.D / 2) % QTR == 0; }

@@ -294,11 +294,11 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
     named_bar(bar, NCT);
 }
 
-// PRO_Q8: the row's staged blocks (a.xq, gemv_act_bytes(1, K) bytes) copied into shared memory by
+// PRO_Q8: the M rows' staged blocks (a.xq, gemv_act_bytes(M, K) bytes) copied into shared memory by
 // the NCT consumer threads.
 template <int NCT>
-__device__ inline void gemv_stage_q8(const FusedArgs &a, int8_t *sq, int bar) {
-    const int n = (int)(gemv_act_bytes(1, a.K) / 16);
+__device__ inline void gemv_stage_q8(const FusedArgs &a, int8_t *sq, int bar, int M = 1) {
+    const int n = (int)(gemv_act_bytes(M, a.K) / 16);
     const int4 *src = (const int4 *)a.xq;
     int4 *dst = (int4 *)sq;
     for (int i = threadIdx.x; i < n; i += NCT) dst[i] = __ldcg(src + i);
@@ -490,8 +490,10 @@ __device__ __forceinline__ void act1_load(Act1 &x, const int8_t *sq, const float
 }
 
 // acc += this lane's blocks of one row of a piece, against the activation registers: every load of
-// the row first, then the products in block order.
-template <int QT>
+// the row first, then the products in block order. FULL: a whole segment (sb == QSEG), so every
+// lane has all GEMV_NI blocks and no bound is tested; the integer dots of the blocks are then
+// independent straight-line code, and only the fma chain is ordered.
+template <int QT, bool FULL>
 __device__ __forceinline__ void piece_row1(float &acc, const unsigned char *codes, const uint16_t *scl, const Act1 &x,
                                            int sb, int lane) {
     constexpr int CB = QT == 0 ? 16 : 32;
@@ -500,7 +502,7 @@ __device__ __forceinline__ void piece_row1(float &acc, const unsigned char *code
 #pragma unroll
     for (int i = 0; i < GEMV_NI; i++) {
         const int j = lane + 32 * i;
-        if (j < sb) {
+        if (FULL || j < sb) {
             w0[i] = *(const int4 *)(codes + j * CB);
             if (QT == 1) w1[i] = *(const int4 *)(codes + j * CB + 16);
             sw[i] = scl[j];
@@ -508,7 +510,7 @@ __device__ __forceinline__ void piece_row1(float &acc, const unsigned char *code
     }
 #pragma unroll
     for (int i = 0; i < GEMV_NI; i++) {
-        if (lane + 32 * i >= sb) break;
+        if (!FULL && lane + 32 * i >= sb) break;
         int v = 0;
         if (QT == 0) {
             // low nibbles as they are; high nibbles masked in place (16 x their value), so that dot
@@ -585,8 +587,12 @@ __device__ inline bool consume_gemv1(const FusedArgs &a, const GemvGeo &G, const
                     const uint32_t t = tb + (uint32_t)((s * n + q) * G.pieces + r);
                     if (!gemv_wait_piece(R, t)) return false;
                     const unsigned char *piece = R.data(t);
-                    piece_row1<QT>(acc[j][r], piece + wt * sb * CB, (const uint16_t *)(piece + QTR * sb * CB) + wt * sb,
-                                   x, sb, lane);
+                    if (sb == QSEG)
+                        piece_row1<QT, true>(acc[j][r], piece + wt * QSEG * CB, (const uint16_t *)(piece + QTR * QSEG * CB) + wt * QSEG,
+                                             x, QSEG, lane);
+                    else
+                        piece_row1<QT, false>(acc[j][r], piece + wt * sb * CB, (const uint16_t *)(piece + QTR * sb * CB) + wt * sb,
+                                              x, sb, lane);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&R.empty[R.slot(t)]);
                 }

@@ -73,22 +73,23 @@ def test_quant_gemm_bit_exact(gpu, tmp_path, wtype, N, K, M):
     np.testing.assert_array_equal(got, ref)
 
 
-@pytest.mark.parametrize("D,H,HKV,NQ,NKV,mask", [
-    (128, 32, 8, 300, 700, "causal"),  # prefill kernel: GQA 4, 11 chunks, -65504 above the diagonal
-    (128, 8, 8, 16, 130, "none"),      # prefill kernel: no GQA, no mask, ragged last chunk
-    (64, 16, 2, 40, 260, "inf"),       # prefill kernel: GQA 8, -inf above the diagonal
-    (64, 4, 4, 70, 64, "random"),      # prefill kernel: one chunk, finite random mask
-    (128, 32, 8, 9, 700, "causal"),    # split-KV kernel (fewer than 16 rows)
-    (128, 32, 8, 1, 768, "causal"),    # one decode row: clusters of 12 chunks, merged in shared memory
-    (64, 8, 2, 1, 130, "inf"),         # one row, 3 chunks (ragged), hidden keys
-    (128, 8, 8, 1, 1024, "none"),      # one row, 16 chunks: the largest cluster
-    (128, 32, 8, 1, 1100, "causal"),   # one row, 18 chunks: the split-KV kernel's global merge
+@pytest.mark.parametrize("D,H,HKV,NQ,NKV,mask,kernel", [
+    (128, 32, 8, 300, 700, "causal", "prefill"),  # GQA 4, 11 chunks, -65504 above the diagonal
+    (128, 8, 8, 16, 130, "none", "prefill"),      # no GQA, no mask, ragged last chunk
+    (64, 16, 2, 40, 260, "inf", "prefill"),       # GQA 8, -inf above the diagonal
+    (64, 4, 4, 70, 64, "random", "prefill"),      # one chunk, finite random mask
+    (128, 32, 8, 9, 700, "causal", "split"),      # fewer than 16 rows
+    (128, 32, 8, 1, 768, "causal", "cluster"),    # one decode row: clusters of 12 chunks
+    (64, 8, 2, 1, 130, "inf", "cluster"),         # one row, 3 chunks (ragged), hidden keys
+    (128, 8, 8, 1, 1024, "none", "cluster"),      # one row, 16 chunks: the largest cluster
+    (128, 32, 8, 1, 1100, "causal", "split"),     # one row, 18 chunks: the split kernel's global merge
 ])
-def test_flash_attn_bit_exact(gpu, tmp_path, D, H, HKV, NQ, NKV, mask):
+def test_flash_attn_bit_exact(gpu, tmp_path, monkeypatch, D, H, HKV, NQ, NKV, mask, kernel):
     """flash_attn as a one-node program against the oracle, bit for bit, through the prefill kernel
-    (16+ query rows) and the split-KV kernel; the causal masks use the reference programs' -65504 (every
-    chunk computed) or -inf (hidden chunks skipped by the merge), with rows whose keys are all hidden
-    in the later chunks."""
+    (16+ query rows), the split-KV kernel and the cluster kernel (one row, 2-16 chunks); the causal
+    masks use the reference programs' -65504 (every chunk computed) or -inf (hidden chunks skipped by
+    the merge), with rows whose keys are all hidden in the later chunks. The per-CTA trace shows
+    which decode kernel ran: only the cluster kernel records its last stamp."""
     from ggml_compiler_b200.gguf_write import write_gguf
     from ggml_compiler_b200.programs import single_node_program
     from oracle.interp import Program
@@ -114,8 +115,15 @@ def test_flash_attn_bit_exact(gpu, tmp_path, D, H, HKV, NQ, NKV, mask):
                                {"scale": float(1.0 / np.sqrt(D))})
     path = tmp_path / "fa.gguf"
     write_gguf(path, prog, [])
+    trace = tmp_path / "trace.tsv"
+    monkeypatch.setenv("GGML_COMPILER_B200_TRACE", str(trace))
     with Model(path) as m:
         got = m.entries["main"](**feed)["out.0"]
     want = Program(path).run("main", **feed)["out.0"]
     assert np.isfinite(got).all()
     np.testing.assert_array_equal(got, want)
+    if kernel != "prefill":
+        rows = [line.split("\t") for line in trace.read_text().splitlines() if "\tflash_attn\t" in line]
+        assert rows, "no flash_attn stamps"
+        cluster = {int(r[12]) >= 0 for r in rows}
+        assert cluster == {kernel == "cluster"}, f"expected the {kernel} kernel"
