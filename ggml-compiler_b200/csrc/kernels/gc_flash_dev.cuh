@@ -49,6 +49,29 @@ __device__ inline void flash_stage(const FlashChunk &c, float *qs, float *ms, in
     }
 }
 
+// f16 operands straight into f32 arithmetic on the FMA pipe (no f16 -> f32 conversions, which run on
+// the narrower XU pipe and bounded the chunk's time). fma.rn.f32.f16 forms the exact product of
+// the two halves and adds c with one rounding: the same result as converting both halves to f32
+// (exact) and one __fmaf_rn.
+// acc = fma(q.lo, k.lo, acc), then fma(q.hi, k.hi, acc): two consecutive elements of a row each.
+__device__ __forceinline__ float fma2_f16(uint32_t q2, uint32_t k2, float acc) {
+    asm("{\n\t.reg .f16 ql, qh, kl, kh;\n\tmov.b32 {ql, qh}, %1;\n\tmov.b32 {kl, kh}, %2;\n\t"
+        "fma.rn.f32.f16 %0, ql, kl, %0;\n\tfma.rn.f32.f16 %0, qh, kh, %0;\n\t}"
+        : "+f"(acc)
+        : "r"(q2), "r"(k2));
+    return acc;
+}
+
+// An f16 value as f32, exactly, on the FMA pipe: h x 1 + (-0) (the -0 addend keeps the sign of a
+// zero; every other value is the product itself).
+__device__ __forceinline__ float f16_to_f32_fma(uint16_t h) {
+    float d;
+    asm("{\n\t.reg .f16 one;\n\tmov.b16 one, 0x3C00;\n\tfma.rn.f32.f16 %0, %1, one, %2;\n\t}"
+        : "=f"(d)
+        : "h"(h), "f"(-0.0f));
+    return d;
+}
+
 // The lane's D/32 consecutive key elements (f16 in shared memory) as floats.
 template <int CPL>
 __device__ __forceinline__ void load_krow(const __half *kr, float (&kv)[CPL]) {
@@ -86,9 +109,19 @@ __device__ inline void flash_scores(const FlashChunk &c, const __half *Ks, const
     const bool active = g < c.G;
     const int gg = active ? g : 0;
     float *sh = sc + hw * FL_CH;
+    // the lane's query elements: as f16 pairs when a lane owns an even count (qs holds values already
+    // rounded to f16, so the conversion back is exact), else as floats
+    constexpr bool PAIRS = CPL % 2 == 0;
+    constexpr int NQ2 = PAIRS ? CPL / 2 : 1;
+    uint32_t q2[NQ2];
     float qv[CPL];
 #pragma unroll
     for (int e = 0; e < CPL; e++) qv[e] = qs[gg * D + lane * CPL + e];
+#pragma unroll
+    for (int e = 0; e < NQ2; e++)
+        q2[e] = PAIRS ? (uint32_t)__half_as_ushort(__float2half_rn(qv[2 * e])) |
+                            ((uint32_t)__half_as_ushort(__float2half_rn(qv[2 * e + 1])) << 16)
+                      : 0u;
     const float *mrow = ms + gg * FL_CH;
     // this warp's CH/WPH keys, 8 at a time
     for (int k0 = quarter * (FL_CH / WPH); k0 < (quarter + 1) * (FL_CH / WPH); k0 += 8) {
@@ -98,10 +131,16 @@ __device__ inline void flash_scores(const FlashChunk &c, const __half *Ks, const
             const int j = k0 + u;
             float acc = 0.0f;
             if (j < n) {
-                float kv[CPL];
-                load_krow<CPL>(Ks + j * D + lane * CPL, kv);
+                if constexpr (PAIRS) {
+                    const uint32_t *kr = (const uint32_t *)(Ks + j * D + lane * CPL);  // 4-byte aligned
 #pragma unroll
-                for (int e = 0; e < CPL; e++) acc = __fmaf_rn(qv[e], kv[e], acc);
+                    for (int e = 0; e < CPL / 2; e++) acc = fma2_f16(q2[e], kr[e], acc);  // elements in order
+                } else {
+                    float kv[CPL];
+                    load_krow<CPL>(Ks + j * D + lane * CPL, kv);
+#pragma unroll
+                    for (int e = 0; e < CPL; e++) acc = __fmaf_rn(qv[e], kv[e], acc);
+                }
             }
             p[u] = acc;
         }
@@ -174,7 +213,8 @@ __device__ inline void flash_values(const FlashChunk &c, const __half *Vs, const
             const __half *vr = vcol + (j0 + u) * D;
 #pragma unroll
             for (int e = 0; e < OE; e++)
-                if (D >= WPH * 32 || quarter * 32 < D) o[e] = __fmaf_rn(pj[u], __half2float(vr[e * WPH * 32]), o[e]);
+                if (D >= WPH * 32 || quarter * 32 < D)
+                    o[e] = __fmaf_rn(pj[u], f16_to_f32_fma(__half_as_ushort(vr[e * WPH * 32])), o[e]);
         }
     }
     if (quarter == 0 && lane == 0) {
