@@ -467,10 +467,25 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
     return d;
 }
 
-// This lane's blocks (lane + 32 i) of one segment of the activation row, from shared memory.
+// Conversions kept off the XU pipe (f16 -> f32 and int -> float there ran at a quarter of the FMA
+// pipe's rate and held up the block loop), with the same results:
+// - the block scale product d_w * d_x as one fma.rn.f32.f16 of the two f16 values with a -0 addend:
+//   the product of two f16 values is exact in f32, so this equals __fmul_rn of their f32 forms
+//   (the -0 keeps a zero product's sign);
+// - the integer dot as a float through the 1.5 * 2^23 bias: for |v| < 2^22 the bits 0x4B400000 + v
+//   are the float 12582912 + v, and subtracting 12582912 leaves v exactly.
+__device__ __forceinline__ float mul_f16(uint32_t a, uint32_t b) {
+    float d;
+    asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"((unsigned short)a), "h"((unsigned short)b), "f"(-0.0f));
+    return d;
+}
+__device__ __forceinline__ float i2f_exact(int v) { return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f); }
+
+// This lane's blocks (lane + 32 i) of one segment of the activation row, from shared memory; the
+// block scales as their f16 bits (the staging layout holds f16 values as f32, so this is exact).
 struct Act1 {
     int4 lo[GEMV_NI], hi[GEMV_NI];
-    float d[GEMV_NI];
+    uint32_t dh[GEMV_NI];
     int s8[GEMV_NI];
 };
 
@@ -483,7 +498,7 @@ __device__ __forceinline__ void act1_load(Act1 &x, const int8_t *sq, const float
             const int4 *x4 = (const int4 *)(sq + (bbase + j) * 32);
             x.lo[i] = x4[0];
             x.hi[i] = x4[1];
-            x.d[i] = sdf[bbase + j];
+            x.dh[i] = __half_as_ushort(__float2half_rn(sdf[bbase + j]));
             x.s8[i] = ss8[bbase + j];
         }
     }
@@ -536,7 +551,7 @@ __device__ __forceinline__ void piece_row1(float &acc, const unsigned char *code
             v = __dp4a(w1[i].z, x.hi[i].z, v);
             v = __dp4a(w1[i].w, x.hi[i].w, v);
         }
-        acc = __fmaf_rn(__fmul_rn(h2f(sw[i]), x.d[i]), (float)v, acc);
+        acc = __fmaf_rn(mul_f16(sw[i], x.dh[i]), i2f_exact(v), acc);
     }
 }
 
@@ -640,7 +655,7 @@ __device__ __forceinline__ void gemv_block(float (&acc)[NR][M], int r, const uns
             v = __dp4a((int)(w.w & 0x0f0f0f0fu), xa.w, v);
             v = __dp4a((int)((w.w >> 4) & 0x0f0f0f0fu), xb.w, v);
             v -= ss8[m * nb + b];
-            acc[r][m] = __fmaf_rn(__fmul_rn(dw, sdf[m * nb + b]), (float)v, acc[r][m]);
+            acc[r][m] = __fmaf_rn(__fmul_rn(dw, sdf[m * nb + b]), i2f_exact(v), acc[r][m]);
         }
     } else {
         const int4 w0 = *(const int4 *)(codes + j * 32), w1 = *(const int4 *)(codes + j * 32 + 16);
@@ -657,7 +672,7 @@ __device__ __forceinline__ void gemv_block(float (&acc)[NR][M], int r, const uns
             v = __dp4a(w1.y, xb.y, v);
             v = __dp4a(w1.z, xb.z, v);
             v = __dp4a(w1.w, xb.w, v);
-            acc[r][m] = __fmaf_rn(__fmul_rn(dw, sdf[m * nb + b]), (float)v, acc[r][m]);
+            acc[r][m] = __fmaf_rn(__fmul_rn(dw, sdf[m * nb + b]), i2f_exact(v), acc[r][m]);
         }
     }
 }
