@@ -121,7 +121,7 @@ void Model::load(const char *path, int backend, int dev, bool allow_cpu_fallback
     if (const char *g = std::getenv("GCB_ACT_HANDOFF")) act_handoff = std::atoi(g);
     if (const char *g = std::getenv("GCB_PROLOGUE_HOLD")) prologue_hold = std::atoi(g);
     if (const char *g = std::getenv("GCB_PRODUCER_WAIT_AFTER_ATTN")) producer_wait_after_attn = std::atoi(g);
-    if (const char *g = std::getenv("GCB_KV_PREFETCH")) kv_prefetch = std::atoi(g) != 0;
+    if (const char *g = std::getenv("GCB_KV_PREFETCH")) kv_prefetch = std::atoi(g);
 
     load_weights();
     for (const auto &sy : prog.symbols) binding.push_back(sy.max);

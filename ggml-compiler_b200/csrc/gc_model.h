@@ -200,7 +200,9 @@ struct Model {
     // GCB_PRODUCER_WAIT_AFTER_ATTN: the GEMV after attention streams only once attention completed
     // (1), or is launched without programmatic dependent launch at all (2)
     int producer_wait_after_attn = 0;    // GCB_PROLOGUE_HOLD: FusedArgs::hold_pieces of the single-row GEMVs
-    bool kv_prefetch = false;  // GCB_KV_PREFETCH=1: a GEMV before one-row attention prefetches its K/V into L2
+    // GCB_KV_PREFETCH=k: the GEMV k launches before a one-row attention prefetches its K/V into L2
+    // (1: the QKV GEMV right before it; 2: the one before that, the previous layer's down GEMV)
+    int kv_prefetch = 0;
     bool stream_evict_first = true;  // GCB_STREAM_EVICT_FIRST=0: GEMV weight streams without the L2 evict-first policy
     std::map<std::string, KernelStat> kstats;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> event_pool;

@@ -726,10 +726,11 @@ void Planner::finish() {
         pf.evict_first = m.stream_evict_first ? 1 : 0;
         pf.hold_pieces = m.prologue_hold;
         if (gi[x] > 0 && std::string(psteps[gi[x] - 1].kind) == "flash_attn") pf.producer_waits = m.producer_wait_after_attn;
-        // a one-row attention step right after: its K and V cache rows into L2 while this GEMV
-        // streams (the attention's bulk copies then read L2)
-        if (m.kv_prefetch && gi[x] + 1 < psteps.size() && psteps[gi[x] + 1].attn_act) {
-            const PlanStep &at = psteps[gi[x] + 1];
+        // a one-row attention step m.kv_prefetch launches later: its K and V cache rows into L2
+        // while this GEMV streams (the attention's bulk copies then read L2)
+        const size_t ahead = (size_t)std::max(0, m.kv_prefetch);
+        if (ahead && gi[x] + ahead < psteps.size() && psteps[gi[x] + ahead].attn_act) {
+            const PlanStep &at = psteps[gi[x] + ahead];
             for (int r = 0; r < 2; r++) {
                 const TD &kv = at.tds[(size_t)(1 + r)];
                 pf.p[r] = kv.data;

@@ -198,20 +198,37 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
     constexpr int NW = NCT / 32;
     constexpr int U = 16;  // loads in flight per thread in the sum of squares
     constexpr int UB = GEMV_UB;
+    const int sub = lane >> 3, e = (lane & 7) * 4;
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    constexpr int STRIDE = NW * 4 * UB;  // blocks of one quantization round (UB 4-block groups per warp)
 #pragma unroll
     for (int m = 0; m < M; m++) {
         const float *x = a.x + m * a.ldx;
+        // a round's loads: the activation values and, for PRO_NORM, the norm weights
+        auto load = [&](int b0, float4 (&v)[UB], float4 (&w)[UB]) {
+#pragma unroll
+            for (int u = 0; u < UB; u++) {
+                const int b = b0 + u * NW * 4 + sub;
+                v[u] = b < nb ? __ldcg((const float4 *)(x + b * 32 + e)) : zero;
+                w[u] = (wpre && m == 0 && b0 == warp * 4) ? wpre[u]  // first round, loaded before the wait
+                                                        : (a.pro == PRO_NORM && b < nb) ? *(const float4 *)(a.norm_w + b * 32 + e) : zero;
+            }
+        };
+        // the first quantization round's loads go out before the norm's sum of squares, so both
+        // passes wait for L2 once
+        float4 v[UB], w[UB], vn[UB], wn[UB];
+        load(warp * 4, v, w);
         float scale = 1.0f;
         if (a.pro == PRO_NORM) {
             if (tid < 256) {
                 double p = 0.0;
                 for (int i0 = tid; i0 < K; i0 += 256 * U) {
-                    float v[U];
+                    float vv[U];
 #pragma unroll
-                    for (int u = 0; u < U; u++) v[u] = i0 + 256 * u < K ? __ldcg(x + i0 + 256 * u) : 0.0f;
+                    for (int u = 0; u < U; u++) vv[u] = i0 + 256 * u < K ? __ldcg(x + i0 + 256 * u) : 0.0f;
 #pragma unroll
                     for (int u = 0; u < U; u++)
-                        if (i0 + 256 * u < K) p = __dadd_rn(p, (double)__fmul_rn(v[u], v[u]));
+                        if (i0 + 256 * u < K) p = __dadd_rn(p, (double)__fmul_rn(vv[u], vv[u]));
                 }
                 red[tid] = p;
             } else if constexpr (NCT > 256) {
@@ -228,10 +245,10 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
                 named_bar(bar, NCT);
             }
             if (tid < 32) {
-                double v = red[tid];
+                double vd = red[tid];
 #pragma unroll
-                for (int off = 16; off >= 1; off >>= 1) v = __dadd_rn(v, __shfl_down_sync(0xffffffffu, v, off));
-                if (tid == 0) red[0] = v;
+                for (int off = 16; off >= 1; off >>= 1) vd = __dadd_rn(vd, __shfl_down_sync(0xffffffffu, vd, off));
+                if (tid == 0) red[0] = vd;
             }
             named_bar(bar, NCT);
             const double tot = red[0];
@@ -239,21 +256,6 @@ __device__ inline void gemv_prologue(const FusedArgs &a, int8_t *sq, float *sdf,
             const float mean = __double2float_rn(__ddiv_rn(tot, (double)K));
             scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
         }
-        const int sub = lane >> 3, e = (lane & 7) * 4;
-        const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-        constexpr int STRIDE = NW * 4 * UB;  // blocks of one round (UB 4-block groups per warp)
-        // a round's loads: the activation values and, for PRO_NORM, the norm weights
-        auto load = [&](int b0, float4 (&v)[UB], float4 (&w)[UB]) {
-#pragma unroll
-            for (int u = 0; u < UB; u++) {
-                const int b = b0 + u * NW * 4 + sub;
-                v[u] = b < nb ? __ldcg((const float4 *)(x + b * 32 + e)) : zero;
-                w[u] = (wpre && b0 == warp * 4) ? wpre[u]  // first round, loaded before the wait
-                                                : (a.pro == PRO_NORM && b < nb) ? *(const float4 *)(a.norm_w + b * 32 + e) : zero;
-            }
-        };
-        float4 v[UB], w[UB], vn[UB], wn[UB];
-        load(warp * 4, v, w);
         for (int b0 = warp * 4; b0 < nb; b0 += STRIDE) {
             if (b0 + STRIDE < nb) load(b0 + STRIDE, vn, wn);  // the next round's loads first
 #pragma unroll
