@@ -240,11 +240,16 @@ struct BatchPlanner {
         const float scale = x.pfloat("scale");
         const bool cluster = k::flash_split_prepare(qt, kt, vt, y);
         auto tr = p.trace_slot("flash_attn", x.id, cluster ? (size_t)(((window + 63) / 64) * Hkv * n) : k::flash_split_ctas(qt, kt));
+        // the QKV launch before writes row pos[i] of slot i: the other rows are copied early
+        const int32_t *kv_pos = cluster && m.attn_overlap ? rt.pos : nullptr;
+        const bool *direct = &m.direct_launch;
         p.add("flash_attn", x.id, {qt, kt, vt, mk, y, scratch},
-              [scale, cnt, err, tr](cudaStream_t st, const std::vector<TD> &t) {
-                  k::flash_attn_split(t[0], t[1], t[2], &t[3], t[4], scale, t[5].data, cnt, err, st, *tr, nullptr);
+              [scale, cnt, err, tr, kv_pos, direct](cudaStream_t st, const std::vector<TD> &t) {
+                  k::flash_attn_split(t[0], t[1], t[2], &t[3], t[4], scale, t[5].data, cnt, err, st, *tr, nullptr,
+                                      *direct ? nullptr : kv_pos);
               },
               (double)n * ((double)window * Hkv * D * 4 + (double)D * H * 8));
+        p.psteps.back().attn_early = kv_pos != nullptr;
         bv[x.id] = as_rows(y, D * H);
     }
 
@@ -615,6 +620,7 @@ BatchRuntime::Plan &Model::batch_plan(const std::string &entry, int n, int64_t w
 }
 
 void Model::batch_launch(SitePlan &p) {
+    direct_launch = profiling || !use_graphs;
     if (profiling) {  // each launch on its own, timed (ggml_compiler_b200_set_profiling)
         for (const auto &st : p.steps) {
             cudaEvent_t a, b;

@@ -352,6 +352,8 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
                 pl.env[qid] = qb;
                 pl.env[kid] = tkc;
                 pl.env[vid] = tvc;
+                pl.kv_rows[tkc.data] = tp;
+                pl.kv_rows[tvc.data] = tp;
             }, [&] {
                 auto ds = std::make_shared<GroupDesc>();
                 ds->kind = GroupDesc::QKV;

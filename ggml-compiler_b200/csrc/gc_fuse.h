@@ -34,6 +34,7 @@ struct GemvExtras {
     int *act_cnt = nullptr;
     int hold_pieces = 0;
     int producer_waits = 0;
+    int max_ctas = 0;
 };
 
 struct PlanStep {
@@ -51,6 +52,7 @@ struct PlanStep {
     std::shared_ptr<char *> attn_act;
     const float *attn_out = nullptr;
     int64_t attn_k = 0;
+    bool attn_early = false;  // the attention loads its K/V before the dependent-launch wait
 };
 
 struct Planner {
@@ -65,6 +67,9 @@ struct Planner {
     int cur = 0;
     bool copy_results = true;  // finish() copies the stage's results into their driver values
     std::set<int> head_sharded;  // tensor parallel: storages holding only this rank's query heads
+    // K/V caches a fused QKV step of this plan writes, by their data pointer: the positions tensor
+    // of the rows it writes (one-row attention over the cache then loads the other rows early)
+    std::unordered_map<const char *, TD> kv_rows;
     // GGML_COMPILER_B200_TRACE: launches that record per-CTA stamps, and where (filled by finish)
     struct TraceReq {
         const char *kind;

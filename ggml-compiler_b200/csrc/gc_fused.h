@@ -85,6 +85,10 @@ struct FusedArgs {
     // The producer waits for the previous kernel to complete (griddepcontrol.wait) before it
     // streams, instead of streaming during that kernel's latency-bound tail.
     int producer_waits = 0;
+    // At most this many CTAs (0: two per SM, or one when the shared memory needs it). One per SM
+    // leaves each SM room for a CTA of the attention launched after this GEMV, which can then
+    // start its K/V copies while this GEMV runs.
+    int max_ctas = 0;
 };
 
 namespace k {

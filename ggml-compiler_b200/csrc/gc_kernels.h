@@ -139,8 +139,14 @@ void flash_attn(const TD &q, const TD &k, const TD &v, const TD *mask, const TD 
 bool flash_split_ok(const TD &q);
 size_t flash_split_scratch_bytes(const TD &q, const TD &k);
 size_t flash_split_counters(const TD &q, const TD &k);
+// kv_pos (one query row; cluster kernel only): the positions [batch] of the K/V rows the kernel
+// launched before this one writes. The cluster kernel then copies the chunk's K/V before its
+// dependent-launch wait (the other rows were written by earlier launches that completed before
+// the kernel before it started: a graph launch or loop iteration boundary) and reads that row
+// again after the wait. Null: every copy after the wait.
 void flash_attn_split(const TD &q, const TD &k, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
-                      int *counters, int *err, cudaStream_t s, uint64_t *trace = nullptr, char *act_out = nullptr);
+                      int *counters, int *err, cudaStream_t s, uint64_t *trace = nullptr, char *act_out = nullptr,
+                      const int32_t *kv_pos = nullptr);
 size_t flash_split_ctas(const TD &q, const TD &k);  // CTAs of one split launch (trace slots)
 // One decode row of 2-16 chunks runs as thread-block clusters (one per K/V head, chunk partials
 // merged through distributed shared memory) when such clusters fit; this asks once, outside any

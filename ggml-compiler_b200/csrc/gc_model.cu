@@ -122,6 +122,8 @@ void Model::load(const char *path, int backend, int dev, bool allow_cpu_fallback
     if (const char *g = std::getenv("GCB_PROLOGUE_HOLD")) prologue_hold = std::atoi(g);
     if (const char *g = std::getenv("GCB_PRODUCER_WAIT_AFTER_ATTN")) producer_wait_after_attn = std::atoi(g);
     if (const char *g = std::getenv("GCB_KV_PREFETCH")) kv_prefetch = std::atoi(g);
+    if (const char *g = std::getenv("GCB_ATTN_OVERLAP")) attn_overlap = std::atoi(g) != 0;
+    if (const char *g = std::getenv("GCB_QKV_ONE_PER_SM")) qkv_one_per_sm = std::atoi(g) != 0;
 
     load_weights();
     for (const auto &sy : prog.symbols) binding.push_back(sy.max);
@@ -368,6 +370,7 @@ static void timed(Model &m, std::vector<int> stages, F &&body) {
 }
 
 void Model::launch_plan(SitePlan &p, int stage_index) {
+    direct_launch = profiling || !profile_path.empty() || !use_graphs;
     timed(*this, {stage_index}, [&] {
         if (profiling || !profile_path.empty()) {  // each launch on its own, timed
             for (const auto &st : p.steps) {

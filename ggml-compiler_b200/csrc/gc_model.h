@@ -203,6 +203,16 @@ struct Model {
     // GCB_KV_PREFETCH=k: the GEMV k launches before a one-row attention prefetches its K/V into L2
     // (1: the QKV GEMV right before it; 2: the one before that, the previous layer's down GEMV)
     int kv_prefetch = 0;
+    // GCB_ATTN_OVERLAP (default 1): one-row cluster attention over a cache a fused QKV GEMV writes
+    // issues its K/V copies before the dependent-launch wait (re-reading the written row after it).
+    // GCB_QKV_ONE_PER_SM=1: that QKV GEMV also runs one CTA per SM so the attention's CTAs can be
+    // resident beside it (measured slower: the GEMV loses half its CTAs and the attention CTAs
+    // still start only at its tail).
+    bool attn_overlap = true;
+    bool qkv_one_per_sm = false;
+    // Launches run one by one (profiling, graphs off) rather than as one graph: early K/V copies
+    // are then off (consecutive steps' launches could overlap under programmatic dependent launch)
+    bool direct_launch = false;
     bool stream_evict_first = true;  // GCB_STREAM_EVICT_FIRST=0: GEMV weight streams without the L2 evict-first policy
     std::map<std::string, KernelStat> kstats;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> event_pool;

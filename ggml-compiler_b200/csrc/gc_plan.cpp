@@ -154,6 +154,7 @@ void Planner::add_gemv(const char *kind, const std::string &node, std::vector<TD
             a.act_cnt = pf->act_cnt;
             a.hold_pieces = pf->hold_pieces;
             a.producer_waits = pf->producer_waits;
+            if (pf->max_ctas) a.max_ctas = pf->max_ctas;
             k::fused_gemv(a, st, pf->producer_waits < 2);
         },
         bytes);
@@ -476,11 +477,21 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
                 auto tr = trace_slot("flash_attn", n.id, cluster ? (size_t)(((kk.ne[1] + 63) / 64) * kk.ne[2] * q.ne[3])
                                                                   : k::flash_split_ctas(q, kk));
                 auto act = std::make_shared<char *>(nullptr);
-                add("flash_attn", n.id, {q, kk, v, mk, y, scratch},
-                    [scale, cnt, err, tr, act](cudaStream_t st, const std::vector<TD> &t) {
-                        k::flash_attn_split(t[0], t[1], t[2], &t[3], t[4], scale, t[5].data, cnt, err, st, *tr, *act);
+                // a fused QKV step of this plan writes the caches' rows at its positions: the cluster
+                // kernel copies the other rows before its dependent-launch wait
+                TD pos;
+                auto kr = kv_rows.find(kk.data), vr = kv_rows.find(v.data);
+                const bool early = cluster && m.attn_overlap && kk.sid < 0 && v.sid < 0 && kr != kv_rows.end() &&
+                                   vr != kv_rows.end() && kr->second.data == vr->second.data && q.ne[3] == 1;
+                if (early) pos = kr->second;
+                const bool *direct = &m.direct_launch;
+                add("flash_attn", n.id, {q, kk, v, mk, y, scratch, pos},
+                    [scale, cnt, err, tr, act, early, direct](cudaStream_t st, const std::vector<TD> &t) {
+                        k::flash_attn_split(t[0], t[1], t[2], &t[3], t[4], scale, t[5].data, cnt, err, st, *tr, *act,
+                                            early && !*direct ? (const int32_t *)t[6].data : nullptr);
                     },
                     bytes);
+                psteps.back().attn_early = early;
                 if (q.ne[1] == 1 && q.ne[3] == 1) {
                     psteps.back().attn_act = act;
                     psteps.back().attn_k = q.ne[0] * q.ne[2];
@@ -726,6 +737,9 @@ void Planner::finish() {
         pf.evict_first = m.stream_evict_first ? 1 : 0;
         pf.hold_pieces = m.prologue_hold;
         if (gi[x] > 0 && std::string(psteps[gi[x] - 1].kind) == "flash_attn") pf.producer_waits = m.producer_wait_after_attn;
+        // a one-row attention that loads its K/V early right after: one CTA per SM, so that the
+        // attention's CTAs fit beside this GEMV's
+        if (m.qkv_one_per_sm && gi[x] + 1 < psteps.size() && psteps[gi[x] + 1].attn_early) pf.max_ctas = k::num_sms();
         // a one-row attention step m.kv_prefetch launches later: its K and V cache rows into L2
         // while this GEMV streams (the attention's bulk copies then read L2)
         const size_t ahead = (size_t)std::max(0, m.kv_prefetch);

@@ -59,6 +59,7 @@ struct SplitArgs {
                       // done, chunk computed, past the arrival counter (the cluster kernel: past the
                       // cluster barrier), and done again in the cluster kernel only
     char *act_out;    // one query row: its Q8_0 blocks in the GEMV staging layout (K = H x D), or null
+    const int32_t *kv_pos;  // cluster kernel: [B] positions the previous kernel writes (early K/V copies)
 };
 
 template <int MAXD>
@@ -216,16 +217,19 @@ __global__ void __launch_bounds__(MAXG * WPH * 32, 2) flash_cluster_kernel(Split
     uint64_t *stamps = a.trace && threadIdx.x == 0 ? a.trace + cta_id * 8 : nullptr;
     if (stamps) stamps[0] = global_ns();
     pdl_trigger();
-    pdl_wait();
-    if (stamps) stamps[2] = global_ns();
-    if (threadIdx.x == 0) {
+    const bool early = a.kv_pos != nullptr;
+    auto copy_kv = [&] {
         mbar_init(&bar, 1);
         mbar_fence_init();
         const uint32_t bytes = (uint32_t)(n * D * 2);
         mbar_expect_tx(&bar, 2 * bytes);
         bulk_g2s(Ks, a.k + hk * a.knb2 + b * a.knb3 + j0 * a.knb1, bytes, &bar);
         bulk_g2s(Vs, a.v + hk * a.vnb2 + b * a.vnb3 + j0 * a.vnb1, bytes, &bar);
-    }
+    };
+    if (early && threadIdx.x == 0) copy_kv();  // rows of earlier steps: complete before this launch
+    pdl_wait();
+    if (stamps) stamps[2] = global_ns();
+    if (!early && threadIdx.x == 0) copy_kv();
     cluster.sync();  // every CTA of the cluster has started: its shared memory may be written
     FlashChunk fc;
     fc.q = a.q + (hk * G) * a.qnb2 + b * a.qnb3;
@@ -247,6 +251,22 @@ __global__ void __launch_bounds__(MAXG * WPH * 32, 2) flash_cluster_kernel(Split
     for (int i = threadIdx.x; !live && i < (int)G * CH; i += blockDim.x) live = (i % CH) < n && ms[i] != ninf;
     live = __syncthreads_or(live);
     const bool landed = __syncthreads_and(mbar_wait(&bar, 0));
+    if (early && landed) {
+        // the row the previous kernel wrote may have been copied before it was written: read it
+        // again (from L2: that kernel has completed)
+        const int64_t p = (int64_t)a.kv_pos[b] - j0;
+        if (p >= 0 && p < n) {
+            const int w = D / 2;  // 32-bit words per row
+            for (int i = threadIdx.x; i < 2 * w; i += blockDim.x) {
+                const bool isv = i >= w;
+                const int c = isv ? i - w : i;
+                const char *src = isv ? a.v + hk * a.vnb2 + b * a.vnb3 + (j0 + p) * a.vnb1
+                                      : a.k + hk * a.knb2 + b * a.knb3 + (j0 + p) * a.knb1;
+                ((uint32_t *)((isv ? Vs : Ks) + p * D))[c] = __ldcg((const unsigned int *)src + c);
+            }
+        }
+        __syncthreads();
+    }
     if (stamps) stamps[3] = global_ns();
     if (!landed) {
         if (threadIdx.x < G) {
@@ -420,7 +440,7 @@ bool flash_split_prepare(const TD &q, const TD &kk, const TD &v, const TD &out) 
 }
 
 void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
-                      int *counters, int *err, cudaStream_t s, uint64_t *trace, char *act_out) {
+                      int *counters, int *err, cudaStream_t s, uint64_t *trace, char *act_out, const int32_t *kv_pos) {
     if (flash_prefill_ok(q, kk, v, out)) {
         flash_prefill(q, kk, v, mask, out, scale, err, s);
         return;
@@ -485,6 +505,7 @@ void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, co
         SplitArgs c = a;
         c.mask = mask ? mask->data : nullptr;
         c.out = (float *)out.data;
+        c.kv_pos = kv_pos;
         if (cluster_decode(c, smem, threads, s, true)) return;
     }
     const size_t per_row = (size_t)(a.H * a.B * a.nch * (a.D + 2)) * 4;

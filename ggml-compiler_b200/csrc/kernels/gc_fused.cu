@@ -19,7 +19,16 @@ namespace k {
 namespace {
 
 constexpr int NCW = 8;  // consumer warps
-constexpr int NTHREADS = (NCW + 1) * 32;
+// One activation row: the 8 consumer warps are one team, one tile row each. Several rows: GEMV_RPW
+// tile rows per warp (gc_gemv_dev.cuh consume_gemv), teams of 8 / GEMV_RPW warps, each team on its
+// own row group, so each piece is released by the warps of one team.
+#ifndef GEMV_RPW
+#define GEMV_RPW 2
+#endif
+template <int M>
+constexpr int teams_of() { return M == 1 ? 1 : GEMV_RPW; }
+template <int M>
+constexpr int threads_of() { return (NCW + 1) * 32; }
 constexpr int MAXNS = 16;
 constexpr int CG = 2;  // row groups per chunk with one activation row (gc_gemv_dev.cuh)
 
@@ -27,7 +36,8 @@ constexpr int CG = 2;  // row groups per chunk with one activation row (gc_gemv_
 // accumulators and the rows' operands stay in registers (at two per SM they spilled to local
 // memory), with the whole shared memory for the staged rows and the ring.
 template <int QT, int NR, int M>
-__global__ void __launch_bounds__(NTHREADS, M == 1 ? 2 : 1) gemv_tma_kernel(FusedArgs a, GemvGeo G, int ns, uint32_t magic, int slot_bytes) {
+__global__ void __launch_bounds__(threads_of<M>(), M == 1 ? 2 : 1) gemv_tma_kernel(FusedArgs a, GemvGeo G, int ns, uint32_t magic, int slot_bytes) {
+    constexpr int TEAMS = teams_of<M>(), TW = NCW / TEAMS, NCT = NCW * 32;  // teams, warps per team, consumer threads
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t *full = (uint64_t *)smem;
     uint64_t *empty = full + MAXNS;
@@ -43,7 +53,7 @@ __global__ void __launch_bounds__(NTHREADS, M == 1 ? 2 : 1) gemv_tma_kernel(Fuse
     if (threadIdx.x == 0) {
         for (int s = 0; s < ns; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NCW);
+            mbar_init(&empty[s], TW);
         }
         mbar_init(hold, 1);
         mbar_fence_init();
@@ -56,7 +66,8 @@ __global__ void __launch_bounds__(NTHREADS, M == 1 ? 2 : 1) gemv_tma_kernel(Fuse
         if (a.trace) a.trace[blockIdx.x * 8 + 0] = global_ns();
         if (a.producer_waits) pdl_wait();
         uint32_t t = 0;
-        if (!produce_gemv(a, G, R, t, blockIdx.x, gridDim.x, gemv_chunk(M, 1, CG), a.hold_pieces > 0 ? hold : nullptr)) {
+        if (!produce_gemv(a, G, R, t, blockIdx.x, gridDim.x, M == 1 ? gemv_chunk(1, 1, CG) : TEAMS,
+                          a.hold_pieces > 0 ? hold : nullptr)) {
             if (a.err) atomicExch(a.err, 2);
             drain_ring(R, t);
         } else {
@@ -66,17 +77,17 @@ __global__ void __launch_bounds__(NTHREADS, M == 1 ? 2 : 1) gemv_tma_kernel(Fuse
         return;
     }
     float4 wpre[GEMV_UB];
-    gemv_norm_prefetch<NCW * 32>(a, wpre);
+    gemv_norm_prefetch<NCT>(a, wpre);
     pdl_wait();
     const bool stamp = a.trace && threadIdx.x == 0;
     if (stamp) a.trace[blockIdx.x * 8 + 2] = global_ns();
-    if (a.pro == PRO_Q8) gemv_stage_q8<NCW * 32>(a, sq, 1, M);
-    else gemv_prologue<M, NCW * 32>(a, sq, sdf, ss8, red, 1, wpre);
+    if (a.pro == PRO_Q8) gemv_stage_q8<NCT>(a, sq, 1, M);
+    else gemv_prologue<M, NCT>(a, sq, sdf, ss8, red, 1, wpre);
     if (stamp) a.trace[blockIdx.x * 8 + 3] = global_ns();
     if (threadIdx.x == 0) mbar_arrive(hold);
-    if (!consume_gemv<QT, NR, M, CG>(a, G, R, 0, blockIdx.x, gridDim.x, 0, 1, warp, sq, sdf, ss8))
+    if (!consume_gemv<QT, NR, M, CG, TEAMS>(a, G, R, 0, blockIdx.x, gridDim.x, warp / TW, TEAMS, warp % TW, sq, sdf, ss8))
         if (a.err) atomicExch(a.err, 2);
-    if (M == 1 && a.act_mode != ACT8_NONE) gemv_emit_act8<NCW * 32>(a, G, red, 1);
+    if (M == 1 && a.act_mode != ACT8_NONE) gemv_emit_act8<NCT>(a, G, red, 1);
     if (stamp) a.trace[blockIdx.x * 8 + 4] = global_ns();
 }
 
@@ -118,10 +129,11 @@ void launch_t(const FusedArgs &a, const GemvGeo &G, cudaStream_t s, bool pdl) {
     const size_t smem = head + (size_t)ns * (size_t)slot_bytes;
     const int per_sm = M == 1 && smem <= 113 * 1024 ? g_ctas_per_sm : 1;
     const int64_t cap = (int64_t)g_num_sms * per_sm;
-    const int64_t ctas = G.groups < cap ? (int64_t)G.groups : cap;
+    int64_t ctas = G.groups < cap ? (int64_t)G.groups : cap;
+    if (a.max_ctas > 0 && ctas > a.max_ctas) ctas = a.max_ctas;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(ctas < 1 ? 1 : ctas));
-    cfg.blockDim = dim3(NTHREADS);
+    cfg.blockDim = dim3(threads_of<M>());
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute at[1];

@@ -636,54 +636,76 @@ __device__ inline bool consume_gemv1(const FusedArgs &a, const GemvGeo &G, const
 
 // ---------------------------------------------------------------- several activation rows
 
-// One quantized block of this lane's row against every activation row.
-template <int QT, int NR, int M>
-__device__ __forceinline__ void gemv_block(float (&acc)[NR][M], int r, const unsigned char *codes, const uint16_t *scl, int j,
-                                           int b, const int8_t *sq, const float *sdf, const int *ss8, int K, int nb) {
-    const float dw = h2f(scl[j]);
+// Several activation rows: one quantized block of RPW tile rows (row rr at codes + rr * cstride,
+// its scales at scl + rr * sstride) against every activation row; each activation block is loaded
+// from shared memory once for the RPW weight rows. Integer dots are exact, so their partial sums
+// may be grouped in any order; the float fma per (row, activation row) is the one-row order.
+template <int QT, int NR, int M, int RPW>
+__device__ __forceinline__ void gemv_blockR(float (&acc)[NR][RPW][M], int r, const unsigned char *codes, int cstride,
+                                            const uint16_t *scl, int sstride, int j, int b, const int8_t *sq,
+                                            const float *sdf, const int *ss8, int K, int nb) {
+    float dw[RPW];
+#pragma unroll
+    for (int rr = 0; rr < RPW; rr++) dw[rr] = h2f(scl[rr * sstride + j]);
     if (QT == 0) {
-        const uint4 w = *(const uint4 *)(codes + j * 16);
+        uint32_t lo[RPW][4], hi[RPW][4];
+#pragma unroll
+        for (int rr = 0; rr < RPW; rr++) {
+            const uint4 w = *(const uint4 *)(codes + rr * cstride + j * 16);
+            const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                lo[rr][q] = wv[q] & 0x0f0f0f0fu;
+                hi[rr][q] = (wv[q] >> 4) & 0x0f0f0f0fu;
+            }
+        }
 #pragma unroll
         for (int m = 0; m < M; m++) {
             const int4 *x4 = (const int4 *)(sq + m * K + b * 32);
             const int4 xa = x4[0], xb = x4[1];
-            int v = 0;
-            v = __dp4a((int)(w.x & 0x0f0f0f0fu), xa.x, v);
-            v = __dp4a((int)((w.x >> 4) & 0x0f0f0f0fu), xb.x, v);
-            v = __dp4a((int)(w.y & 0x0f0f0f0fu), xa.y, v);
-            v = __dp4a((int)((w.y >> 4) & 0x0f0f0f0fu), xb.y, v);
-            v = __dp4a((int)(w.z & 0x0f0f0f0fu), xa.z, v);
-            v = __dp4a((int)((w.z >> 4) & 0x0f0f0f0fu), xb.z, v);
-            v = __dp4a((int)(w.w & 0x0f0f0f0fu), xa.w, v);
-            v = __dp4a((int)((w.w >> 4) & 0x0f0f0f0fu), xb.w, v);
-            v -= ss8[m * nb + b];
-            acc[r][m] = __fmaf_rn(__fmul_rn(dw, sdf[m * nb + b]), i2f_exact(v), acc[r][m]);
+            const int xl[4] = {xa.x, xa.y, xa.z, xa.w}, xh[4] = {xb.x, xb.y, xb.z, xb.w};
+            const float dx = sdf[m * nb + b];
+            const int s8 = ss8[m * nb + b];
+#pragma unroll
+            for (int rr = 0; rr < RPW; rr++) {
+                const int v = (__dp4a((int)lo[rr][0], xl[0], __dp4a((int)hi[rr][0], xh[0], 0)) +
+                               __dp4a((int)lo[rr][1], xl[1], __dp4a((int)hi[rr][1], xh[1], 0))) +
+                              (__dp4a((int)lo[rr][2], xl[2], __dp4a((int)hi[rr][2], xh[2], 0)) +
+                               __dp4a((int)lo[rr][3], xl[3], __dp4a((int)hi[rr][3], xh[3], -s8)));
+                acc[r][rr][m] = __fmaf_rn(__fmul_rn(dw[rr], dx), i2f_exact(v), acc[r][rr][m]);
+            }
         }
     } else {
-        const int4 w0 = *(const int4 *)(codes + j * 32), w1 = *(const int4 *)(codes + j * 32 + 16);
+        int w[RPW][8];
+#pragma unroll
+        for (int rr = 0; rr < RPW; rr++) {
+            const int4 a = *(const int4 *)(codes + rr * cstride + j * 32), c = *(const int4 *)(codes + rr * cstride + j * 32 + 16);
+            w[rr][0] = a.x, w[rr][1] = a.y, w[rr][2] = a.z, w[rr][3] = a.w;
+            w[rr][4] = c.x, w[rr][5] = c.y, w[rr][6] = c.z, w[rr][7] = c.w;
+        }
 #pragma unroll
         for (int m = 0; m < M; m++) {
             const int4 *x4 = (const int4 *)(sq + m * K + b * 32);
             const int4 xa = x4[0], xb = x4[1];
-            int v = 0;
-            v = __dp4a(w0.x, xa.x, v);
-            v = __dp4a(w0.y, xa.y, v);
-            v = __dp4a(w0.z, xa.z, v);
-            v = __dp4a(w0.w, xa.w, v);
-            v = __dp4a(w1.x, xb.x, v);
-            v = __dp4a(w1.y, xb.y, v);
-            v = __dp4a(w1.z, xb.z, v);
-            v = __dp4a(w1.w, xb.w, v);
-            acc[r][m] = __fmaf_rn(__fmul_rn(dw, sdf[m * nb + b]), i2f_exact(v), acc[r][m]);
+            const int xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+            const float dx = sdf[m * nb + b];
+#pragma unroll
+            for (int rr = 0; rr < RPW; rr++) {
+                const int v = (__dp4a(w[rr][0], xv[0], __dp4a(w[rr][1], xv[1], 0)) + __dp4a(w[rr][2], xv[2], __dp4a(w[rr][3], xv[3], 0))) +
+                              (__dp4a(w[rr][4], xv[4], __dp4a(w[rr][5], xv[5], 0)) + __dp4a(w[rr][6], xv[6], __dp4a(w[rr][7], xv[7], 0)));
+                acc[r][rr][m] = __fmaf_rn(__fmul_rn(dw[rr], dx), i2f_exact(v), acc[r][rr][m]);
+            }
         }
     }
 }
 
-// Consumer side of one GEMV: this team's groups (every `teams`-th local group, starting at `team`),
-// pieces numbered from t0, then the epilogue. `wt` is the warp index within the team (the row of
-// the tile it owns). CG: groups per team in one chunk with one activation row. False on a
-// timed-out wait.
-template <int QT, int NR, int M, int CG>
+// Consumer side of one GEMV. One activation row: consume_gemv1. Several: the CTA's row groups are
+// taken in chunks of `teams` groups, segment-major inside a chunk (the producer's order for a
+// chunk of that size), team `team` owning group `team` of each chunk; a team is 8 / RPW warps, warp
+// `wt` owning tile rows RPW wt .. RPW wt + RPW - 1, so each activation block is read from shared
+// memory once for RPW weight rows. Each row keeps the one-row arithmetic: lane l, blocks l, l + 32,
+// ... in order, then the butterfly. False on a timed-out wait.
+template <int QT, int NR, int M, int CG, int RPW = 1>
 __device__ inline bool consume_gemv(const FusedArgs &a, const GemvGeo &G, const Ring &R, uint32_t t0, int cta, int nctas,
                                     int team, int teams, int wt, const int8_t *sq, const float *sdf, const int *ss8) {
     if constexpr (M == 1) {
@@ -694,45 +716,56 @@ __device__ inline bool consume_gemv(const FusedArgs &a, const GemvGeo &G, const 
         const int K = (int)a.K, nb = G.nb;
         const int per_group = G.nseg * G.pieces;
         const int L = local_groups(G.groups, cta, nctas);
-        for (int gl = team; gl < L; gl += teams) {
+        for (int c0 = 0; c0 < L; c0 += teams) {
+            const int n = c0 + teams < L ? teams : L - c0;
+            if (team >= n) break;
             int mat, tile;
-            gemv_piece(a, G, cta + gl * nctas, 0, 0, &mat, &tile);
-            const int row0 = tile * QTR + wt;
-            float e0[M], e1[M];
-            if (lane == 0) gemv_epi_load<M>(a, mat, row0, e0, e1);
-            float acc[NR][M];
+            gemv_piece(a, G, cta + (c0 + team) * nctas, 0, 0, &mat, &tile);
+            const int row0 = tile * QTR + RPW * wt;
+            float e0[RPW][M], e1[RPW][M];
+            if (lane == 0)
+#pragma unroll
+                for (int rr = 0; rr < RPW; rr++) gemv_epi_load<M>(a, mat, row0 + rr, e0[rr], e1[rr]);
+            float acc[NR][RPW][M];
 #pragma unroll
             for (int r = 0; r < NR; r++)
 #pragma unroll
-                for (int m = 0; m < M; m++) acc[r][m] = 0.0f;
-            uint32_t t = t0 + (uint32_t)(gl * per_group);
+                for (int rr = 0; rr < RPW; rr++)
+#pragma unroll
+                    for (int m = 0; m < M; m++) acc[r][rr][m] = 0.0f;
+            const uint32_t tb = t0 + (uint32_t)(c0 * per_group);
             for (int s = 0; s < G.nseg; s++) {
                 const int sb = (int)qw_seg_blocks(nb, s);
                 const int bbase = s * QSEG;
 #pragma unroll
-                for (int r = 0; r < NR; r++, t++) {
+                for (int r = 0; r < NR; r++) {
+                    const uint32_t t = tb + (uint32_t)((s * n + team) * G.pieces + r);
                     if (!gemv_wait_piece(R, t)) return false;
                     const unsigned char *piece = R.data(t);
-                    const unsigned char *codes = piece + wt * sb * CB;
-                    const uint16_t *scl = (const uint16_t *)(piece + QTR * sb * CB) + wt * sb;
+                    const unsigned char *codes = piece + RPW * wt * sb * CB;
+                    const uint16_t *scl = (const uint16_t *)(piece + QTR * sb * CB) + RPW * wt * sb;
                     if (sb == QSEG) {
 #pragma unroll
                         for (int i = 0; i < QSEG / 32; i++)
-                            gemv_block<QT, NR, M>(acc, r, codes, scl, lane + 32 * i, bbase + lane + 32 * i, sq, sdf, ss8, K, nb);
+                            gemv_blockR<QT, NR, M, RPW>(acc, r, codes, QSEG * CB, scl, QSEG, lane + 32 * i, bbase + lane + 32 * i,
+                                                        sq, sdf, ss8, K, nb);
                     } else {
                         for (int j = lane; j < sb; j += 32)
-                            gemv_block<QT, NR, M>(acc, r, codes, scl, j, bbase + j, sq, sdf, ss8, K, nb);
+                            gemv_blockR<QT, NR, M, RPW>(acc, r, codes, sb * CB, scl, sb, j, bbase + j, sq, sdf, ss8, K, nb);
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&R.empty[R.slot(t)]);
                 }
             }
-            float y[NR][M];
 #pragma unroll
-            for (int m = 0; m < M; m++)
+            for (int rr = 0; rr < RPW; rr++) {
+                float y[NR][M];
 #pragma unroll
-                for (int r = 0; r < NR; r++) y[r][m] = warp_butterfly(acc[r][m]);
-            if (lane == 0) gemv_epi_store<NR, M>(a, mat, row0, y, e0, e1);
+                for (int m = 0; m < M; m++)
+#pragma unroll
+                    for (int r = 0; r < NR; r++) y[r][m] = warp_butterfly(acc[r][rr][m]);
+                if (lane == 0) gemv_epi_store<NR, M>(a, mat, row0 + rr, y, e0[rr], e1[rr]);
+            }
         }
         return true;
     }
