@@ -97,6 +97,11 @@ bool fused_gemv_supported(int64_t K, int64_t M, int map);
 // Shape preconditions of one set of arguments (the rope map needs head sizes that are multiples of 16).
 bool fused_gemv_args_ok(const FusedArgs &a);
 void fused_gemv(const FusedArgs &a, cudaStream_t s, bool pdl);
+// 2-8 staged activation rows (PRO_Q8), K a multiple of 1024, one shard: the block dots on the tensor
+// cores (kernels/gc_gemv_mma.cu), the same results; fused_gemv takes this path when it applies
+// (GCB_GEMV_MMA=0: never).
+bool gemv_mma_ok(const FusedArgs &a);
+void gemv_mma(const FusedArgs &a, cudaStream_t s, bool pdl);
 // a's M activation rows (x, ldx, K; normed for PRO_NORM) into the PRO_Q8 staging layout for M
 // rows at dst (gemv_act_bytes(M, K) bytes), one CTA per row: the launch that reads them then only
 // copies them into shared memory.

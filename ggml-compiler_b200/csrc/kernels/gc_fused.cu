@@ -199,6 +199,10 @@ bool fused_gemv_args_ok(const FusedArgs &a) { return a.map != MAP_ROPE_QKV || (a
 void fused_gemv(const FusedArgs &a, cudaStream_t s, bool pdl) {
     num_sms();
     if (!fused_gemv_args_ok(a)) throw std::runtime_error("gemv_tma: head size must be a multiple of 16");
+    if (gemv_mma_ok(a)) {
+        gemv_mma(a, s, pdl);
+        return;
+    }
     const GemvGeo G = gemv_geo(a);
     const bool q4 = a.qtype == T_Q4_0;
     if (G.pieces == 1) {
