@@ -632,6 +632,21 @@ def decode_bench(args) -> None:
         "clocks": clk.summary(),
         "kernel_breakdown_ms_per_step": {k: v["ms"] / n_prof for k, v in sorted(ks.items(), key=lambda kv: -kv[1]["ms"])},
     }
+    if not tp and world == 1:
+        # batched decode (include/ggml_compiler_b200.h): 8 sequences of the same model and prompt
+        # length, one step for all of them, greedy tokens fed back on the device
+        nbat, bsteps = 8, min(64, NKV - P)
+        bprompts = [np.random.default_rng(10 + i).integers(0, sh.vocab, P).tolist() for i in range(nbat)]
+        bfirst, bstart = d.fill_slots(bprompts)
+        m.generate_batch(bfirst, bstart, 3)  # plans and graphs
+        m.generate_batch(bfirst, bstart, bsteps)
+        bms = m.device_ms
+        out["batched_decode"] = {
+            "value": nbat * bsteps / (bms / 1000.0), "unit": "tok/s", "batch": nbat, "steps": bsteps,
+            "ms_per_step": bms / bsteps, "vs_batch1": (nbat * bsteps / (bms / 1000.0)) / value,
+            "weight_gb_s": weight_bytes(sh) / (bms / bsteps / 1000.0) / 1e9,
+            "how": "8 sequences prefilled (512 ids each) into KV-cache slots, then generate_batch: one step decodes "
+                   "all 8 (tensor-core GEMVs over 8 rows, attention over the 8 slots), device time of the steps"}
     m.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:

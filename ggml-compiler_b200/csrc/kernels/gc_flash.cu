@@ -23,6 +23,7 @@
 #include <string>
 #include <utility>
 
+#include "../gc_fused.h"
 #include "../gc_kernels.h"
 #include "gc_flash_dev.cuh"
 #include "gc_math.cuh"
@@ -60,6 +61,7 @@ struct SplitArgs {
                       // cluster barrier), and done again in the cluster kernel only
     char *act_out;    // one query row: its Q8_0 blocks in the GEMV staging layout (K = H x D), or null
     const int32_t *kv_pos;  // cluster kernel: [B] positions the previous kernel writes (early K/V copies)
+    int64_t cpc;            // multi-chunk kernel: consecutive chunks per CTA
 };
 
 template <int MAXD>
@@ -180,6 +182,117 @@ __global__ void __launch_bounds__(MAXG * WPH * 32, 2) flash_split_kernel(SplitAr
             }
         __syncthreads();  // qs / ms / sc / ps and `last` are reused by the next row
     }
+    if (stamps) stamps[4] = global_ns();
+}
+
+// One query row per batch (decode; K/V rows contiguous) over many CTAs' worth of chunks: each CTA
+// takes a.cpc consecutive chunks of one (K/V head, batch), the next chunk's K/V copy in flight
+// (double buffer) while the current one is computed, each chunk's partial exactly the split
+// kernel's; the last CTA of a (batch, K/V head) merges every chunk in chunk order. Used when the
+// cluster kernel would need more CTAs than fit at once (batched decode), so each CTA's fixed costs
+// (copy latency, barriers, the arrival counter) are paid once per a.cpc chunks.
+template <int MAXD>
+__global__ void __launch_bounds__(MAXG * WPH * 32, 2) flash_multi_kernel(SplitArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int D = (int)a.D;
+    __shared__ uint64_t bar[2];
+    __shared__ int last;
+    __half *Kb[2], *Vb[2];
+    Kb[0] = (__half *)smem;
+    Vb[0] = Kb[0] + CH * D;
+    Kb[1] = Vb[0] + CH * D;
+    Vb[1] = Kb[1] + CH * D;
+    float *sc = (float *)(Vb[1] + CH * D);
+    float *ps = sc + MAXG * CH;
+    const int64_t G = a.H / a.Hkv;
+    float *qs = ps + MAXG * WPH * CH;
+    float *ms = qs + G * D;
+    const int64_t hk = blockIdx.y % a.Hkv, b = blockIdx.y / a.Hkv;
+    const int64_t c0 = blockIdx.x * a.cpc, c1 = min(a.nch, c0 + a.cpc);
+    const int warp = threadIdx.x >> 5;
+    const float ninf = -__int_as_float(0x7f800000);
+    const int64_t cta_id = blockIdx.x + (int64_t)gridDim.x * blockIdx.y;
+    uint64_t *stamps = a.trace && threadIdx.x == 0 ? a.trace + cta_id * 8 : nullptr;
+    if (stamps) stamps[0] = global_ns();
+    pdl_trigger();
+    pdl_wait();
+    if (stamps) stamps[2] = global_ns();
+    auto issue = [&](int64_t c, int buf) {
+        const int64_t j0 = c * CH;
+        const uint32_t bytes = (uint32_t)(min((int64_t)CH, a.nkv - j0) * D * 2);
+        mbar_expect_tx(&bar[buf], 2 * bytes);
+        bulk_g2s(Kb[buf], a.k + hk * a.knb2 + b * a.knb3 + j0 * a.knb1, bytes, &bar[buf]);
+        bulk_g2s(Vb[buf], a.v + hk * a.vnb2 + b * a.vnb3 + j0 * a.vnb1, bytes, &bar[buf]);
+    };
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        mbar_fence_init();
+        if (c0 < c1) issue(c0, 0);
+    }
+    __syncthreads();
+    for (int64_t c = c0; c < c1; c++) {
+        const int ci = (int)(c - c0), buf = ci & 1;
+        // the other buffer was last read by chunk c - 1, whose iteration ended in a barrier
+        if (threadIdx.x == 0 && c + 1 < c1) issue(c + 1, buf ^ 1);
+        const int64_t j0 = c * CH;
+        const int n = (int)min((int64_t)CH, a.nkv - j0);
+        FlashChunk fc;
+        fc.q = a.q + (hk * G) * a.qnb2 + b * a.qnb3;
+        fc.qnb0 = a.qnb0;
+        fc.qnbh = a.qnb2;
+        fc.mask = a.mask ? a.mask + ((hk * G) % a.mne2) * a.mnb2 + (b % a.mne3) * a.mnb3 + j0 * 2 : nullptr;
+        fc.mne2 = a.mne2;
+        fc.mnbh = a.mnb2;
+        fc.hbase = (int)(hk * G);
+        fc.scale = a.scale;
+        fc.D = D;
+        fc.n = n;
+        fc.G = (int)G;
+        fc.part = a.part + (((b * a.H + hk * G) * a.nch + c) * (a.D + 2));
+        fc.pstride = a.nch * (a.D + 2);
+        flash_stage(fc, qs, ms, threadIdx.x, blockDim.x);
+        int live = !fc.mask;
+        for (int i = threadIdx.x; !live && i < (int)G * CH; i += blockDim.x) live = (i % CH) < n && ms[i] != ninf;
+        live = __syncthreads_or(live);
+        const bool landed = __syncthreads_and(mbar_wait(&bar[buf], (uint32_t)((ci >> 1) & 1)));
+        if (!landed) {  // a NaN partial: the merged rows come out NaN; the error word says why
+            if (threadIdx.x < G) {
+                fc.part[threadIdx.x * fc.pstride] = __int_as_float(0x7fc00000);
+                fc.part[threadIdx.x * fc.pstride + 1] = 0.0f;
+            }
+            if (threadIdx.x == 0 && a.err) atomicExch(a.err, 2);
+        } else if (live) {
+            const int nslots = (int)(blockDim.x / 32) / WPH;
+            flash_chunk<WPH, MAXD>(fc, Kb[buf], Vb[buf], qs, ms, sc, ps, nslots, SyncCta());
+        } else if (threadIdx.x < G) {
+            fc.part[threadIdx.x * fc.pstride] = ninf;
+            fc.part[threadIdx.x * fc.pstride + 1] = 0.0f;
+        }
+        __syncthreads();  // buffers, qs / ms / sc / ps free for the next chunk
+    }
+    if (stamps) stamps[5] = global_ns();
+    if (threadIdx.x == 0) {
+        __threadfence();  // this CTA's partials (ordered before by the barrier) are visible first
+        int *cnt = a.counters + b * a.Hkv + hk;
+        last = atomicAdd(cnt, 1) == (int)gridDim.x - 1;
+        if (last) {
+            *cnt = 0;
+            __threadfence();
+        }
+    }
+    __syncthreads();
+    if (stamps) stamps[6] = global_ns();
+    if (last)
+        for (int64_t g = warp; g < G; g += blockDim.x / 32) {
+            const int64_t h = hk * G + g;
+            const int64_t K = a.H * a.D;
+            int8_t *qc = a.act_out ? (int8_t *)a.act_out + h * a.D : nullptr;
+            float *qd = a.act_out ? (float *)(a.act_out + K) + h * a.D / 32 : nullptr;
+            int *qs8 = a.act_out ? (int *)((float *)(a.act_out + K) + K / 32) + h * a.D / 32 : nullptr;
+            flash_merge<MAXD>(a.part + ((b * a.H + h) * a.nch) * (a.D + 2), (int)a.nch, a.out + a.D * (h + a.oH * b), qc, qd,
+                              qs8);
+        }
     if (stamps) stamps[4] = global_ns();
 }
 
@@ -359,6 +472,9 @@ bool cluster_decode(const SplitArgs &a, size_t smem, int threads, cudaStream_t s
     const bool rows_contig = a.knb1 == 2 * a.D && a.vnb1 == 2 * a.D &&
                              (((uintptr_t)a.k | (uintptr_t)a.v | (uintptr_t)a.knb2 | (uintptr_t)a.vnb2) % 16) == 0;
     if (a.nch < 2 || a.nch > FL_CLUSTER_MAX || !rows_contig || !flash_cluster_enabled()) return false;
+    // more CTAs than two per SM (batched decode): the multi-chunk kernel pays each CTA's fixed costs
+    // once per several chunks instead
+    if (a.nch * a.Hkv * a.B > 2 * (int64_t)num_sms()) return false;
     void (*ck)(SplitArgs) = nullptr;
     switch (a.D) {
         case 32: ck = flash_cluster_kernel<32>; break;
@@ -507,6 +623,44 @@ void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, co
         c.out = (float *)out.data;
         c.kv_pos = kv_pos;
         if (cluster_decode(c, smem, threads, s, true)) return;
+        const bool rows_contig = a.knb1 == 2 * a.D && a.vnb1 == 2 * a.D &&
+                                 (((uintptr_t)a.k | (uintptr_t)a.v | (uintptr_t)a.knb2 | (uintptr_t)a.vnb2 |
+                                   (uintptr_t)a.knb3 | (uintptr_t)a.vnb3) % 16) == 0;
+        const int64_t pairs = a.Hkv * a.B, wave = 4 * (int64_t)num_sms();  // two waves of two CTAs per SM
+        if (rows_contig && a.nch >= 2 && (size_t)(a.H * a.B * a.nch * (a.D + 2)) * 4 <= kMaxPartBytes) {
+            void (*mk)(SplitArgs) = nullptr;
+            switch (a.D) {
+                case 32: mk = flash_multi_kernel<32>; break;
+                case 64: mk = flash_multi_kernel<64>; break;
+                case 96: mk = flash_multi_kernel<96>; break;
+                case 128: mk = flash_multi_kernel<128>; break;
+                case 160: mk = flash_multi_kernel<160>; break;
+                case 192: mk = flash_multi_kernel<192>; break;
+                case 224: mk = flash_multi_kernel<224>; break;
+                case 256: mk = flash_multi_kernel<256>; break;
+                default: break;
+            }
+            if (mk) {
+                SplitArgs g = c;
+                g.Sq = 1;
+                g.cpc = std::max<int64_t>(1, (a.nch * pairs + wave - 1) / wave);
+                const size_t msmem = smem + (size_t)CH * a.D * 2 * 2;  // the second K/V buffer
+                cudaFuncSetAttribute(mk, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3((unsigned)((a.nch + g.cpc - 1) / g.cpc), (unsigned)pairs, 1);
+                cfg.blockDim = dim3(threads);
+                cfg.dynamicSmemBytes = msmem;
+                cfg.stream = s;
+                cudaLaunchAttribute at[1];
+                at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+                at[0].val.programmaticStreamSerializationAllowed = 1;
+                cfg.attrs = at;
+                cfg.numAttrs = 1;
+                const cudaError_t e = cudaLaunchKernelEx(&cfg, mk, g);
+                if (e != cudaSuccess) throw std::runtime_error(std::string("CUDA launch of flash_multi failed: ") + cudaGetErrorString(e));
+                return;
+            }
+        }
     }
     const size_t per_row = (size_t)(a.H * a.B * a.nch * (a.D + 2)) * 4;
     const int64_t rows_per = std::max<int64_t>(1, (int64_t)(kMaxPartBytes / per_row));

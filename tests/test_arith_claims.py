@@ -10,7 +10,9 @@ CPU checker (no GPU needed; numpy float32 stands in for the device's IEEE single
   the checker use (off = 16, 8, 4, 2, 1).
 - The flash-prefill kernel skips a chunk in its first pass when |q|_1 · max|k| · |scale| (× 1.01,
   + 1) plus the chunk's largest mask value lies 128 below a maximum already seen. The bound must
-  hold for the float32 dot as computed: lane chains of fmas, then the tree."""
+  hold for the float32 dot as computed: lane chains of fmas, then the tree.
+- Batched decode attends over one window per step with a -inf mask past each sequence's position;
+  the checker's attention gives the same bits over any window and either mask value."""
 
 import numpy as np
 
@@ -84,3 +86,38 @@ def test_score_bound_holds():
                     l1 = f32(l1 + abs(x))
                 bound = f32(f32(f32(f32(l1 * np.max(np.abs(k))) * scale) * f32(1.01)) + f32(1.0))
                 assert s <= bound
+
+
+def test_attention_window_past_the_position_changes_nothing():
+    """Batched decode attends each sequence over one window for the whole step (the longest
+    sequence's, in 256-key steps) with a -inf mask past the sequence's position; the single-sequence
+    decode attends over its own window with the reference programs' -65504 mask. The checker's
+    64-key chunks merged in order give the same bits either way: a key past the position weighs
+    exactly 0, and a chunk wholly past it adds exactly 0 to the merge."""
+    import ctypes
+
+    import oracle
+
+    lib = oracle.lib()
+    rng = np.random.default_rng(5)
+    D, pos = 128, 300
+    q = rng.standard_normal(D, dtype=np.float32)
+    k = (rng.standard_normal((2304, D), dtype=np.float32) * 0.5).astype(np.float16)
+    v = rng.standard_normal((2304, D), dtype=np.float32).astype(np.float16)
+    q = q.astype(np.float16).astype(np.float32)  # the kernels round the query to f16 first
+
+    def row(nkv, hide):
+        m = np.zeros(nkv, np.float32)
+        m[pos + 1:] = hide
+        mh = np.ascontiguousarray(m.astype(np.float16)).view(np.uint16)
+        kk = np.ascontiguousarray(k[:nkv]).view(np.uint16)
+        vv = np.ascontiguousarray(v[:nkv]).view(np.uint16)
+        out = np.empty(D, np.float32)
+        lib.orc_flash_attn_row(q.ctypes.data, kk.ctypes.data, D, vv.ctypes.data, D, nkv, D, mh.ctypes.data,
+                               ctypes.c_float(1.0 / np.sqrt(D)), out.ctypes.data)
+        return out
+
+    want = row(768, -65504.0)  # the decode entry: n_kv 768, the reference's clamped mask
+    for nkv in (320, 512, 1024, 2304):
+        np.testing.assert_array_equal(row(nkv, -np.inf), want)
+        np.testing.assert_array_equal(row(nkv, -65504.0), want)

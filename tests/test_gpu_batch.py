@@ -136,10 +136,11 @@ def test_batch_refusals(gpu):
 
 @pytest.mark.parametrize("wtype", ["q4_0", "q8_0"])
 def test_long_windows_split_kernel(gpu, tmp_path, wtype):
-    """Head size 128, 8 query / 2 K/V heads, prompts of 1100-1300 ids: attention windows of 1280
-    and 1536 keys (more than the 16 chunks of 64 that one thread-block cluster merges, so the
-    split-KV kernel with its global partials runs), 9 sequences (8 + 1 rows per GEMV)."""
-    sh = LlamaShape(layers=2, d_model=1024, heads=8, kv_heads=2, head_dim=128, ffn=2048, vocab=2000,
+    """Head size 128, 16 query / 8 K/V heads, prompts of 1100-1300 ids: attention windows of 1280
+    and 1536 keys over 9 sequences, 1440-1728 chunks of 64 keys in all, so the multi-chunk kernel
+    runs with several chunks per CTA (double-buffered K/V) and merges through global partials;
+    9 sequences are 8 + 1 rows per GEMV (the tensor-core GEMV and the one-row GEMV)."""
+    sh = LlamaShape(layers=2, d_model=2048, heads=16, kv_heads=8, head_dim=128, ffn=2048, vocab=2000,
                     rope_theta=500000.0, max_context=1536, max_prompt=512, weight_type=wtype)
     path = tmp_path / f"long_{wtype}.gguf"
     build_llama_gguf(path, sh, seed=7)
