@@ -297,6 +297,35 @@ def attn(args) -> None:
                           "reps": args.steps, "l2": "flushed before each rep (256 MB write)"}), flush=True)
 
 
+def batch_layers(args) -> None:
+    """Batched decode at the 8B layer shape on a 2-layer model (d_model 4096, 32 / 8 heads, FFN 14336,
+    vocab 2000, Q4_0 or --wtype): 8 sequences of 512 ids prefilled into KV-cache slots, then
+    generate_batch steps. Small enough on the device (about 0.3 GB of weights) for full ncu
+    captures of the batched kernels. One JSON line: batched decode tok/s and the step's weight rate."""
+    from ggml_compiler_b200.llm import Decoder, LlamaShape, build_llama_gguf
+    from ggml_compiler_b200.runtime import Model
+
+    wt = args.wtype or "q4_0"
+    sh = LlamaShape(layers=2, d_model=4096, heads=32, kv_heads=8, ffn=14336, vocab=2000, rope_theta=500000.0,
+                    max_context=1024, max_prompt=512, weight_type=wt)
+    CACHE.mkdir(parents=True, exist_ok=True)
+    gguf = CACHE / f"layers2_8b_width_{wt}_seed3.gguf"
+    if not gguf.exists():
+        tmp = gguf.with_suffix(f".part{os.getpid()}")
+        build_llama_gguf(tmp, sh, seed=3)
+        tmp.rename(gguf)
+    n, P = 8, 512
+    with Model(gguf) as m:
+        first, start = Decoder(m).fill_slots(np.random.default_rng(4).integers(0, sh.vocab, (n, P)).tolist())
+        for _ in range(max(3, args.warmup)):
+            m.generate_batch(first, start, 4)
+        m.generate_batch(first, start, args.steps)
+        ms = m.device_ms
+    print(json.dumps({"metric": "batched decode at the 8B layer shape (2 layers)", "value": n * args.steps / (ms / 1000.0),
+                      "unit": "tok/s", "batch": n, "steps": args.steps, "ms_per_step": ms / args.steps,
+                      "weight_gb_s": weight_bytes(sh) / (ms / args.steps / 1000.0) / 1e9, "weights": wt}), flush=True)
+
+
 PREFILL_METRIC = "8B-shape Q8_0 prefill tok/s (8 sequences x 2048-token prompts); tensor-core TFLOP/s"
 
 
@@ -421,7 +450,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="8b", choices=["8b", "70b", "tiny", "sweep", "prefill", "attn"])
+    ap.add_argument("--config", default="8b", choices=["8b", "70b", "tiny", "sweep", "prefill", "attn", "batch"])
     ap.add_argument("--shape", default=None, help="sweep: one weight shape NxK")
     ap.add_argument("--m", type=int, default=None, help="sweep: one activation row count")
     ap.add_argument("--wtype", default=None, choices=["q4_0", "q8_0"], help="sweep: one weight type")
@@ -446,6 +475,11 @@ def main() -> None:
         if args.steps == ap.get_default("steps"):
             args.steps = 10
         attn(args)
+        return
+    if args.config == "batch":
+        if args.steps == ap.get_default("steps"):
+            args.steps = 16
+        batch_layers(args)
         return
     decode_bench(args)
 

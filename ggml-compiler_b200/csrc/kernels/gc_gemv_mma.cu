@@ -65,9 +65,15 @@ __device__ __forceinline__ void mma_dot(int &c0, int &c1, uint32_t a0, uint32_t 
                      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "r"(0));
 }
 
-// Geometry of a slot: the piece's 8 code rows `rs` bytes apart (sb * CB + 16), then the scales.
+// Geometry of a slot: the piece's 8 code rows `rs` bytes apart (sb * CB + 16), then its 8 scale rows
+// `ss` bytes apart (sb * 2 + 16): every row one bulk copy, each 16-byte pad moving the next row
+// to other banks.
 __host__ __device__ inline int mm_row_stride(int sb, int cb) { return sb * cb + 16; }
-__host__ __device__ inline int mm_slot_bytes(int sb, int cb) { return QTR * mm_row_stride(sb, cb) + QTR * sb * 2; }
+__host__ __device__ inline int mm_scale_stride(int sb) { return sb * 2 + 16; }
+__host__ __device__ inline int mm_slot_bytes(int sb, int cb) { return QTR * (mm_row_stride(sb, cb) + mm_scale_stride(sb)); }
+// Staged activation rows: scales (f16 bits) nb + 8 apart, code sums nb + 4 apart (16-byte pads).
+__host__ __device__ inline int mm_dh_stride(int nb) { return nb + 8; }
+__host__ __device__ inline int mm_s8_stride(int nb) { return nb + 4; }
 
 // One row's epilogue value(s) y[r] for (activation row m, weight row `row` of matrix `mat`):
 // the one-row GEMV's epilogue (gemv_epi_store) for one activation row.
@@ -137,10 +143,11 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_kernel(FusedArgs a, Ge
     uint64_t *empty = full + MM_MAXNS;
     float2 *xch = (float2 *)(empty + MM_MAXNS);  // [team][2][NR][8 chains][32 lanes] chain exchange
     const int K = (int)a.K, nb = G.nb, M = a.M, kp = K + 16;
+    const int dhs = mm_dh_stride(nb), s8s = mm_s8_stride(nb);
     int8_t *sx = (int8_t *)(xch + MM_TEAMS * 2 * MM_MAXNR * 8 * 32);
     uint16_t *sdh = (uint16_t *)(sx + (size_t)M * kp);
-    int *ss8 = (int *)(sdh + (size_t)M * nb + ((M * nb) & 1));  // 4-byte aligned
-    unsigned char *slots = (unsigned char *)smem + ((((size_t)((char *)(ss8 + (size_t)M * nb) - (char *)smem)) + 127) & ~(size_t)127);
+    int *ss8 = (int *)(sdh + (size_t)M * dhs);  // nb + 8 halves a row: 16-byte aligned
+    unsigned char *slots = (unsigned char *)smem + ((((size_t)((char *)(ss8 + (size_t)M * s8s) - (char *)smem)) + 127) & ~(size_t)127);
     const Ring R{full, empty, slots, (uint32_t)ns, magic, slot_bytes};
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -174,17 +181,23 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_kernel(FusedArgs a, Ge
                             ok = false;
                             break;
                         }
-                        const uint32_t code_row = (uint32_t)(sb * CB), scl = (uint32_t)(QTR * sb * 2);
-                        mbar_expect_tx(&R.full[slot], QTR * code_row + scl);
+                        const uint32_t code_row = (uint32_t)(sb * CB), scl_row = (uint32_t)(sb * 2);
+                        const int ss = mm_scale_stride(sb);
+                        mbar_expect_tx(&R.full[slot], QTR * (code_row + scl_row));
                         int mat, tile;
                         const char *src = gemv_piece(a, G, (int)blockIdx.x + (c0 + q) * (int)gridDim.x, r, s, &mat, &tile);
                         unsigned char *dst = R.data(t);
                         for (int rr = 0; rr < QTR; rr++) {
-                            if (a.stream_evict_first) bulk_g2s_hint(dst + rr * rs, src + rr * code_row, code_row, &R.full[slot], policy);
-                            else bulk_g2s(dst + rr * rs, src + rr * code_row, code_row, &R.full[slot]);
+                            unsigned char *dc = dst + rr * rs, *ds = dst + QTR * rs + rr * ss;
+                            const char *sc = src + rr * code_row, *sl = src + QTR * code_row + rr * scl_row;
+                            if (a.stream_evict_first) {
+                                bulk_g2s_hint(dc, sc, code_row, &R.full[slot], policy);
+                                bulk_g2s_hint(ds, sl, scl_row, &R.full[slot], policy);
+                            } else {
+                                bulk_g2s(dc, sc, code_row, &R.full[slot]);
+                                bulk_g2s(ds, sl, scl_row, &R.full[slot]);
+                            }
                         }
-                        if (a.stream_evict_first) bulk_g2s_hint(dst + QTR * rs, src + QTR * code_row, scl, &R.full[slot], policy);
-                        else bulk_g2s(dst + QTR * rs, src + QTR * code_row, scl, &R.full[slot]);
                     }
             }
         }
@@ -210,8 +223,9 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_kernel(FusedArgs a, Ge
             *(int4 *)(sx + (size_t)m * kp + c * 16) = __ldcg((const int4 *)(gc + (size_t)m * K) + c);
         }
         for (int i = threadIdx.x; i < M * nb; i += MMW * 32) {
-            sdh[i] = __half_as_ushort(__float2half_rn(__ldcg(gd + i)));  // the scales are f16 values: exact
-            ss8[i] = __ldcg(gs + i);
+            const int m = i / nb, b = i - m * nb;
+            sdh[m * dhs + b] = __half_as_ushort(__float2half_rn(__ldcg(gd + i)));  // the scales are f16 values: exact
+            ss8[m * s8s + b] = __ldcg(gs + i);
         }
         named_bar(1, MMW * 32);
     }
@@ -250,16 +264,17 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_kernel(FusedArgs a, Ge
                 if (ok && !gemv_wait_piece(R, t)) ok = false;
                 if (!ok) continue;
                 const unsigned char *piece = R.data(t);
+                const int ssh = mm_scale_stride(sb) / 2;  // halves between scale rows
                 const uint16_t *scl = (const uint16_t *)(piece + QTR * rs);
                 for (int u = 0; u < sb / 32; u++) {
                     const int j0 = 32 * u + 8 * q;  // this warp's 8 consecutive blocks of the segment
                     // the 8 blocks' scales of weight rows row0, row0 + 1 and the activation row's
-                    uint4 w0s = *(const uint4 *)(scl + (2 * tg) * sb + j0), w1s = *(const uint4 *)(scl + (2 * tg + 1) * sb + j0);
-                    const uint4 dxs = *(const uint4 *)(sdh + msrc * nb + bbase + j0);
+                    uint4 w0s = *(const uint4 *)(scl + (2 * tg) * ssh + j0), w1s = *(const uint4 *)(scl + (2 * tg + 1) * ssh + j0);
+                    const uint4 dxs = *(const uint4 *)(sdh + msrc * dhs + bbase + j0);
                     const uint16_t *sw0 = (const uint16_t *)&w0s, *sw1 = (const uint16_t *)&w1s, *sdx = (const uint16_t *)&dxs;
                     int s8v[8];
                     if (QT == 0) {
-                        const int4 lo = *(const int4 *)(ss8 + msrc * nb + bbase + j0), hi = *(const int4 *)(ss8 + msrc * nb + bbase + j0 + 4);
+                        const int4 lo = *(const int4 *)(ss8 + msrc * s8s + bbase + j0), hi = *(const int4 *)(ss8 + msrc * s8s + bbase + j0 + 4);
                         s8v[0] = lo.x, s8v[1] = lo.y, s8v[2] = lo.z, s8v[3] = lo.w;
                         s8v[4] = hi.x, s8v[5] = hi.y, s8v[6] = hi.z, s8v[7] = hi.w;
                     }
@@ -381,7 +396,7 @@ void launch_mma(const FusedArgs &a, const GemvGeo &G, cudaStream_t s, bool pdl) 
     const int nb = (int)(a.K / 32), M = a.M;
     const int slot_bytes = mm_slot_bytes(QSEG < nb ? QSEG : nb, CB);
     size_t head = (size_t)2 * MM_MAXNS * 8 + (size_t)MM_TEAMS * 2 * MM_MAXNR * 8 * 32 * sizeof(float2);
-    head += (size_t)M * (a.K + 16) + (size_t)M * nb * 2 + 4 + (size_t)M * nb * 4;
+    head += (size_t)M * (a.K + 16) + (size_t)M * mm_dh_stride(nb) * 2 + (size_t)M * mm_s8_stride(nb) * 4;
     head = (head + 127) / 128 * 128;
     int ns = ring_slots(224 * 1024, head, (size_t)slot_bytes, MM_MAXNS);
     if (ns < 2) throw std::runtime_error("gemv_mma: the staged rows leave no room for the weight ring");
