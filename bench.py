@@ -193,7 +193,8 @@ def sweep(args) -> None:
     bytes / FLOPs rates. `--shape NxK --m M --wtype T` runs one case (the ncu captures use that)."""
     import torch
 
-    from ggml_compiler_b200.programs import write_mul_mat
+    from ggml_compiler_b200.gguf_write import BLOCKS
+    from ggml_compiler_b200.programs import random_block_rows, write_mul_mat
     from ggml_compiler_b200.runtime import Model
 
     peak, peak_kind = peaks()
@@ -213,7 +214,9 @@ def sweep(args) -> None:
             for M in ms_:
                 p = CACHE / f"mm_{wt}_{N}x{Kd}_m{M}.gguf"
                 if not p.exists():
-                    if w is None:
+                    if w is None and wt in ("iq4_nl", "q4_k", "q5_k", "q6_k"):  # no encoder: synthetic blocks
+                        w = random_block_rows(wt, N, Kd, seed=0)
+                    elif w is None:
                         w = rng.standard_normal((N, Kd), dtype=np.float32) * np.float32(0.02)
                     write_mul_mat(p, w, wt, M)
                 x = np.random.default_rng(1).standard_normal((1, M, Kd), dtype=np.float32)
@@ -230,7 +233,7 @@ def sweep(args) -> None:
                     s.profile(False)
                 kinds = [k for k in ks if k.startswith(("gemv", "mul_mat"))]
                 ms = sum(ks[k]["ms"] for k in kinds) / max(1, sum(ks[k]["launches"] for k in kinds))
-                wbytes = N * Kd * (18 if wt == "q4_0" else 34) / 32
+                wbytes = N * Kd * BLOCKS[wt][1] / BLOCKS[wt][0]  # the format's stored bytes
                 byts = wbytes + 4.0 * M * Kd + 4.0 * M * N
                 flops = 2.0 * M * N * Kd
                 print(json.dumps({"metric": "isolated quantized mul_mat (BASELINE config 2)", "kernel": "+".join(kinds),
@@ -453,7 +456,9 @@ def main() -> None:
     ap.add_argument("--config", default="8b", choices=["8b", "70b", "tiny", "sweep", "prefill", "attn", "batch"])
     ap.add_argument("--shape", default=None, help="sweep: one weight shape NxK")
     ap.add_argument("--m", type=int, default=None, help="sweep: one activation row count")
-    ap.add_argument("--wtype", default=None, choices=["q4_0", "q8_0"], help="sweep: one weight type")
+    ap.add_argument("--wtype", default=None,
+                    choices=["q4_0", "q8_0", "q4_1", "q5_0", "q5_1", "iq4_nl", "q4_k", "q5_k", "q6_k"],
+                    help="sweep: one weight type (the other block formats run only when named)")
     ap.add_argument("--parallel", default="replicas", choices=["tp", "replicas"],
                     help="N>1: N independent sequences (replicas), or one sequence tensor-parallel over the N GPUs (tp)")
     ap.add_argument("--cpu-tokens", type=int, default=12)  # about 10 s of the oracle on 16 host threads

@@ -168,9 +168,10 @@ size_t ggml_compiler_quantize(const char *type, const float *src, int64_t nrows,
         if (!type || !src || !dst) throw std::runtime_error("NULL argument");
         const gcb::TypeTraits *t = gcb::type_by_name(type);
         if (!t) throw std::runtime_error(std::string("unknown tensor type '") + type + "'");
-        if (t->type != gcb::T_Q4_0 && t->type != gcb::T_Q8_0 && t->type != gcb::T_F32 && t->type != gcb::T_F16 &&
-            t->type != gcb::T_BF16)
-            throw std::runtime_error(std::string("this backend encodes q4_0, q8_0, f16, bf16 and f32; not '") + type + "'");
+        if (t->type != gcb::T_Q4_0 && t->type != gcb::T_Q8_0 && t->type != gcb::T_Q4_1 && t->type != gcb::T_Q5_0 &&
+            t->type != gcb::T_Q5_1 && t->type != gcb::T_F32 && t->type != gcb::T_F16 && t->type != gcb::T_BF16)
+            throw std::runtime_error(std::string("this backend encodes q4_0, q4_1, q5_0, q5_1, q8_0, f16, bf16 and f32; not '") +
+                                     type + "' (it computes with iq4_nl and the K-quants stored by another encoder)");
         if (n_per_row <= 0 || nrows < 0) throw std::runtime_error("bad row count or length");
         if (n_per_row % t->block)
             throw std::runtime_error("row length " + std::to_string(n_per_row) + " is not a multiple of " + type +

@@ -188,12 +188,25 @@ FusionPlan find_fusions(Model &m, const StageSpec &s, Planner &p) {
     fp.group_of.assign(s.nodes.size(), -1);
     if (std::getenv("GGML_COMPILER_B200_NOFUSE")) return fp;
     Graph g(s);
+    // Emitter marks: a stage whose nodes carry "fuse" marks fuses exactly the groups it marked (a
+    // matched group whose nodes are one whole mark of the matched kind); other matches run unfused.
+    // A stage without marks (a program from an emitter that writes none) is matched as a whole.
+    std::map<std::string, size_t> mark_size;
+    for (const auto &n : s.nodes)
+        if (!n.fuse.empty()) mark_size[n.fuse]++;
+    static const char *kind_mark[] = {"qkv.", "glu.", "head.", "resid."};
     auto claim = [&](std::vector<int> nodes, std::function<void(Planner &)> emit, std::shared_ptr<GroupDesc> desc) {
         for (int x : nodes)
             if (fp.group_of[(size_t)x] >= 0) return false;
         FusionGroup grp;
         std::sort(nodes.begin(), nodes.end());
         nodes.erase(std::unique(nodes.begin(), nodes.end()), nodes.end());
+        if (!mark_size.empty()) {
+            const std::string &mk = g.n(nodes.front()).fuse;
+            if (mk.empty() || mk.rfind(kind_mark[desc->kind], 0) != 0 || mark_size[mk] != nodes.size()) return false;
+            for (int x : nodes)
+                if (g.n(x).fuse != mk) return false;
+        }
         for (int x : nodes) grp.nodes.push_back((size_t)x);
         grp.anchor = (size_t)nodes.front();
         grp.emit = std::move(emit);

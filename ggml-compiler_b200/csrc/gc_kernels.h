@@ -45,6 +45,16 @@ namespace k {
 size_t quant_device_bytes(Type t, int64_t rows, int64_t K);
 void repack_quant(Type t, const uint8_t *raw, int64_t nrows, int64_t K, char *dst, cudaStream_t s);
 
+// The other GGUF block formats (kernels/gc_blockq.cu). q5_0 and iq4_nl are expanded at load into
+// the Q8_0 tiled layout (quant_device_bytes(T_Q8_0, ...) bytes) and then are Q8_0 weights; q4_1,
+// q5_1, q4_K, q5_K and q6_K stay in their GGUF layout (nb[0] = unit bytes, nb[1] = row bytes) and
+// multiply through mul_mat_block.
+bool expands_to_q8_0(Type t);
+bool raw_block_type(Type t);
+void expand_to_q8_0(Type t, const uint8_t *raw, int64_t nrows, int64_t K, char *dst, cudaStream_t s);
+size_t mul_mat_block_scratch_bytes(const TD &a, const TD &b);
+void mul_mat_block(const TD &a, const TD &b, const TD &out, void *scratch, cudaStream_t s);
+
 // Elementwise and row ops (generic strides).
 void copy(const TD &src, const TD &dst, cudaStream_t s);  // cont / cpy / cast (f32, f16, bf16, i32)
 enum BinOp { ADD = 0, SUB = 1, MUL = 2, DIV = 3 };

@@ -158,7 +158,8 @@ void Model::load_weights() {
             Weight w;
             w.td.type = t.type;
             for (int i = 0; i < 4; i++) w.td.ne[i] = t.ne[i];
-            const bool q = t.type == T_Q4_0 || t.type == T_Q8_0;
+            // Q4_0 / Q8_0 are repacked into the tiled layout; q5_0 / iq4_nl expanded into it as Q8_0
+            const bool q = t.type == T_Q4_0 || t.type == T_Q8_0 || k::expands_to_q8_0(t.type);
             char *dst;
             if (q) {
                 if (raw.size() < t.nbytes) raw.alloc(t.nbytes);
@@ -180,8 +181,14 @@ void Model::load_weights() {
             }
             if (q) {
                 const int64_t K = t.ne[0], rows = t.ne[1] * t.ne[2] * t.ne[3];
-                w.data.alloc(k::quant_device_bytes(t.type, rows, K));
-                k::repack_quant(t.type, (const uint8_t *)raw.get(), rows, K, w.data.get(), stream);
+                if (k::expands_to_q8_0(t.type)) {
+                    w.td.type = T_Q8_0;
+                    w.data.alloc(k::quant_device_bytes(T_Q8_0, rows, K));
+                    k::expand_to_q8_0(t.type, (const uint8_t *)raw.get(), rows, K, w.data.get(), stream);
+                } else {
+                    w.data.alloc(k::quant_device_bytes(t.type, rows, K));
+                    k::repack_quant(t.type, (const uint8_t *)raw.get(), rows, K, w.data.get(), stream);
+                }
                 cuda_check(cudaStreamSynchronize(stream), "repack");
             }
             w.td.data = w.data.get();

@@ -366,13 +366,16 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
         if (a.ne[0] != b.ne[0] || b.ne[2] % a.ne[2] != 0 || b.ne[3] % a.ne[3] != 0)
             fail(n, "cannot multiply " + shape_str(a.ne) + " by " + shape_str(b.ne));
         if (a.ne[0] > 1 && a.nb[0] > a.nb[1] && !is_quant(a.type)) fail(n, "weight operand is transposed; it needs a cont first");
-        if (is_quant(a.type) && !a.contiguous()) fail(n, "quantized weight must be contiguous");
-        if (!is_quant(a.type) && a.type != T_F32 && a.type != T_F16 && a.type != T_BF16)
-            fail(n, std::string("weight type ") + type_name(a.type) + " is not supported by this backend (Q4_0, Q8_0, f16, bf16, f32 are)");
+        const bool raw_q = k::raw_block_type(a.type);
+        if ((is_quant(a.type) || raw_q) && !a.contiguous()) fail(n, "quantized weight must be contiguous");
+        if (!is_quant(a.type) && !raw_q && a.type != T_F32 && a.type != T_F16 && a.type != T_BF16)
+            fail(n, std::string("weight type ") + type_name(a.type) +
+                        " is not supported by this backend (q4_0, q4_1, q5_0, q5_1, q8_0, iq4_nl, q4_K, q5_K, q6_K, f16, bf16, f32 are)");
         if (b.type != T_F32) fail(n, "activation operand must be f32");
         int64_t ne[4] = {a.ne[1], b.ne[1], b.ne[2], b.ne[3]};
         TD y = out_like(T_F32, ne);
         const double bytes = (double)(is_quant(a.type) ? (double)a.nrows() * (a.ne[0] / 32) * (quant_code_bytes(a.type) + 2)
+                                      : raw_q           ? (double)a.nrows() * (double)row_size(a.type, a.ne[0])
                                                         : (double)a.nelements() * a.elsize()) +
                              (double)b.nelements() * 4 + (double)y.nelements() * 4;
         if (is_quant(a.type) && a.ne[2] == 1 && a.ne[3] == 1 && b.ne[2] == 1 && b.ne[3] == 1 && b.nb[0] == 4 &&
@@ -599,7 +602,9 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
         need_src(n, sv, 2, 2);
         const TD &tab = sv[0], &idx = sv[1];
         if (idx.type != T_I32) fail(n, "row indices must be i32");
-        if (is_quant(tab.type) && !tab.contiguous()) fail(n, "quantized table must be contiguous");
+        if ((is_quant(tab.type) || k::raw_block_type(tab.type)) && !tab.contiguous()) fail(n, "quantized table must be contiguous");
+        if (is_quantized(tab.type) && !is_quant(tab.type) && !k::raw_block_type(tab.type))
+            fail(n, std::string("table type ") + type_name(tab.type) + " is not supported by this backend");
         int64_t ne[4] = {tab.ne[0], idx.ne[0], idx.ne[1], idx.ne[2]};
         TD y = out_like(T_F32, ne);
         add("get_rows", n.id, {tab, idx, y}, [](cudaStream_t st, const std::vector<TD> &t) { k::get_rows(t[0], t[1], t[2], st); },

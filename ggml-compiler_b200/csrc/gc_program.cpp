@@ -242,6 +242,7 @@ class Reader {
             n.ne_expr = dims4(jn.at("ne"), s.reads);
             if (const Json *p = jn.find("p")) n.p = *p;
             if (const Json *l = jn.find("loc"); l && l->is_string()) n.loc = l->as_string();
+            if (const Json *f = jn.find("fuse"); f && f->is_string()) n.fuse = f->as_string();
             // a view's start and an arange's bounds may be dims too (format 3)
             for (const char *key : {"start", "stop"})
                 if (const Json *v = n.p.find(key); v && !v->is_number()) {

@@ -88,6 +88,9 @@ struct NodeSpec {
     std::vector<std::pair<std::string, DimExpr>> dim_params;
     std::vector<std::pair<std::string, int64_t>> p_bound;
     std::string loc;
+    // Optional emitter fusion mark ("<kind>.<n>", kind qkv / glu / head / resid): every node of
+    // one group the emitter expects to run as a fused kernel carries the same mark.
+    std::string fuse;
 
     bool has(const char *key) const;
     double pnum(const char *key) const;  // bound value of a parameter; throws if missing

@@ -156,6 +156,70 @@ void quantize_row_q4_0(const float *x, uint8_t *dst, int64_t n) {
     }
 }
 
+// Q4_1 / Q5_1: d = (max - min) / 15 or / 31, the block minimum as an fp16 offset, unsigned codes
+// min(top, trunc((x - min) / d + 0.5)) (ggml quantize_row_q4_1_ref / quantize_row_q5_1_ref). Q5_1
+// stores bit 4 of code j in bit j of a 32-bit word after the two scales.
+void quantize_row_q_min(const float *x, uint8_t *dst, int64_t n, int bits) {
+    const int bs = bits == 4 ? 20 : 24, top = (1 << bits) - 1;
+    for (int64_t b = 0; b < n / QK; b++) {
+        const float *xb = x + b * QK;
+        uint8_t *yb = dst + b * bs;
+        float lo = xb[0], hi = xb[0];
+        for (int j = 1; j < QK; j++) {
+            lo = xb[j] < lo ? xb[j] : lo;
+            hi = xb[j] > hi ? xb[j] : hi;
+        }
+        const float d = (hi - lo) / (float)top;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        const uint16_t dh = f32_to_f16(d), mh = f32_to_f16(lo);
+        std::memcpy(yb, &dh, 2);
+        std::memcpy(yb + 2, &mh, 2);
+        uint32_t qh = 0;
+        uint8_t *qs = yb + (bits == 4 ? 4 : 8);
+        for (int j = 0; j < QK / 2; j++) {
+            int q0 = (int)std::trunc((xb[j] - lo) * id + 0.5f);
+            int q1 = (int)std::trunc((xb[QK / 2 + j] - lo) * id + 0.5f);
+            q0 = q0 < 0 ? 0 : (q0 > top ? top : q0);
+            q1 = q1 < 0 ? 0 : (q1 > top ? top : q1);
+            qs[j] = (uint8_t)((q0 & 15) | ((q1 & 15) << 4));
+            qh |= (uint32_t)(q0 >> 4) << j;
+            qh |= (uint32_t)(q1 >> 4) << (j + QK / 2);
+        }
+        if (bits == 5) std::memcpy(yb + 4, &qh, 4);
+    }
+}
+
+// Q5_0: the signed value of largest magnitude (first on ties) sets d = max / -16; codes
+// min(31, trunc(x / d + 16.5)), bit 4 of code j in bit j of the word after the scale
+// (ggml quantize_row_q5_0_ref).
+void quantize_row_q5_0(const float *x, uint8_t *dst, int64_t n) {
+    for (int64_t b = 0; b < n / QK; b++) {
+        const float *xb = x + b * QK;
+        uint8_t *yb = dst + b * 22;
+        float amax = 0.0f, max = 0.0f;
+        for (int j = 0; j < QK; j++)
+            if (amax < std::fabs(xb[j])) {
+                amax = std::fabs(xb[j]);
+                max = xb[j];
+            }
+        const float d = max / -16.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        const uint16_t dh = f32_to_f16(d);
+        std::memcpy(yb, &dh, 2);
+        uint32_t qh = 0;
+        for (int j = 0; j < QK / 2; j++) {
+            int q0 = (int)(xb[j] * id + 16.5f);
+            int q1 = (int)(xb[QK / 2 + j] * id + 16.5f);
+            q0 = q0 < 0 ? 0 : (q0 > 31 ? 31 : q0);
+            q1 = q1 < 0 ? 0 : (q1 > 31 ? 31 : q1);
+            yb[6 + j] = (uint8_t)((q0 & 15) | ((q1 & 15) << 4));
+            qh |= (uint32_t)(q0 >> 4) << j;
+            qh |= (uint32_t)(q1 >> 4) << (j + QK / 2);
+        }
+        std::memcpy(yb + 2, &qh, 4);
+    }
+}
+
 size_t quantize_rows(Type t, const float *src, int64_t nrows, int64_t n, uint8_t *dst) {
     const size_t rb = row_size(t, n);
     auto work = [&](int64_t r0, int64_t r1) {
@@ -165,6 +229,9 @@ size_t quantize_rows(Type t, const float *src, int64_t nrows, int64_t n, uint8_t
             switch (t) {
                 case T_Q8_0: quantize_row_q8_0(x, y, n); break;
                 case T_Q4_0: quantize_row_q4_0(x, y, n); break;
+                case T_Q4_1: quantize_row_q_min(x, y, n, 4); break;
+                case T_Q5_1: quantize_row_q_min(x, y, n, 5); break;
+                case T_Q5_0: quantize_row_q5_0(x, y, n); break;
                 case T_F32: std::memcpy(y, x, (size_t)n * 4); break;
                 case T_F16:
                     for (int64_t i = 0; i < n; i++) {

@@ -49,6 +49,8 @@ uint16_t f32_to_bf16(float f);
 // Q8_0 :378-402, which state bit-equality with ggml-quants.c). Rows are n elements, n % 32 == 0.
 void quantize_row_q8_0(const float *x, uint8_t *dst, int64_t n);
 void quantize_row_q4_0(const float *x, uint8_t *dst, int64_t n);
+void quantize_row_q_min(const float *x, uint8_t *dst, int64_t n, int bits);  // q4_1 (4), q5_1 (5)
+void quantize_row_q5_0(const float *x, uint8_t *dst, int64_t n);
 // Multithreaded over rows; returns bytes written.
 size_t quantize_rows(Type t, const float *src, int64_t nrows, int64_t n, uint8_t *dst);
 

@@ -1,0 +1,348 @@
+// mul_mat with a weight in one of the other GGUF block formats the reference can store
+// (ggml_compiler/quant/types.py:6-19), and the load-time expansion of q5_0 / iq4_nl.
+//
+// q5_0 and iq4_nl: ggml's CPU dots (vec_dot_q5_0_q8_0, vec_dot_iq4_nl_q8_0) are the integer dot of
+// the block's signed codes (q - 16, or the iq4_nl table value) with the Q8_0 activation codes,
+// scaled by d_w * d_x: exactly a Q8_0 x Q8_0 block dot. So these weights are expanded once at load
+// into the Q8_0 tiled layout (same fp16 scale, codes as int8) and every Q8_0 kernel (the fused
+// decode GEMVs, the tensor-core GEMV and GEMM) runs them with unchanged results.
+//
+// q4_1, q5_1, q4_K, q5_K, q6_K stay in their GGUF layout. Their activation rows are quantized the
+// way ggml's CPU backend quantizes src1 for them (Q8_1: the Q8_0 codes and scale plus the fp16
+// s = d * sum(codes); Q8_K: 256-value super-blocks with an f32 scale 1 / (-127 / max) and int16
+// sums of 16 codes), and one warp computes one output: unit u (a 32-block, or a 256-value
+// super-block) of the row into lane u % 32, then the 32-lane butterfly. The integer parts of a unit
+// are exact; its float steps:
+//   q4_1, q5_1:  p = fma(d_w * d_x, isum, p);  p = fma(m_w, s_x, p)
+//   q4_K, q5_K:  p = fma(d_w * d_x, sum_j sc_j isum_j, p);  p = fma(-(dmin_w * d_x), sum_j m_j bsum_j, p)
+//   q6_K:        p = fma(d_w * d_x, sum_j sc_j isum_j, p)
+// These are the per-unit terms of ggml's vec_dot_q4_1_q8_1 ... vec_dot_q6_K_q8_K; the CPU checker
+// sums them in the same order.
+#include <algorithm>
+#include <stdexcept>
+#include <string>
+
+#include "../gc_kernels.h"
+#include "gc_blockq.cuh"
+#include "gc_qweight.cuh"
+
+namespace gcb {
+namespace k {
+
+namespace {
+
+void check(const char *what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) throw std::runtime_error(std::string("CUDA launch of ") + what + " failed: " + cudaGetErrorString(e));
+}
+
+unsigned grid_for(int64_t threads) {
+    int64_t b = (threads + 255) / 256;
+    b = std::min<int64_t>(std::max<int64_t>(b, 1), 148 * 32);
+    return (unsigned)b;
+}
+
+// q5_0 / iq4_nl GGUF rows -> the Q8_0 tiled layout (gc_qweight.cuh), one thread per block.
+__global__ void expand_q8_0_kernel(int type, const uint8_t *raw, int64_t rows, int64_t nb, char *dst) {
+    const int bs = type == T_Q5_0 ? 22 : 18;
+    const QW w{dst, nb, 32};
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < rows * nb; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = t / nb, blk = t % nb;
+        const uint8_t *src = raw + t * bs;
+        const uint8_t *qs = src + (type == T_Q5_0 ? 6 : 2);
+        const uint32_t qh = type == T_Q5_0 ? (uint32_t)src[2] | ((uint32_t)src[3] << 8) | ((uint32_t)src[4] << 16) |
+                                                 ((uint32_t)src[5] << 24)
+                                           : 0u;
+        uint32_t words[8];
+        for (int i = 0; i < 8; i++) {
+            uint32_t word = 0;
+            for (int b = 0; b < 4; b++) {
+                const int j = 4 * i + b;  // value j
+                const uint8_t byte = qs[j & 15];
+                int q = j < 16 ? (byte & 15) : (byte >> 4);
+                if (type == T_Q5_0) q = (q | (int)(((qh >> j) & 1u) << 4)) - 16;
+                else q = iq4nl_value(q);
+                word |= (uint32_t)(uint8_t)(int8_t)q << (8 * b);
+            }
+            words[i] = word;
+        }
+        char *code = (char *)qw_code(w, row, blk);
+        *(uint4 *)code = make_uint4(words[0], words[1], words[2], words[3]);
+        *(uint4 *)(code + 16) = make_uint4(words[4], words[5], words[6], words[7]);
+        const int64_t g = blk / QSEG, sb = qw_seg_blocks(nb, g);
+        uint16_t *sc = (uint16_t *)(dst + qw_piece_off(nb, 32, row / QTR, g) + QTR * sb * 32);
+        sc[(row % QTR) * sb + blk % QSEG] = (uint16_t)(src[0] | (src[1] << 8));
+    }
+}
+
+struct Act {  // activation rows [K, M, B2, B3] (f32, any strides) and their quantized form
+    const char *b;
+    int64_t K, M, B2, B3;
+    int64_t bnb0, bnb1, bnb2, bnb3;
+    int8_t *qx;    // [rows][K] codes
+    uint16_t *dx;  // Q8_1: [rows][K/32] fp16 scales
+    uint16_t *sx;  // Q8_1: [rows][K/32] fp16 d * sum(codes)
+    float *dk;     // Q8_K: [rows][K/256] scales
+    int16_t *bs;   // Q8_K: [rows][K/16] sums of 16 codes
+};
+
+__device__ __forceinline__ float act_x(const Act &a, int64_t r, int64_t k) {
+    const int64_t m = r % a.M, i2 = (r / a.M) % a.B2, i3 = r / (a.M * a.B2);
+    return *(const float *)(a.b + m * a.bnb1 + i2 * a.bnb2 + i3 * a.bnb3 + k * a.bnb0);
+}
+
+// Q8_1 (ggml's x86 quantize_row_q8_1): one warp per 32-block; d = amax / 127 (fp16), codes
+// nearest-even(x * (127 / amax)), s = fp16((amax / 127) * sum(codes)).
+__global__ void act_q8_1_kernel(Act a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nb = a.K / 32, nblk = nb * a.M * a.B2 * a.B3;
+    for (int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; w < nblk; w += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+        const int64_t r = w / nb, blk = w % nb;
+        const float x = act_x(a, r, blk * 32 + lane);
+        const float amax = warp_max(fabsf(x));
+        const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        const int q = __float2int_rn(__fmul_rn(x, id));
+        a.qx[r * a.K + blk * 32 + lane] = (int8_t)q;
+        const int sum = __reduce_add_sync(0xffffffffu, q);
+        if (lane == 0) {
+            const float d = __fdiv_rn(amax, 127.0f);
+            a.dx[r * nb + blk] = f2h(d);
+            a.sx[r * nb + blk] = f2h(__fmul_rn(d, __int2float_rn(sum)));
+        }
+    }
+}
+
+// Q8_K (ggml quantize_row_q8_K_ref): one warp per 256 values, lane l owns values 8l .. 8l + 7. The
+// value of largest magnitude (first on ties) sets iscale = -127 / max; codes min(127,
+// nearest-even(iscale * x)); d = 1 / iscale; an all-zero super-block gets d = 0 and zero codes.
+__global__ void act_q8_K_kernel(Act a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nsb = a.K / 256, n = nsb * a.M * a.B2 * a.B3;
+    for (int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; w < n; w += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+        const int64_t r = w / nsb, sb = w % nsb;
+        float x[8], amax = 0.0f, mx = 0.0f;
+        for (int i = 0; i < 8; i++) {
+            x[i] = act_x(a, r, sb * 256 + lane * 8 + i);
+            if (fabsf(x[i]) > amax) {
+                amax = fabsf(x[i]);
+                mx = x[i];
+            }
+        }
+        int at = lane;  // the winning lane: larger magnitude, the lower lane (earlier values) on ties
+        for (int off = 16; off >= 1; off >>= 1) {
+            const float oa = __shfl_xor_sync(0xffffffffu, amax, off), om = __shfl_xor_sync(0xffffffffu, mx, off);
+            const int ol = __shfl_xor_sync(0xffffffffu, at, off);
+            if (oa > amax || (oa == amax && ol < at)) {
+                amax = oa;
+                mx = om;
+                at = ol;
+            }
+        }
+        int8_t *q = a.qx + r * a.K + sb * 256 + lane * 8;
+        int sum = 0;
+        if (amax == 0.0f) {
+            for (int i = 0; i < 8; i++) q[i] = 0;
+        } else {
+            const float iscale = __fdiv_rn(-127.0f, mx);
+            for (int i = 0; i < 8; i++) {
+                const int v = min(127, __float2int_rn(__fmul_rn(iscale, x[i])));
+                q[i] = (int8_t)v;
+                sum += v;
+            }
+            if (lane == 0) a.dk[r * nsb + sb] = __fdiv_rn(1.0f, iscale);
+        }
+        if (amax == 0.0f && lane == 0) a.dk[r * nsb + sb] = 0.0f;
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        if ((lane & 1) == 0) a.bs[r * (a.K / 16) + sb * 16 + lane / 2] = (int16_t)sum;
+    }
+}
+
+struct MMb {
+    const char *a;
+    int64_t anb1, anb2, anb3;
+    int64_t K, N, A2, A3, M, B2, B3;
+    Act x;
+    float *out;
+};
+
+// Integer dot of 32 unsigned 4/5-bit codes (4 words of low values 0..15, 4 of high values 16..31,
+// already carrying bit 4) with 32 activation codes.
+__device__ __forceinline__ int dot32(const uint32_t *lo, const uint32_t *hi, const int8_t *x) {
+    const int4 xa = *(const int4 *)x, xb = *(const int4 *)(x + 16);
+    int s = __dp4a((int)lo[0], xa.x, 0);
+    s = __dp4a((int)lo[1], xa.y, s);
+    s = __dp4a((int)lo[2], xa.z, s);
+    s = __dp4a((int)lo[3], xa.w, s);
+    s = __dp4a((int)hi[0], xb.x, s);
+    s = __dp4a((int)hi[1], xb.y, s);
+    s = __dp4a((int)hi[2], xb.z, s);
+    return __dp4a((int)hi[3], xb.w, s);
+}
+
+// 32 codes of a K-quant sub-block (8 words, value order) against its activation codes
+__device__ __forceinline__ int dot8w(const uint32_t *c, const int8_t *x) {
+    const int4 xa = *(const int4 *)x, xb = *(const int4 *)(x + 16);
+    int s = __dp4a((int)c[0], xa.x, 0);
+    s = __dp4a((int)c[1], xa.y, s);
+    s = __dp4a((int)c[2], xa.z, s);
+    s = __dp4a((int)c[3], xa.w, s);
+    s = __dp4a((int)c[4], xb.x, s);
+    s = __dp4a((int)c[5], xb.y, s);
+    s = __dp4a((int)c[6], xb.z, s);
+    return __dp4a((int)c[7], xb.w, s);
+}
+
+template <int T>
+__global__ void mm_block_kernel(MMb p) {
+    constexpr int UN = (T == T_Q4_1 || T == T_Q5_1) ? 32 : 256;
+    constexpr int UB = T == T_Q4_1 ? 20 : T == T_Q5_1 ? 24 : T == T_Q4_K ? 144 : T == T_Q5_K ? 176 : 210;
+    const int lane = threadIdx.x & 31;
+    const int64_t nu = p.K / UN, nout = p.N * p.M * p.B2 * p.B3;
+    for (int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; w < nout; w += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+        const int64_t n = w % p.N, r = w / p.N;
+        const int64_t i2 = (r / p.M) % p.B2, i3 = r / (p.M * p.B2);
+        const int64_t a2 = i2 / (p.B2 / p.A2), a3 = i3 / (p.B3 / p.A3);
+        const uint8_t *row = (const uint8_t *)(p.a + n * p.anb1 + a2 * p.anb2 + a3 * p.anb3);
+        const int8_t *xq = p.x.qx + r * p.K;
+        float acc = 0.0f;
+        for (int64_t u = lane; u < nu; u += 32) {
+            const uint8_t *blk = row + u * UB;
+            const int8_t *xu = xq + u * UN;
+            if constexpr (T == T_Q4_1 || T == T_Q5_1) {
+                const uint8_t *qs = blk + (T == T_Q4_1 ? 4 : 8);
+                uint32_t lo[4], hi[4];
+                const uint32_t qh = T == T_Q5_1 ? ld32(blk + 4) : 0u;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const uint32_t v = ld32(qs + 4 * i);
+                    lo[i] = (v & 0x0f0f0f0fu) | spread4((qh >> (4 * i)) & 15u);
+                    hi[i] = ((v >> 4) & 0x0f0f0f0fu) | spread4((qh >> (16 + 4 * i)) & 15u);
+                }
+                const int isum = dot32(lo, hi, xu);
+                const int64_t bi = r * nu + u;
+                acc = __fmaf_rn(__fmul_rn(h2f((uint16_t)ld16(blk)), h2f(p.x.dx[bi])), __int2float_rn(isum), acc);
+                acc = __fmaf_rn(h2f((uint16_t)ld16(blk + 2)), h2f(p.x.sx[bi]), acc);
+            } else if constexpr (T == T_Q6_K) {
+                int isc = 0;
+#pragma unroll 4
+                for (int j = 0; j < 16; j++) {  // sub-block j: values 16j .. 16j + 15
+                    const int v0 = 16 * j, h = v0 / 128, rr = v0 % 128;
+                    const int4 xv = *(const int4 *)(xu + v0);
+                    const int xs[4] = {xv.x, xv.y, xv.z, xv.w};
+                    int t = 0;
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const int r4 = rr + 4 * i;
+                        const uint32_t ql = ld32a2(blk + 64 * h + r4 % 64), qh = ld32a2(blk + 128 + 32 * h + r4 % 32);
+                        const uint32_t q = ((ql >> (4 * (r4 / 64))) & 0x0f0f0f0fu) | (((qh >> (2 * (r4 / 32))) & 0x03030303u) << 4);
+                        t = __dp4a((int)__vsub4(q, 0x20202020u), xs[i], t);
+                    }
+                    isc += (int)(int8_t)blk[192 + j] * t;
+                }
+                const float dx = p.x.dk[r * nu + u];
+                acc = __fmaf_rn(__fmul_rn(h2f((uint16_t)ld16(blk + 208)), dx), __int2float_rn(isc), acc);
+            } else {  // q4_K, q5_K
+                uint8_t s12[12];
+#pragma unroll
+                for (int i = 0; i < 3; i++) {
+                    const uint32_t v = ld32(blk + 4 + 4 * i);
+                    s12[4 * i] = (uint8_t)v, s12[4 * i + 1] = (uint8_t)(v >> 8), s12[4 * i + 2] = (uint8_t)(v >> 16),
+                            s12[4 * i + 3] = (uint8_t)(v >> 24);
+                }
+                const int16_t *bs = p.x.bs + (r * nu + u) * 16;
+                const uint8_t *qs = blk + (T == T_Q4_K ? 16 : 48);
+                int isc = 0, imn = 0;
+#pragma unroll 2
+                for (int g = 0; g < 4; g++) {  // sub-blocks 2g (low nibbles) and 2g + 1 (high nibbles)
+                    uint32_t c0[8], c1[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const uint32_t v = ld32(qs + 32 * g + 4 * i);
+                        c0[i] = v & 0x0f0f0f0fu;
+                        c1[i] = (v >> 4) & 0x0f0f0f0fu;
+                        if constexpr (T == T_Q5_K) {
+                            const uint32_t hv = ld32(blk + 16 + 4 * i);
+                            c0[i] |= ((hv >> (2 * g)) & 0x01010101u) << 4;
+                            c1[i] |= ((hv >> (2 * g + 1)) & 0x01010101u) << 4;
+                        }
+                    }
+                    int sc, m;
+                    kq_scale_min(s12, 2 * g, sc, m);
+                    isc += sc * dot8w(c0, xu + 64 * g);
+                    imn += m * ((int)bs[4 * g] + (int)bs[4 * g + 1]);
+                    kq_scale_min(s12, 2 * g + 1, sc, m);
+                    isc += sc * dot8w(c1, xu + 64 * g + 32);
+                    imn += m * ((int)bs[4 * g + 2] + (int)bs[4 * g + 3]);
+                }
+                const float dx = p.x.dk[r * nu + u];
+                acc = __fmaf_rn(__fmul_rn(h2f((uint16_t)ld16(blk)), dx), __int2float_rn(isc), acc);
+                acc = __fmaf_rn(-__fmul_rn(h2f((uint16_t)ld16(blk + 2)), dx), __int2float_rn(imn), acc);
+            }
+        }
+        acc = warp_butterfly(acc);
+        if (lane == 0) p.out[w] = acc;
+    }
+}
+
+bool k_quant(Type t) { return t == T_Q4_K || t == T_Q5_K || t == T_Q6_K; }
+
+}  // namespace
+
+bool raw_block_type(Type t) { return t == T_Q4_1 || t == T_Q5_1 || k_quant(t); }
+bool expands_to_q8_0(Type t) { return t == T_Q5_0 || t == T_IQ4_NL; }
+
+void expand_to_q8_0(Type t, const uint8_t *raw, int64_t nrows, int64_t K, char *dst, cudaStream_t s) {
+    if (!expands_to_q8_0(t) || K % 32) throw std::runtime_error("expand_to_q8_0: not a q5_0 / iq4_nl row set");
+    expand_q8_0_kernel<<<grid_for(nrows * (K / 32)), 256, 0, s>>>((int)t, raw, nrows, K / 32, dst);
+    check("expand_q8_0");
+}
+
+size_t mul_mat_block_scratch_bytes(const TD &a, const TD &b) {
+    const int64_t rows = b.ne[1] * b.ne[2] * b.ne[3], K = a.ne[0];
+    const size_t q = ((size_t)(rows * K) + 255) / 256 * 256;
+    if (k_quant(a.type)) return q + ((size_t)(rows * (K / 256)) * 4 + 255) / 256 * 256 + (size_t)(rows * (K / 16)) * 2 + 256;
+    return q + 2 * (((size_t)(rows * (K / 32)) * 2 + 255) / 256 * 256) + 256;
+}
+
+void mul_mat_block(const TD &a, const TD &b, const TD &out, void *scratch, cudaStream_t s) {
+    const int un = k_quant(a.type) ? 256 : 32;
+    if (!raw_block_type(a.type) || a.ne[0] % un) throw std::runtime_error("mul_mat_block: unsupported weight");
+    MMb p{};
+    p.a = a.data;
+    p.anb1 = a.nb[1], p.anb2 = a.nb[2], p.anb3 = a.nb[3];
+    p.K = a.ne[0], p.N = a.ne[1], p.A2 = a.ne[2], p.A3 = a.ne[3];
+    p.M = b.ne[1], p.B2 = b.ne[2], p.B3 = b.ne[3];
+    Act &x = p.x;
+    x.b = b.data;
+    x.K = p.K, x.M = p.M, x.B2 = p.B2, x.B3 = p.B3;
+    x.bnb0 = b.nb[0], x.bnb1 = b.nb[1], x.bnb2 = b.nb[2], x.bnb3 = b.nb[3];
+    const int64_t rows = p.M * p.B2 * p.B3;
+    char *sp = (char *)scratch;
+    x.qx = (int8_t *)sp;
+    sp += ((size_t)(rows * p.K) + 255) / 256 * 256;
+    if (k_quant(a.type)) {
+        x.dk = (float *)sp;
+        sp += ((size_t)(rows * (p.K / 256)) * 4 + 255) / 256 * 256;
+        x.bs = (int16_t *)sp;
+        act_q8_K_kernel<<<grid_for(rows * (p.K / 256) * 32), 256, 0, s>>>(x);
+    } else {
+        x.dx = (uint16_t *)sp;
+        sp += ((size_t)(rows * (p.K / 32)) * 2 + 255) / 256 * 256;
+        x.sx = (uint16_t *)sp;
+        act_q8_1_kernel<<<grid_for(rows * (p.K / 32) * 32), 256, 0, s>>>(x);
+    }
+    check("act_q8_1 / act_q8_K");
+    p.out = (float *)out.data;
+    const unsigned g = grid_for(p.N * rows * 32);
+    switch (a.type) {
+        case T_Q4_1: mm_block_kernel<T_Q4_1><<<g, 256, 0, s>>>(p); break;
+        case T_Q5_1: mm_block_kernel<T_Q5_1><<<g, 256, 0, s>>>(p); break;
+        case T_Q4_K: mm_block_kernel<T_Q4_K><<<g, 256, 0, s>>>(p); break;
+        case T_Q5_K: mm_block_kernel<T_Q5_K><<<g, 256, 0, s>>>(p); break;
+        default: mm_block_kernel<T_Q6_K><<<g, 256, 0, s>>>(p); break;
+    }
+    check("mul_mat_block");
+}
+
+}  // namespace k
+}  // namespace gcb

@@ -8,6 +8,7 @@
 #include <string>
 
 #include "../gc_kernels.h"
+#include "gc_blockq.cuh"
 #include "gc_math.cuh"
 #include "gc_qweight.cuh"
 
@@ -29,6 +30,10 @@ void set_contiguous(TD &t) {
     if (t.type == T_Q4_0 || t.type == T_Q8_0) {
         t.nb[0] = 1;
         t.nb[1] = (int64_t)(t.ne[0] / 32 * quant_code_bytes(t.type));
+    } else if (is_quantized(t.type)) {  // other block formats: GGUF rows (ggml's nb)
+        const TypeTraits *tr = type_traits(t.type);
+        t.nb[0] = tr ? tr->block_size : 0;
+        t.nb[1] = (int64_t)row_size(t.type, t.ne[0]);
     } else {
         t.nb[0] = (int64_t)t.elsize();
         t.nb[1] = t.nb[0] * t.ne[0];
@@ -357,6 +362,9 @@ __global__ void get_rows_kernel(Dk tab, Dk idx, Dk out) {
                     q = (j < 16 ? (byte & 15) : (byte >> 4)) - 8;
                 }
                 v = __fmul_rn(d, (float)q);
+            } else if (tab.type == T_Q4_1 || tab.type == T_Q5_1 || tab.type == T_Q4_K || tab.type == T_Q5_K ||
+                       tab.type == T_Q6_K) {
+                v = dequant_raw(tab.type, (const uint8_t *)tab.data + row * tab.nb1 + i11 * tab.nb2 + i12 * tab.nb3, i0);
             } else {
                 v = ldf(at(tab, i0, row, i11, i12), tab.type);
             }

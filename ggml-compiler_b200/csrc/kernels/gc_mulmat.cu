@@ -10,7 +10,8 @@
 // round the activation to f16 first; f32 weights use it as is; element k then feeds lane k % 32.
 //
 // This is the correctness path for every shape; the decode-time fused GEMVs (gc_gemv.cu) and the
-// tensor-core prefill GEMM replace it on the hot path.
+// tensor-core prefill GEMM replace it on the hot path. Weights in the other block formats that stay
+// in their GGUF layout (q4_1, q5_1, K-quants) go to mul_mat_block (gc_blockq.cu).
 #include <algorithm>
 #include <cstdlib>
 #include <stdexcept>
@@ -201,6 +202,7 @@ MMk make(const TD &a, const TD &b, const TD &out) {
 }  // namespace
 
 size_t mul_mat_scratch_bytes(const TD &a, const TD &b) {
+    if (raw_block_type(a.type)) return mul_mat_block_scratch_bytes(a, b);
     if (a.type != T_Q4_0 && a.type != T_Q8_0) return 0;
     const int64_t rows = b.ne[1] * b.ne[2] * b.ne[3];
     const size_t q = (size_t)(rows * a.ne[0]);
@@ -208,6 +210,10 @@ size_t mul_mat_scratch_bytes(const TD &a, const TD &b) {
 }
 
 void mul_mat(const TD &a, const TD &b, const TD &out, void *scratch, cudaStream_t s, int *err) {
+    if (raw_block_type(a.type)) {
+        mul_mat_block(a, b, out, scratch, s);
+        return;
+    }
     MMk p = make(a, b, out);
     const int64_t nout = p.N * p.M * p.B2 * p.B3;
     if (a.type == T_Q4_0 || a.type == T_Q8_0) {

@@ -19,8 +19,11 @@ import numpy as np
 GGUF_VERSION = 3
 ALIGN = 32
 # GGUF type ids and (block elements, block bytes) of the types this writer stores.
-TYPE_IDS = {"f32": 0, "f16": 1, "q4_0": 2, "q8_0": 8, "i32": 26, "bf16": 30}
-BLOCKS = {"f32": (1, 4), "f16": (1, 2), "q4_0": (32, 18), "q8_0": (32, 34), "i32": (1, 4), "bf16": (1, 2)}
+TYPE_IDS = {"f32": 0, "f16": 1, "q4_0": 2, "q4_1": 3, "q5_0": 6, "q5_1": 7, "q8_0": 8, "q4_k": 12, "q5_k": 13,
+            "q6_k": 14, "iq4_nl": 20, "i32": 26, "bf16": 30}
+BLOCKS = {"f32": (1, 4), "f16": (1, 2), "q4_0": (32, 18), "q4_1": (32, 20), "q5_0": (32, 22), "q5_1": (32, 24),
+          "q8_0": (32, 34), "q4_k": (256, 144), "q5_k": (256, 176), "q6_k": (256, 210), "iq4_nl": (32, 18),
+          "i32": (1, 4), "bf16": (1, 2)}
 
 _T_U32, _T_STRING = 4, 8
 

@@ -27,6 +27,7 @@ from typing import Any, Callable, Sequence
 
 import numpy as np
 
+from .fusion import mark_fusion_groups
 from .gguf_write import TensorEntry, write_gguf
 
 KV_BLOCK = 256
@@ -367,14 +368,18 @@ def normal_weights(shape: tuple[int, ...], seed: int, index: int, std: float = 0
 
 def build_llama_gguf(path: str | Path, sh: LlamaShape, seed: int = 0,
                      encoder: Callable[[np.ndarray, str], np.ndarray] | None = None,
-                     weights: dict[str, np.ndarray] | None = None) -> dict[str, Any]:
+                     weights: dict[str, np.ndarray] | None = None, fusion_marks: bool = True) -> dict[str, Any]:
     """Write a Llama-shaped model as a ggml-compiler GGUF; returns its metadata. The weights are
     `weights` (f32 arrays by Hugging Face name, e.g. a LlamaForCausalLM's state dict) or, without
     it, seeded synthetic ones. `encoder(w, type)` encodes the quantized matrices (default: this
-    library's `runtime.encode`; any bit-exact Q4_0 / Q8_0 encoder writes the same bytes)."""
+    library's `runtime.encode`; any bit-exact Q4_0 / Q8_0 encoder writes the same bytes).
+    `fusion_marks`: the program's fusable node groups carry `"fuse"` marks (fusion.py); without
+    them the program is exactly the reference compiler's and the backend finds the groups itself."""
     if encoder is None:
         from .runtime import encode as encoder
     program, meta = llama_program(sh)
+    if fusion_marks:
+        program = mark_fusion_groups(program, {g: t for g, _, _, t in llama_weights(sh)}, in_place=True)
     entries = []
     names = {}
     for idx, (gname, hf, shape, typ) in enumerate(llama_weights(sh)):

@@ -38,6 +38,8 @@ def lib() -> ctypes.CDLL:
             "orc_dequantize": ([i, p, i64, i64, p], None),
             "orc_row_size": ([i, i64], ctypes.c_size_t),
             "orc_act_q8_0": ([p, i64, p, p], None),
+            "orc_act_q8_1": ([p, i64, p, p, p], None),
+            "orc_act_q8_K": ([p, i64, p, p, p], None),
             "orc_mul_mat": ([i, p, ctypes.c_size_t, i64, i64, p, i64, i64, p, i64], i),
             "orc_rms_norm": ([p, i64, f, p], None),
             "orc_soft_max": ([p, p, i64, f, p], None),
@@ -61,7 +63,9 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
-TYPES = {"f32": 0, "f16": 1, "q4_0": 2, "q8_0": 8}
+TYPES = {"f32": 0, "f16": 1, "q4_0": 2, "q4_1": 3, "q5_0": 6, "q5_1": 7, "q8_0": 8, "q4_k": 12, "q5_k": 13,
+         "q6_k": 14, "iq4_nl": 20}
+BLOCK_TYPES = ("q4_0", "q4_1", "q5_0", "q5_1", "q8_0", "q4_k", "q5_k", "q6_k", "iq4_nl")
 
 
 def _ptr(a: np.ndarray) -> int:
@@ -106,6 +110,26 @@ def act_q8_0(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     d = np.empty(x.size // 32, np.uint16)
     lib().orc_act_q8_0(_ptr(x), x.size, _ptr(q), _ptr(d))
     return q, d
+
+
+def act_q8_1(x: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Q8_1 activation blocks: codes, fp16 scale bits, fp16 d * sum(codes) bits."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    q = np.empty(x.size, np.int8)
+    d = np.empty(x.size // 32, np.uint16)
+    s = np.empty(x.size // 32, np.uint16)
+    lib().orc_act_q8_1(_ptr(x), x.size, _ptr(q), _ptr(d), _ptr(s))
+    return q, d, s
+
+
+def act_q8_k(x: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Q8_K activation super-blocks: codes, f32 scales, int16 sums of 16 codes."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    q = np.empty(x.size, np.int8)
+    d = np.empty(x.size // 256, np.float32)
+    bs = np.empty(x.size // 16, np.int16)
+    lib().orc_act_q8_K(_ptr(x), x.size, _ptr(q), _ptr(d), _ptr(bs))
+    return q, d, bs
 
 
 def rms_norm_rows(x: np.ndarray, eps: float) -> np.ndarray:

@@ -53,7 +53,11 @@
 #define QK 32
 #define FA_CHUNK 64
 
-enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q8_0 = 8 };
+enum {
+    ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q4_1 = 3, ORC_Q5_0 = 6, ORC_Q5_1 = 7, ORC_Q8_0 = 8,
+    ORC_Q4_K = 12, ORC_Q5_K = 13, ORC_Q6_K = 14, ORC_IQ4_NL = 20
+};
+#define QKK 256
 
 /* ---------------------------------------------------------------------------------------------
  * A static-schedule parallel for over [0, n) on all host threads (ORC_THREADS overrides). */
@@ -169,12 +173,82 @@ static void quant_q4_0_row(const float *x, uint8_t *y, int64_t n) {
     }
 }
 
+/* Q4_1 / Q5_1: d = (max - min) / (2^bits - 1), codes trunc((x - min) / d + 0.5) clipped, min kept
+ * as the block's fp16 offset (gguf-py quants.py Q4_1.quantize_blocks, Q5_1.quantize_blocks). */
+static void quant_q_min_row(const float *x, uint8_t *y, int64_t n, int bits) {
+    const int bs = bits == 4 ? 20 : 24, top = (1 << bits) - 1;
+    for (int64_t b = 0; b < n / QK; b++) {
+        const float *xb = x + b * QK;
+        uint8_t *yb = y + b * bs;
+        float mx = xb[0], mn = xb[0];
+        for (int j = 1; j < QK; j++) {
+            if (xb[j] > mx) mx = xb[j];
+            if (xb[j] < mn) mn = xb[j];
+        }
+        const float d = (mx - mn) / (float)top;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        const uint16_t dh = f2h(d), mh = f2h(mn);
+        memcpy(yb, &dh, 2);
+        memcpy(yb + 2, &mh, 2);
+        uint8_t q[QK];
+        for (int j = 0; j < QK; j++) {
+            const float t = truncf((xb[j] - mn) * id + 0.5f);
+            const int v = (int)t;
+            q[j] = (uint8_t)(v < 0 ? 0 : (v > top ? top : v));
+        }
+        uint8_t *qs = yb + (bits == 4 ? 4 : 8);
+        for (int j = 0; j < QK / 2; j++) qs[j] = (uint8_t)((q[j] & 15) | ((q[j + QK / 2] & 15) << 4));
+        if (bits == 5) {
+            uint32_t qh = 0;
+            for (int j = 0; j < QK; j++) qh |= (uint32_t)(q[j] >> 4) << j;
+            memcpy(yb + 4, &qh, 4);
+        }
+    }
+}
+
+/* Q5_0: the value of largest magnitude (first on ties) sets d = max / -16; codes
+ * trunc(x / d + 16.5) clipped to 0..31; bit 4 of code j in bit j of qh (gguf-py quants.py
+ * Q5_0.quantize_blocks). */
+static void quant_q5_0_row(const float *x, uint8_t *y, int64_t n) {
+    for (int64_t b = 0; b < n / QK; b++) {
+        const float *xb = x + b * QK;
+        uint8_t *yb = y + b * 22;
+        int imax = 0;
+        float amax = fabsf(xb[0]);
+        for (int j = 1; j < QK; j++)
+            if (fabsf(xb[j]) > amax) {
+                amax = fabsf(xb[j]);
+                imax = j;
+            }
+        const float d = xb[imax] / -16.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        const uint16_t dh = f2h(d);
+        memcpy(yb, &dh, 2);
+        uint8_t q[QK];
+        for (int j = 0; j < QK; j++) {
+            const int v = (int)truncf(xb[j] * id + 16.5f);
+            q[j] = (uint8_t)(v < 0 ? 0 : (v > 31 ? 31 : v));
+        }
+        uint32_t qh = 0;
+        for (int j = 0; j < QK; j++) qh |= (uint32_t)(q[j] >> 4) << j;
+        memcpy(yb + 2, &qh, 4);
+        for (int j = 0; j < QK / 2; j++) yb[6 + j] = (uint8_t)((q[j] & 15) | ((q[j + QK / 2] & 15) << 4));
+    }
+}
+
 size_t orc_row_size(int type, int64_t n) {
     switch (type) {
         case ORC_F32: return (size_t)n * 4;
         case ORC_F16: return (size_t)n * 2;
         case ORC_Q4_0: return (size_t)(n / QK) * 18;
         case ORC_Q8_0: return (size_t)(n / QK) * 34;
+        case ORC_Q4_1: return (size_t)(n / QK) * 20;
+        case ORC_Q5_0: return (size_t)(n / QK) * 22;
+        case ORC_Q5_1: return (size_t)(n / QK) * 24;
+        case ORC_IQ4_NL: return (size_t)(n / QK) * 18;
+        case ORC_Q4_K: return (size_t)(n / QKK) * 144;
+        case ORC_Q5_K: return (size_t)(n / QKK) * 176;
+        case ORC_Q6_K: return (size_t)(n / QKK) * 210;
         default: return 0;
     }
 }
@@ -190,38 +264,140 @@ typedef struct {
 static void quant_rows(void *c, int64_t r0, int64_t r1) {
     const quant_ctx *q = (const quant_ctx *)c;
     for (int64_t r = r0; r < r1; r++) {
-        if (q->type == ORC_Q8_0) quant_q8_0_row(q->src + r * q->n, q->dst + r * q->rb, q->n);
-        else if (q->type == ORC_Q4_0) quant_q4_0_row(q->src + r * q->n, q->dst + r * q->rb, q->n);
+        const float *x = q->src + r * q->n;
+        uint8_t *y = q->dst + r * q->rb;
+        switch (q->type) {
+            case ORC_Q8_0: quant_q8_0_row(x, y, q->n); break;
+            case ORC_Q4_0: quant_q4_0_row(x, y, q->n); break;
+            case ORC_Q4_1: quant_q_min_row(x, y, q->n, 4); break;
+            case ORC_Q5_1: quant_q_min_row(x, y, q->n, 5); break;
+            case ORC_Q5_0: quant_q5_0_row(x, y, q->n); break;
+            default: break;
+        }
     }
 }
 
 size_t orc_quantize(int type, const float *src, int64_t nrows, int64_t n, uint8_t *dst) {
     const size_t rb = orc_row_size(type, n);
-    if (rb == 0 || n % QK || (type != ORC_Q8_0 && type != ORC_Q4_0)) return 0;
+    if (rb == 0 || n % QK ||
+        (type != ORC_Q8_0 && type != ORC_Q4_0 && type != ORC_Q4_1 && type != ORC_Q5_0 && type != ORC_Q5_1))
+        return 0;
     quant_ctx c = {type, src, n, dst, rb};
     orc_parallel_for(nrows, quant_rows, &c);
     return rb * (size_t)nrows;
 }
 
+/* ---------------------------------------------------------------------------------------------
+ * Block layouts (the GGUF bytes; gguf-py quants.py dequantize_blocks restates each one):
+ *   q4_1 [d f16][m f16][16 B nibbles]        value j: low nibble of byte j, j + 16: high nibble
+ *   q5_0 [d f16][qh u32][16 B nibbles]       bit 4 of value j is bit j of qh; values q - 16
+ *   q5_1 [d f16][m f16][qh u32][16 B]
+ *   iq4_nl [d f16][16 B nibbles]             values IQ4_NL_VALUES[nibble]
+ *   q4_K [d f16][dmin f16][12 B 6-bit scales and mins][128 B nibbles]       256 values, 8 x 32
+ *   q5_K [d f16][dmin f16][12 B][32 B qh][128 B nibbles]
+ *   q6_K [128 B low nibbles][64 B 2-bit highs][16 int8 scales][d f16]          16 x 16, q - 32
+ * The iq4_nl value table is part of the format (gguf-py IQ4_NL.kvalues). */
+static const int8_t IQ4_NL_VALUES[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+static inline float blk_h(const uint8_t *p) {
+    uint16_t h;
+    memcpy(&h, p, 2);
+    return h2f(h);
+}
+
+/* Codes of one 32-value block as ggml's integer dot sees them: signed for q5_0 / iq4_nl (q4_0 and
+ * q8_0 too), unsigned (0..15 / 0..31, the offset m applied separately) for q4_1 / q5_1. */
+static void block_codes(int type, const uint8_t *blk, int *c) {
+    uint32_t qh = 0;
+    const uint8_t *qs;
+    switch (type) {
+        case ORC_Q4_0: qs = blk + 2; break;
+        case ORC_Q4_1: qs = blk + 4; break;
+        case ORC_Q5_0: memcpy(&qh, blk + 2, 4); qs = blk + 6; break;
+        case ORC_Q5_1: memcpy(&qh, blk + 4, 4); qs = blk + 8; break;
+        case ORC_IQ4_NL: qs = blk + 2; break;
+        default: /* q8_0 */
+            for (int j = 0; j < QK; j++) c[j] = (int8_t)blk[2 + j];
+            return;
+    }
+    for (int j = 0; j < QK / 2; j++) {
+        int lo = qs[j] & 15, hi = qs[j] >> 4;
+        lo |= (int)((qh >> j) & 1) << 4;
+        hi |= (int)((qh >> (j + 16)) & 1) << 4;
+        if (type == ORC_IQ4_NL) {
+            lo = IQ4_NL_VALUES[lo];
+            hi = IQ4_NL_VALUES[hi];
+        } else if (type == ORC_Q4_0) {
+            lo -= 8;
+            hi -= 8;
+        } else if (type == ORC_Q5_0) {
+            lo -= 16;
+            hi -= 16;
+        }
+        c[j] = lo;
+        c[j + 16] = hi;
+    }
+}
+
+/* q4_K / q5_K sub-block j (0..7): its 6-bit scale and min. */
+static void kq_scale_min(const uint8_t *sc12, int j, int *sc, int *m) {
+    if (j < 4) {
+        *sc = sc12[j] & 63;
+        *m = sc12[j + 4] & 63;
+    } else {
+        *sc = (sc12[j + 4] & 15) | ((sc12[j - 4] >> 6) << 4);
+        *m = (sc12[j + 4] >> 4) | ((sc12[j] >> 6) << 4);
+    }
+}
+
+/* Codes of one 256-value super-block: q4_K / q5_K unsigned (0..15 / 0..31), q6_K signed (q - 32). */
+static void kq_codes(int type, const uint8_t *blk, int *c) {
+    for (int v = 0; v < QKK; v++) {
+        const int j = v / 32, l = v % 32;
+        if (type == ORC_Q4_K) {
+            c[v] = (blk[16 + 32 * (j / 2) + l] >> (4 * (j % 2))) & 15;
+        } else if (type == ORC_Q5_K) {
+            c[v] = ((blk[48 + 32 * (j / 2) + l] >> (4 * (j % 2))) & 15) | (((blk[16 + l] >> j) & 1) << 4);
+        } else {
+            const int h = v / 128, r = v % 128;
+            const int lo = (blk[64 * h + r % 64] >> (4 * (r / 64))) & 15;
+            const int hi = (blk[128 + 32 * h + r % 32] >> (2 * (r / 32))) & 3;
+            c[v] = (lo | (hi << 4)) - 32;
+        }
+    }
+}
+
 void orc_dequantize(int type, const uint8_t *src, int64_t nrows, int64_t n, float *dst) {
     const size_t rb = orc_row_size(type, n);
+    const int kq = type == ORC_Q4_K || type == ORC_Q5_K || type == ORC_Q6_K;
+    const size_t ub = kq ? orc_row_size(type, QKK) : orc_row_size(type, QK);
+    const int64_t un = kq ? QKK : QK;
     for (int64_t r = 0; r < nrows; r++) {
         const uint8_t *x = src + r * rb;
         float *y = dst + r * n;
-        for (int64_t b = 0; b < n / QK; b++) {
-            if (type == ORC_Q8_0) {
-                uint16_t dh;
-                memcpy(&dh, x + b * 34, 2);
-                const float d = h2f(dh);
-                for (int j = 0; j < QK; j++) y[b * QK + j] = d * (float)(int8_t)x[b * 34 + 2 + j];
+        for (int64_t u = 0; u < n / un; u++) {
+            const uint8_t *blk = x + u * ub;
+            float *yu = y + u * un;
+            int c[QKK];
+            if (!kq) {
+                block_codes(type, blk, c);
+                const float d = blk_h(blk);
+                for (int j = 0; j < QK; j++) {
+                    if (type == ORC_Q4_1 || type == ORC_Q5_1) yu[j] = d * (float)c[j] + blk_h(blk + 2);
+                    else yu[j] = d * (float)c[j];
+                }
+            } else if (type == ORC_Q6_K) {
+                kq_codes(type, blk, c);
+                const float d = blk_h(blk + 208);
+                for (int v = 0; v < QKK; v++) yu[v] = (d * (float)(int8_t)blk[192 + v / 16]) * (float)c[v];
             } else {
-                uint16_t dh;
-                memcpy(&dh, x + b * 18, 2);
-                const float d = h2f(dh);
-                for (int j = 0; j < QK / 2; j++) {
-                    const uint8_t v = x[b * 18 + 2 + j];
-                    y[b * QK + j] = d * (float)((int)(v & 15) - 8);
-                    y[b * QK + j + 16] = d * (float)((int)(v >> 4) - 8);
+                kq_codes(type, blk, c);
+                const float d = blk_h(blk), dmin = blk_h(blk + 2);
+                for (int j = 0; j < 8; j++) {
+                    int sc, m;
+                    kq_scale_min(blk + 4, j, &sc, &m);
+                    const float d1 = d * (float)sc, m1 = dmin * (float)m;
+                    for (int l = 0; l < 32; l++) yu[32 * j + l] = d1 * (float)c[32 * j + l] - m1;
                 }
             }
         }
@@ -240,6 +416,56 @@ void orc_act_q8_0(const float *x, int64_t n, int8_t *q, uint16_t *d) {
         d[b] = f2h(amax / 127.0f);
         const float id = amax != 0.0f ? 127.0f / amax : 0.0f;
         for (int j = 0; j < QK; j++) q[b * QK + j] = (int8_t)(int)rintf(x[b * QK + j] * id);
+    }
+}
+
+/* Activation row -> Q8_1 blocks (src1 of a q4_1 / q5_1 mul_mat): the Q8_0 codes and scale above,
+ * plus s = d * sum(codes) with d = amax / 127 in f32, stored fp16 (ggml's x86 quantize_row_q8_1). */
+void orc_act_q8_1(const float *x, int64_t n, int8_t *q, uint16_t *d, uint16_t *s) {
+    orc_act_q8_0(x, n, q, d);
+    for (int64_t b = 0; b < n / QK; b++) {
+        float amax = 0.0f;
+        int sum = 0;
+        for (int j = 0; j < QK; j++) {
+            const float a = fabsf(x[b * QK + j]);
+            if (a > amax) amax = a;
+            sum += q[b * QK + j];
+        }
+        s[b] = f2h((amax / 127.0f) * (float)sum);
+    }
+}
+
+/* Activation row -> Q8_K super-blocks (src1 of a K-quant mul_mat; ggml quantize_row_q8_K_ref): the
+ * value of largest magnitude (first on ties) sets iscale = -127 / max; codes nearest-even(iscale * x)
+ * capped at 127; d = 1 / iscale in f32; bsums = sums of 16 consecutive codes. */
+void orc_act_q8_K(const float *x, int64_t n, int8_t *q, float *d, int16_t *bsums) {
+    for (int64_t b = 0; b < n / QKK; b++) {
+        const float *xb = x + b * QKK;
+        float amax = 0.0f, mx = 0.0f;
+        for (int j = 0; j < QKK; j++) {
+            const float a = fabsf(xb[j]);
+            if (a > amax) {
+                amax = a;
+                mx = xb[j];
+            }
+        }
+        if (amax == 0.0f) {
+            d[b] = 0.0f;
+            memset(q + b * QKK, 0, QKK);
+            memset(bsums + b * 16, 0, 32);
+            continue;
+        }
+        const float iscale = -127.0f / mx;
+        for (int j = 0; j < QKK; j++) {
+            const int v = (int)rintf(iscale * xb[j]);
+            q[b * QKK + j] = (int8_t)(v > 127 ? 127 : v);
+        }
+        for (int g = 0; g < 16; g++) {
+            int sum = 0;
+            for (int j = 0; j < 16; j++) sum += q[b * QKK + 16 * g + j];
+            bsums[b * 16 + g] = (int16_t)sum;
+        }
+        d[b] = 1.0f / iscale;
     }
 }
 
@@ -392,8 +618,135 @@ static void mm_float(int wtype, const uint8_t *W, size_t wrb, int64_t N, int64_t
     free(xr);
 }
 
+/* q4_1 / q5_1 / q4_K / q5_K / q6_K weights: one unit (a 32-value block, or a 256-value super-block
+ * for the K-quants) per step of the lane chains: unit u into partial u % 32, then the butterfly, for
+ * any number of activation rows. The integer parts are exact; the float steps per unit:
+ *   q4_1, q5_1:  p = fmaf(d_w * d_x, isum, p);  p = fmaf(m_w, s_x, p)
+ *   q4_K, q5_K:  p = fmaf(d_w * d_x, sum_j sc_j * isum_j, p);  p = fmaf(-(dmin_w * d_x), sum_j m_j * bsum_j, p)
+ *   q6_K:        p = fmaf(d_w * d_x, sum_j sc_j * isum_j, p)
+ * (d_x of a Q8_K row is f32; j runs over the 8 sub-blocks of 32, or the 16 of 16 for q6_K). ggml's
+ * CPU vec_dot_{q4_1_q8_1, q5_1_q8_1, q4_K_q8_K, q5_K_q8_K, q6_K_q8_K} compute the same per-unit terms. */
+typedef struct {
+    int wtype;
+    const uint8_t *W;
+    size_t wrb;
+    int64_t K, M, ldy;
+    const int8_t *qx;
+    const uint16_t *dx, *sx;
+    const float *dk;
+    const int16_t *bs;
+    float *Y;
+} mb_ctx;
+
+static void mm_block_rows(void *cv, int64_t n0, int64_t n1) {
+    const mb_ctx *c = (const mb_ctx *)cv;
+    const int kq = c->wtype == ORC_Q4_K || c->wtype == ORC_Q5_K || c->wtype == ORC_Q6_K;
+    const int64_t un = kq ? QKK : QK, nu = c->K / un;
+    const size_t ub = orc_row_size(c->wtype, un);
+    int codes[QKK];
+    for (int64_t n = n0; n < n1; n++) {
+        const uint8_t *w = c->W + (size_t)n * c->wrb;
+        for (int64_t m = 0; m < c->M; m++) {
+            float p[32] = {0};
+            const int8_t *xq = c->qx + m * c->K;
+            for (int64_t u = 0; u < nu; u++) {
+                const uint8_t *blk = w + u * ub;
+                const int8_t *xu = xq + u * un;
+                float *pp = &p[u & 31];
+                if (!kq) {
+                    block_codes(c->wtype, blk, codes);
+                    int32_t isum = 0;
+                    for (int j = 0; j < QK; j++) isum += codes[j] * xu[j];
+                    const int64_t bi = m * nu + u;
+                    *pp = fmaf(blk_h(blk) * h2f(c->dx[bi]), (float)isum, *pp);
+                    *pp = fmaf(blk_h(blk + 2), h2f(c->sx[bi]), *pp);
+                    continue;
+                }
+                kq_codes(c->wtype, blk, codes);
+                const float dx = c->dk[m * nu + u];
+                int32_t isc = 0, imn = 0;
+                if (c->wtype == ORC_Q6_K) {
+                    for (int j = 0; j < 16; j++) {
+                        int32_t t = 0;
+                        for (int l = 0; l < 16; l++) t += codes[16 * j + l] * xu[16 * j + l];
+                        isc += (int8_t)blk[192 + j] * t;
+                    }
+                    *pp = fmaf(blk_h(blk + 208) * dx, (float)isc, *pp);
+                    continue;
+                }
+                const int16_t *bs = c->bs + (m * nu + u) * 16;
+                for (int j = 0; j < 8; j++) {
+                    int sc, mn;
+                    kq_scale_min(blk + 4, j, &sc, &mn);
+                    int32_t t = 0;
+                    for (int l = 0; l < 32; l++) t += codes[32 * j + l] * xu[32 * j + l];
+                    isc += sc * t;
+                    imn += mn * (bs[2 * j] + bs[2 * j + 1]);
+                }
+                *pp = fmaf(blk_h(blk) * dx, (float)isc, *pp);
+                *pp = fmaf(-(blk_h(blk + 2) * dx), (float)imn, *pp);
+            }
+            c->Y[m * c->ldy + n] = butterfly32(p);
+        }
+    }
+}
+
+static void mm_block(int wtype, const uint8_t *W, size_t wrb, int64_t N, int64_t K, const float *X, int64_t ldx,
+                     int64_t M, float *Y, int64_t ldy) {
+    const int kq = wtype == ORC_Q4_K || wtype == ORC_Q5_K || wtype == ORC_Q6_K;
+    const int64_t nu = K / (kq ? QKK : QK);
+    int8_t *qx = (int8_t *)malloc((size_t)(M * K));
+    uint16_t *dx = (uint16_t *)malloc((size_t)(M * nu) * 2 + 2), *sx = (uint16_t *)malloc((size_t)(M * nu) * 2 + 2);
+    float *dk = (float *)malloc((size_t)(M * nu) * 4 + 4);
+    int16_t *bs = (int16_t *)malloc((size_t)(M * nu) * 32 + 2);
+    for (int64_t m = 0; m < M; m++) {
+        if (kq) orc_act_q8_K(X + m * ldx, K, qx + m * K, dk + m * nu, bs + m * nu * 16);
+        else orc_act_q8_1(X + m * ldx, K, qx + m * K, dx + m * nu, sx + m * nu);
+    }
+    mb_ctx c = {wtype, W, wrb, K, M, ldy, qx, dx, sx, dk, bs, Y};
+    orc_parallel_for(N, mm_block_rows, &c);
+    free(qx);
+    free(dx);
+    free(sx);
+    free(dk);
+    free(bs);
+}
+
+/* q5_0 / iq4_nl rows -> Q8_0 rows with the same fp16 scale: ggml's vec_dot_q5_0_q8_0 and
+ * vec_dot_iq4_nl_q8_0 take exactly the integer dot of these codes with the Q8_0 activation, scaled
+ * by d_w * d_x, so a q5_0 / iq4_nl matmul is the Q8_0 matmul of the expanded codes. */
+static uint8_t *expand_to_q8_0(int wtype, const uint8_t *W, size_t wrb, int64_t N, int64_t K) {
+    const int64_t nb = K / QK;
+    const size_t sb = orc_row_size(wtype, QK);
+    uint8_t *out = (uint8_t *)malloc((size_t)(N * nb) * 34);
+    int c[QK];
+    for (int64_t n = 0; n < N; n++)
+        for (int64_t b = 0; b < nb; b++) {
+            const uint8_t *blk = W + (size_t)n * wrb + b * sb;
+            uint8_t *o = out + (size_t)(n * nb + b) * 34;
+            block_codes(wtype, blk, c);
+            o[0] = blk[0];
+            o[1] = blk[1];
+            for (int j = 0; j < QK; j++) o[2 + j] = (uint8_t)(int8_t)c[j];
+        }
+    return out;
+}
+
 int orc_mul_mat(int wtype, const void *W, size_t w_row_bytes, int64_t N, int64_t K, const float *X, int64_t ldx,
                 int64_t M, float *Y, int64_t ldy) {
+    if (wtype == ORC_Q5_0 || wtype == ORC_IQ4_NL) {
+        if (K % QK) return -1;
+        uint8_t *w8 = expand_to_q8_0(wtype, (const uint8_t *)W, w_row_bytes, N, K);
+        mm_quant(ORC_Q8_0, w8, (size_t)(K / QK) * 34, N, K, X, ldx, M, Y, ldy);
+        free(w8);
+        return 0;
+    }
+    if (wtype == ORC_Q4_1 || wtype == ORC_Q5_1 || wtype == ORC_Q4_K || wtype == ORC_Q5_K || wtype == ORC_Q6_K) {
+        const int64_t un = (wtype == ORC_Q4_1 || wtype == ORC_Q5_1) ? QK : QKK;
+        if (K % un) return -1;
+        mm_block(wtype, (const uint8_t *)W, w_row_bytes, N, K, X, ldx, M, Y, ldy);
+        return 0;
+    }
     if (wtype == ORC_Q4_0 || wtype == ORC_Q8_0) {
         if (K % QK) return -1;
         mm_quant(wtype, (const uint8_t *)W, w_row_bytes, N, K, X, ldx, M, Y, ldy);

@@ -15,10 +15,10 @@ from typing import Any
 
 import numpy as np
 
-from . import dequantize, lib, mul_mat, rms_norm_rows
+from . import BLOCK_TYPES, dequantize, lib, mul_mat, rms_norm_rows
 
 _NP = {"f32": np.float32, "f16": np.float16, "i32": np.int32}
-_QUANT = ("q4_0", "q8_0")
+_QUANT = BLOCK_TYPES
 
 
 class Q:
