@@ -381,11 +381,30 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
         if (is_quant(a.type) && a.ne[2] == 1 && a.ne[3] == 1 && b.ne[2] == 1 && b.ne[3] == 1 && b.nb[0] == 4 &&
             (b.ne[1] == 1 || b.nb[1] == 4 * b.ne[0]) && k::fused_gemv_supported(a.ne[0], b.ne[1], MAP_SINGLE)) {
             const int64_t K = a.ne[0], N = a.ne[1], M = b.ne[1];
-            add_gemv(a.type == T_Q4_0 ? "gemv_q4_0" : "gemv_q8_0", n.id, {a, b, y},
-                     [K, N, M](const std::vector<TD> &t) {
+            // 2-8 rows: quantized once into the staging layout by act_rows, so the GEMV (the
+            // tensor-core one where it takes the shape) reads them instead of quantizing per CTA
+            TD act;
+            if (M >= 2 && !m.tp.active()) {
+                scratch_marker((size_t)((M * K + M * (K / 32) * 8 + 127) / 128 * 128), &act);
+                add("act_rows", n.id, {b, act},
+                    [K, M](cudaStream_t st, const std::vector<TD> &t) {
+                        FusedArgs fa;
+                        fa.pro = PRO_ACT;
+                        fa.x = (const float *)t[0].data;
+                        fa.ldx = K;
+                        fa.M = (int)M;
+                        fa.K = K;
+                        k::act_rows(fa, t[1].data, st);
+                    },
+                    (double)M * K * 5.25);
+            }
+            const bool staged = act.sid >= 0;
+            add_gemv(a.type == T_Q4_0 ? "gemv_q4_0" : "gemv_q8_0", n.id, {a, b, y, act},
+                     [K, N, M, staged](const std::vector<TD> &t) {
                          FusedArgs fa;
                          fa.qtype = t[0].type;
-                         fa.pro = PRO_ACT;
+                         fa.pro = staged ? PRO_Q8 : PRO_ACT;
+                         fa.xq = staged ? t[3].data : nullptr;
                          fa.map = MAP_SINGLE;
                          fa.x = (const float *)t[1].data;
                          fa.ldx = K;

@@ -10,9 +10,10 @@
 // q4_1, q5_1, q4_K, q5_K, q6_K stay in their GGUF layout. Their activation rows are quantized the
 // way ggml's CPU backend quantizes src1 for them (Q8_1: the Q8_0 codes and scale plus the fp16
 // s = d * sum(codes); Q8_K: 256-value super-blocks with an f32 scale 1 / (-127 / max) and int16
-// sums of 16 codes), and one warp computes one output: unit u (a 32-block, or a 256-value
-// super-block) of the row into lane u % 32, then the 32-lane butterfly. The integer parts of a unit
-// are exact; its float steps:
+// sums of 16 codes). A warp takes one weight row and up to 8 activation rows; for each output, unit
+// u of the row (a 32-block, or a 256-value super-block) is folded into the chain of lane u % 32 in
+// order of u, then the 32 chains are summed by the butterfly. The integer parts of a unit are
+// exact; its float steps:
 //   q4_1, q5_1:  p = fma(d_w * d_x, isum, p);  p = fma(m_w, s_x, p)
 //   q4_K, q5_K:  p = fma(d_w * d_x, sum_j sc_j isum_j, p);  p = fma(-(dmin_w * d_x), sum_j m_j bsum_j, p)
 //   q6_K:        p = fma(d_w * d_x, sum_j sc_j isum_j, p)
@@ -179,108 +180,172 @@ __device__ __forceinline__ int dot32(const uint32_t *lo, const uint32_t *hi, con
     return __dp4a((int)hi[3], xb.w, s);
 }
 
-// 32 codes of a K-quant sub-block (8 words, value order) against its activation codes
-__device__ __forceinline__ int dot8w(const uint32_t *c, const int8_t *x) {
-    const int4 xa = *(const int4 *)x, xb = *(const int4 *)(x + 16);
-    int s = __dp4a((int)c[0], xa.x, 0);
-    s = __dp4a((int)c[1], xa.y, s);
-    s = __dp4a((int)c[2], xa.z, s);
-    s = __dp4a((int)c[3], xa.w, s);
-    s = __dp4a((int)c[4], xb.x, s);
-    s = __dp4a((int)c[5], xb.y, s);
-    s = __dp4a((int)c[6], xb.z, s);
-    return __dp4a((int)c[7], xb.w, s);
-}
+constexpr int KQ_ROWS = 8;  // activation rows a warp takes at once (the weight codes stay in registers)
 
+// q4_1 / q5_1: a warp takes one weight row and up to KQ_ROWS activation rows of one batch index;
+// lane u owns blocks u, u + 32, ... (the chain of block u % 32) and decodes each block's codes once
+// for every activation row.
 template <int T>
-__global__ void mm_block_kernel(MMb p) {
-    constexpr int UN = (T == T_Q4_1 || T == T_Q5_1) ? 32 : 256;
-    constexpr int UB = T == T_Q4_1 ? 20 : T == T_Q5_1 ? 24 : T == T_Q4_K ? 144 : T == T_Q5_K ? 176 : 210;
+__global__ void mm_q1_kernel(MMb p) {
+    constexpr int UB = T == T_Q4_1 ? 20 : 24;
     const int lane = threadIdx.x & 31;
-    const int64_t nu = p.K / UN, nout = p.N * p.M * p.B2 * p.B3;
-    for (int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; w < nout; w += ((int64_t)gridDim.x * blockDim.x) >> 5) {
-        const int64_t n = w % p.N, r = w / p.N;
-        const int64_t i2 = (r / p.M) % p.B2, i3 = r / (p.M * p.B2);
+    const int64_t nu = p.K / 32;
+    const int64_t mgroups = (p.M + KQ_ROWS - 1) / KQ_ROWS;
+    const int64_t ntask = p.N * mgroups * p.B2 * p.B3;
+    for (int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; w < ntask; w += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+        const int64_t n = w % p.N;
+        int64_t t = w / p.N;
+        const int64_t mg = t % mgroups;
+        t /= mgroups;
+        const int64_t i2 = t % p.B2, i3 = t / p.B2;
         const int64_t a2 = i2 / (p.B2 / p.A2), a3 = i3 / (p.B3 / p.A3);
         const uint8_t *row = (const uint8_t *)(p.a + n * p.anb1 + a2 * p.anb2 + a3 * p.anb3);
-        const int8_t *xq = p.x.qx + r * p.K;
-        float acc = 0.0f;
+        const int m0 = (int)(mg * KQ_ROWS);
+        const int mr = (int)(p.M - m0 < KQ_ROWS ? p.M - m0 : KQ_ROWS);
+        const int64_t r0 = m0 + p.M * (i2 + p.B2 * i3);
+        float acc[KQ_ROWS];
+#pragma unroll
+        for (int k = 0; k < KQ_ROWS; k++) acc[k] = 0.0f;
         for (int64_t u = lane; u < nu; u += 32) {
             const uint8_t *blk = row + u * UB;
-            const int8_t *xu = xq + u * UN;
-            if constexpr (T == T_Q4_1 || T == T_Q5_1) {
-                const uint8_t *qs = blk + (T == T_Q4_1 ? 4 : 8);
-                uint32_t lo[4], hi[4];
-                const uint32_t qh = T == T_Q5_1 ? ld32(blk + 4) : 0u;
+            const uint8_t *qs = blk + (T == T_Q4_1 ? 4 : 8);
+            uint32_t lo[4], hi[4];
+            const uint32_t qh = T == T_Q5_1 ? ld32(blk + 4) : 0u;
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const uint32_t v = ld32(qs + 4 * i);
-                    lo[i] = (v & 0x0f0f0f0fu) | spread4((qh >> (4 * i)) & 15u);
-                    hi[i] = ((v >> 4) & 0x0f0f0f0fu) | spread4((qh >> (16 + 4 * i)) & 15u);
-                }
-                const int isum = dot32(lo, hi, xu);
-                const int64_t bi = r * nu + u;
-                acc = __fmaf_rn(__fmul_rn(h2f((uint16_t)ld16(blk)), h2f(p.x.dx[bi])), __int2float_rn(isum), acc);
-                acc = __fmaf_rn(h2f((uint16_t)ld16(blk + 2)), h2f(p.x.sx[bi]), acc);
-            } else if constexpr (T == T_Q6_K) {
-                int isc = 0;
-#pragma unroll 4
-                for (int j = 0; j < 16; j++) {  // sub-block j: values 16j .. 16j + 15
-                    const int v0 = 16 * j, h = v0 / 128, rr = v0 % 128;
-                    const int4 xv = *(const int4 *)(xu + v0);
-                    const int xs[4] = {xv.x, xv.y, xv.z, xv.w};
-                    int t = 0;
+            for (int i = 0; i < 4; i++) {
+                const uint32_t v = ld32(qs + 4 * i);
+                lo[i] = (v & 0x0f0f0f0fu) | spread4((qh >> (4 * i)) & 15u);
+                hi[i] = ((v >> 4) & 0x0f0f0f0fu) | spread4((qh >> (16 + 4 * i)) & 15u);
+            }
+            const float dw = h2f((uint16_t)ld16(blk)), mw = h2f((uint16_t)ld16(blk + 2));
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const int r4 = rr + 4 * i;
-                        const uint32_t ql = ld32a2(blk + 64 * h + r4 % 64), qh = ld32a2(blk + 128 + 32 * h + r4 % 32);
-                        const uint32_t q = ((ql >> (4 * (r4 / 64))) & 0x0f0f0f0fu) | (((qh >> (2 * (r4 / 32))) & 0x03030303u) << 4);
-                        t = __dp4a((int)__vsub4(q, 0x20202020u), xs[i], t);
-                    }
-                    isc += (int)(int8_t)blk[192 + j] * t;
-                }
-                const float dx = p.x.dk[r * nu + u];
-                acc = __fmaf_rn(__fmul_rn(h2f((uint16_t)ld16(blk + 208)), dx), __int2float_rn(isc), acc);
-            } else {  // q4_K, q5_K
-                uint8_t s12[12];
-#pragma unroll
-                for (int i = 0; i < 3; i++) {
-                    const uint32_t v = ld32(blk + 4 + 4 * i);
-                    s12[4 * i] = (uint8_t)v, s12[4 * i + 1] = (uint8_t)(v >> 8), s12[4 * i + 2] = (uint8_t)(v >> 16),
-                            s12[4 * i + 3] = (uint8_t)(v >> 24);
-                }
-                const int16_t *bs = p.x.bs + (r * nu + u) * 16;
-                const uint8_t *qs = blk + (T == T_Q4_K ? 16 : 48);
-                int isc = 0, imn = 0;
-#pragma unroll 2
-                for (int g = 0; g < 4; g++) {  // sub-blocks 2g (low nibbles) and 2g + 1 (high nibbles)
-                    uint32_t c0[8], c1[8];
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        const uint32_t v = ld32(qs + 32 * g + 4 * i);
-                        c0[i] = v & 0x0f0f0f0fu;
-                        c1[i] = (v >> 4) & 0x0f0f0f0fu;
-                        if constexpr (T == T_Q5_K) {
-                            const uint32_t hv = ld32(blk + 16 + 4 * i);
-                            c0[i] |= ((hv >> (2 * g)) & 0x01010101u) << 4;
-                            c1[i] |= ((hv >> (2 * g + 1)) & 0x01010101u) << 4;
-                        }
-                    }
-                    int sc, m;
-                    kq_scale_min(s12, 2 * g, sc, m);
-                    isc += sc * dot8w(c0, xu + 64 * g);
-                    imn += m * ((int)bs[4 * g] + (int)bs[4 * g + 1]);
-                    kq_scale_min(s12, 2 * g + 1, sc, m);
-                    isc += sc * dot8w(c1, xu + 64 * g + 32);
-                    imn += m * ((int)bs[4 * g + 2] + (int)bs[4 * g + 3]);
-                }
-                const float dx = p.x.dk[r * nu + u];
-                acc = __fmaf_rn(__fmul_rn(h2f((uint16_t)ld16(blk)), dx), __int2float_rn(isc), acc);
-                acc = __fmaf_rn(-__fmul_rn(h2f((uint16_t)ld16(blk + 2)), dx), __int2float_rn(imn), acc);
+            for (int k = 0; k < KQ_ROWS; k++) {
+                if (k >= mr) break;
+                const int64_t r = r0 + k, bi = r * nu + u;
+                const int isum = dot32(lo, hi, p.x.qx + r * p.K + u * 32);
+                acc[k] = __fmaf_rn(__fmul_rn(dw, h2f(p.x.dx[bi])), __int2float_rn(isum), acc[k]);
+                acc[k] = __fmaf_rn(mw, h2f(p.x.sx[bi]), acc[k]);
             }
         }
-        acc = warp_butterfly(acc);
-        if (lane == 0) p.out[w] = acc;
+#pragma unroll
+        for (int k = 0; k < KQ_ROWS; k++) {
+            if (k >= mr) break;
+            const float v = warp_butterfly(acc[k]);
+            if (lane == 0) p.out[(r0 + k) * p.N + n] = v;
+        }
+    }
+}
+
+// K-quants, sub-block parallel: a warp takes one weight row and up to KQ_ROWS activation rows of
+// one batch index; in step i its four 8-lane groups take super-blocks 4i .. 4i + 3, lane (g, j)
+// sub-block j of super-block 4i + g (32 values; for q6_K its two 16-value sub-blocks). The codes
+// stay in registers for every activation row. The 8 lanes' integer parts are summed exactly by
+// shuffles, and super-block s is folded into the chain of lane s % 32.
+template <int T>
+__global__ void mm_kq_kernel(MMb p) {
+    constexpr int UB = T == T_Q4_K ? 144 : T == T_Q5_K ? 176 : 210;
+    const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
+    const int64_t nu = p.K / 256;
+    const int64_t mgroups = (p.M + KQ_ROWS - 1) / KQ_ROWS;
+    const int64_t ntask = p.N * mgroups * p.B2 * p.B3;
+    for (int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; w < ntask; w += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+        const int64_t n = w % p.N;
+        int64_t t = w / p.N;
+        const int64_t mg = t % mgroups;
+        t /= mgroups;
+        const int64_t i2 = t % p.B2, i3 = t / p.B2;
+        const int64_t a2 = i2 / (p.B2 / p.A2), a3 = i3 / (p.B3 / p.A3);
+        const uint8_t *row = (const uint8_t *)(p.a + n * p.anb1 + a2 * p.anb2 + a3 * p.anb3);
+        const int m0 = (int)(mg * KQ_ROWS);
+        const int mr = (int)(p.M - m0 < KQ_ROWS ? p.M - m0 : KQ_ROWS);
+        const int64_t r0 = m0 + p.M * (i2 + p.B2 * i3);  // activation row index of m0
+        float acc[KQ_ROWS];
+#pragma unroll
+        for (int k = 0; k < KQ_ROWS; k++) acc[k] = 0.0f;
+        for (int64_t s0 = 0; s0 < nu; s0 += 4) {
+            const int64_t s = s0 + grp;
+            const bool have = s < nu;
+            const uint8_t *blk = row + (have ? s : 0) * UB;
+            uint32_t c[8];  // this lane's 32 codes (value order), signed bytes for q6_K
+            int sc0 = 0, sc1 = 0, mn = 0;
+            if (have) {
+                if constexpr (T == T_Q6_K) {
+                    const int h = sub / 4, r = 32 * (sub % 4);  // values 32 sub .. 32 sub + 31
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int r4 = r + 4 * i;
+                        const uint32_t ql = ld32a2(blk + 64 * h + r4 % 64), qh = ld32a2(blk + 128 + 32 * h + r4 % 32);
+                        c[i] = __vsub4(((ql >> (4 * (r4 / 64))) & 0x0f0f0f0fu) | (((qh >> (2 * (r4 / 32))) & 0x03030303u) << 4),
+                                       0x20202020u);
+                    }
+                    sc0 = (int8_t)blk[192 + 2 * sub];
+                    sc1 = (int8_t)blk[193 + 2 * sub];
+                } else {
+                    const uint8_t *qs = blk + (T == T_Q4_K ? 16 : 48) + 32 * (sub / 2);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        uint32_t v = (ld32(qs + 4 * i) >> (4 * (sub % 2))) & 0x0f0f0f0fu;
+                        if constexpr (T == T_Q5_K) v |= ((ld32(blk + 16 + 4 * i) >> sub) & 0x01010101u) << 4;
+                        c[i] = v;
+                    }
+                    kq_scale_min(blk + 4, sub, sc0, mn);
+                }
+            }
+            const uint16_t dh = have ? (uint16_t)ld16(blk + (T == T_Q6_K ? 208 : 0)) : (uint16_t)0;
+            const uint16_t mh = (have && T != T_Q6_K) ? (uint16_t)ld16(blk + 2) : (uint16_t)0;
+            const int base = (int)(s0 & 31), g2 = lane - base;
+            const bool mine = g2 >= 0 && g2 < 4 && s0 + g2 < nu;  // lane owns the chain of super-block s0 + g2
+            const int src = (mine ? g2 : 0) * 8;
+#pragma unroll
+            for (int k = 0; k < KQ_ROWS; k++) {
+                if (k >= mr) break;  // mr is the same on every lane
+                const int64_t r = r0 + k;
+                int isc = 0, imn = 0;
+                float dx = 0.0f;
+                if (have) {
+                    const int8_t *xu = p.x.qx + r * p.K + s * 256 + 32 * sub;
+                    const int4 xa = *(const int4 *)xu, xb = *(const int4 *)(xu + 16);
+                    int t0 = __dp4a((int)c[0], xa.x, 0);
+                    t0 = __dp4a((int)c[1], xa.y, t0);
+                    t0 = __dp4a((int)c[2], xa.z, t0);
+                    t0 = __dp4a((int)c[3], xa.w, t0);
+                    int t1 = __dp4a((int)c[4], xb.x, 0);
+                    t1 = __dp4a((int)c[5], xb.y, t1);
+                    t1 = __dp4a((int)c[6], xb.z, t1);
+                    t1 = __dp4a((int)c[7], xb.w, t1);
+                    if constexpr (T == T_Q6_K) {
+                        isc = sc0 * t0 + sc1 * t1;
+                    } else {
+                        isc = sc0 * (t0 + t1);
+                        const int16_t *bs = p.x.bs + (r * nu + s) * 16;
+                        imn = mn * ((int)bs[2 * sub] + (int)bs[2 * sub + 1]);
+                    }
+                    dx = p.x.dk[r * nu + s];
+                }
+                isc += __shfl_xor_sync(0xffffffffu, isc, 1);
+                isc += __shfl_xor_sync(0xffffffffu, isc, 2);
+                isc += __shfl_xor_sync(0xffffffffu, isc, 4);
+                if constexpr (T != T_Q6_K) {
+                    imn += __shfl_xor_sync(0xffffffffu, imn, 1);
+                    imn += __shfl_xor_sync(0xffffffffu, imn, 2);
+                    imn += __shfl_xor_sync(0xffffffffu, imn, 4);
+                }
+                const int visc = __shfl_sync(0xffffffffu, isc, src), vimn = __shfl_sync(0xffffffffu, imn, src);
+                const float vdx = __shfl_sync(0xffffffffu, dx, src);
+                const uint16_t vdh = (uint16_t)__shfl_sync(0xffffffffu, (int)dh, src);
+                const uint16_t vmh = (uint16_t)__shfl_sync(0xffffffffu, (int)mh, src);
+                if (mine) {
+                    acc[k] = __fmaf_rn(__fmul_rn(h2f(vdh), vdx), __int2float_rn(visc), acc[k]);
+                    if constexpr (T != T_Q6_K) acc[k] = __fmaf_rn(-__fmul_rn(h2f(vmh), vdx), __int2float_rn(vimn), acc[k]);
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < KQ_ROWS; k++) {
+            if (k >= mr) break;
+            const float v = warp_butterfly(acc[k]);
+            if (lane == 0) p.out[(r0 + k) * p.N + n] = v;
+        }
     }
 }
 
@@ -333,13 +398,13 @@ void mul_mat_block(const TD &a, const TD &b, const TD &out, void *scratch, cudaS
     }
     check("act_q8_1 / act_q8_K");
     p.out = (float *)out.data;
-    const unsigned g = grid_for(p.N * rows * 32);
+    const unsigned gk = grid_for(p.N * ((p.M + KQ_ROWS - 1) / KQ_ROWS) * p.B2 * p.B3 * 32);
     switch (a.type) {
-        case T_Q4_1: mm_block_kernel<T_Q4_1><<<g, 256, 0, s>>>(p); break;
-        case T_Q5_1: mm_block_kernel<T_Q5_1><<<g, 256, 0, s>>>(p); break;
-        case T_Q4_K: mm_block_kernel<T_Q4_K><<<g, 256, 0, s>>>(p); break;
-        case T_Q5_K: mm_block_kernel<T_Q5_K><<<g, 256, 0, s>>>(p); break;
-        default: mm_block_kernel<T_Q6_K><<<g, 256, 0, s>>>(p); break;
+        case T_Q4_1: mm_q1_kernel<T_Q4_1><<<gk, 256, 0, s>>>(p); break;
+        case T_Q5_1: mm_q1_kernel<T_Q5_1><<<gk, 256, 0, s>>>(p); break;
+        case T_Q4_K: mm_kq_kernel<T_Q4_K><<<gk, 256, 0, s>>>(p); break;
+        case T_Q5_K: mm_kq_kernel<T_Q5_K><<<gk, 256, 0, s>>>(p); break;
+        default: mm_kq_kernel<T_Q6_K><<<gk, 256, 0, s>>>(p); break;
     }
     check("mul_mat_block");
 }
