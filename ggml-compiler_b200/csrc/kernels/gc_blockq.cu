@@ -185,12 +185,12 @@ constexpr int KQ_ROWS = 8;  // activation rows a warp takes at once (the weight 
 // q4_1 / q5_1: a warp takes one weight row and up to KQ_ROWS activation rows of one batch index;
 // lane u owns blocks u, u + 32, ... (the chain of block u % 32) and decodes each block's codes once
 // for every activation row.
-template <int T>
+template <int T, int R>
 __global__ void mm_q1_kernel(MMb p) {
     constexpr int UB = T == T_Q4_1 ? 20 : 24;
     const int lane = threadIdx.x & 31;
     const int64_t nu = p.K / 32;
-    const int64_t mgroups = (p.M + KQ_ROWS - 1) / KQ_ROWS;
+    const int64_t mgroups = (p.M + R - 1) / R;
     const int64_t ntask = p.N * mgroups * p.B2 * p.B3;
     for (int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; w < ntask; w += ((int64_t)gridDim.x * blockDim.x) >> 5) {
         const int64_t n = w % p.N;
@@ -200,12 +200,12 @@ __global__ void mm_q1_kernel(MMb p) {
         const int64_t i2 = t % p.B2, i3 = t / p.B2;
         const int64_t a2 = i2 / (p.B2 / p.A2), a3 = i3 / (p.B3 / p.A3);
         const uint8_t *row = (const uint8_t *)(p.a + n * p.anb1 + a2 * p.anb2 + a3 * p.anb3);
-        const int m0 = (int)(mg * KQ_ROWS);
-        const int mr = (int)(p.M - m0 < KQ_ROWS ? p.M - m0 : KQ_ROWS);
+        const int m0 = (int)(mg * R);
+        const int mr = (int)(p.M - m0 < R ? p.M - m0 : R);
         const int64_t r0 = m0 + p.M * (i2 + p.B2 * i3);
-        float acc[KQ_ROWS];
+        float acc[R];
 #pragma unroll
-        for (int k = 0; k < KQ_ROWS; k++) acc[k] = 0.0f;
+        for (int k = 0; k < R; k++) acc[k] = 0.0f;
         for (int64_t u = lane; u < nu; u += 32) {
             const uint8_t *blk = row + u * UB;
             const uint8_t *qs = blk + (T == T_Q4_1 ? 4 : 8);
@@ -219,7 +219,7 @@ __global__ void mm_q1_kernel(MMb p) {
             }
             const float dw = h2f((uint16_t)ld16(blk)), mw = h2f((uint16_t)ld16(blk + 2));
 #pragma unroll
-            for (int k = 0; k < KQ_ROWS; k++) {
+            for (int k = 0; k < R; k++) {
                 if (k >= mr) break;
                 const int64_t r = r0 + k, bi = r * nu + u;
                 const int isum = dot32(lo, hi, p.x.qx + r * p.K + u * 32);
@@ -228,7 +228,7 @@ __global__ void mm_q1_kernel(MMb p) {
             }
         }
 #pragma unroll
-        for (int k = 0; k < KQ_ROWS; k++) {
+        for (int k = 0; k < R; k++) {
             if (k >= mr) break;
             const float v = warp_butterfly(acc[k]);
             if (lane == 0) p.out[(r0 + k) * p.N + n] = v;
@@ -236,115 +236,179 @@ __global__ void mm_q1_kernel(MMb p) {
     }
 }
 
-// K-quants, sub-block parallel: a warp takes one weight row and up to KQ_ROWS activation rows of
+// K-quants, sub-block parallel: a warp takes KQ_WR weight rows and up to KQ_ROWS activation rows of
 // one batch index; in step i its four 8-lane groups take super-blocks 4i .. 4i + 3, lane (g, j)
 // sub-block j of super-block 4i + g (32 values; for q6_K its two 16-value sub-blocks). The codes
 // stay in registers for every activation row. The 8 lanes' integer parts are summed exactly by
 // shuffles, and super-block s is folded into the chain of lane s % 32.
+
+// One lane's share of one super-block: its 32 codes (value order; signed bytes for q6_K), its
+// sub-block scales (q6_K: two int8 scales; q4_K/q5_K: 6-bit scale and min) and the fp16 d / dmin.
+struct KqPart {
+    uint32_t c[8];
+    int sc0, sc1, mn;
+    uint32_t dh, mh;
+};
+
 template <int T>
+__device__ __forceinline__ void kq_load(KqPart &k, const uint8_t *row, int64_t s, int64_t nu, int sub) {
+    constexpr int UB = T == T_Q4_K ? 144 : T == T_Q5_K ? 176 : 210;
+    k.sc0 = k.sc1 = k.mn = 0;
+    k.dh = k.mh = 0;
+    if (s >= nu) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) k.c[i] = 0;
+        return;
+    }
+    const uint8_t *blk = row + s * UB;
+    if constexpr (T == T_Q6_K) {
+        const int h = sub / 4, r = 32 * (sub % 4);  // values 32 sub .. 32 sub + 31
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int r4 = r + 4 * i;
+            const uint32_t ql = ld32a2(blk + 64 * h + r4 % 64), qh = ld32a2(blk + 128 + 32 * h + r4 % 32);
+            k.c[i] = __vsub4(((ql >> (4 * (r4 / 64))) & 0x0f0f0f0fu) | (((qh >> (2 * (r4 / 32))) & 0x03030303u) << 4),
+                             0x20202020u);
+        }
+        k.sc0 = (int8_t)blk[192 + 2 * sub];
+        k.sc1 = (int8_t)blk[193 + 2 * sub];
+        k.dh = ld16(blk + 208);
+    } else {
+        const uint4 *qs = (const uint4 *)(blk + (T == T_Q4_K ? 16 : 48) + 32 * (sub / 2));  // 16-byte aligned
+        const uint4 q0 = qs[0], q1 = qs[1];
+        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        uint32_t hb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if constexpr (T == T_Q5_K) {
+            const uint4 h0 = ((const uint4 *)(blk + 16))[0], h1 = ((const uint4 *)(blk + 16))[1];
+            const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++) hb[i] = ((hw[i] >> sub) & 0x01010101u) << 4;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) k.c[i] = ((w[i] >> (4 * (sub % 2))) & 0x0f0f0f0fu) | hb[i];
+        kq_scale_min(blk + 4, sub, k.sc0, k.mn);
+        k.dh = ld16(blk);
+        k.mh = ld16(blk + 2);
+    }
+}
+
+// Folds super-blocks s0 .. s0 + 3 (lane group g holds s0 + g) of KQ_WR weight rows into their
+// chains, for every activation row: each activation code slice is loaded once for the KQ_WR rows;
+// the 8 lanes' integer parts are summed by shuffles, then super-block s goes into lane s % 32's
+// chain.
+constexpr int KQ_WR = 2;  // weight rows per warp
+
+template <int T, int R>
+__device__ __forceinline__ void kq_fold(const KqPart *k, const MMb &p, int64_t s0, int64_t nu, int lane, int mr,
+                                        int64_t r0, float (*acc)[R]) {
+    const int sub = lane & 7;
+    const int64_t s = s0 + (lane >> 3);
+    const bool have = s < nu;
+    const int base = (int)(s0 & 31), g2 = lane - base;
+    const bool mine = g2 >= 0 && g2 < 4 && s0 + g2 < nu;  // lane owns the chain of super-block s0 + g2
+    const int src = (mine ? g2 : 0) * 8;
+#pragma unroll
+    for (int m = 0; m < R; m++) {
+        if (m >= mr) break;  // mr is the same on every lane
+        const int64_t r = r0 + m;
+        int isc[KQ_WR], imn[KQ_WR];
+        float dx = 0.0f;
+        int4 xa = make_int4(0, 0, 0, 0), xb = xa;
+        int bsum = 0;
+        if (have) {
+            const int8_t *xu = p.x.qx + r * p.K + s * 256 + 32 * sub;
+            xa = *(const int4 *)xu;
+            xb = *(const int4 *)(xu + 16);
+            dx = p.x.dk[r * nu + s];
+            if constexpr (T != T_Q6_K) {
+                const int16_t *bs = p.x.bs + (r * nu + s) * 16;
+                bsum = (int)bs[2 * sub] + (int)bs[2 * sub + 1];
+            }
+        }
+#pragma unroll
+        for (int w = 0; w < KQ_WR; w++) {
+            const uint32_t *c = k[w].c;
+            int t0 = __dp4a((int)c[0], xa.x, 0);
+            t0 = __dp4a((int)c[1], xa.y, t0);
+            t0 = __dp4a((int)c[2], xa.z, t0);
+            t0 = __dp4a((int)c[3], xa.w, t0);
+            int t1 = __dp4a((int)c[4], xb.x, 0);
+            t1 = __dp4a((int)c[5], xb.y, t1);
+            t1 = __dp4a((int)c[6], xb.z, t1);
+            t1 = __dp4a((int)c[7], xb.w, t1);
+            isc[w] = T == T_Q6_K ? k[w].sc0 * t0 + k[w].sc1 * t1 : k[w].sc0 * (t0 + t1);
+            imn[w] = k[w].mn * bsum;
+            isc[w] += __shfl_xor_sync(0xffffffffu, isc[w], 1);
+            isc[w] += __shfl_xor_sync(0xffffffffu, isc[w], 2);
+            isc[w] += __shfl_xor_sync(0xffffffffu, isc[w], 4);
+            if constexpr (T != T_Q6_K) {
+                imn[w] += __shfl_xor_sync(0xffffffffu, imn[w], 1);
+                imn[w] += __shfl_xor_sync(0xffffffffu, imn[w], 2);
+                imn[w] += __shfl_xor_sync(0xffffffffu, imn[w], 4);
+            }
+        }
+        const float vdx = __shfl_sync(0xffffffffu, dx, src);
+#pragma unroll
+        for (int w = 0; w < KQ_WR; w++) {
+            const int visc = __shfl_sync(0xffffffffu, isc[w], src), vimn = __shfl_sync(0xffffffffu, imn[w], src);
+            const uint16_t vdh = (uint16_t)__shfl_sync(0xffffffffu, k[w].dh, src);
+            const uint16_t vmh = (uint16_t)__shfl_sync(0xffffffffu, k[w].mh, src);
+            if (mine) {
+                acc[w][m] = __fmaf_rn(__fmul_rn(h2f(vdh), vdx), __int2float_rn(visc), acc[w][m]);
+                if constexpr (T != T_Q6_K)
+                    acc[w][m] = __fmaf_rn(-__fmul_rn(h2f(vmh), vdx), __int2float_rn(vimn), acc[w][m]);
+            }
+        }
+    }
+}
+
+template <int T, int R>
 __global__ void mm_kq_kernel(MMb p) {
     constexpr int UB = T == T_Q4_K ? 144 : T == T_Q5_K ? 176 : 210;
     const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
     const int64_t nu = p.K / 256;
-    const int64_t mgroups = (p.M + KQ_ROWS - 1) / KQ_ROWS;
-    const int64_t ntask = p.N * mgroups * p.B2 * p.B3;
+    const int64_t npair = (p.N + KQ_WR - 1) / KQ_WR;
+    const int64_t mgroups = (p.M + R - 1) / R;
+    const int64_t ntask = npair * mgroups * p.B2 * p.B3;
     for (int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; w < ntask; w += ((int64_t)gridDim.x * blockDim.x) >> 5) {
-        const int64_t n = w % p.N;
-        int64_t t = w / p.N;
+        const int64_t n0 = (w % npair) * KQ_WR;
+        int64_t t = w / npair;
         const int64_t mg = t % mgroups;
         t /= mgroups;
         const int64_t i2 = t % p.B2, i3 = t / p.B2;
         const int64_t a2 = i2 / (p.B2 / p.A2), a3 = i3 / (p.B3 / p.A3);
-        const uint8_t *row = (const uint8_t *)(p.a + n * p.anb1 + a2 * p.anb2 + a3 * p.anb3);
-        const int m0 = (int)(mg * KQ_ROWS);
-        const int mr = (int)(p.M - m0 < KQ_ROWS ? p.M - m0 : KQ_ROWS);
-        const int64_t r0 = m0 + p.M * (i2 + p.B2 * i3);  // activation row index of m0
-        float acc[KQ_ROWS];
+        const uint8_t *rows[KQ_WR];
+        int64_t ulim[KQ_WR];  // super-blocks to load from each weight row (0 past the last row)
 #pragma unroll
-        for (int k = 0; k < KQ_ROWS; k++) acc[k] = 0.0f;
-        for (int64_t s0 = 0; s0 < nu; s0 += 4) {
-            const int64_t s = s0 + grp;
-            const bool have = s < nu;
-            const uint8_t *blk = row + (have ? s : 0) * UB;
-            uint32_t c[8];  // this lane's 32 codes (value order), signed bytes for q6_K
-            int sc0 = 0, sc1 = 0, mn = 0;
-            if (have) {
-                if constexpr (T == T_Q6_K) {
-                    const int h = sub / 4, r = 32 * (sub % 4);  // values 32 sub .. 32 sub + 31
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        const int r4 = r + 4 * i;
-                        const uint32_t ql = ld32a2(blk + 64 * h + r4 % 64), qh = ld32a2(blk + 128 + 32 * h + r4 % 32);
-                        c[i] = __vsub4(((ql >> (4 * (r4 / 64))) & 0x0f0f0f0fu) | (((qh >> (2 * (r4 / 32))) & 0x03030303u) << 4),
-                                       0x20202020u);
-                    }
-                    sc0 = (int8_t)blk[192 + 2 * sub];
-                    sc1 = (int8_t)blk[193 + 2 * sub];
-                } else {
-                    const uint8_t *qs = blk + (T == T_Q4_K ? 16 : 48) + 32 * (sub / 2);
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        uint32_t v = (ld32(qs + 4 * i) >> (4 * (sub % 2))) & 0x0f0f0f0fu;
-                        if constexpr (T == T_Q5_K) v |= ((ld32(blk + 16 + 4 * i) >> sub) & 0x01010101u) << 4;
-                        c[i] = v;
-                    }
-                    kq_scale_min(blk + 4, sub, sc0, mn);
-                }
-            }
-            const uint16_t dh = have ? (uint16_t)ld16(blk + (T == T_Q6_K ? 208 : 0)) : (uint16_t)0;
-            const uint16_t mh = (have && T != T_Q6_K) ? (uint16_t)ld16(blk + 2) : (uint16_t)0;
-            const int base = (int)(s0 & 31), g2 = lane - base;
-            const bool mine = g2 >= 0 && g2 < 4 && s0 + g2 < nu;  // lane owns the chain of super-block s0 + g2
-            const int src = (mine ? g2 : 0) * 8;
-#pragma unroll
-            for (int k = 0; k < KQ_ROWS; k++) {
-                if (k >= mr) break;  // mr is the same on every lane
-                const int64_t r = r0 + k;
-                int isc = 0, imn = 0;
-                float dx = 0.0f;
-                if (have) {
-                    const int8_t *xu = p.x.qx + r * p.K + s * 256 + 32 * sub;
-                    const int4 xa = *(const int4 *)xu, xb = *(const int4 *)(xu + 16);
-                    int t0 = __dp4a((int)c[0], xa.x, 0);
-                    t0 = __dp4a((int)c[1], xa.y, t0);
-                    t0 = __dp4a((int)c[2], xa.z, t0);
-                    t0 = __dp4a((int)c[3], xa.w, t0);
-                    int t1 = __dp4a((int)c[4], xb.x, 0);
-                    t1 = __dp4a((int)c[5], xb.y, t1);
-                    t1 = __dp4a((int)c[6], xb.z, t1);
-                    t1 = __dp4a((int)c[7], xb.w, t1);
-                    if constexpr (T == T_Q6_K) {
-                        isc = sc0 * t0 + sc1 * t1;
-                    } else {
-                        isc = sc0 * (t0 + t1);
-                        const int16_t *bs = p.x.bs + (r * nu + s) * 16;
-                        imn = mn * ((int)bs[2 * sub] + (int)bs[2 * sub + 1]);
-                    }
-                    dx = p.x.dk[r * nu + s];
-                }
-                isc += __shfl_xor_sync(0xffffffffu, isc, 1);
-                isc += __shfl_xor_sync(0xffffffffu, isc, 2);
-                isc += __shfl_xor_sync(0xffffffffu, isc, 4);
-                if constexpr (T != T_Q6_K) {
-                    imn += __shfl_xor_sync(0xffffffffu, imn, 1);
-                    imn += __shfl_xor_sync(0xffffffffu, imn, 2);
-                    imn += __shfl_xor_sync(0xffffffffu, imn, 4);
-                }
-                const int visc = __shfl_sync(0xffffffffu, isc, src), vimn = __shfl_sync(0xffffffffu, imn, src);
-                const float vdx = __shfl_sync(0xffffffffu, dx, src);
-                const uint16_t vdh = (uint16_t)__shfl_sync(0xffffffffu, (int)dh, src);
-                const uint16_t vmh = (uint16_t)__shfl_sync(0xffffffffu, (int)mh, src);
-                if (mine) {
-                    acc[k] = __fmaf_rn(__fmul_rn(h2f(vdh), vdx), __int2float_rn(visc), acc[k]);
-                    if constexpr (T != T_Q6_K) acc[k] = __fmaf_rn(-__fmul_rn(h2f(vmh), vdx), __int2float_rn(vimn), acc[k]);
-                }
-            }
+        for (int r = 0; r < KQ_WR; r++) {
+            const int64_t n = n0 + r < p.N ? n0 + r : n0;
+            rows[r] = (const uint8_t *)(p.a + n * p.anb1 + a2 * p.anb2 + a3 * p.anb3);
+            ulim[r] = n0 + r < p.N ? nu : 0;
         }
+        const int m0 = (int)(mg * R);
+        const int mr = (int)(p.M - m0 < R ? p.M - m0 : R);
+        const int64_t r0 = m0 + p.M * (i2 + p.B2 * i3);  // activation row index of m0
+        float acc[KQ_WR][R];
 #pragma unroll
-        for (int k = 0; k < KQ_ROWS; k++) {
-            if (k >= mr) break;
-            const float v = warp_butterfly(acc[k]);
-            if (lane == 0) p.out[(r0 + k) * p.N + n] = v;
+        for (int r = 0; r < KQ_WR; r++)
+#pragma unroll
+            for (int k = 0; k < R; k++) acc[r][k] = 0.0f;
+        for (int64_t s0 = 0; s0 < nu; s0 += 4) {
+            KqPart parts[KQ_WR];
+#pragma unroll
+            for (int r = 0; r < KQ_WR; r++) kq_load<T>(parts[r], rows[r], s0 + grp, ulim[r], sub);
+            kq_fold<T, R>(parts, p, s0, nu, lane, mr, r0, acc);
+        }
+        (void)UB;
+#pragma unroll
+        for (int r = 0; r < KQ_WR; r++) {
+            if (n0 + r >= p.N) break;
+#pragma unroll
+            for (int k = 0; k < R; k++) {
+                if (k >= mr) break;
+                const float v = warp_butterfly(acc[r][k]);
+                if (lane == 0) p.out[(r0 + k) * p.N + n0 + r] = v;
+            }
         }
     }
 }
@@ -398,14 +462,24 @@ void mul_mat_block(const TD &a, const TD &b, const TD &out, void *scratch, cudaS
     }
     check("act_q8_1 / act_q8_K");
     p.out = (float *)out.data;
-    const unsigned gk = grid_for(p.N * ((p.M + KQ_ROWS - 1) / KQ_ROWS) * p.B2 * p.B3 * 32);
-    switch (a.type) {
-        case T_Q4_1: mm_q1_kernel<T_Q4_1><<<gk, 256, 0, s>>>(p); break;
-        case T_Q5_1: mm_q1_kernel<T_Q5_1><<<gk, 256, 0, s>>>(p); break;
-        case T_Q4_K: mm_kq_kernel<T_Q4_K><<<gk, 256, 0, s>>>(p); break;
-        case T_Q5_K: mm_kq_kernel<T_Q5_K><<<gk, 256, 0, s>>>(p); break;
-        default: mm_kq_kernel<T_Q6_K><<<gk, 256, 0, s>>>(p); break;
+    // one activation row (decode): kernels sized for it; more: KQ_ROWS rows per warp
+    const int R = p.M == 1 ? 1 : KQ_ROWS;
+    const unsigned gk = grid_for(p.N * ((p.M + R - 1) / R) * p.B2 * p.B3 * 32);
+    const unsigned gkq = grid_for((p.N + KQ_WR - 1) / KQ_WR * ((p.M + R - 1) / R) * p.B2 * p.B3 * 32);
+#define GCB_BLOCKQ_LAUNCH(RR)                                                      \
+    switch (a.type) {                                                              \
+        case T_Q4_1: mm_q1_kernel<T_Q4_1, RR><<<gk, 256, 0, s>>>(p); break;        \
+        case T_Q5_1: mm_q1_kernel<T_Q5_1, RR><<<gk, 256, 0, s>>>(p); break;        \
+        case T_Q4_K: mm_kq_kernel<T_Q4_K, RR><<<gkq, 256, 0, s>>>(p); break;       \
+        case T_Q5_K: mm_kq_kernel<T_Q5_K, RR><<<gkq, 256, 0, s>>>(p); break;       \
+        default: mm_kq_kernel<T_Q6_K, RR><<<gkq, 256, 0, s>>>(p); break;           \
     }
+    if (R == 1) {
+        GCB_BLOCKQ_LAUNCH(1)
+    } else {
+        GCB_BLOCKQ_LAUNCH(KQ_ROWS)
+    }
+#undef GCB_BLOCKQ_LAUNCH
     check("mul_mat_block");
 }
 
