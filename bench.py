@@ -355,6 +355,8 @@ def prefill_bench(args) -> None:
         tmp.rename(gguf)
     n_seq, plen, n_dec = 8, 2048, 64
     prompts = np.random.default_rng(2).integers(0, sh.vocab, (n_seq, plen))
+    if args.prefill_attn == "tc":  # read when the model loads
+        os.environ["GGML_COMPILER_B200_PREFILL_ATTN"] = "tc"
     s = Model(gguf)
     g = Decoder(s)
     # warm-up: one sequence (plans and graphs for the 2048-row call and decode at n_kv 2304)
@@ -417,7 +419,9 @@ def prefill_bench(args) -> None:
         "config": {"workload": "llama3-8b-shape Q8_0, 8 x 2048-token prefill (one call each) + 64 decode steps each "
                                "(BASELINE config 4; batch 1 per call: the reference program has no batch dim)",
                    "layers": sh.layers, "d_model": d, "heads": H, "kv_heads": Hkv, "ffn": F, "vocab": sh.vocab,
-                   "weights": "q8_0", "l2": "no flush: each call streams 7.5 GB of weights and GBs of activations"},
+                   "weights": "q8_0", "l2": "no flush: each call streams 7.5 GB of weights and GBs of activations",
+                   "prefill_attn": ("tensor cores (mma.sync f16, within tolerance of the checker)" if args.prefill_attn == "tc"
+                                    else "CUDA cores, bit-exact with the checker")},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s",
                      "frac": achieved / tflops_peak, "kernel": "mul_mat (gemm_tc)",
                      "traffic": GEMM_TRAFFIC_RATIO * gemm_alg_bytes / max(1, mm["launches"]),
@@ -454,6 +458,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="8b", choices=["8b", "70b", "tiny", "sweep", "prefill", "attn", "batch"])
+    ap.add_argument("--prefill-attn", default="exact", choices=["exact", "tc"],
+                    help="prefill: attention on the CUDA cores bit-exact with the checker (exact) or on the tensor cores (tc)")
     ap.add_argument("--shape", default=None, help="sweep: one weight shape NxK")
     ap.add_argument("--m", type=int, default=None, help="sweep: one activation row count")
     ap.add_argument("--wtype", default=None,

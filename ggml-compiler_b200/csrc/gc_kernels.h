@@ -156,7 +156,7 @@ size_t flash_split_counters(const TD &q, const TD &k);
 // again after the wait. Null: every copy after the wait.
 void flash_attn_split(const TD &q, const TD &k, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
                       int *counters, int *err, cudaStream_t s, uint64_t *trace = nullptr, char *act_out = nullptr,
-                      const int32_t *kv_pos = nullptr);
+                      const int32_t *kv_pos = nullptr, bool prefill_tc = false);
 size_t flash_split_ctas(const TD &q, const TD &k);  // CTAs of one split launch (trace slots)
 // One decode row of 2-16 chunks runs as thread-block clusters (one per K/V head, chunk partials
 // merged through distributed shared memory) when such clusters fit; this asks once, outside any
@@ -169,6 +169,10 @@ bool flash_split_prepare(const TD &q, const TD &k, const TD &v, const TD &out);
 bool flash_prefill_ok(const TD &q, const TD &k, const TD &v, const TD &out);
 void flash_prefill(const TD &q, const TD &k, const TD &v, const TD *mask, const TD &out, float scale, int *err,
                    cudaStream_t s);
+// The same shapes on the tensor cores (gc_flash_prefill_tc.cu): within tolerance of the checker, not
+// bit-exact; flash_attn_split takes it instead of flash_prefill when asked (prefill_tc: the model
+// was loaded with GGML_COMPILER_B200_PREFILL_ATTN=tc).
+void flash_prefill_tc(const TD &q, const TD &k, const TD &v, const TD *mask, const TD &out, float scale, cudaStream_t s);
 
 // Tensor-parallel exchange (gc_tp.cu). A window is TP_FLAG_BYTES of flag words (one per sender)
 // followed by two slots of slot_bytes; every rank maps every window.

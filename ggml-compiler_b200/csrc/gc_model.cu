@@ -124,6 +124,7 @@ void Model::load(const char *path, int backend, int dev, bool allow_cpu_fallback
     if (const char *g = std::getenv("GCB_KV_PREFETCH")) kv_prefetch = std::atoi(g);
     if (const char *g = std::getenv("GCB_ATTN_OVERLAP")) attn_overlap = std::atoi(g) != 0;
     if (const char *g = std::getenv("GCB_QKV_ONE_PER_SM")) qkv_one_per_sm = std::atoi(g) != 0;
+    if (const char *g = std::getenv("GGML_COMPILER_B200_PREFILL_ATTN")) prefill_attn_tc = std::strcmp(g, "tc") == 0;
 
     load_weights();
     for (const auto &sy : prog.symbols) binding.push_back(sy.max);

@@ -210,6 +210,9 @@ struct Model {
     // still start only at its tail).
     bool attn_overlap = true;
     bool qkv_one_per_sm = false;
+    // GGML_COMPILER_B200_PREFILL_ATTN=tc: prefill attention (16+ query rows) on the tensor cores,
+    // within tolerance of the checker instead of bit-exact
+    bool prefill_attn_tc = false;
     // Launches run one by one (profiling, graphs off) rather than as one graph: early K/V copies
     // are then off (consecutive steps' launches could overlap under programmatic dependent launch)
     bool direct_launch = false;

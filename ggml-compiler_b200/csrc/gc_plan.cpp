@@ -507,10 +507,11 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
                                    vr != kv_rows.end() && kr->second.data == vr->second.data && q.ne[3] == 1;
                 if (early) pos = kr->second;
                 const bool *direct = &m.direct_launch;
+                const bool tc = m.prefill_attn_tc;
                 add("flash_attn", n.id, {q, kk, v, mk, y, scratch, pos},
-                    [scale, cnt, err, tr, act, early, direct](cudaStream_t st, const std::vector<TD> &t) {
+                    [scale, cnt, err, tr, act, early, direct, tc](cudaStream_t st, const std::vector<TD> &t) {
                         k::flash_attn_split(t[0], t[1], t[2], &t[3], t[4], scale, t[5].data, cnt, err, st, *tr, *act,
-                                            early && !*direct ? (const int32_t *)t[6].data : nullptr);
+                                            early && !*direct ? (const int32_t *)t[6].data : nullptr, tc);
                     },
                     bytes);
                 psteps.back().attn_early = early;
@@ -531,9 +532,11 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
             const bool cluster = k::flash_split_prepare(q, kk, v, y);
             auto tr = trace_slot("flash_attn", n.id, cluster ? (size_t)(((kk.ne[1] + 63) / 64) * kk.ne[2] * q.ne[3])
                                                               : k::flash_split_ctas(q, kk));
+            const bool tc = m.prefill_attn_tc;
             add("flash_attn", n.id, {q, kk, v, y, scratch},
-                [scale, cnt, err, tr](cudaStream_t st, const std::vector<TD> &t) {
-                    k::flash_attn_split(t[0], t[1], t[2], nullptr, t[3], scale, t[4].data, cnt, err, st, *tr, nullptr);
+                [scale, cnt, err, tr, tc](cudaStream_t st, const std::vector<TD> &t) {
+                    k::flash_attn_split(t[0], t[1], t[2], nullptr, t[3], scale, t[4].data, cnt, err, st, *tr, nullptr,
+                                        nullptr, tc);
                 },
                 bytes);
         } else {

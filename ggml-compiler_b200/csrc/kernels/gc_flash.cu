@@ -556,9 +556,11 @@ bool flash_split_prepare(const TD &q, const TD &kk, const TD &v, const TD &out) 
 }
 
 void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, const TD &out, float scale, void *scratch,
-                      int *counters, int *err, cudaStream_t s, uint64_t *trace, char *act_out, const int32_t *kv_pos) {
+                      int *counters, int *err, cudaStream_t s, uint64_t *trace, char *act_out, const int32_t *kv_pos,
+                      bool prefill_tc) {
     if (flash_prefill_ok(q, kk, v, out)) {
-        flash_prefill(q, kk, v, mask, out, scale, err, s);
+        if (prefill_tc) flash_prefill_tc(q, kk, v, mask, out, scale, s);
+        else flash_prefill(q, kk, v, mask, out, scale, err, s);
         return;
     }
     SplitArgs a{};
