@@ -62,6 +62,7 @@ struct SplitArgs {
     char *act_out;    // one query row: its Q8_0 blocks in the GEMV staging layout (K = H x D), or null
     const int32_t *kv_pos;  // cluster kernel: [B] positions the previous kernel writes (early K/V copies)
     int64_t cpc;            // multi-chunk kernel: consecutive chunks per CTA
+    size_t merge_smem;      // multi-chunk kernel: dynamic shared memory the merging CTA may stage partials in
 };
 
 template <int MAXD>
@@ -283,16 +284,31 @@ __global__ void __launch_bounds__(MAXG * WPH * 32, 2) flash_multi_kernel(SplitAr
     }
     __syncthreads();
     if (stamps) stamps[6] = global_ns();
-    if (last)
+    if (last) {
+        // every chunk partial of this (batch, K/V head) into shared memory at once (all warps, many
+        // loads in flight), then the in-order merge from there: same arithmetic, no per-batch L2
+        // round trips in the merging warps
+        const int64_t plen = G * a.nch * (a.D + 2);
+        const float *pg = a.part + ((b * a.H + hk * G) * a.nch) * (a.D + 2);
+        const bool staged = (size_t)plen * 4 <= a.merge_smem;
+        float *pl = (float *)smem;
+        if (staged) {
+            for (int64_t i = threadIdx.x; i < plen; i += blockDim.x) pl[i] = __ldcg(pg + i);
+            __syncthreads();
+        }
         for (int64_t g = warp; g < G; g += blockDim.x / 32) {
             const int64_t h = hk * G + g;
             const int64_t K = a.H * a.D;
             int8_t *qc = a.act_out ? (int8_t *)a.act_out + h * a.D : nullptr;
             float *qd = a.act_out ? (float *)(a.act_out + K) + h * a.D / 32 : nullptr;
             int *qs8 = a.act_out ? (int *)((float *)(a.act_out + K) + K / 32) + h * a.D / 32 : nullptr;
-            flash_merge<MAXD>(a.part + ((b * a.H + h) * a.nch) * (a.D + 2), (int)a.nch, a.out + a.D * (h + a.oH * b), qc, qd,
-                              qs8);
+            float *orow = a.out + a.D * (h + a.oH * b);
+            if (staged)
+                flash_merge<MAXD, true>(pl + g * a.nch * (a.D + 2), (int)a.nch, orow, qc, qd, qs8);
+            else
+                flash_merge<MAXD>(pg + g * a.nch * (a.D + 2), (int)a.nch, orow, qc, qd, qs8);
         }
+    }
     if (stamps) stamps[4] = global_ns();
 }
 
@@ -645,9 +661,29 @@ void flash_attn_split(const TD &q, const TD &kk, const TD &v, const TD *mask, co
             if (mk) {
                 SplitArgs g = c;
                 g.Sq = 1;
-                g.cpc = std::max<int64_t>(1, (a.nch * pairs + wave - 1) / wave);
                 const size_t msmem = smem + (size_t)CH * a.D * 2 * 2;  // the second K/V buffer
                 cudaFuncSetAttribute(mk, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+                g.merge_smem = msmem;
+                // chunks per CTA: the fewest chunk-times over the waves the grid needs, given how many
+                // CTAs are resident at once (fewer chunks per CTA on ties); without an occupancy
+                // answer, two waves of two CTAs per SM
+                int per_sm = 0;
+                if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mk, threads, msmem) != cudaSuccess) {
+                    (void)cudaGetLastError();
+                    per_sm = 0;
+                }
+                if (per_sm > 0) {
+                    const int64_t slots = (int64_t)per_sm * num_sms();
+                    int64_t best = -1, best_cost = 0;
+                    for (int64_t cpc = 1; cpc <= a.nch; cpc++) {
+                        const int64_t ncta = (a.nch + cpc - 1) / cpc * pairs;
+                        const int64_t cost = (ncta + slots - 1) / slots * cpc;
+                        if (best < 0 || cost < best_cost) best = cpc, best_cost = cost;
+                    }
+                    g.cpc = best;
+                } else {
+                    g.cpc = std::max<int64_t>(1, (a.nch * pairs + wave - 1) / wave);
+                }
                 cudaLaunchConfig_t cfg = {};
                 cfg.gridDim = dim3((unsigned)((a.nch + g.cpc - 1) / g.cpc), (unsigned)pairs, 1);
                 cfg.blockDim = dim3(threads);
