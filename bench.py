@@ -261,6 +261,8 @@ def attn(args) -> None:
     from ggml_compiler_b200.runtime import Model
 
     D, H, HKV = 128, 32, 8
+    if args.prefill_attn == "tc":  # read when a model loads
+        os.environ["GGML_COMPILER_B200_PREFILL_ATTN"] = "tc"
     flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
     CACHE.mkdir(parents=True, exist_ok=True)
     for nq, nkv, kind in ATTN_CASES:
@@ -297,7 +299,8 @@ def attn(args) -> None:
         kv_bytes = 2.0 * HKV * nkv * D * 2
         print(json.dumps({"metric": "isolated flash_attn (8B shape)", "case": kind, "rows": nq, "n_kv": nkv, "us": us,
                           "TFLOP_s_visible": flops / (us * 1e-6) / 1e12, "kv_GB_s": kv_bytes / (us * 1e-6) / 1e9,
-                          "reps": args.steps, "l2": "flushed before each rep (256 MB write)"}), flush=True)
+                          "reps": args.steps, "l2": "flushed before each rep (256 MB write)",
+                          "prefill_attn": args.prefill_attn if kind == "prefill" else None}), flush=True)
 
 
 def batch_layers(args) -> None:
