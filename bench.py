@@ -332,6 +332,58 @@ def batch_layers(args) -> None:
                       "weight_gb_s": weight_bytes(sh) / (ms / args.steps / 1000.0) / 1e9, "weights": wt}), flush=True)
 
 
+def layers_decode(args) -> None:
+    """Single-sequence decode at the 8B layer shape on a 2-layer model (d_model 4096, 32 / 8 heads,
+    FFN 14336, vocab 2000) in any weight format (--wtype; the formats this library cannot encode
+    get seeded synthetic blocks): 512 prompt ids, then greedy steps through the generate entry's
+    device loop. One JSON line: tok/s, ms per step and per layer, the step's weight rate. Q4_0 /
+    Q8_0 / q5_0 / iq4_nl groups run fused; q4_1 / q5_1 / K-quant groups run as separate ops."""
+    from ggml_compiler_b200.llm import Decoder, LlamaShape, build_llama_gguf
+    from ggml_compiler_b200.programs import random_block_rows
+    from ggml_compiler_b200.runtime import Model, encode
+    from ggml_compiler_b200.gguf_write import BLOCKS
+
+    wt = args.wtype or "q4_0"
+    sh = LlamaShape(layers=2, d_model=4096, heads=32, kv_heads=8, ffn=14336, vocab=2000, rope_theta=500000.0,
+                    max_context=1024, max_prompt=512, weight_type=wt)
+
+    def encoder(w, typ):
+        if typ in ("iq4_nl", "q4_k", "q5_k", "q6_k"):
+            return random_block_rows(typ, w.shape[0], w.shape[1], seed=w.shape[0] * 7 + w.shape[1])
+        return encode(w, typ)
+
+    CACHE.mkdir(parents=True, exist_ok=True)
+    gguf = CACHE / f"layers2_8b_width_{wt}_seed3.gguf"
+    if not gguf.exists():
+        tmp = gguf.with_suffix(f".part{os.getpid()}")
+        build_llama_gguf(tmp, sh, seed=3, encoder=encoder)
+        tmp.rename(gguf)
+    P, n = 512, max(8, args.steps)
+    wbytes = 0.0
+    from ggml_compiler_b200.llm import llama_weights
+    for _, hf, shape, typ in llama_weights(sh):
+        if "embed_tokens" not in hf:
+            blk, size = BLOCKS[typ]
+            wbytes += float(np.prod(shape)) * size / blk
+    with Model(gguf) as m:
+        d = Decoder(m)
+        gen = m.entries["generate"]
+        prompt = np.random.default_rng(1).integers(0, sh.vocab, P).tolist()
+        ms = 0.0
+        for rep in range(max(3, args.warmup) + 1):
+            d.restart()
+            first = int(np.argmax(d.prompt(prompt)))
+            m.bind(max_new=n)
+            gen.upload({"first": np.array([[first]], np.int32), "start": np.array([P], np.int32)})
+            gen.launch()
+            ms = m.device_ms
+    step = ms / n
+    print(json.dumps({"metric": "single-sequence decode at the 8B layer shape (2 layers)", "weights": wt,
+                      "value": 1000.0 / step, "unit": "tok/s", "steps": n, "ms_per_step": step,
+                      "us_per_layer_incl_head": 1000.0 * step / sh.layers, "weight_gb_s": wbytes / (step / 1000.0) / 1e9,
+                      "weight_bytes_per_step": wbytes}), flush=True)
+
+
 PREFILL_METRIC = "8B-shape Q8_0 prefill tok/s (8 sequences x 2048-token prompts); tensor-core TFLOP/s"
 
 
@@ -460,7 +512,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="8b", choices=["8b", "70b", "tiny", "sweep", "prefill", "attn", "batch"])
+    ap.add_argument("--config", default="8b", choices=["8b", "70b", "tiny", "sweep", "prefill", "attn", "batch", "layers"])
     ap.add_argument("--prefill-attn", default="exact", choices=["exact", "tc"],
                     help="prefill: attention on the CUDA cores bit-exact with the checker (exact) or on the tensor cores (tc)")
     ap.add_argument("--shape", default=None, help="sweep: one weight shape NxK")
@@ -489,6 +541,11 @@ def main() -> None:
         if args.steps == ap.get_default("steps"):
             args.steps = 10
         attn(args)
+        return
+    if args.config == "layers":
+        if args.steps == ap.get_default("steps"):
+            args.steps = 64
+        layers_decode(args)
         return
     if args.config == "batch":
         if args.steps == ap.get_default("steps"):

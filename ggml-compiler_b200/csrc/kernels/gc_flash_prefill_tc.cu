@@ -140,6 +140,37 @@ __global__ void __launch_bounds__(TC_NT) flash_prefill_tc_kernel(TcArgs a) {
     float ma = ninf, mb = ninf, la = 0.0f, lb = 0.0f;  // running maxima (log2 units) and partial sums
     const float sl2 = a.scale * 1.4426950408889634f;   // scores in log2 units
 
+    // This thread's mask values of a chunk as f16 pairs (keys k, k + 1 of rows ra and rb), -inf for
+    // keys past n_kv and rows past Sq; fetched one chunk ahead so the loads overlap the chunk before.
+    // Pairs are one 32-bit load when the mask rows are 4-byte aligned.
+    const bool m32 = a.mask && (a.mnb1 % 4 == 0) && ((uintptr_t)mra % 4 == 0);
+    auto fetch = [&](int64_t c, uint32_t (&mp)[8][2]) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int64_t k0 = c * TC_KC + 8 * j + 2 * tig;
+#pragma unroll
+            for (int rr = 0; rr < 2; rr++) {
+                const bool rowok = (rr == 0 ? ra : rb) < a.Sq;
+                const char *mr = rr == 0 ? mra : mrb;
+                uint32_t v = 0xFC00FC00u;  // -inf, -inf
+                if (rowok && k0 < a.nkv) {
+                    if (!a.mask) {
+                        v = k0 + 1 < a.nkv ? 0u : 0xFC000000u;
+                    } else if (m32 && k0 + 1 < a.nkv) {
+                        v = __ldg((const unsigned int *)(mr + k0 * 2));
+                    } else {
+                        const uint32_t lo = __ldg((const unsigned short *)(mr + k0 * 2));
+                        const uint32_t hi = k0 + 1 < a.nkv ? (uint32_t)__ldg((const unsigned short *)(mr + k0 * 2 + 2)) : 0xFC00u;
+                        v = lo | (hi << 16);
+                    }
+                }
+                mp[j][rr] = v;
+            }
+        }
+    };
+    uint32_t mnext[8][2];
+    fetch(0, mnext);
+
     for (int64_t c = 0; c < nch; c++) {
         const int buf = (int)(c & 1);
         cp_async_wait<0>();
@@ -150,20 +181,15 @@ __global__ void __launch_bounds__(TC_NT) flash_prefill_tc_kernel(TcArgs a) {
         bool hidden = true;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            const int64_t k0 = c * TC_KC + 8 * j + 2 * tig;
 #pragma unroll
             for (int e = 0; e < 4; e++) {
-                const int64_t key = k0 + (e & 1);
-                const bool rowok = (e < 2 ? ra : rb) < a.Sq;
-                float m = ninf;
-                if (rowok && key < a.nkv) {
-                    m = 0.0f;
-                    if (a.mask) m = __half2float(*(const __half *)((e < 2 ? mra : mrb) + key * 2));
-                }
+                const uint32_t pr = mnext[j][e >> 1];
+                const float m = __half2float(__ushort_as_half((unsigned short)((e & 1) ? pr >> 16 : pr & 0xFFFFu)));
                 mk[j][e] = m;
                 hidden = hidden && !(m > -65504.0f);
             }
         }
+        if (c + 1 < nch) fetch(c + 1, mnext);
         // skip only once each row has seen a visible key: a row whose every key is masked with the
         // finite -65504 still averages V uniformly, as the checker does
         const bool live = (ra >= a.Sq || ma > -40000.0f) && (rb >= a.Sq || mb > -40000.0f);
