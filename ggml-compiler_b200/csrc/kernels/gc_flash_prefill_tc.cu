@@ -79,6 +79,14 @@ __device__ __forceinline__ void mma16816(float *c, const uint32_t *a, uint32_t b
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// 2^x by the hardware approximation (PTX ex2.approx, about 2 ulp; -inf gives 0): the
+// probabilities are rounded to f16 right after, so its error is far below the kernel's tolerance
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);
     uint32_t u;
@@ -225,7 +233,7 @@ __global__ void __launch_bounds__(TC_NT) flash_prefill_tc_kernel(TcArgs a) {
         cmb = fmaxf(cmb, __shfl_xor_sync(0xffffffffu, cmb, 1));
         cmb = fmaxf(cmb, __shfl_xor_sync(0xffffffffu, cmb, 2));
         const float na = fmaxf(ma, cma), nb = fmaxf(mb, cmb);
-        const float aa = na == ninf ? 1.0f : exp2f(ma - na), ab = nb == ninf ? 1.0f : exp2f(mb - nb);
+        const float aa = na == ninf ? 1.0f : ex2(ma - na), ab = nb == ninf ? 1.0f : ex2(mb - nb);
         ma = na;
         mb = nb;
         la *= aa;
@@ -240,10 +248,10 @@ __global__ void __launch_bounds__(TC_NT) flash_prefill_tc_kernel(TcArgs a) {
         uint32_t pf[4][4];  // P as A fragments, 4 slices of 16 keys
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            const float p0 = s[j][0] == ninf ? 0.0f : exp2f(s[j][0] - na);
-            const float p1 = s[j][1] == ninf ? 0.0f : exp2f(s[j][1] - na);
-            const float p2 = s[j][2] == ninf ? 0.0f : exp2f(s[j][2] - nb);
-            const float p3 = s[j][3] == ninf ? 0.0f : exp2f(s[j][3] - nb);
+            const float p0 = s[j][0] == ninf ? 0.0f : ex2(s[j][0] - na);
+            const float p1 = s[j][1] == ninf ? 0.0f : ex2(s[j][1] - na);
+            const float p2 = s[j][2] == ninf ? 0.0f : ex2(s[j][2] - nb);
+            const float p3 = s[j][3] == ninf ? 0.0f : ex2(s[j][3] - nb);
             la += p0 + p1;
             lb += p2 + p3;
             pf[j / 2][(j % 2) * 2] = pack_h2(p0, p1);

@@ -43,7 +43,8 @@ def run_mm(tmp_path, raw, typ, x, batch=1):
         return m.entries["main"](x=x.reshape(batch, x.shape[-2], -1))["out.0"].reshape(batch, x.shape[-2], raw.shape[0])
 
 
-CASES = [(256, 1024, 1), (300, 4096, 3), (64, 2048, 8), (100, 1024, 9), (128, 512, 33), (1000, 4096, 1)]
+CASES = [(256, 1024, 1), (300, 4096, 3), (64, 2048, 8), (100, 1024, 9), (128, 512, 33), (1000, 4096, 1),
+         (14336, 4096, 1), (4096, 14336, 8)]  # the last two: BASELINE config 2's FFN shapes
 
 
 @pytest.mark.parametrize("typ", ENCODED + RAW_ONLY)
