@@ -513,6 +513,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="8b", choices=["8b", "70b", "tiny", "sweep", "prefill", "attn", "batch", "layers"])
+    ap.add_argument("--no-tp-probe", action="store_true",
+                    help="N>1 replicas: skip the extra tensor-parallel measurement of the same model")
     ap.add_argument("--prefill-attn", default="exact", choices=["exact", "tc"],
                     help="prefill: attention on the CUDA cores bit-exact with the checker (exact) or on the tensor cores (tc)")
     ap.add_argument("--shape", default=None, help="sweep: one weight shape NxK")
@@ -752,6 +754,25 @@ def decode_bench(args) -> None:
             "weight_gb_s": weight_bytes(sh) / (bms / bsteps / 1000.0) / 1e9,
             "how": "8 sequences prefilled (512 ids each) into KV-cache slots, then generate_batch: one step decodes "
                    "all 8 (tensor-core GEMVs over 8 rows, attention over the 8 slots), device time of the steps"}
+    if world > 1 and not tp and not args.no_tp_probe:
+        # the same model decoded as one sequence split over the N GPUs (the tensor-parallel path:
+        # rows / heads per rank, exchanges over NVLink peer memory), beside the N replicas above
+        try:
+            m.join_tensor_parallel(rank, world, torch_all_gather())
+            tfirst = prefill()
+            generate(tfirst, W)
+            tfirst = prefill()
+            barrier()
+            tms = generate(tfirst, K)
+            barrier()
+            tms = max_over_ranks(tms)
+            out["tensor_parallel"] = {
+                "value": K / (tms / 1000.0), "unit": "tok/s", "ranks": world, "steps": K, "ms_per_step": tms / K,
+                "vs_one_replica": (K / (tms / 1000.0)) / (value / world),
+                "how": "one sequence, rows and heads split over the ranks, four exchanges per layer over NVLink "
+                       "peer memory (bit-exact with one GPU); the headline value is the N replicas"}
+        except Exception as e:  # reported beside the headline number, which stands on its own
+            out["tensor_parallel"] = {"value": None, "error": str(e)[:200]}
     m.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
