@@ -378,8 +378,23 @@ TD Planner::plan_node(const NodeSpec &n, const std::vector<TD> &sv) {
                                       : raw_q           ? (double)a.nrows() * (double)row_size(a.type, a.ne[0])
                                                         : (double)a.nelements() * a.elsize()) +
                              (double)b.nelements() * 4 + (double)y.nelements() * 4;
+        // 2-8 rows whose staged form is too large for the CUDA-core GEMV's shared memory (K = 14336 at
+        // 8 rows) still take the tensor-core GEMV, which stages them itself
+        auto mma_takes = [&]() {
+            if (b.ne[1] < 2 || b.ne[1] > 8 || m.tp.active()) return false;
+            FusedArgs fa;
+            fa.qtype = a.type;
+            fa.pro = PRO_Q8;
+            fa.xq = b.data ? b.data : (const char *)&fa;  // only its presence matters here
+            fa.map = MAP_SINGLE;
+            fa.M = (int)b.ne[1];
+            fa.K = a.ne[0];
+            fa.wrows[0] = a.ne[1];
+            return k::gemv_mma_ok(fa);
+        };
         if (is_quant(a.type) && a.ne[2] == 1 && a.ne[3] == 1 && b.ne[2] == 1 && b.ne[3] == 1 && b.nb[0] == 4 &&
-            (b.ne[1] == 1 || b.nb[1] == 4 * b.ne[0]) && k::fused_gemv_supported(a.ne[0], b.ne[1], MAP_SINGLE)) {
+            (b.ne[1] == 1 || b.nb[1] == 4 * b.ne[0]) &&
+            (k::fused_gemv_supported(a.ne[0], b.ne[1], MAP_SINGLE) || mma_takes())) {
             const int64_t K = a.ne[0], N = a.ne[1], M = b.ne[1];
             // 2-8 rows: quantized once into the staging layout by act_rows, so the GEMV (the
             // tensor-core one where it takes the shape) reads them instead of quantizing per CTA
