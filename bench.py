@@ -564,7 +564,8 @@ def decode_bench(args) -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     sh, workload, P, NKV = shape_for(args.config)
     K, W = min(args.steps, NKV - P), max(3, args.warmup)
-    metric = METRIC if args.config != "70b" else "70B-shape Q4_0 decode tok/s; quant-GEMV HBM GB/s as % of B200 peak"
+    metric = {"70b": "70B-shape Q4_0 decode tok/s; quant-GEMV HBM GB/s as % of B200 peak",
+              "tiny": "tiny-Llama (BASELINE config 1 shape) Q8_0 decode tok/s"}.get(args.config, METRIC)
     wgb = weight_bytes(sh) / 1e9
     tp = world > 1 and args.parallel == "tp"
     config = {"workload": workload, "layers": sh.layers, "d_model": sh.d_model, "heads": sh.heads,
