@@ -79,3 +79,30 @@ def test_gguf_writer_stores_marks(tmp_path):
             assert strip(prog) == want
         else:
             assert prog == want
+
+
+def test_no_mark_when_a_group_value_escapes():
+    """A group whose inner value is read outside it (here: the normed rows also feed a stage output,
+    and a gate/up product read by a later node) is not marked; the rest of the layer still is."""
+    ref = json.loads((GOLDEN / "ref_program_gqa2.json").read_text())["program"]
+    prog = json.loads(json.dumps(ref))
+    st = next(s for s in prog["stages"] if s["name"] == "decode")
+    nodes = st["nodes"]
+    marked = fusion_groups(mark_fusion_groups(prog))["decode"]
+    qkv0 = set(marked["qkv.0"])
+    mul = next(n for n in nodes if n["id"] in qkv0 and n["op"] == "mul")
+    st["outputs"] = st["outputs"] + [mul["id"]]  # the normed rows become a stage output
+    glu0 = set(marked["glu.0"])
+    gate = next(n for n in nodes if n["id"] in glu0 and n["op"] == "mul_mat")
+    nodes.append({"id": f"%{len(nodes)}", "op": "cont", "src": [gate["id"]], "type": "f32", "ne": gate["ne"], "p": {}})
+    again = fusion_groups(mark_fusion_groups(prog))["decode"]
+    kinds = collections.Counter(m.split(".")[0] for m in again)
+    assert kinds == {"qkv": 1, "glu": 1, "resid": 4, "head": 1}
+    assert not (set().union(*again.values()) & (qkv0 | glu0))
+
+
+def test_marking_is_idempotent_and_does_not_touch_input():
+    ref = json.loads((GOLDEN / "ref_program_config1.json").read_text())["program"]
+    once = mark_fusion_groups(ref)
+    assert mark_fusion_groups(once) == once
+    assert "fuse" not in json.dumps(ref)
