@@ -133,3 +133,47 @@ def test_oracle_expanded_formats_are_q8_0_matmuls():
         x = np.random.default_rng(7).standard_normal((9, K)).astype(np.float32)
         if ok:
             np.testing.assert_array_equal(oracle.mul_mat(raw, typ, K, x), oracle.mul_mat(q8, "q8_0", K, x))
+
+
+@pytest.mark.parametrize("typ", ["q4_k", "q6_k", "q4_1"])
+def test_oracle_model_close_to_its_decoded_weights(tmp_path, typ):
+    """A whole decoder in `typ` on the oracle against the same decoder with every block decoded to
+    f32 (the oracle's decoding, pinned to gguf-py above): they differ only by the activation
+    quantization ggml applies for the format (Q8_K / Q8_1), so the logits agree to a few percent of
+    their range and the greedy token is the same."""
+    import gguf
+
+    from ggml_compiler_b200.llm import LlamaShape, build_llama_gguf, llama_weights
+    from ggml_compiler_b200.programs import random_block_rows
+    from oracle.interp import OracleGenerator, Program
+
+    sh = LlamaShape(layers=2, d_model=256, heads=4, kv_heads=2, ffn=512, vocab=128, max_context=768,
+                    max_prompt=64, weight_type=typ)
+
+    def enc(w, t):
+        if t in ENCODED:
+            return runtime.encode(w, t)
+        return random_block_rows(t, w.shape[0], w.shape[1], seed=w.shape[0] * 7 + w.shape[1])
+
+    qpath = tmp_path / f"{typ}.gguf"
+    build_llama_gguf(qpath, sh, seed=21, encoder=enc)
+    hf_of = {g: hf for g, hf, _, _ in llama_weights(sh)}
+    full = {}
+    for t in gguf.GGUFReader(str(qpath)).tensors:
+        shape = tuple(int(x) for x in reversed(t.shape))  # [rows, row length]
+        data = np.asarray(t.data)
+        if t.tensor_type.name.lower() == typ:
+            full[hf_of[t.name]] = oracle.dequantize(data.reshape(shape[0], -1), typ, shape[-1]).reshape(shape)
+        else:
+            full[hf_of[t.name]] = np.asarray(data, np.float32).reshape(shape)
+    fpath = tmp_path / "f32.gguf"
+    build_llama_gguf(fpath, LlamaShape(**{**sh.__dict__, "weight_type": "f32"}), weights=full)
+    prompt = [1, 7, 33, 90, 4, 12]
+    a, b = OracleGenerator(Program(qpath)), OracleGenerator(Program(fpath))
+    a.reset()
+    b.reset()
+    la, lb = a.feed(prompt), b.feed(prompt)
+    rng = float(np.max(np.abs(lb)))
+    # measured: 1.1 % (q4_k), 2.2 % (q6_k), 1.1 % (q4_1) of the logits' range
+    assert float(np.max(np.abs(la - lb))) <= 0.04 * rng, (float(np.max(np.abs(la - lb))), rng)
+    assert int(np.argmax(la)) == int(np.argmax(lb))
