@@ -93,9 +93,10 @@ GGML_COMPILER_API ggml_compiler_options ggml_compiler_default_options(void);
 GGML_COMPILER_API bool                  ggml_compiler_has_backend(ggml_compiler_backend backend);
 
 /* reference :86-87 - encode nrows rows of n_per_row f32 values in a ggml block type, byte for
-   byte as ggml's reference encoder stores them. Types: "q8_0", "q4_0" (also "f32", "f16",
-   "bf16"). Returns the bytes written, or 0 on error (unknown type, n_per_row not a multiple of the
-   block size, dst_size too small). Host code; needs no GPU. */
+   byte as ggml's reference encoder stores them. Types: "q8_0", "q4_0", "q4_1", "q5_0", "q5_1"
+   (also "f32", "f16", "bf16"); iq4_nl and the K-quants are computed with but not encoded here.
+   Returns the bytes written, or 0 on error (unknown or unencodable type, n_per_row not a multiple
+   of the block size, dst_size too small). Host code; needs no GPU. */
 GGML_COMPILER_API size_t ggml_compiler_quantize(const char * type, const float * src, int64_t nrows,
                                                 int64_t n_per_row, void * dst, size_t dst_size);
 /* reference :89 - bytes of one row of n elements of that type; 0 if the type is unknown. */
