@@ -16,7 +16,8 @@
  *
  * This backend runs on NVIDIA B200 GPUs only. Every stage runs as hand-written CUDA kernels; there
  * is no CPU backend and no CPU fallback. Loading with GGML_COMPILER_BACKEND_CPU fails with an
- * error, and ggml_compiler_has_backend(CPU) is false. Quantized weights may be Q4_0 or Q8_0.
+ * error, and ggml_compiler_has_backend(CPU) is false. Quantized weights may be Q4_0, Q8_0, q4_1,
+ * q5_0, q5_1, iq4_nl, q4_K, q5_K or q6_K (the decode layers fuse for Q4_0, Q8_0, q5_0 and iq4_nl).
  */
 #ifndef GGML_COMPILER_RT_H
 #define GGML_COMPILER_RT_H
