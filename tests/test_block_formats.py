@@ -177,3 +177,15 @@ def test_oracle_model_close_to_its_decoded_weights(tmp_path, typ):
     # measured: 1.1 % (q4_k), 2.2 % (q6_k), 1.1 % (q4_1) of the logits' range
     assert float(np.max(np.abs(la - lb))) <= 0.04 * rng, (float(np.max(np.abs(la - lb))), rng)
     assert int(np.argmax(la)) == int(np.argmax(lb))
+
+
+@pytest.mark.parametrize("typ", ENCODED)
+def test_encoder_refusals(rtlib, typ):
+    with pytest.raises(runtime.BackendError, match="multiple of"):
+        runtime.encode(np.zeros((2, 48), np.float32), typ)  # 48 values: not whole 32-blocks
+    # a row of one block at each edge of the code range round-trips through the oracle's decoding
+    x = np.array([np.linspace(-1, 1, 32, dtype=np.float32)])
+    raw = runtime.encode(x, typ)
+    assert raw.shape == (1, oracle.lib().orc_row_size(oracle.TYPES[typ], 32))
+    dec = oracle.dequantize(raw, typ, 32)
+    assert np.max(np.abs(dec - x)) <= 2.0 / (15 if typ == "q4_1" else 31) + 1e-3
