@@ -16,6 +16,13 @@
  *   by d_w * d_x in f32.
  * - mul_mat with an f16 weight converts the activation to f16 first (ggml's vec_dot_type for f16);
  *   products are then exact in f32.
+ * - The other block formats the reference stores weights in (ggml_compiler/quant/types.py:6-19):
+ *   q4_1, q5_0, q5_1 encoders (gguf-py quants.py Q4_1 / Q5_0 / Q5_1 quantize_blocks); the layouts
+ *   of all seven (gguf-py dequantize_blocks, pinned bit for bit by tests/test_block_formats.py);
+ *   q5_0 / iq4_nl matmuls as ggml's vec_dot_q5_0_q8_0 / vec_dot_iq4_nl_q8_0 (a Q8_0 block dot of
+ *   the expanded codes); q4_1 / q5_1 over Q8_1 activations and q4_K / q5_K / q6_K over Q8_K
+ *   activations (ggml quantize_row_q8_1 on x86, quantize_row_q8_K_ref) with the per-unit terms of
+ *   ggml's vec_dot_*_q8_1 / vec_dot_*_q8_K.
  * - rms_norm (ops.cpp:144-148): the sum of squares in double, 1/sqrtf(mean + eps) in float.
  * - rope NEOX (ops.cpp:277-291): angles theta_i = p * s^i by repeated float multiplication,
  *   s = powf(base, -2/n_dims), cos/sin from libm, halves rotated together.
@@ -29,6 +36,8 @@
  * order for every reduction; the B200 kernels follow the same orders, so their decode results can
  * be compared bit for bit. The orders:
  * - 32-lane butterfly: 32 partial sums, then p[i] += p[i ^ off] for off = 16, 8, 4, 2, 1.
+ * - other block formats: unit u (32-block, or 256-value super-block for the K-quants) goes to
+ *   partial u % 32, then the butterfly, for any number of rows.
  * - quantized dot, up to 8 activation rows: block b goes to partial b % 32
  *   (fmaf(d_w*d_x, isum, p)), then the butterfly; 9 or more rows: every block in order into one sum
  *   (the integer block dots are exact, so only the order of the fmaf chain matters).
